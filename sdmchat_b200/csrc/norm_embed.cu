@@ -1,0 +1,174 @@
+// RMSNorm, token-table lookup, SwiGLU activation, RunTimeSdm finish and TrainedSdm value gather.
+#include "kernels.cuh"
+
+namespace sdm {
+
+// RMSNorm.forward (track4_sdmllm_models.py:69-71): y = (x * rsqrt(mean x^2 + eps)).to(T) * w, one warp per row.
+// In bfloat16 the normalised value is rounded before the weight product, whose result is rounded again.
+template <typename T>
+__global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t rows, int d, float eps,
+                               T* __restrict__ y) {
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + row * d;
+  float ss = 0.f;
+  for (int c = lane; c < d; c += 32) {
+    float v = to_f32(xr[c]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  float r = rsqrt_rn(__fdiv_rn(ss, (float)d) + eps);
+  T* yr = y + row * d;
+  for (int c = lane; c < d; c += 32) {
+    float v = round_to<T>(to_f32(xr[c]) * r);
+    yr[c] = from_f32<T>(v * to_f32(w[c]));
+  }
+}
+
+template <typename T>
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restrict__ emb, int64_t N, int d, int V,
+                             T* __restrict__ out, int* bad) {
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (row >= N) return;
+  int id = ids[row];
+  bool ok = id >= 0 && id < V;
+  if (!ok && lane == 0 && bad) atomicExch(bad, 1);
+  for (int c = lane; c < d; c += 32) out[row * d + c] = ok ? emb[(int64_t)id * d + c] : from_f32<T>(0.f);
+}
+
+// SwiGLU activation (track4_sdmllm_models.py:96-97): p = silu(g) * u with the bf16 roundings of a bf16 module.
+template <typename T>
+__global__ void swiglu_act_kernel(const T* __restrict__ g, const T* __restrict__ u, int64_t n, T* __restrict__ p) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    float gv = to_f32(g[i]);
+    float s = round_to<T>(gv / (1.f + expf(-gv)));
+    p[i] = from_f32<T>(s * to_f32(u[i]));
+  }
+}
+
+// RunTimeSdm.finish up to wo (track4_onesdm_models.py:243-246): mean (or sum) read, per-head RMS out-norm with
+// onorm_w.  num (N, h, dh), den (N, h) float32 -> r (N, h*dh) in T.  One warp per (token, head).
+template <typename T>
+__global__ void rt_finish_kernel(const float* __restrict__ num, const float* __restrict__ den, int64_t N, int h,
+                                 int dh, int read_sum, float read_eps, int out_norm, float out_norm_eps,
+                                 const float* __restrict__ onorm_w, T* __restrict__ r) {
+  int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (item >= N * h) return;
+  int hh = (int)(item % h);
+  const float* nr = num + item * dh;
+  float dv = read_sum ? 0.f : den[item] + read_eps;
+  float vals[8];
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    int c = lane + 32 * q;
+    float v = 0.f;
+    if (c < dh) {
+      v = read_sum ? nr[c] : __fdiv_rn(nr[c], dv);
+      ss = fmaf(v, v, ss);
+    }
+    vals[q] = v;
+  }
+  float rs = 1.f;
+  if (out_norm) rs = rsqrt_rn(__fdiv_rn(warp_sum(ss), (float)dh) + out_norm_eps);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    int c = lane + 32 * q;
+    if (c < dh) {
+      float v = vals[q];
+      if (out_norm) v = (v * rs) * onorm_w[hh * dh + c];
+      r[item * dh + c] = from_f32<T>(v);
+    }
+  }
+}
+
+// TrainedSdm read (track4_onesdm_models.py:452-456): r[n, hh, :] = sum_j w[n, hh, j] * values[hh, si[n, hh, j], :]
+// (embedding_bag, mode "sum", accumulated in float32 in j order).  One warp per (token, head).
+template <typename T>
+__global__ void ts_gather_kernel(const int32_t* __restrict__ si, const float* __restrict__ w,
+                                 const T* __restrict__ values, int64_t N, int h, int M, int dh, int k,
+                                 T* __restrict__ r) {
+  int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (item >= N * h) return;
+  int hh = (int)(item % h);
+  const int32_t* sr = si + item * k;
+  const float* wr = w + item * k;
+  for (int c0 = 0; c0 < dh; c0 += 256) {
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+    for (int j = 0; j < k; ++j) {
+      int slot = sr[j];
+      float wj = wr[j];
+      const T* row = values + ((int64_t)hh * M + slot) * dh;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        int c = c0 + lane + 32 * q;
+        if (c < dh) acc[q] = fmaf(wj, to_f32(row[c]), acc[q]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      int c = c0 + lane + 32 * q;
+      if (c < dh) r[item * dh + c] = from_f32<T>(acc[q]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------- launchers
+template <typename T>
+cudaError_t launch_rmsnorm(const T* x, const T* w, int64_t rows, int d, float eps, T* y, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  rmsnorm_kernel<T><<<(unsigned)ceil_div(rows, 8), 256, 0, st>>>(x, w, rows, d, eps, y);
+  return cudaGetLastError();
+}
+template <typename T>
+cudaError_t launch_embed(const int32_t* ids, const T* emb, int64_t N, int d, int V, T* out, int* bad,
+                         cudaStream_t st) {
+  if (N == 0) return cudaSuccess;
+  embed_kernel<T><<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(ids, emb, N, d, V, out, bad);
+  return cudaGetLastError();
+}
+template <typename T>
+cudaError_t launch_swiglu_act(const T* g, const T* u, int64_t n, T* p, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  int64_t blocks = ceil_div(n, 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  swiglu_act_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(g, u, n, p);
+  return cudaGetLastError();
+}
+template <typename T>
+cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int h, int dh, int read_sum,
+                             float read_eps, int out_norm, float out_norm_eps, const float* onorm_w, T* r,
+                             cudaStream_t st) {
+  if (N == 0) return cudaSuccess;
+  rt_finish_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(num, den, N, h, dh, read_sum, read_eps,
+                                                                    out_norm, out_norm_eps, onorm_w, r);
+  return cudaGetLastError();
+}
+template <typename T>
+cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values, int64_t N, int h, int M, int dh,
+                             int k, T* r, cudaStream_t st) {
+  if (N == 0) return cudaSuccess;
+  ts_gather_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r);
+  return cudaGetLastError();
+}
+
+#define SDM_INST(T)                                                                                              \
+  template cudaError_t launch_rmsnorm<T>(const T*, const T*, int64_t, int, float, T*, cudaStream_t);            \
+  template cudaError_t launch_embed<T>(const int32_t*, const T*, int64_t, int, int, T*, int*, cudaStream_t);    \
+  template cudaError_t launch_swiglu_act<T>(const T*, const T*, int64_t, T*, cudaStream_t);                     \
+  template cudaError_t launch_rt_finish<T>(const float*, const float*, int64_t, int, int, int, float, int, float, \
+                                           const float*, T*, cudaStream_t);                                      \
+  template cudaError_t launch_ts_gather<T>(const int32_t*, const float*, const T*, int64_t, int, int, int, int, T*, \
+                                           cudaStream_t);
+SDM_INST(float)
+SDM_INST(bf16_t)
+
+}  // namespace sdm

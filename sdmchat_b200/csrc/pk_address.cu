@@ -1,0 +1,258 @@
+// Product-key addressing on CUDA cores, float32-exact (track4_onesdm_models.py:134-148, soft weights :203-206).
+//
+// One thread owns one (token, head) address.  The address halves are L2-normalised, scored against the head's
+// normalised sub-keys (kept in shared memory), and each half's top-c1 is found with a register bitonic network
+// under the total order (score descending, sub-key index ascending).  The c1 x c1 cartesian combine is never
+// built: a frontier walk over the two sorted lists emits the top-kk combined scores in (score descending,
+// flat index a*c1+b ascending) order, which is the order a stable top-k of the reference's flattened `comb`
+// gives.  Only exactly equal scores can order differently from aten::topk, whose tie order is unspecified.
+#include "kernels.cuh"
+
+namespace sdm {
+
+__device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+template <int C>
+__device__ __forceinline__ void cswap(float (&v)[C], int (&ix)[C], int i, int j, bool sw) {
+  float tv = v[i];
+  int ti = ix[i];
+  v[i] = sw ? v[j] : tv;
+  ix[i] = sw ? ix[j] : ti;
+  v[j] = sw ? tv : v[j];
+  ix[j] = sw ? ti : ix[j];
+}
+
+// Sort C (power of two) elements descending under `better`.
+template <int C>
+__device__ __forceinline__ void bitonic_sort_desc(float (&v)[C], int (&ix)[C]) {
+#pragma unroll
+  for (int size = 2; size <= C; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < C; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool desc = (i & size) == 0;
+          const bool sw = desc ? better(v[j], ix[j], v[i], ix[i]) : better(v[i], ix[i], v[j], ix[j]);
+          cswap<C>(v, ix, i, j, sw);
+        }
+      }
+    }
+  }
+}
+
+// t <- top-C of (t U g), both sorted descending; result sorted descending.
+template <int C>
+__device__ __forceinline__ void merge_top(float (&t)[C], int (&ti)[C], const float (&g)[C], const int (&gi)[C]) {
+#pragma unroll
+  for (int q = 0; q < C; ++q) {
+    const float gv = g[C - 1 - q];
+    const int gx = gi[C - 1 - q];
+    const bool take = better(gv, gx, t[q], ti[q]);
+    t[q] = take ? gv : t[q];
+    ti[q] = take ? gx : ti[q];
+  }
+#pragma unroll
+  for (int stride = C >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int j = i ^ stride;
+      if (j > i) cswap<C>(t, ti, i, j, better(t[j], ti[j], t[i], ti[i]));
+    }
+  }
+}
+
+// Top-C of the n_sub cosine scores of one normalised half against the sub-keys kn (n_sub, HALF) in shared memory.
+template <int HALF, int C>
+__device__ __forceinline__ void half_topc(const float (&zn)[HALF], const float* kn, int n_sub, float (&tv)[C],
+                                          int (&ti)[C]) {
+  for (int g0 = 0; g0 < n_sub; g0 += C) {
+    float gv[C];
+    int gi[C];
+#pragma unroll
+    for (int q = 0; q < C; ++q) {
+      const int j = g0 + q;
+      float s = -INFINITY;
+      if (j < n_sub) {
+        const float* kr = kn + j * HALF;
+        s = 0.f;
+#pragma unroll
+        for (int dd = 0; dd < HALF; ++dd) s = fmaf(zn[dd], kr[dd], s);
+        if (s != s) s = -INFINITY;  // a NaN address orders last, so a padding entry can never be selected
+      }
+      gv[q] = s;
+      gi[q] = j < n_sub ? j : 0x7fffffff;
+    }
+    bitonic_sort_desc<C>(gv, gi);
+    if (g0 == 0) {
+#pragma unroll
+      for (int q = 0; q < C; ++q) {
+        tv[q] = gv[q];
+        ti[q] = gi[q];
+      }
+    } else {
+      merge_top<C>(tv, ti, gv, gi);
+    }
+  }
+}
+
+template <int HALF>
+__device__ __forceinline__ void normalize_half(const float* src, float (&zn)[HALF]) {
+  float ss = 0.f;
+#pragma unroll
+  for (int dd = 0; dd < HALF; ++dd) {
+    zn[dd] = src[dd];
+    ss = fmaf(zn[dd], zn[dd], ss);
+  }
+  const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
+#pragma unroll
+  for (int dd = 0; dd < HALF; ++dd) zn[dd] = __fdiv_rn(zn[dd], nrm);
+}
+
+constexpr int PK_THREADS = 128;
+
+template <int HALF, int C>
+__global__ void __launch_bounds__(PK_THREADS) pk_kernel(PkArgs a, int c1, int kk) {
+  extern __shared__ float pk_smem[];
+  const int hh = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int n_sub = a.n_sub;
+  float* kn1 = pk_smem;                    // (n_sub, HALF)
+  float* kn2 = kn1 + n_sub * HALF;         // (n_sub, HALF)
+  float* v1s = kn2 + n_sub * HALF;         // (C, PK_THREADS) per-thread sorted half lists
+  int* i1s = reinterpret_cast<int*>(v1s + C * PK_THREADS);
+  float* v2s = reinterpret_cast<float*>(i1s + C * PK_THREADS);
+  int* i2s = reinterpret_cast<int*>(v2s + C * PK_THREADS);
+  float* ov = reinterpret_cast<float*>(i2s + C * PK_THREADS);  // (32, PK_THREADS) emitted scores
+  int* oi = reinterpret_cast<int*>(ov + 32 * PK_THREADS);       // (32, PK_THREADS) emitted slot ids
+
+  // F.normalize(keys, dim=-1) for this head
+  for (int j = tid; j < 2 * n_sub; j += PK_THREADS) {
+    const float* src = (j < n_sub ? a.keys1 + ((int64_t)hh * n_sub + j) * HALF
+                                  : a.keys2 + ((int64_t)hh * n_sub + (j - n_sub)) * HALF);
+    float kv[HALF];
+    normalize_half<HALF>(src, kv);
+    float* dst = (j < n_sub ? kn1 + j * HALF : kn2 + (j - n_sub) * HALF);
+#pragma unroll
+    for (int dd = 0; dd < HALF; ++dd) dst[dd] = kv[dd];
+  }
+  __syncthreads();
+
+  const int64_t n = (int64_t)blockIdx.x * PK_THREADS + tid;
+  if (n >= a.N) return;
+  const float* zr = a.z + n * a.ldz + (int64_t)hh * a.d_a;
+  float tv1[C], tv2[C];
+  int ti1[C], ti2[C];
+  {
+    float zn[HALF];
+    normalize_half<HALF>(zr, zn);
+    half_topc<HALF, C>(zn, kn1, n_sub, tv1, ti1);
+    normalize_half<HALF>(zr + HALF, zn);
+    half_topc<HALF, C>(zn, kn2, n_sub, tv2, ti2);
+  }
+#pragma unroll
+  for (int q = 0; q < C; ++q) {
+    v1s[q * PK_THREADS + tid] = tv1[q];
+    i1s[q * PK_THREADS + tid] = ti1[q];
+    v2s[q * PK_THREADS + tid] = tv2[q];
+    i2s[q * PK_THREADS + tid] = ti2[q];
+  }
+  // frontier walk over the c1 x c1 grid: row a's next candidate is (a, fb[a])
+  int fb[C];
+  float fv[C];
+#pragma unroll
+  for (int q = 0; q < C; ++q) {
+    fb[q] = 0;
+    fv[q] = q < c1 ? (tv1[q] + tv2[0]) * 0.5f : -INFINITY;
+  }
+  for (int step = 0; step < kk; ++step) {
+    int best = 0;
+    float bv = fv[0];
+    int bflat = fb[0];
+#pragma unroll
+    for (int q = 1; q < C; ++q) {
+      const int flat = q * c1 + fb[q];
+      const bool take = q <= step && (fv[q] > bv || (fv[q] == bv && flat < bflat));
+      best = take ? q : best;
+      bv = take ? fv[q] : bv;
+      bflat = take ? flat : bflat;
+    }
+    const int b = bflat - best * c1;
+    ov[step * PK_THREADS + tid] = bv;
+    oi[step * PK_THREADS + tid] = i1s[best * PK_THREADS + tid] * n_sub + i2s[b * PK_THREADS + tid];
+    const int nb = b + 1;
+    const float nv = nb < c1 ? (v1s[best * PK_THREADS + tid] + v2s[min(nb, C - 1) * PK_THREADS + tid]) * 0.5f
+                             : -INFINITY;
+#pragma unroll
+    for (int q = 0; q < C; ++q) {
+      if (q == best) {
+        fb[q] = nb;
+        fv[q] = nv;
+      }
+    }
+  }
+  // outputs and softmax(scale * score) (* gate)
+  int64_t dst;
+  if (a.T_bh > 0) {
+    const int64_t bb = n / a.T_bh, t = n % a.T_bh;
+    dst = ((bb * a.h + hh) * a.T_bh + t) * kk;
+  } else {
+    dst = (n * a.h + hh) * kk;
+  }
+  float scale = 0.f, mx = -INFINITY, sum = 0.f, g = 1.f;
+  if (a.w) {
+    scale = expf(a.log_scale[hh]);
+    for (int j = 0; j < kk; ++j) mx = fmaxf(mx, ov[j * PK_THREADS + tid] * scale);
+    for (int j = 0; j < kk; ++j) sum += expf(ov[j * PK_THREADS + tid] * scale - mx);
+    if (a.gate) g = a.gate[n * a.ldgate + hh];
+  }
+  for (int j = 0; j < kk; ++j) {
+    const float s = ov[j * PK_THREADS + tid];
+    a.si[dst + j] = oi[j * PK_THREADS + tid];
+    if (a.sv) a.sv[dst + j] = s;
+    if (a.w) {
+      float wj = __fdiv_rn(expf(s * scale - mx), sum);
+      if (a.gate) wj = wj * g;
+      a.w[dst + j] = wj;
+    }
+  }
+}
+
+template <int HALF, int C>
+static cudaError_t launch_pk_tc(const PkArgs& a, int c1, int kk, cudaStream_t st) {
+  const size_t smem = (size_t)2 * a.n_sub * HALF * 4 + (size_t)4 * C * PK_THREADS * 4 + (size_t)2 * 32 * PK_THREADS * 4;
+  auto kern = pk_kernel<HALF, C>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)ceil_div(a.N, PK_THREADS), (unsigned)a.h);
+  kern<<<grid, PK_THREADS, smem, st>>>(a, c1, kk);
+  return cudaGetLastError();
+}
+
+template <int HALF>
+static cudaError_t launch_pk_half(const PkArgs& a, int c1, int kk, cudaStream_t st) {
+  if (c1 <= 4) return launch_pk_tc<HALF, 4>(a, c1, kk, st);
+  if (c1 <= 8) return launch_pk_tc<HALF, 8>(a, c1, kk, st);
+  if (c1 <= 16) return launch_pk_tc<HALF, 16>(a, c1, kk, st);
+  return launch_pk_tc<HALF, 32>(a, c1, kk, st);
+}
+
+cudaError_t launch_pk_address(const PkArgs& a, cudaStream_t st) {
+  if (a.N == 0) return cudaSuccess;
+  const int c1 = a.k < a.n_sub ? a.k : a.n_sub;
+  const int kk = a.k < c1 * c1 ? a.k : c1 * c1;
+  switch (a.d_a / 2) {
+    case 2: return launch_pk_half<2>(a, c1, kk, st);
+    case 4: return launch_pk_half<4>(a, c1, kk, st);
+    case 6: return launch_pk_half<6>(a, c1, kk, st);
+    case 8: return launch_pk_half<8>(a, c1, kk, st);
+    case 16: return launch_pk_half<16>(a, c1, kk, st);
+    case 32: return launch_pk_half<32>(a, c1, kk, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace sdm

@@ -1,0 +1,127 @@
+"""GPU parity at BASELINE's shapes: the d768 / 12 heads x 64 / k16 / 1,024-slot layer against the CPU oracle on
+identical inputs, and size-independent properties of the full FULL d768 L12 T2048 stack (determinism, causality,
+loss = CE of its own logits, decode = recurrence across a state renormalisation)."""
+import numpy as np
+import pytest
+import torch
+
+import sdmchat_b200 as S
+from goldens import rel
+from oracle import sdm_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def zipf_ids(rng, shape, V=32768, s=1.1):
+    return np.minimum(rng.zipf(s, size=shape) - 1, V - 1).astype(np.int64)
+
+
+def d768_layer(seed=0, k=16, fades=None):
+    torch.manual_seed(seed)
+    m = S.RunTimeSdm(768, heads=12, n_sub=32, d_a=32, k=k, decays=fades or S.readme_fades(12))
+    with torch.no_grad():
+        for lin in (m.wk, m.wq, m.wv):
+            torch.nn.init.normal_(lin.weight, std=0.02)
+        torch.nn.init.normal_(m.wo.weight, std=0.02)
+        torch.nn.init.normal_(m.wg.weight, std=0.5 / 768 ** 0.5)
+    return m
+
+
+def oracle_params(m):
+    sd = {k: v.detach().float().cpu().numpy() for k, v in m.state_dict().items()}
+    return O.RunTimeSdmParams(sd, m.h, m.n_sub, m.d_a, m.k)
+
+
+def test_d768_layer_bf16_against_oracle(cuda_ok):
+    rng = np.random.default_rng(1)
+    m = d768_layer()
+    m = m.to(DEV).to(torch.bfloat16)
+    emb = (rng.standard_normal((32768, 768)) * 0.02).astype(np.float32)
+    ids = zipf_ids(rng, (2, 512))
+    x = O.bf16(emb[ids])
+    with torch.no_grad():
+        out, o = m.forward_with(torch.from_numpy(x).to(DEV).bfloat16())
+    p = oracle_params(m)
+    want, st = O.rt_forward(p, x, bf16_stream=True)
+    flips = 0
+    for key, mk in (("siw", "margin_w"), ("sir", "margin_r")):
+        got = o[key].cpu().numpy()
+        bad = (np.sort(got, -1) != np.sort(st[key], -1)).any(-1)
+        live = st[mk] > 1e-6
+        assert not (bad & live).any(), f"{key}: {(bad & live).sum()} flips above margin 1e-6"
+        flips += int(bad.sum())
+    assert flips <= 0.001 * 2 * 2 * 12 * 512  # near-tie flips only
+    num = o["num"].cpu().numpy().transpose(0, 2, 1, 3)
+    assert rel(num, st["num"]) < 2e-3
+    assert rel(m.last_state[0].cpu().numpy(), st["mem"]) < 2e-3
+    assert rel(m.last_state[1].cpu().numpy(), st["cnt"]) < 2e-3
+    assert rel(out.float().cpu().numpy(), want) < 2e-3
+
+
+def test_state_renormalisation_in_decode(cuda_ok):
+    """fade 0.8 over 400 tokens drives the lazy scale below 2^-60 (0.8^187): the decode path folds it into the
+    state and still equals the chunked form; fade 0 exercises the cleared previous rows."""
+    torch.manual_seed(3)
+    m = S.RunTimeSdm(128, heads=4, n_sub=16, d_a=16, k=8, decays=(0.8, 0.0, 0.5, 0.97)).to(DEV)
+    with torch.no_grad():
+        torch.nn.init.normal_(m.wo.weight, std=0.3)
+        torch.nn.init.normal_(m.wg.weight, std=0.5)
+        x = torch.randn(3, 400, 128, device=DEV)
+        a = m(x)
+        mem_a = m.last_state[0].clone()
+        b = m.forward_sequential(x)
+        mem_b = m.last_state[0]
+    torch.testing.assert_close(b, a, atol=1e-5, rtol=1e-4)
+    assert float((mem_b - mem_a).abs().max() / mem_a.abs().max()) < 1e-4
+
+
+def full_model(layers=12, seed=0):
+    torch.manual_seed(seed)
+    model = S.build_onesdm("onesdm_allsdm", 32768, dict(d=768, layers=layers, mlp_f=2048, heads=12,
+                                                         decays=S.readme_fades(12)))
+    with torch.no_grad():
+        for m in model.mems:
+            torch.nn.init.normal_(m.wo.weight, std=0.02)
+            torch.nn.init.normal_(m.wg.weight, std=0.5 / 768 ** 0.5)
+        for s in model.sdms:
+            torch.nn.init.normal_(s.values, std=0.02)
+    return model.to_bf16_stream().to(DEV)
+
+
+def test_full_d768_L12_T2048_properties(cuda_ok):
+    rng = np.random.default_rng(2)
+    model = full_model()
+    idx = torch.from_numpy(zipf_ids(rng, (2, 2048))).to(DEV)
+    with torch.no_grad():
+        a = model(idx)
+        b = model(idx)
+        assert torch.isfinite(a.float()).all()
+        assert torch.equal(a, b), "forward is not bit-reproducible"
+        idx2 = idx.clone()
+        p = 1500
+        idx2[:, p] = (idx2[:, p] + 5) % 32768
+        c = model(idx2)
+        assert torch.equal(a[:, :p], c[:, :p]), "a later token changed an earlier position (causality)"
+        assert not torch.equal(a[:, p:], c[:, p:])
+        tgt = torch.roll(idx, -1, 1)
+        tgt[:, -1] = -1
+        loss = float(model.loss_sum(idx, tgt).item())
+        lg = a.double()[:, :-1]
+        want = float((torch.logsumexp(lg, -1) - lg.gather(-1, idx[:, 1:, None])[..., 0]).sum())
+    assert abs(loss - want) / abs(want) < 1e-4
+
+
+def test_full_decode_matches_prefill(cuda_ok):
+    """Greedy decode on the carried state = argmax of the chunked forward on the whole prefix."""
+    rng = np.random.default_rng(4)
+    model = full_model(layers=2, seed=1)
+    idx = torch.from_numpy(zipf_ids(rng, (4, 300))).to(DEV)
+    with torch.no_grad():
+        gen = model.generate(idx, 8)
+        seq = torch.cat([idx, gen], 1)
+        lg = model(seq[:, :-1]).float()[:, 299:]
+    top = torch.topk(lg, 2, -1).values
+    clear = (top[..., 0] - top[..., 1]) > 1e-2
+    assert (lg.argmax(-1) == gen)[clear].all()
+    assert clear.float().mean() > 0.5
