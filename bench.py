@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""Benchmark of the SDMCHAT FULL arm (onesdm_allsdm) d768 L12 T2048 on B200: prefill + tied-head loss tokens/s.
+
+    python bench.py [--gpus N --steps K --warmup W]              this build (libsdm_b200, sm_100a)
+    python bench.py --impl reference [...]                        the reference algorithm on the host CPU cores
+    torchrun --nproc-per-node N bench.py --gpus N ...             one process per GPU (NCCL)
+
+Workload: OneSdmLM FULL arm, d 768, 12 layers, 12 run-time memory heads x 64, 1,024 slots per
+head (32 x 32 product keys), k 16, fades (0, .8, .99, 1) x 3, TrainedSdm body at the reference defaults (4 heads,
+n_sub 72, k 32, value width 192), tied 32,768-row token table; bf16 weights and activations, float32 memory state.
+Weights: random init of that architecture (seed 0) with the zero-initialised output maps / value tables perturbed
+(std 0.02) so no module is a no-op.  Data: synthetic Zipf(1.1) token ids (numpy default_rng, ids = min(rank-1,
+32767)), 32 rows x 2048 tokens per GPU (weak scaling: global batch 32 * N).  A step = forward of every row + the
+tied-head cross-entropy sum against the next token, then an NCCL all-reduce of (loss sum, token count) when N > 1.
+Every step's working set (activations, 0.4 GB per layer) is larger than the 126 MB L2, so no L2 flush is added.
+
+The JSON line adds: e2e (the same step through the public API from pinned host ids, H2D + D2H inside the timed
+region), decode (config 4: 32 streams per GPU carried-state greedy decode after a 2,048-token prefill), roofline of
+the dominant kernel (measured live with CUDA events around every launch of the timed region), cpu_baseline (the CPU
+oracle port of the reference algorithm, bounded sample, rank 0 at N = 1), clocks sampled during the timed region.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+V, D, LAYERS, HEADS, T_SEQ, ROWS = 32768, 768, 12, 12, 2048, 32
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--rows", type=int, default=ROWS, help="rows of T_SEQ tokens per GPU")
+    ap.add_argument("--seq", type=int, default=T_SEQ)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--decode-streams", type=int, default=32)
+    ap.add_argument("--decode-steps", type=int, default=64)
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def zipf_ids(seed, rows, T):
+    rng = np.random.default_rng(seed)
+    return np.minimum(rng.zipf(1.1, size=(rows, T)) - 1, V - 1).astype(np.int64)
+
+
+def model_cfg(layers):
+    return dict(d=D, layers=layers, mlp_f=2048, heads=HEADS, n_sub=32, d_a=32, k=16,
+                decays=(0.0, 0.8, 0.99, 1.0) * (HEADS // 4))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            js = json.load(f)
+        return {k: float(js[k]) for k in FALLBACK_PEAKS}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ------------------------------------------------------------------------------------------- reference (CPU)
+def oracle_params(layers, seed=0):
+    """The benchmark model's weights (same seed and perturbation as the GPU arm) as oracle parameter objects."""
+    import torch
+    import sdmchat_b200 as S
+    from oracle import sdm_oracle as O
+    torch.manual_seed(seed)
+    model = S.build_onesdm("onesdm_allsdm", V, model_cfg(layers))
+    perturb(model)
+    sd = {k: v.to(torch.bfloat16).float().numpy() if v.dim() >= 1 and not k.endswith(
+        ("keys1", "keys2", "addr_b", "log_scale", "onorm_w", "wg.bias", "decays_fixed")) else v.float().numpy()
+          for k, v in model.state_dict().items()}
+    P = {"emb": sd["emb.weight"], "nf_w": sd["nf.w"], "layers": []}
+    for i in range(layers):
+        msd = {k[len(f"mems.{i}."):]: v for k, v in sd.items() if k.startswith(f"mems.{i}.")}
+        ssd = {k[len(f"sdms.{i}."):]: v for k, v in sd.items() if k.startswith(f"sdms.{i}.")}
+        P["layers"].append({"mem": O.RunTimeSdmParams(msd, HEADS, 32, 32, 16),
+                            "sdm": O.TrainedSdmParams(ssd, 4, model.sdm_n_sub, model.sdm_d_a, 32)})
+    return P
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        return max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def time_oracle(P, tokens, reps=1):
+    """Best-of-reps wall time of the oracle forward + CE sum on one row of `tokens` ids (cost_bench's method,
+    track4_onesdm_puzzles.py:342-377)."""
+    from oracle import sdm_oracle as O
+    ids = zipf_ids(99, 1, tokens + 1)
+    O.lm_forward(P, ids[:, :16], bf16_stream=True, margins=False)  # warm
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        lg = O.lm_forward(P, ids[:, :-1], bf16_stream=True, margins=False)
+        O.ce_sum(lg, ids[:, 1:])
+        best = min(best, time.perf_counter() - t0)
+    return tokens / best
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    P = oracle_params(a.layers)
+    tokens = 64
+    from oracle import sdm_oracle as O
+    ids = zipf_ids(99, 1, tokens + 1)
+    for _ in range(a.warmup):
+        O.lm_forward(P, ids[:, :-1], bf16_stream=True, margins=False)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        lg = O.lm_forward(P, ids[:, :-1], bf16_stream=True, margins=False)
+        O.ce_sum(lg, ids[:, 1:])
+    dt = time.perf_counter() - t0
+    val = tokens * a.steps / dt
+    cores = cpu_threads()
+    sample = f"1 row x {tokens} tokens per step of the FULL d768 L{a.layers} forward + CE (numpy float32 oracle port)"
+    out = {"metric": "tokens/sec FULL d768 L12 T2048 prefill (forward + tied-head CE sum)", "impl": "reference",
+           "value": round(val, 3), "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+           "ms_per_step": round(1e3 * dt / a.steps, 3), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic Zipf(1.1) token ids",
+           "config": {"workload": f"FULL onesdm_allsdm d768 L{a.layers} h12x64 k16 V32768, host CPU oracle port"},
+           "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------- ours (GPU)
+def perturb(model):
+    import torch
+    with torch.no_grad():
+        for m in model.mems:
+            torch.nn.init.normal_(m.wo.weight, std=0.02)
+            torch.nn.init.normal_(m.wg.weight, std=0.5 / D ** 0.5)
+        for s in getattr(model, "sdms", []):
+            torch.nn.init.normal_(s.values, std=0.02)
+
+
+class Clocks:
+    """nvidia-smi samples of this GPU's clocks and throttle reasons while the timed region runs."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev_index):
+        self.proc = None
+        self.lines = []
+        try:
+            import torch
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(dev_index).uuid)
+            self.cmd = ["nvidia-smi", "-i", uuid, f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                        "-lms", "100"]
+        except Exception:
+            self.cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100"]
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=lambda: self.lines.extend(self.proc.stdout), daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gemm_flops(tag, rows, layers):
+    """Algorithmic FLOPs of the tensor-core GEMM launches of one step, by call site (2 * rows * K * N of the
+    reference's matmul; the float32-accurate hi/lo split of the wo inputs is not counted)."""
+    hda, C = HEADS * 32, 2 * HEADS * 32 + D + HEADS
+    per_row = {"rt_proj": 2 * D * C, "rt_out": 2 * D * D, "ts": 2 * D * (4 * 32) + 2 * D * D,
+               "head_ce": 2 * D * V, "head_logits": 2 * D * V, "head_argmax": 2 * D * V}
+    del hda
+    return per_row.get(tag, 0) * rows
+
+
+def scan_bytes(rows_tokens):
+    """Compulsory HBM bytes of the scan per launch: per (token, head) it reads k (slot id, weight) pairs for the
+    write and the read (16 * 16 B), the value row (64 float32) and writes num (64 float32) + den."""
+    return rows_tokens * HEADS * (16 * 16 + 64 * 4 + 64 * 4 + 4)
+
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+    import sdmchat_b200 as S
+    from sdmchat_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    lib = _lib.lib()
+
+    torch.manual_seed(0)
+    model = S.build_onesdm("onesdm_allsdm", V, model_cfg(a.layers))
+    perturb(model)
+    model = model.to_bf16_stream().to(dev)
+    B, T = a.rows, a.seq
+    ids_np = zipf_ids(1000 + rank, B, T + 1)
+    ids_host = torch.from_numpy(ids_np[:, :-1].astype(np.int32)).pin_memory()
+    tgt_host = torch.from_numpy(ids_np[:, 1:].astype(np.int32)).pin_memory()
+    ids = ids_host.to(dev)
+    tgt = tgt_host.to(dev)
+    loss_buf = torch.zeros(2, dtype=torch.float64, device=dev)  # (loss sum, token count)
+
+    def step(idx, tg):
+        loss_buf.zero_()
+        with torch.no_grad():
+            model.loss_sum(idx, tg, out=loss_buf[:1])
+        loss_buf[1] = float(B * T)
+        if world > 1:
+            dist.all_reduce(loss_buf)
+        return loss_buf
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(a.warmup):
+        step(ids, tgt)
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = lib.sdm_kernel_launch_count()
+    lib.sdm_profile_begin()
+    e0.record(st)
+    for _ in range(a.steps):
+        step(ids, tgt)
+    e1.record(st)
+    torch.cuda.synchronize()
+    groups = _lib.profile_groups()
+    launches = lib.sdm_kernel_launch_count() - n0
+    barrier()
+    clk = clocks.stop()
+    t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    loss_mean = float(loss_buf[0].item() / loss_buf[1].item())
+    tokens = world * B * T * a.steps
+    value = tokens / t_dev
+
+    # e2e: the same step through the public API from pinned host memory, loss read back every step
+    host_loss = torch.zeros(2, dtype=torch.float64).pin_memory()
+    for _ in range(2):
+        ids.copy_(ids_host, non_blocking=True)
+        tgt.copy_(tgt_host, non_blocking=True)
+        host_loss.copy_(step(ids, tgt), non_blocking=True)
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(st)
+    for _ in range(a.steps):
+        ids.copy_(ids_host, non_blocking=True)
+        tgt.copy_(tgt_host, non_blocking=True)
+        host_loss.copy_(step(ids, tgt), non_blocking=True)
+    e3.record(st)
+    torch.cuda.synchronize()
+    barrier()
+    t_e2e = max_over_ranks(e2.elapsed_time(e3) / 1e3)
+    e2e = {"value": round(tokens / t_e2e, 1), "unit": "tokens/s",
+           "h2d_bytes_per_step": int(ids_host.numel() * 4 + tgt_host.numel() * 4), "d2h_bytes_per_step": 16}
+
+    # roofline of the dominant kernel, from the events recorded around every launch of the timed region
+    pk, how = peaks()
+    per_kernel = {}
+    for k, tag, n, ms in groups:
+        d = per_kernel.setdefault(k, {"launches": 0, "ms": 0.0, "tags": {}})
+        d["launches"] += n
+        d["ms"] += ms
+        d["tags"][tag] = d["tags"].get(tag, 0.0) + ms
+    dom = max(per_kernel, key=lambda k: per_kernel[k]["ms"])
+    rows_tokens = B * T
+    if dom == "gemm_tc":
+        flops = sum(gemm_flops(tag, rows_tokens, a.layers) * n for k, tag, n, ms in groups if k == "gemm_tc")
+        launches_dom = per_kernel[dom]["launches"]
+        ach = flops / (per_kernel[dom]["ms"] / 1e3) / 1e12
+        roof = {"kernel": "gemm_tc (tcgen05 bf16 GEMM, all call sites)", "bound": "tensor",
+                "achieved": round(ach, 1), "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": round(ach / pk["bf16_tflops_sustained"], 4), "traffic": None,
+                "peak_source": f"{how} bf16_tflops_sustained",
+                "avg_launch_ms": round(per_kernel[dom]["ms"] / launches_dom, 4)}
+    else:
+        n_scan = per_kernel[dom]["launches"]
+        byts = scan_bytes(rows_tokens) * n_scan
+        ach = byts / (per_kernel[dom]["ms"] / 1e3) / 1e9
+        roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(ach / pk["hbm_gbs"], 4), "traffic": None, "peak_source": f"{how} hbm_gbs"}
+    breakdown = {k: {"ms_per_step": round(v["ms"] / a.steps, 3), "launches_per_step": v["launches"] / a.steps}
+                 for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1]["ms"])}
+
+    # decode (config 4): S streams per GPU, 2,048-token prompt prefilled, then carried-state greedy steps
+    decode = None
+    if not a.no_decode:
+        Sd = a.decode_streams
+        prompt = torch.from_numpy(zipf_ids(2000 + rank, Sd, T)).to(dev)
+        with torch.no_grad():
+            state = model.init_decode(Sd, dev)
+            nxt = model.prefill(prompt, state)
+            for _ in range(3):
+                nxt = model.decode_step(nxt, state)
+            barrier()
+            e4, e5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e4.record(st)
+            for _ in range(a.decode_steps):
+                nxt = model.decode_step(nxt, state)
+            e5.record(st)
+            torch.cuda.synchronize()
+        barrier()
+        t_dec = max_over_ranks(e4.elapsed_time(e5) / 1e3)
+        decode = {"value": round(world * Sd * a.decode_steps / t_dec, 1), "unit": "tokens/s",
+                  "streams_per_gpu": Sd, "prompt": T, "steps": a.decode_steps,
+                  "ms_per_step": round(1e3 * t_dec / a.decode_steps, 3)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        P = oracle_params(a.layers)
+        tok = 128
+        v = time_oracle(P, tok)
+        cpu = {"value": round(v, 2), "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+               "sample": f"1 row x {tok} tokens of the same FULL d768 L{a.layers} model, forward + CE sum, "
+                         "numpy float32 oracle port (best of 1 after a warm run)"}
+
+    if rank == 0:
+        out = {"metric": "tokens/sec FULL d768 L12 T2048 prefill (forward + tied-head CE sum)",
+               "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+               "warmup": a.warmup, "ms_per_step": round(1e3 * t_dev / a.steps, 3), "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic Zipf(1.1) token ids; random-init weights (seed 0, output maps perturbed)",
+               "config": {"workload": f"FULL onesdm_allsdm d768 L{a.layers} h12x64 M1024 k16, TrainedSdm n_sub72 "
+                                      f"k32, V32768, {B} rows x {T} tokens per GPU",
+                          "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world} (batch shards)",
+                          "l2": "per-step working set > 126 MB L2 (no flush)"},
+               "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu,
+               "clocks": clk, "decode": decode, "loss_mean": round(loss_mean, 5), "kernels": breakdown}
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

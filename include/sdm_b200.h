@@ -45,6 +45,18 @@ enum { SDM_F32 = 0, SDM_BF16 = 1 };
 int sdm_abi_version(void);
 /* Static text for a status code. */
 const char* sdm_status_string(sdm_status s);
+/* Number of kernels this library has launched since it was loaded (host-side counter; for launch accounting). */
+int64_t sdm_kernel_launch_count(void);
+/* Launch profiler: between sdm_profile_begin() and sdm_profile_end() every launch is bracketed by CUDA events on
+ * its stream.  sdm_profile_end() synchronises those events and returns the number of (kernel, call-site tag)
+ * groups (or -1 on a CUDA error); sdm_profile_group(i, ...) reports group i: kernel and tag names (NUL-terminated,
+ * at most name_len bytes), launch count and summed device milliseconds. */
+sdm_status sdm_profile_begin(void);
+int sdm_profile_end(void);
+sdm_status sdm_profile_group(int i, char* kernel, char* tag, int name_len, int* launches, double* total_ms);
+/* Synchronises `stream`, then reports SDM_ERR_TIMEOUT if any bounded device-side wait (the tensor-core GEMM's
+ * mbarrier waits give up after about 4 s) gave up since the previous call, and clears the flag. */
+sdm_status sdm_device_status(void* stream);
 
 /* ---------------------------------------------------------------------------------------- product-key address
  * pk_address (M:134-148).  z (N, h, d_a) float32, keys1/keys2 (h, n_sub, d_a/2) float32 ->

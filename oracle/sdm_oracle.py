@@ -131,15 +131,19 @@ class RunTimeSdmParams:
         self.read_eps, self.out_norm_eps = F32(read_eps), F32(out_norm_eps)
 
 
-def rt_prepare(p, x, bf16_stream=False):
+def rt_prepare(p, x, bf16_stream=False, margins=True):
     """RunTimeSdm.prepare (M:195-213): x (B, T, d) -> siw, ww, sir, wr (B, h, T, k), V (B, h, T, dh), gate
-    (B, T, h), and the address margins of the write and read selections (B, h, T)."""
+    (B, T, h), and (with margins) the address margins of the write and read selections (B, h, T)."""
     B, T, _ = x.shape
     hx = rmsnorm(x, p.norm_w, bf16_stream=bf16_stream).reshape(B * T, p.d)
     kz = linear(hx, p.wk).reshape(B * T, p.h, p.d_a) + p.addr_b
     qz = linear(hx, p.wq).reshape(B * T, p.h, p.d_a) + p.addr_b
-    svw, siw, mw = pk_address(kz, p.keys1, p.keys2, p.k, return_margin=True)
-    svr, sir, mr = pk_address(qz, p.keys1, p.keys2, p.k, return_margin=True)
+    if margins:
+        svw, siw, mw = pk_address(kz, p.keys1, p.keys2, p.k, return_margin=True)
+        svr, sir, mr = pk_address(qz, p.keys1, p.keys2, p.k, return_margin=True)
+    else:
+        (svw, siw), (svr, sir) = pk_address(kz, p.keys1, p.keys2, p.k), pk_address(qz, p.keys1, p.keys2, p.k)
+        mw = mr = np.full(siw.shape[:2], np.inf, F32)
     scale = np.exp(p.log_scale)[None, :, None].astype(F32)
     ww = softmax((svw * scale).astype(F32))
     wr = softmax((svr * scale).astype(F32))
@@ -251,9 +255,9 @@ def rt_finish(p, num, den, bf16_out=False):
     return linear(y, p.wo, bf16_out=bf16_out)
 
 
-def rt_forward(p, x, chunk=128, reset=None, bf16_stream=False, sequential=False):
+def rt_forward(p, x, chunk=128, reset=None, bf16_stream=False, sequential=False, margins=True):
     """RunTimeSdm.forward (M:249-274) / forward_sequential (M:276-300): returns (out, dict of intermediates)."""
-    prep = rt_prepare(p, x, bf16_stream)
+    prep = rt_prepare(p, x, bf16_stream, margins)
     if sequential:
         num, den, mem, cnt = rt_scan_sequential(prep, p.lam, p.M, reset)
     else:
@@ -276,12 +280,15 @@ class TrainedSdmParams:
         self.dh, self.M = self.d // heads, n_sub * n_sub
 
 
-def trained_sdm(p, x, bf16_stream=False):
+def trained_sdm(p, x, bf16_stream=False, margins=True):
     """TrainedSdm.address + forward (M:438-457): q = wq RMSNorm(x); product-key top-k; softmax; weighted sum of
     the picked value rows (embedding_bag, sum mode); wo.  Returns (out, si, margin)."""
     B, T, _ = x.shape
     q = linear(rmsnorm(x, p.norm_w, bf16_stream=bf16_stream).reshape(B * T, p.d), p.wq).reshape(B * T, p.h, p.d_a)
-    sv, si, margin = pk_address(q, p.keys1, p.keys2, p.k, return_margin=True)
+    if margins:
+        sv, si, margin = pk_address(q, p.keys1, p.keys2, p.k, return_margin=True)
+    else:
+        (sv, si), margin = pk_address(q, p.keys1, p.keys2, p.k), None
     w = softmax((sv * np.exp(p.log_scale)[None, :, None]).astype(F32))
     r = np.zeros((B * T, p.h, p.dh), F32)
     for j in range(si.shape[-1]):
@@ -308,7 +315,7 @@ def add_stream(x, y, bf16_stream):
     return bf16(s) if bf16_stream else s
 
 
-def lm_forward(P, idx, bf16_stream=True, chunk=128, reset_at_bos=False, bos_id=0, collect=False):
+def lm_forward(P, idx, bf16_stream=True, chunk=128, reset_at_bos=False, bos_id=0, collect=False, margins=True):
     """OneSdmLM.forward (M:525-555): enfold, L x (RunTimeSdm, then SwiGLU(RMSNorm) or TrainedSdm), nf, tied
     logits.  P is a dict: emb (V, d), nf_w (d,), layers: list of dicts with 'mem' (RunTimeSdmParams) and either
     'mlp' = (mnorm_w, wg, wu, wd) or 'sdm' (TrainedSdmParams).  Returns logits (B, T, V) and, with collect, the
@@ -318,7 +325,7 @@ def lm_forward(P, idx, bf16_stream=True, chunk=128, reset_at_bos=False, bos_id=0
     trace = []
     for lay in P["layers"]:
         rec = {"x_in": x}
-        m_out, prep = rt_forward(lay["mem"], x, chunk=chunk, reset=reset, bf16_stream=bf16_stream)
+        m_out, prep = rt_forward(lay["mem"], x, chunk=chunk, reset=reset, bf16_stream=bf16_stream, margins=margins)
         x = add_stream(x, m_out, bf16_stream)
         rec["prep"] = prep
         rec["x_mid"] = x
@@ -326,7 +333,7 @@ def lm_forward(P, idx, bf16_stream=True, chunk=128, reset_at_bos=False, bos_id=0
             nw, wg, wu, wd = lay["mlp"]
             x = add_stream(x, swiglu(rmsnorm(x, nw, bf16_stream=bf16_stream), wg, wu, wd, bf16_stream), bf16_stream)
         else:
-            s_out, si, margin = trained_sdm(lay["sdm"], x, bf16_stream)
+            s_out, si, margin = trained_sdm(lay["sdm"], x, bf16_stream, margins)
             rec["sdm_si"], rec["sdm_margin"] = si, margin
             x = add_stream(x, s_out, bf16_stream)
         trace.append(rec)

@@ -41,6 +41,12 @@ P = c_void_p
 _SIGS = {
     "sdm_abi_version": (c_int, []),
     "sdm_status_string": (ctypes.c_char_p, [c_int]),
+    "sdm_kernel_launch_count": (c_int64, []),
+    "sdm_profile_begin": (c_int, []),
+    "sdm_profile_end": (c_int, []),
+    "sdm_profile_group": (c_int, [c_int, ctypes.c_char_p, ctypes.c_char_p, c_int, ctypes.POINTER(c_int),
+                                  ctypes.POINTER(c_double)]),
+    "sdm_device_status": (c_int, [P]),
     "sdm_pk_address": (c_int, [P, P, P, c_int64, c_int, c_int, c_int, c_int, P, P, P]),
     "sdm_rmsnorm": (c_int, [P, P, c_int64, c_int, c_float, c_int, P, P]),
     "sdm_rt_forward_workspace_size": (c_size_t, [ctypes.POINTER(RtParams), c_int, c_int]),
@@ -117,3 +123,17 @@ def dtype_code(dt):
     if dt == torch.bfloat16:
         return SDM_BF16
     raise TypeError(f"libsdm_b200 computes in float32 or bfloat16, not {dt}")
+
+
+def profile_groups():
+    """After sdm_profile_end(): list of (kernel, tag, launches, total_ms)."""
+    n = lib().sdm_profile_end()
+    if n < 0:
+        raise RuntimeError("sdm_profile_end: CUDA error while reading launch events")
+    out = []
+    for i in range(n):
+        k, t = ctypes.create_string_buffer(64), ctypes.create_string_buffer(64)
+        cnt, ms = c_int(0), c_double(0.0)
+        check(lib().sdm_profile_group(i, k, t, 64, ctypes.byref(cnt), ctypes.byref(ms)), "sdm_profile_group")
+        out.append((k.value.decode(), t.value.decode(), cnt.value, ms.value))
+    return out

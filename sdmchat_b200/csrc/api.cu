@@ -4,6 +4,10 @@
 
 using namespace sdm;
 
+namespace sdm {
+cudaError_t read_and_clear_timeout(int* flag, cudaStream_t st);
+}  // namespace sdm
+
 namespace {
 
 // Bump allocator over a caller-provided workspace; with base == nullptr it only measures.
@@ -75,7 +79,7 @@ RtWs carve_rt(Bump& bp, const sdm_rt_params* p, int64_t N, bool own_sel, bool ow
     w.num = bp.take<float>(N * d);
     w.den = bp.take<float>(N * h);
   }
-  w.rbuf = bp.take<char>(N * d * es);
+  w.rbuf = bp.take<char>(N * d * es * (es == 2 ? 2 : 1));  // bf16: hi | lo halves of the float32 read
   return w;
 }
 
@@ -88,8 +92,10 @@ cudaError_t rt_prepare(const sdm_rt_params* p, const T* x, int64_t N, int T_bh, 
   cudaError_t e = launch_rmsnorm<T>(x, static_cast<const T*>(p->norm_w), N, d, p->norm_eps, hx, st);
   if (e != cudaSuccess) return e;
   EpiProj ep{proj, C, p->addr_b, p->wg_bias, h * p->d_a, 2 * h * p->d_a + d};
+  OpTag tag_("rt_proj");
   e = launch_gemm<T, EpiProj>(hx, d, static_cast<const T*>(p->w_proj), d, N, d, (int)C, ep, st);
   if (e != cudaSuccess) return e;
+  OpTag tag2_("rt_address");
   PkArgs pa{};
   pa.ldz = C;
   pa.keys1 = p->keys1;
@@ -167,11 +173,14 @@ sdm_status rt_forward_t(const sdm_rt_params* p, const void* xv, int B, int T_, c
   sa.mem_out = mem_out;
   sa.cnt_out = cnt_out;
   SDM_TRY(launch_rt_scan(sa, st));
+  OpTag tag_("rt_out");
   T* rbuf = static_cast<T*>(w.rbuf);
+  constexpr int split = sizeof(T) == 2;  // wo's reference input is float32: feed it as bf16 hi + lo
   SDM_TRY(launch_rt_finish<T>(num, den, N, h, dh, p->read_sum, p->read_eps, p->out_norm, p->out_norm_eps, p->onorm_w,
-                              rbuf, st));
+                              rbuf, split, st));
   EpiResid<T> er{add_res ? x : nullptr, static_cast<T*>(outv), d};
-  SDM_TRY(launch_gemm<T, EpiResid<T>>(rbuf, d, static_cast<const T*>(p->wo), d, N, d, d, er, st));
+  SDM_TRY(launch_gemm<T, EpiResid<T>>(rbuf, (1 + split) * d, static_cast<const T*>(p->wo), d, N, (1 + split) * d, d,
+                                      er, st, d));
   return SDM_OK;
 }
 
@@ -195,7 +204,7 @@ size_t ts_ws(const sdm_ts_params* p, int64_t N, bool own_si, void* base, void** 
   *q = bp.take<float>(N * p->heads * p->d_a);
   *si = own_si ? bp.take<int32_t>(N * p->heads * kk) : nullptr;
   *w = bp.take<float>(N * p->heads * kk);
-  *rbuf = bp.take<char>(N * p->d * es);
+  *rbuf = bp.take<char>(N * p->d * es * (es == 2 ? 2 : 1));  // bf16: hi | lo halves of the float32 read
   return bp.off;
 }
 
@@ -214,6 +223,7 @@ sdm_status ts_forward_t(const sdm_ts_params* p, const void* xv, int64_t N, int a
   const T* x = static_cast<const T*>(xv);
   const int h = p->heads, d = p->d, dh = d / h, kk = sel_k(p->k, p->n_sub);
   SDM_TRY(launch_rmsnorm<T>(x, static_cast<const T*>(p->norm_w), N, d, p->norm_eps, static_cast<T*>(hs), st));
+  OpTag tag_("ts");
   EpiF32 eq{q, (int64_t)h * p->d_a};
   SDM_TRY(launch_gemm<T, EpiF32>(static_cast<T*>(hs), d, static_cast<const T*>(p->wq), d, N, d, h * p->d_a, eq, st));
   PkArgs pa{};
@@ -231,10 +241,12 @@ sdm_status ts_forward_t(const sdm_ts_params* p, const void* xv, int64_t N, int a
   pa.si = si;
   pa.log_scale = p->log_scale;
   SDM_TRY(launch_pk_address(pa, st));
+  constexpr int split = sizeof(T) == 2;
   SDM_TRY(launch_ts_gather<T>(si, w, static_cast<const T*>(p->values), N, h, p->n_sub * p->n_sub, dh, kk,
-                              static_cast<T*>(rb), st));
+                              static_cast<T*>(rb), split, st));
   EpiResid<T> er{add_res ? x : nullptr, static_cast<T*>(outv), d};
-  SDM_TRY(launch_gemm<T, EpiResid<T>>(static_cast<T*>(rb), d, static_cast<const T*>(p->wo), d, N, d, d, er, st));
+  SDM_TRY(launch_gemm<T, EpiResid<T>>(static_cast<T*>(rb), (1 + split) * d, static_cast<const T*>(p->wo), d, N,
+                                      (1 + split) * d, d, er, st, d));
   return SDM_OK;
 }
 
@@ -258,6 +270,7 @@ sdm_status swiglu_t(const void* xv, const void* nw, const void* wg, const void* 
   swiglu_ws(N, d, f, dtype, ws, &hm, &g, &u, &pp);
   if (N == 0) return SDM_OK;
   const T* x = static_cast<const T*>(xv);
+  OpTag tag_("swiglu");
   SDM_TRY(launch_rmsnorm<T>(x, static_cast<const T*>(nw), N, d, eps, static_cast<T*>(hm), st));
   SDM_TRY(launch_gemm<T, EpiStore<T>>(static_cast<T*>(hm), d, static_cast<const T*>(wg), d, N, d, f,
                                       EpiStore<T>{static_cast<T*>(g), f}, st));
@@ -293,6 +306,7 @@ sdm_status head_t(int mode, const void* xv, const void* nf_w, const void* emb, c
   if (N == 0) return SDM_OK;
   const T* x = static_cast<const T*>(xv);
   T* h = static_cast<T*>(hb);
+  OpTag tag_(mode == 0 ? "head_logits" : mode == 1 ? "head_ce" : "head_argmax");
   SDM_TRY(launch_rmsnorm<T>(x, static_cast<const T*>(nf_w), N, d, eps, h, st));
   const T* E = static_cast<const T*>(emb);
   if (mode == 0) {
@@ -315,6 +329,12 @@ sdm_status head_t(int mode, const void* xv, const void* nf_w, const void* emb, c
 extern "C" {
 
 int sdm_abi_version(void) { return 1; }
+
+sdm_status sdm_device_status(void* stream) {
+  int flag = 0;
+  if (read_and_clear_timeout(&flag, S(stream)) != cudaSuccess) return SDM_ERR_CUDA;
+  return flag ? SDM_ERR_TIMEOUT : SDM_OK;
+}
 
 const char* sdm_status_string(sdm_status s) {
   switch (s) {
@@ -441,6 +461,7 @@ sdm_status sdm_rt_decode_step(const sdm_rt_params* p, const void* x, int S_, con
   } else {
     SDM_TRY(rt_prepare<float>(p, (const float*)x, S_, 1, (float*)w.hx, w.proj, w.siw, w.ww, w.sir, w.wr, st));
   }
+  OpTag tag_("rt_decode");
   DecodeArgs da{};
   da.siw = w.siw;
   da.ww = w.ww;
@@ -464,12 +485,13 @@ sdm_status sdm_rt_decode_step(const sdm_rt_params* p, const void* x, int S_, con
   SDM_TRY(launch_rt_decode(da, st));
   if (p->dtype == SDM_BF16) {
     SDM_TRY(launch_rt_finish<bf16_t>(w.num, w.den, S_, h, dh, p->read_sum, p->read_eps, p->out_norm, p->out_norm_eps,
-                                     p->onorm_w, (bf16_t*)w.rbuf, st));
+                                     p->onorm_w, (bf16_t*)w.rbuf, 1, st));
     EpiResid<bf16_t> er{add_residual ? (const bf16_t*)x : nullptr, (bf16_t*)out, d};
-    SDM_TRY(launch_gemm<bf16_t, EpiResid<bf16_t>>((bf16_t*)w.rbuf, d, (const bf16_t*)p->wo, d, S_, d, d, er, st));
+    SDM_TRY(launch_gemm<bf16_t, EpiResid<bf16_t>>((bf16_t*)w.rbuf, 2 * d, (const bf16_t*)p->wo, d, S_, 2 * d, d, er, st,
+                                                  d));
   } else {
     SDM_TRY(launch_rt_finish<float>(w.num, w.den, S_, h, dh, p->read_sum, p->read_eps, p->out_norm, p->out_norm_eps,
-                                    p->onorm_w, (float*)w.rbuf, st));
+                                    p->onorm_w, (float*)w.rbuf, 0, st));
     EpiResid<float> er{add_residual ? (const float*)x : nullptr, (float*)out, d};
     SDM_TRY(launch_gemm<float, EpiResid<float>>((float*)w.rbuf, d, (const float*)p->wo, d, S_, d, d, er, st));
   }

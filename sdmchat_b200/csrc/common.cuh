@@ -38,6 +38,21 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Every kernel launch sits inside a LaunchScope: it counts the launch (sdm_kernel_launch_count) and, while
+// sdm_profile_begin/end is recording, brackets it with CUDA events on the launch stream, grouped by kernel name
+// and the call-site tag of the innermost OpTag.
+struct LaunchScope {
+  LaunchScope(const char* kernel, cudaStream_t st);
+  ~LaunchScope();
+  int rec_;
+  cudaStream_t st_;
+};
+struct OpTag {
+  explicit OpTag(const char* tag);
+  ~OpTag();
+  const char* prev_;
+};
+
 }  // namespace sdm
 
 // Host-side status helpers.

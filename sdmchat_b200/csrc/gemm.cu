@@ -10,7 +10,7 @@ constexpr int SG_BM = 128, SG_BN = 64, SG_BK = 16;
 template <typename TA, typename Epi>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const TA* __restrict__ x, int64_t ldx,
                                                         const TA* __restrict__ w, int64_t ldw, int64_t rows, int K,
-                                                        int n, Epi epi) {
+                                                        int n, Epi epi, int kwrap) {
   __shared__ float As[SG_BK][SG_BM + 4];
   __shared__ float Bs[SG_BK][SG_BN + 4];
   const int tid = threadIdx.x;
@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const TA* __restrict__ x
       const int nn = idx / SG_BK, kk = idx % SG_BK;
       const int c = col0 + nn;
       const int kg = k0 + kk;
-      Bs[kk][nn] = (c < n && kg < K) ? to_f32(w[(int64_t)c * ldw + kg]) : 0.f;
+      Bs[kk][nn] = (c < n && kg < K) ? to_f32(w[(int64_t)c * ldw + (kg % kwrap)]) : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -68,29 +68,33 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const TA* __restrict__ x
 
 template <typename TA, typename Epi>
 cudaError_t launch_gemm_simt(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int n, Epi epi,
-                             cudaStream_t st) {
+                             cudaStream_t st, int kwrap) {
   if (rows == 0 || n == 0) return cudaSuccess;
   dim3 grid((unsigned)ceil_div(n, SG_BN), (unsigned)ceil_div(rows, SG_BM));
-  gemm_simt_kernel<TA, Epi><<<grid, 256, 0, st>>>(x, ldx, w, ldw, rows, K, n, epi);
+  LaunchScope scope_("gemm_simt", st);
+  gemm_simt_kernel<TA, Epi><<<grid, 256, 0, st>>>(x, ldx, w, ldw, rows, K, n, epi, kwrap);
   return cudaGetLastError();
 }
 
 template <typename Epi>
 cudaError_t launch_gemm_tc(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K, int n,
-                           Epi epi, cudaStream_t st);
+                           Epi epi, cudaStream_t st, int kwrap);
 
 template <typename TA, typename Epi>
 cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int n, Epi epi,
-                        cudaStream_t st) {
+                        cudaStream_t st, int kwrap) {
+  if (kwrap <= 0) kwrap = K;
+  if (K % kwrap) return cudaErrorInvalidValue;
   if constexpr (sizeof(TA) == 2) {
-    if (tc_gemm_supported(x, ldx, w, ldw, K)) return launch_gemm_tc<Epi>(x, ldx, w, ldw, rows, K, n, epi, st);
+    if (tc_gemm_supported(x, ldx, w, ldw, K, kwrap))
+      return launch_gemm_tc<Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
   }
-  return launch_gemm_simt<TA, Epi>(x, ldx, w, ldw, rows, K, n, epi, st);
+  return launch_gemm_simt<TA, Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
 }
 
 #define SDM_GEMM_INST(TA, EPI)                                                                                 \
   template cudaError_t launch_gemm<TA, EPI>(const TA*, int64_t, const TA*, int64_t, int64_t, int, int, EPI, \
-                                            cudaStream_t);
+                                            cudaStream_t, int);
 SDM_GEMM_INST(float, EpiF32)
 SDM_GEMM_INST(bf16_t, EpiF32)
 SDM_GEMM_INST(float, EpiProj)

@@ -70,12 +70,14 @@ struct EpiResid {
 };
 
 // Generic GEMM y = x @ w^T; x (rows, K) row-major (ldx), w (n, K) row-major (ldw) (nn.Linear weight layout).
-// float: CUDA-core FMA; bf16: tcgen05 tensor cores (falls back to nothing: an unsupported shape is an error).
+// kwrap (0 = K): w's K index is taken modulo kwrap, so x = [hi | lo] (K = 2*kwrap) against one w computes
+// hi @ w^T + lo @ w^T -- the float32-accurate product of a value split into two bfloat16 halves.
+// float: CUDA-core FMA; bf16: tcgen05 tensor cores when tc_gemm_supported(), else CUDA cores.
 template <typename TA, typename Epi>
 cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int n, Epi epi,
-                        cudaStream_t st);
+                        cudaStream_t st, int kwrap = 0);
 // Can the tensor-core GEMM take this shape (K a multiple of 64, 16-byte aligned rows and pointers)?
-bool tc_gemm_supported(const void* x, int64_t ldx, const void* w, int64_t ldw, int K);
+bool tc_gemm_supported(const void* x, int64_t ldx, const void* w, int64_t ldw, int K, int kwrap);
 
 // ---------------------------------------------------------------------------------------------- other kernels
 template <typename T>
@@ -85,13 +87,15 @@ cudaError_t launch_embed(const int32_t* ids, const T* emb, int64_t N, int d, int
                          cudaStream_t st);
 template <typename T>
 cudaError_t launch_swiglu_act(const T* g, const T* u, int64_t n, T* p, cudaStream_t st);
+// The module outputs below feed a wo GEMM whose reference input is float32: with split, row n of r holds the
+// bfloat16 high part in columns [0, d) and the bfloat16 remainder in [d, 2d) (r is (N, 2d)); else r is (N, d).
 template <typename T>
 cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int h, int dh, int read_sum,
-                             float read_eps, int out_norm, float out_norm_eps, const float* onorm_w, T* r,
+                             float read_eps, int out_norm, float out_norm_eps, const float* onorm_w, T* r, int split,
                              cudaStream_t st);
 template <typename T>
 cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values, int64_t N, int h, int M, int dh,
-                             int k, T* r, cudaStream_t st);
+                             int k, T* r, int split, cudaStream_t st);
 
 // Product-key addressing (track4_onesdm_models.py:134-148) with the soft weights of prepare (:203-206).
 struct PkArgs {

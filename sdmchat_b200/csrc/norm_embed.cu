@@ -50,12 +50,24 @@ __global__ void swiglu_act_kernel(const T* __restrict__ g, const T* __restrict__
   }
 }
 
+// Store v at row n, column c of a row of width d: plain, or as bfloat16 hi (column c) + lo (column d + c).
+template <typename T>
+__device__ __forceinline__ void store_split(T* r, int64_t n, int64_t d, int64_t c, float v, int split) {
+  if (split) {
+    const float hi = round_to<T>(v);
+    r[n * 2 * d + c] = from_f32<T>(hi);
+    r[n * 2 * d + d + c] = from_f32<T>(v - hi);
+  } else {
+    r[n * d + c] = from_f32<T>(v);
+  }
+}
+
 // RunTimeSdm.finish up to wo (track4_onesdm_models.py:243-246): mean (or sum) read, per-head RMS out-norm with
 // onorm_w.  num (N, h, dh), den (N, h) float32 -> r (N, h*dh) in T.  One warp per (token, head).
 template <typename T>
 __global__ void rt_finish_kernel(const float* __restrict__ num, const float* __restrict__ den, int64_t N, int h,
                                  int dh, int read_sum, float read_eps, int out_norm, float out_norm_eps,
-                                 const float* __restrict__ onorm_w, T* __restrict__ r) {
+                                 const float* __restrict__ onorm_w, T* __restrict__ r, int split) {
   int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (item >= N * h) return;
@@ -82,7 +94,7 @@ __global__ void rt_finish_kernel(const float* __restrict__ num, const float* __r
     if (c < dh) {
       float v = vals[q];
       if (out_norm) v = (v * rs) * onorm_w[hh * dh + c];
-      r[item * dh + c] = from_f32<T>(v);
+      store_split<T>(r, item / h, (int64_t)h * dh, hh * dh + c, v, split);
     }
   }
 }
@@ -92,7 +104,7 @@ __global__ void rt_finish_kernel(const float* __restrict__ num, const float* __r
 template <typename T>
 __global__ void ts_gather_kernel(const int32_t* __restrict__ si, const float* __restrict__ w,
                                  const T* __restrict__ values, int64_t N, int h, int M, int dh, int k,
-                                 T* __restrict__ r) {
+                                 T* __restrict__ r, int split) {
   int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (item >= N * h) return;
@@ -116,7 +128,7 @@ __global__ void ts_gather_kernel(const int32_t* __restrict__ si, const float* __
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       int c = c0 + lane + 32 * q;
-      if (c < dh) r[item * dh + c] = from_f32<T>(acc[q]);
+      if (c < dh) store_split<T>(r, item / h, (int64_t)h * dh, hh * dh + c, acc[q], split);
     }
   }
 }
@@ -125,6 +137,7 @@ __global__ void ts_gather_kernel(const int32_t* __restrict__ si, const float* __
 template <typename T>
 cudaError_t launch_rmsnorm(const T* x, const T* w, int64_t rows, int d, float eps, T* y, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
+  LaunchScope scope_("rmsnorm", st);
   rmsnorm_kernel<T><<<(unsigned)ceil_div(rows, 8), 256, 0, st>>>(x, w, rows, d, eps, y);
   return cudaGetLastError();
 }
@@ -132,6 +145,7 @@ template <typename T>
 cudaError_t launch_embed(const int32_t* ids, const T* emb, int64_t N, int d, int V, T* out, int* bad,
                          cudaStream_t st) {
   if (N == 0) return cudaSuccess;
+  LaunchScope scope_("embed", st);
   embed_kernel<T><<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(ids, emb, N, d, V, out, bad);
   return cudaGetLastError();
 }
@@ -140,23 +154,26 @@ cudaError_t launch_swiglu_act(const T* g, const T* u, int64_t n, T* p, cudaStrea
   if (n == 0) return cudaSuccess;
   int64_t blocks = ceil_div(n, 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
+  LaunchScope scope_("swiglu_act", st);
   swiglu_act_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(g, u, n, p);
   return cudaGetLastError();
 }
 template <typename T>
 cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int h, int dh, int read_sum,
-                             float read_eps, int out_norm, float out_norm_eps, const float* onorm_w, T* r,
+                             float read_eps, int out_norm, float out_norm_eps, const float* onorm_w, T* r, int split,
                              cudaStream_t st) {
   if (N == 0) return cudaSuccess;
+  LaunchScope scope_("rt_finish", st);
   rt_finish_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(num, den, N, h, dh, read_sum, read_eps,
-                                                                    out_norm, out_norm_eps, onorm_w, r);
+                                                                    out_norm, out_norm_eps, onorm_w, r, split);
   return cudaGetLastError();
 }
 template <typename T>
 cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values, int64_t N, int h, int M, int dh,
-                             int k, T* r, cudaStream_t st) {
+                             int k, T* r, int split, cudaStream_t st) {
   if (N == 0) return cudaSuccess;
-  ts_gather_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r);
+  LaunchScope scope_("ts_gather", st);
+  ts_gather_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r, split);
   return cudaGetLastError();
 }
 
@@ -165,9 +182,9 @@ cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values,
   template cudaError_t launch_embed<T>(const int32_t*, const T*, int64_t, int, int, T*, int*, cudaStream_t);    \
   template cudaError_t launch_swiglu_act<T>(const T*, const T*, int64_t, T*, cudaStream_t);                     \
   template cudaError_t launch_rt_finish<T>(const float*, const float*, int64_t, int, int, int, float, int, float, \
-                                           const float*, T*, cudaStream_t);                                      \
+                                           const float*, T*, int, cudaStream_t);                                 \
   template cudaError_t launch_ts_gather<T>(const int32_t*, const float*, const T*, int64_t, int, int, int, int, T*, \
-                                           cudaStream_t);
+                                           int, cudaStream_t);
 SDM_INST(float)
 SDM_INST(bf16_t)
 

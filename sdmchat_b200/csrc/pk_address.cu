@@ -228,6 +228,7 @@ static cudaError_t launch_pk_tc(const PkArgs& a, int c1, int kk, cudaStream_t st
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)ceil_div(a.N, PK_THREADS), (unsigned)a.h);
+  LaunchScope scope_("pk_address", st);
   kern<<<grid, PK_THREADS, smem, st>>>(a, c1, kk);
   return cudaGetLastError();
 }

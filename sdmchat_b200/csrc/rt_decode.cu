@@ -91,6 +91,7 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
 cudaError_t launch_rt_decode(const DecodeArgs& a, cudaStream_t st) {
   if (a.S == 0) return cudaSuccess;
   const int threads = ((a.dh + 31) / 32) * 32;  // one thread per value column (dh <= 1024)
+  LaunchScope scope_("rt_decode", st);
   rt_decode_kernel<<<(unsigned)((int64_t)a.S * a.h), threads, 0, st>>>(a);
   return cudaGetLastError();
 }
@@ -176,11 +177,13 @@ __global__ void argmax_rows_kernel(const float* __restrict__ lg, int64_t rows, i
 cudaError_t launch_ce_rows(const float* logits, int64_t rows, int V, const int32_t* targets, double* loss_sum,
                            cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
+  LaunchScope scope_("ce_rows", st);
   ce_rows_kernel<<<(unsigned)rows, 256, 0, st>>>(logits, rows, V, targets, loss_sum);
   return cudaGetLastError();
 }
 cudaError_t launch_argmax_rows(const float* logits, int64_t rows, int V, int32_t* ids, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
+  LaunchScope scope_("argmax_rows", st);
   argmax_rows_kernel<<<(unsigned)rows, 256, 0, st>>>(logits, rows, V, ids);
   return cudaGetLastError();
 }

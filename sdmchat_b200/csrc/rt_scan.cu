@@ -259,6 +259,7 @@ cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int n_slices = (a.dh + SCAN_CW - 1) / SCAN_CW;
   const int64_t grid = (int64_t)a.B * a.h * n_slices;
+  LaunchScope scope_("rt_scan", st);
   rt_scan_kernel<<<(unsigned)grid, SCAN_THREADS, lay.total, st>>>(a, L, n_slices);
   return cudaGetLastError();
 }
