@@ -49,6 +49,15 @@ def rel(a, b):
     return float(np.abs(a - b).max() / (np.abs(b).max() + 1e-12))
 
 
+def rel_bf16(a, b):
+    """`rel` for bfloat16-stored outputs: each element may first differ by one bfloat16 rounding step (at most
+    2^-7 |b|, when the float32 accumulations on either side straddle a rounding boundary); the remainder is
+    measured like `rel`.  Tests bound it by the same 2e-3."""
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    excess = np.maximum(np.abs(a - b) - np.abs(b) * 2.0 ** -7, 0.0)
+    return float(excess.max() / (np.abs(b).max() + 1e-12))
+
+
 def same_selection(si_a, si_b, margin, min_margin=0.0):
     """Sorted slot sets equal wherever the selection margin exceeds min_margin; returns (ok, n_checked, n_bad)."""
     a = np.sort(si_a, -1)
