@@ -77,14 +77,19 @@ def _early_exit_worker(rank, world, port, q):
     from sdmchat_b200 import dist as D
     D.init("gloo", timeout_s=5)
     dist.barrier()
+    def report(msg):
+        q.put((rank, msg))
+        q.close()
+        q.join_thread()  # flush the queue's feeder thread before the hard exit
+
     if rank == 1:
-        q.put((rank, "left"))
+        report("left")
         os._exit(0)  # leaves between steps, with no collective in flight
     try:
         D.reduce_loss(torch.tensor(1.0), 1)
-        q.put((rank, "no error"))
+        report("no error")
     except Exception as e:  # the peer is gone: the all-reduce must fail, not hang
-        q.put((rank, "error:" + type(e).__name__))
+        report("error:" + type(e).__name__)
     os._exit(0)
 
 
