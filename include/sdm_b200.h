@@ -128,6 +128,17 @@ sdm_status sdm_rt_decode_step(const sdm_rt_params* p, const void* x, int S, cons
                               int add_residual, void* out, float* mem, float* cnt, float* scale, int32_t* last_w,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same decode step for callers that cannot allocate device memory (no counterpart in the reference, which has
+ * no decode API at all).  It allocates nothing and takes no workspace: its scratch is a fixed 8 MiB array inside
+ * the library (sdm_rt_decode_noalloc_scratch_bytes()), held on every GPU that loads the library until exit.
+ * Returns SDM_ERR_WORKSPACE when sdm_rt_decode_workspace_size(p, S) exceeds it (about 490 streams at d 768,
+ * 12 heads, k 16).  The first call on a device looks up the scratch's device address with that device current:
+ * make it before any stream capture.  Calls share the scratch; calls that overlap on the GPU race on it. */
+size_t sdm_rt_decode_noalloc_scratch_bytes(void);
+sdm_status sdm_rt_decode_step_noalloc(const sdm_rt_params* p, const void* x, int S, const uint8_t* reset,
+                                      int add_residual, void* out, float* mem, float* cnt, float* scale,
+                                      int32_t* last_w, void* stream);
+
 /* --------------------------------------------------------------------------------------------------- TrainedSdm
  * TrainedSdm.forward (M:448-457): q = wq RMSNorm(x); product-key top-k over n_sub^2 slots; softmax(scale *
  * score); weighted sum of the picked value rows; wo.  values (h, n_sub^2, dh) in dtype. */
