@@ -1,30 +1,47 @@
-// The run-time memory's write-then-read over a whole window (RunTimeSdm._chunk over every chunk,
-// track4_onesdm_models.py:215-241 and the loop :255-272), with the per-head state resident in shared memory.
+// The run-time memory's write-then-read over a whole window (RunTimeSdm.forward's chunk loop,
+// track4_onesdm_models.py:215-241 and :255-272), with the per-head state resident in shared memory.
 //
 // One CTA owns one (batch row b, head hh, slice of SCAN_CW value columns) for the WHOLE window: its slice of
 // mem (M x SCAN_CW float32) and the slot counts cnt (M) live in shared memory from the first token to the last,
 // so the state never travels through HBM (the reference's chunked form re-reads and re-writes it every chunk).
 // Columns are independent in the recurrence, so slices of one head never communicate.
 //
-// Per chunk of L tokens (the reference's math, sparse):
-//   read   num[t] = sum_i wr[t,i] * ( lam^(t-c0) * mem[sir[t,i]]  +  sum_{s<t in chunk, siw[s,j]=sir[t,i]}
+// Schedule: micro-steps of up to 16 tokens.  Within a step every token reads in parallel (one warp per token,
+// lane per column): the exact state at the step start, faded lam^(t-t0), plus the writes of earlier tokens of the
+// same step to the slots it reads, found through a per-step slot list (with 16 tokens x k writes over M slots such
+// collisions are rare).  Then the step's writes go straight into the state, one job per distinct written slot,
+// jobs dealt round-robin to the warps; a job walks its slot's list (every write to that slot in this step, newest
+// first).  That is the reference's math (chunked form = token recurrence, :728-755) with a step of 16:
+//   read   num[t] = sum_i wr[t,i] * ( lam^(t-t0) * mem[sir[t,i]] + sum_{t0<=s<t, siw[s,j]=sir[t,i]}
 //                                                                      lam^(t-1-s) * ww[s,j] * v[s] )
-//   write  mem[r] <- lam^L * mem[r] + sum_{s, j: siw[s,j]=r} lam^(L-1-s) * ww[s,j] * v[s]
-// with cnt the same recurrence on a value of 1.  The chunk's L*k writes are bucketed by slot (a counting sort in
-// shared memory, each bucket in (s, j) order) so a read finds the earlier in-chunk writes to its slot, and the
-// write phase walks every slot once (its decay plus its bucket).  Reads of the whole chunk run in parallel (one
-// warp per token, one lane per column), then the writes (one warp per slot); no atomics touch float data, so
-// results are bit-reproducible.  BOS resets (:229-233) mask by segment number exactly as the reference does.
+//   write  mem <- lam^U * mem + sum_{s, j} lam^(t0+U-1-s) * ww[s,j] * e_{siw[s,j]} v[s]^T
+// The fade is applied lazily: the state is held as sigma * P and a step multiplies sigma by lam^U instead of
+// touching every row; writes add their term / sigma.  P is renormalised (one pass) when sigma would fall below
+// 2^-40.  Fade 1 keeps sigma = 1; fade 0 (and fades below 2^-100) keep only the last token's writes.  A BOS reset
+// (:229-233) starts a new step and empties the state.
+//
+// Warps 0-15 ("workers") read and write, synchronising among themselves with a named barrier between the two
+// phases; warp 16 ("builder") builds the NEXT step's slot lists and job list meanwhile (double-buffered) and
+// meets the workers only at the step boundary.  Chunk inputs (slot ids, weights, values of 128 tokens) are
+// prefetched into registers one chunk ahead.  No atomics touch float data and every sum runs in a fixed order, so
+// results are bit-reproducible.
 #include "kernels.cuh"
 
 namespace sdm {
 
-constexpr int SCAN_CW = 32;        // value columns per CTA
-constexpr int SCAN_THREADS = 512;  // 16 warps
-constexpr int SCAN_MAX_ENTRIES = 2048;  // L * k per chunk
+constexpr int SCAN_CW = 32;                            // value columns per CTA
+constexpr int SCAN_WORKERS = 16;                       // warps that read and write
+constexpr int SCAN_THREADS = (SCAN_WORKERS + 1) * 32;  // + the list-builder warp
+constexpr int SCAN_U = 16;                             // tokens per micro-step (max)
+constexpr int SCAN_MAX_ENTRIES = 2048;                 // L * k of one prefetched chunk
+constexpr int SCAN_MAX_L = 128;
+constexpr int SCAN_MAX_K = 32;
+constexpr int SCAN_EB = SCAN_U * SCAN_MAX_K;           // entries (and jobs) per list buffer
+constexpr int PF_E = SCAN_MAX_ENTRIES / (SCAN_WORKERS * 32);
+constexpr int PF_V = SCAN_MAX_L * SCAN_CW / (SCAN_WORKERS * 32);
 
 struct ScanSmem {
-  size_t P, Pc, siw, ww, sir, wr, Vs, bstart, bcount, entries, lampow, seg, total;
+  size_t P, Pc, siw, ww, sir, wr, Vs, rst, head, nxt, ent_s, ent_w, jobs, lastr, total;
 };
 
 __host__ __device__ inline ScanSmem scan_layout(int M, int L, int k) {
@@ -42,61 +59,126 @@ __host__ __device__ inline ScanSmem scan_layout(int M, int L, int k) {
   s.sir = take((size_t)L * k * 4);
   s.wr = take((size_t)L * k * 4);
   s.Vs = take((size_t)L * SCAN_CW * 4);
-  s.bstart = take((size_t)(M + 1) * 4);
-  s.bcount = take((size_t)M * 4);
-  s.entries = take((size_t)L * k * 8);
-  s.lampow = take((size_t)(L + 1) * 4);
-  s.seg = take((size_t)L * 4);
+  s.rst = take((size_t)L * 4);
+  s.head = take((size_t)2 * M * 4);
+  s.nxt = take((size_t)2 * SCAN_EB * 4);
+  s.ent_s = take((size_t)2 * SCAN_EB * 4);
+  s.ent_w = take((size_t)2 * SCAN_EB * 4);
+  s.jobs = take((size_t)2 * (SCAN_EB + 1) * 4);
+  s.lastr = take((size_t)2 * SCAN_MAX_K * 4);
   s.total = o;
   return s;
 }
 
 static int scan_chunk_len(int k) {
   int L = SCAN_MAX_ENTRIES / k;
-  return L > 128 ? 128 : L;
+  return L > SCAN_MAX_L ? SCAN_MAX_L : L;
 }
 
-// Exclusive prefix sum of cnt[0..M) into start[0..M] (start[M] = total) by the whole block.
-__device__ void block_exclusive_scan(const int* cnt, int* start, int M, int* warp_tot) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = (M + SCAN_THREADS - 1) / SCAN_THREADS;
-  const int lo = tid * per;
-  int local = 0;
-  for (int q = 0; q < per; ++q)
-    if (lo + q < M) local += cnt[lo + q];
-  int incl = local;
+__device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(SCAN_WORKERS * 32) : "memory"); }
+
+// Inputs of one chunk held in registers between their load and their store to shared memory (worker warps).
+struct Prefetch {
+  int siw[PF_E], sir[PF_E];
+  float ww[PF_E], wr[PF_E], v[PF_V];
+  int rst;
+};
+
+__device__ __forceinline__ void prefetch_load(Prefetch& pf, const ScanArgs& a, int b, int hh, int cs, int c0,
+                                              int Lc) {
+  const int tid = threadIdx.x, k = a.k, nk = Lc * k;
+  const int64_t base = (((int64_t)b * a.h + hh) * a.T + c0) * k;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
-  if (lane == 31) warp_tot[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    int v = lane < SCAN_THREADS / 32 ? warp_tot[lane] : 0;
-    int inc = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int u = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += u;
-    }
-    if (lane < SCAN_THREADS / 32) warp_tot[lane] = inc - v;  // exclusive warp offsets
-  }
-  __syncthreads();
-  int run = warp_tot[warp] + incl - local;
-  for (int q = 0; q < per; ++q) {
-    if (lo + q < M) {
-      start[lo + q] = run;
-      run += cnt[lo + q];
+  for (int q = 0; q < PF_E; ++q) {
+    const int e = tid + q * SCAN_WORKERS * 32;
+    if (e < nk) {
+      pf.siw[q] = a.siw[base + e];
+      pf.ww[q] = a.ww[base + e];
+      pf.sir[q] = a.sir[base + e];
+      pf.wr[q] = a.wr[base + e];
     }
   }
-  if (tid == SCAN_THREADS - 1) start[M] = run;
-  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < PF_V; ++q) {
+    const int i = tid + q * SCAN_WORKERS * 32;
+    const int s = i / SCAN_CW, c = i % SCAN_CW, gc = cs * SCAN_CW + c;
+    pf.v[q] = (s < Lc && gc < a.dh) ? a.V[((int64_t)b * a.T + c0 + s) * a.ldv + (int64_t)hh * a.dh + gc] : 0.f;
+  }
+  pf.rst = (a.reset && tid < Lc) ? (int)a.reset[(int64_t)b * a.T + c0 + tid] : 0;
+}
+
+__device__ __forceinline__ void prefetch_store(const Prefetch& pf, int M, int k, int Lc, int* siw_s, float* ww_s,
+                                               int* sir_s, float* wr_s, float* Vs, int* rst_s) {
+  const int tid = threadIdx.x, nk = Lc * k;
+#pragma unroll
+  for (int q = 0; q < PF_E; ++q) {
+    const int e = tid + q * SCAN_WORKERS * 32;
+    if (e < nk) {
+      // slot ids outside [0, M) (never produced by the address kernel) are clamped so no access leaves the state
+      siw_s[e] = min(max(pf.siw[q], 0), M - 1);
+      ww_s[e] = pf.ww[q];
+      sir_s[e] = min(max(pf.sir[q], 0), M - 1);
+      wr_s[e] = pf.wr[q];
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < PF_V; ++q) {
+    const int i = tid + q * SCAN_WORKERS * 32;
+    if (i < Lc * SCAN_CW) Vs[i] = pf.v[q];
+  }
+  if (tid < Lc) rst_s[tid] = pf.rst;
+}
+
+// Length of the micro-step starting at chunk position t0: at most ustep tokens, within the chunk, and cut before
+// any BOS reset after t0 (a reset always starts a step).
+__device__ __forceinline__ int step_len(int t0, int Lc, int ustep, const int* rst_s, bool has_reset) {
+  int ue = min(ustep, Lc - t0);
+  if (has_reset)
+    for (int q = 1; q < ue; ++q)
+      if (rst_s[t0 + q]) return q;
+  return ue;
+}
+
+// The builder warp's lists for the step [t0, t0 + ue).  Entry e = q*k + j is write j of token t0 + q.
+// head[r] = newest entry writing slot r (-1 if none), nxt[e] = next older entry of the same slot, ent_s / ent_w =
+// chunk position and weight of e, jobs[1..] = the distinct written slots in first-write order, jobs[0] = count.
+// Tokens are inserted 32/k at a time; writes of one group to the same slot are ordered with __match_any_sync.
+__device__ __forceinline__ void build_lists(int t0, int ue, int k, int M, const int* siw_s, const float* ww_s,
+                                            int* head, int* nxt, int* ent_s, float* ent_w, int* jobs) {
+  const int lane = threadIdx.x & 31;
+  const unsigned FULL = 0xffffffffu;
+  const int G = 32 / k;  // tokens per group
+  int njobs = 0;
+  for (int g0 = 0; g0 < ue; g0 += G) {
+    const int q = g0 + lane / k, j = lane % k;
+    const bool valid = lane < G * k && q < ue;
+    const int e = g0 * k + lane;
+    const int s = t0 + q;
+    const int r = valid ? siw_s[s * k + j] : M + lane;  // invalid lanes match nothing
+    const unsigned peers = __match_any_sync(FULL, r);
+    const unsigned lower = peers & ((1u << lane) - 1u);
+    const unsigned higher = peers & ~((2u << lane) - 1u);
+    const int old_head = valid ? head[r] : -1;
+    if (valid) {
+      nxt[e] = lower ? g0 * k + (31 - __clz(lower)) : old_head;
+      ent_s[e] = s;
+      ent_w[e] = ww_s[s * k + j];
+    }
+    __syncwarp();
+    if (valid && higher == 0) head[r] = e;
+    const bool newjob = valid && old_head < 0 && lower == 0;
+    const unsigned jm = __ballot_sync(FULL, newjob);
+    if (newjob) jobs[1 + njobs + __popc(jm & ((1u << lane) - 1u))] = r;
+    njobs += __popc(jm);
+    __syncwarp();
+  }
+  if (lane == 0) jobs[0] = njobs;
+  __syncwarp();
 }
 
 __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, int L, int n_slices) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int warp_tot[SCAN_THREADS / 32];
+  __shared__ float lampow[SCAN_U + 2];
   const int M = a.M, k = a.k, dh = a.dh, T = a.T, h = a.h;
   const ScanSmem lay = scan_layout(M, L, k);
   float* P = reinterpret_cast<float*>(smem + lay.P);
@@ -106,148 +188,227 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
   int* sir_s = reinterpret_cast<int*>(smem + lay.sir);
   float* wr_s = reinterpret_cast<float*>(smem + lay.wr);
   float* Vs = reinterpret_cast<float*>(smem + lay.Vs);
-  int* bstart = reinterpret_cast<int*>(smem + lay.bstart);
-  int* bcount = reinterpret_cast<int*>(smem + lay.bcount);
-  int2* entries = reinterpret_cast<int2*>(smem + lay.entries);
-  float* lampow = reinterpret_cast<float*>(smem + lay.lampow);
-  int* seg_s = reinterpret_cast<int*>(smem + lay.seg);
+  int* rst_s = reinterpret_cast<int*>(smem + lay.rst);
+  int* head_b = reinterpret_cast<int*>(smem + lay.head);
+  int* nxt_b = reinterpret_cast<int*>(smem + lay.nxt);
+  int* ents_b = reinterpret_cast<int*>(smem + lay.ent_s);
+  float* entw_b = reinterpret_cast<float*>(smem + lay.ent_w);
+  int* jobs_b = reinterpret_cast<int*>(smem + lay.jobs);
+  int* lastr_b = reinterpret_cast<int*>(smem + lay.lastr);
 
   const int cs = blockIdx.x % n_slices;
   const int bh = blockIdx.x / n_slices;
   const int hh = bh % h;
   const int b = bh / h;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int NW = SCAN_THREADS / 32;
+  const bool builder = warp == SCAN_WORKERS;
   const int col = cs * SCAN_CW + lane;
   const bool col_ok = col < dh;
   const float lam = a.decay[hh];
   const bool has_reset = a.reset != nullptr;
+  const unsigned FULL = 0xffffffffu;
+  // fade mode: 0 = only the last token's writes survive (lam = 0 or below 2^-100), 1 = no fade, 2 = lazy scale
+  const int mode = (lam < 7.8886e-31f) ? 0 : (lam == 1.f ? 1 : 2);
+  int ustep = SCAN_U;
+  if (mode == 2 && lam < 0.0131f) ustep = max(1, min(SCAN_U, (int)floorf(100.f / -log2f(lam))));  // lam^U >= 2^-100
 
   for (int i = tid; i < M * SCAN_CW; i += SCAN_THREADS) P[i] = 0.f;
-  for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] = 0.f;
-  for (int e = tid; e <= L; e += SCAN_THREADS) lampow[e] = powf(lam, (float)e);  // powf(0, 0) = 1, as torch.pow
-  int seg_prev = 0;  // segment number of the position just before the chunk (BOS count so far)
+  for (int i = tid; i < M; i += SCAN_THREADS) {
+    Pc[i] = 0.f;
+    head_b[i] = -1;
+    head_b[M + i] = -1;
+  }
+  if (tid <= SCAN_U) lampow[tid] = mode == 0 ? (tid == 0 ? 1.f : 0.f) : powf(lam, (float)tid);
+  if (tid < 2 * SCAN_MAX_K) lastr_b[tid] = -1;
+  float sigma = 1.f;  // state = sigma * P (mode 2)
+  Prefetch pf;
+  if (!builder) {
+    const int Lc0 = min(L, T);
+    prefetch_load(pf, a, b, hh, cs, 0, Lc0);
+    prefetch_store(pf, M, k, Lc0, siw_s, ww_s, sir_s, wr_s, Vs, rst_s);
+  }
   __syncthreads();
+  int buf = 0;   // list buffer of the current step
+  int lbuf = 0;  // survivor-row buffer (fade 0)
 
   for (int c0 = 0; c0 < T; c0 += L) {
     const int Lc = min(L, T - c0);
-    const int nk = Lc * k;
-    const int64_t base = (((int64_t)b * h + hh) * T + c0) * k;
-    for (int e = tid; e < nk; e += SCAN_THREADS) {
-      // slot ids outside [0, M) (never produced by the address kernel) are clamped so no access leaves the state
-      siw_s[e] = min(max(a.siw[base + e], 0), M - 1);
-      ww_s[e] = a.ww[base + e];
-      sir_s[e] = min(max(a.sir[base + e], 0), M - 1);
-      wr_s[e] = a.wr[base + e];
-    }
-    for (int i = tid; i < Lc * SCAN_CW; i += SCAN_THREADS) {
-      const int s = i / SCAN_CW, c = i % SCAN_CW, gc = cs * SCAN_CW + c;
-      Vs[i] = gc < dh ? a.V[((int64_t)b * T + c0 + s) * a.ldv + (int64_t)hh * dh + gc] : 0.f;
-    }
-    if (has_reset && warp == 0) {
-      int run = seg_prev;
-      for (int p0 = 0; p0 < Lc; p0 += 32) {
-        const int s = p0 + lane;
-        const bool f = s < Lc && a.reset[(int64_t)b * T + c0 + s] != 0;
-        const unsigned m = __ballot_sync(0xffffffffu, f);
-        if (s < Lc) seg_s[s] = run + __popc(m & (0xffffffffu >> (31 - lane)));
-        run += __popc(m);
-      }
-    }
-    for (int r = tid; r < M; r += SCAN_THREADS) bcount[r] = 0;
+    const int c0n = c0 + L;
+    const int Lcn = c0n < T ? min(L, T - c0n) : 0;
+    if (!builder && Lcn > 0) prefetch_load(pf, a, b, hh, cs, c0n, Lcn);  // lands while this chunk computes
+    if (builder)
+      build_lists(0, step_len(0, Lc, ustep, rst_s, has_reset), k, M, siw_s, ww_s, head_b + buf * M,
+                  nxt_b + buf * SCAN_EB, ents_b + buf * SCAN_EB, entw_b + buf * SCAN_EB, jobs_b + buf * (SCAN_EB + 1));
     __syncthreads();
-    // bucket the chunk's writes by slot
-    for (int e = tid; e < nk; e += SCAN_THREADS) atomicAdd(&bcount[siw_s[e]], 1);
-    __syncthreads();
-    block_exclusive_scan(bcount, bstart, M, warp_tot);
-    for (int r = tid; r < M; r += SCAN_THREADS) bcount[r] = 0;
-    __syncthreads();
-    for (int e = tid; e < nk; e += SCAN_THREADS) {
-      const int slot = siw_s[e];
-      const int pos = bstart[slot] + atomicAdd(&bcount[slot], 1);
-      entries[pos].x = e;
-    }
-    __syncthreads();
-    for (int r = tid; r < M; r += SCAN_THREADS) {
-      const int lo = bstart[r], hi = bstart[r + 1];
-      for (int p = lo + 1; p < hi; ++p) {  // insertion sort: (s, j) order
-        const int key = entries[p].x;
-        int q = p - 1;
-        while (q >= lo && entries[q].x > key) {
-          entries[q + 1].x = entries[q].x;
-          --q;
+
+    for (int t0 = 0; t0 < Lc;) {
+      const int ue = step_len(t0, Lc, ustep, rst_s, has_reset);
+      const int t1 = t0 + ue;
+      if (builder) {
+        // the next step's lists, into the other buffer (its heads were cleared by the previous step's writes)
+        if (t1 < Lc) {
+          const int nb = buf ^ 1;
+          build_lists(t1, step_len(t1, Lc, ustep, rst_s, has_reset), k, M, siw_s, ww_s, head_b + nb * M,
+                      nxt_b + nb * SCAN_EB, ents_b + nb * SCAN_EB, entw_b + nb * SCAN_EB,
+                      jobs_b + nb * (SCAN_EB + 1));
         }
-        entries[q + 1].x = key;
-      }
-      for (int p = lo; p < hi; ++p) {
-        const int e = entries[p].x;
-        entries[p] = make_int2(e / k, __float_as_int(ww_s[e]));
-      }
-    }
-    __syncthreads();
-    // read phase: warp per token, lane per column
-    for (int tau = warp; tau < Lc; tau += NW) {
-      const int seg_t = has_reset ? seg_s[tau] : 0;
-      const float fade = (!has_reset || seg_t == seg_prev) ? lampow[tau] : 0.f;
-      float acc = 0.f, accd = 0.f;
-      for (int i = 0; i < k; ++i) {
-        const int r = sir_s[tau * k + i];
-        const float w = wr_s[tau * k + i];
-        const float pv = P[r * SCAN_CW + lane];
-        const float pd = Pc[r];
-        float iv = 0.f, id = 0.f;
-        const int hi = bstart[r + 1];
-        for (int p = bstart[r]; p < hi; ++p) {
-          const int2 en = entries[p];
-          if (en.x >= tau) break;
-          if (has_reset && seg_s[en.x] != seg_t) continue;
-          const float coef = __int_as_float(en.y) * lampow[tau - 1 - en.x];
-          iv = fmaf(coef, Vs[en.x * SCAN_CW + lane], iv);
-          id += coef;
+      } else {
+        int* head = head_b + buf * M;
+        const int* nxt = nxt_b + buf * SCAN_EB;
+        const int* ent_s = ents_b + buf * SCAN_EB;
+        const float* ent_w = entw_b + buf * SCAN_EB;
+        const int* jobs = jobs_b + buf * (SCAN_EB + 1);
+        // a BOS empties the memory before its token reads; a tiny scale is folded into the state
+        const bool clear = has_reset && rst_s[t0] != 0;
+        const bool renorm = !clear && mode == 2 && sigma * lampow[ue] < 9.094947e-13f;  // 2^-40
+        if (clear || renorm) {
+          const float f = clear ? 0.f : sigma;
+          for (int i = tid; i < M * SCAN_CW; i += SCAN_WORKERS * 32) P[i] *= f;
+          for (int i = tid; i < M; i += SCAN_WORKERS * 32) Pc[i] *= f;
+          if (clear && tid < SCAN_MAX_K) lastr_b[lbuf * SCAN_MAX_K + tid] = -1;
+          sigma = 1.f;
+          workers_sync();
         }
-        acc = fmaf(w, fmaf(fade, pv, iv), acc);
-        accd = fmaf(w, fmaf(fade, pd, id), accd);
+
+        // reads: worker warp w takes token t0 + w
+        if (warp < ue) {
+          const int tau = t0 + warp;
+          const float fade = (mode == 2 ? sigma : 1.f) * lampow[warp];
+          int ri = 0, hd = -1;
+          float wi = 0.f, pdi = 0.f;
+          if (lane < k) {
+            ri = sir_s[tau * k + lane];
+            wi = wr_s[tau * k + lane];
+            pdi = Pc[ri];
+            hd = head[ri];
+          }
+          float pv[SCAN_MAX_K];
+#pragma unroll
+          for (int i = 0; i < SCAN_MAX_K; ++i)
+            if (i < k) pv[i] = P[__shfl_sync(FULL, ri, i) * SCAN_CW + lane];
+          float acc = 0.f;
+#pragma unroll
+          for (int i = 0; i < SCAN_MAX_K; ++i)
+            if (i < k) acc = fmaf(__shfl_sync(FULL, wi, i), pv[i], acc);
+          const float dcar = warp_sum(wi * pdi);
+          float iv = 0.f, idn = 0.f;
+          unsigned mask = __ballot_sync(FULL, hd >= 0);
+          while (mask) {
+            const int i = __ffs(mask) - 1;
+            mask &= mask - 1u;
+            const float w = __shfl_sync(FULL, wi, i);
+            for (int e = __shfl_sync(FULL, hd, i); e >= 0; e = nxt[e]) {
+              const int s = ent_s[e];
+              if (s >= tau) continue;
+              const float coef = w * ent_w[e] * lampow[tau - 1 - s];
+              iv = fmaf(coef, Vs[s * SCAN_CW + lane], iv);
+              idn += coef;
+            }
+          }
+          const int64_t tok = (int64_t)b * T + c0 + tau;
+          if (col_ok) a.num[(tok * h + hh) * dh + col] = fmaf(fade, acc, iv);
+          if (cs == 0 && lane == 0) a.den[tok * h + hh] = fmaf(fade, dcar, idn);
+        }
+        workers_sync();
+
+        // writes
+        const int njobs = jobs[0];
+        if (mode != 0) {
+          const float inv = mode == 2 ? 1.f / (sigma * lampow[ue]) : 1.f;
+          for (int jb = warp; jb < njobs; jb += 2 * SCAN_WORKERS) {
+            // two jobs per pass for memory-level parallelism
+            const int jb2 = jb + SCAN_WORKERS;
+            const bool two = jb2 < njobs;
+            const int r0 = jobs[1 + jb];
+            const int r1 = two ? jobs[1 + jb2] : r0;
+            int e0 = head[r0];
+            int e1 = two ? head[r1] : -1;
+            float p0 = P[r0 * SCAN_CW + lane], pc0 = Pc[r0];
+            float p1 = two ? P[r1 * SCAN_CW + lane] : 0.f, pc1 = two ? Pc[r1] : 0.f;
+            while (e0 >= 0 || e1 >= 0) {
+              if (e0 >= 0) {
+                const int se = ent_s[e0];
+                const float f = ent_w[e0] * lampow[t1 - 1 - se] * inv;
+                p0 = fmaf(f, Vs[se * SCAN_CW + lane], p0);
+                pc0 += f;
+                e0 = nxt[e0];
+              }
+              if (e1 >= 0) {
+                const int se = ent_s[e1];
+                const float f = ent_w[e1] * lampow[t1 - 1 - se] * inv;
+                p1 = fmaf(f, Vs[se * SCAN_CW + lane], p1);
+                pc1 += f;
+                e1 = nxt[e1];
+              }
+            }
+            P[r0 * SCAN_CW + lane] = p0;
+            if (two) P[r1 * SCAN_CW + lane] = p1;
+            __syncwarp();
+            if (lane == 0) {
+              Pc[r0] = pc0;
+              head[r0] = -1;
+              if (two) {
+                Pc[r1] = pc1;
+                head[r1] = -1;
+              }
+            }
+          }
+          if (mode == 2) sigma *= lampow[ue];
+        } else {
+          // fade 0: the state becomes the step's last token's writes alone.  Warp w < k sets new row w and clears
+          // old survivor row w unless it is among the new rows (the two sets of rows touched are disjoint).
+          const int sl = t1 - 1;
+          const int* lold = lastr_b + lbuf * SCAN_MAX_K;
+          int* lnew = lastr_b + (lbuf ^ 1) * SCAN_MAX_K;
+          const int rn_l = lane < k ? siw_s[sl * k + lane] : -2;
+          for (int jj = warp; jj < k; jj += SCAN_WORKERS) {
+            const int rn = siw_s[sl * k + jj];
+            const float wn = ww_s[sl * k + jj];
+            P[rn * SCAN_CW + lane] = wn * Vs[sl * SCAN_CW + lane];
+            if (lane == 0) {
+              Pc[rn] = wn;
+              lnew[jj] = rn;
+            }
+            const int ro = lold[jj];
+            if (ro >= 0 && __ballot_sync(FULL, rn_l == ro) == 0u) {
+              P[ro * SCAN_CW + lane] = 0.f;
+              if (lane == 0) Pc[ro] = 0.f;
+            }
+          }
+          for (int jb = warp; jb < njobs; jb += SCAN_WORKERS)
+            if (lane == 0) head[jobs[1 + jb]] = -1;
+          lbuf ^= 1;
+        }
       }
-      const int64_t tok = (int64_t)b * T + c0 + tau;
-      if (col_ok) a.num[(tok * h + hh) * dh + col] = acc;
-      if (cs == 0 && lane == 0) a.den[tok * h + hh] = accd;
+      buf ^= 1;
+      t0 = t1;
+      __syncthreads();
     }
-    __syncthreads();
-    // write phase: warp per slot, lane per column
-    const int seg_last = has_reset ? seg_s[Lc - 1] : 0;
-    const float dec = (!has_reset || seg_last == seg_prev) ? lampow[Lc] : 0.f;
-    for (int r = warp; r < M; r += NW) {
-      float pv = P[r * SCAN_CW + lane] * dec;
-      float pc = Pc[r] * dec;
-      const int hi = bstart[r + 1];
-      for (int p = bstart[r]; p < hi; ++p) {
-        const int2 en = entries[p];
-        if (has_reset && seg_s[en.x] != seg_last) continue;
-        const float f = __int_as_float(en.y) * lampow[Lc - 1 - en.x];
-        pv = fmaf(f, Vs[en.x * SCAN_CW + lane], pv);
-        pc += f;
+    // the next chunk's inputs
+    if (Lcn > 0) {
+      if (!builder) prefetch_store(pf, M, k, Lcn, siw_s, ww_s, sir_s, wr_s, Vs, rst_s);
+      __syncthreads();
+    }
+  }
+  // the final state, unscaled
+  if (!builder) {
+    const float fs = mode == 2 ? sigma : 1.f;
+    if (a.mem_out) {
+      float* mo = a.mem_out + ((int64_t)b * h + hh) * (int64_t)M * dh;
+      for (int i = tid; i < M * SCAN_CW; i += SCAN_WORKERS * 32) {
+        const int r = i / SCAN_CW, c = i % SCAN_CW, gc = cs * SCAN_CW + c;
+        if (gc < dh) mo[(int64_t)r * dh + gc] = P[i] * fs;
       }
-      P[r * SCAN_CW + lane] = pv;
-      if (lane == 0) Pc[r] = pc;
     }
-    if (has_reset) seg_prev = seg_last;
-    __syncthreads();
-  }
-  if (a.mem_out) {
-    float* mo = a.mem_out + ((int64_t)b * h + hh) * (int64_t)M * dh;
-    for (int i = tid; i < M * SCAN_CW; i += SCAN_THREADS) {
-      const int r = i / SCAN_CW, c = i % SCAN_CW, gc = cs * SCAN_CW + c;
-      if (gc < dh) mo[(int64_t)r * dh + gc] = P[i];
+    if (a.cnt_out && cs == 0) {
+      float* co = a.cnt_out + ((int64_t)b * h + hh) * (int64_t)M;
+      for (int r = tid; r < M; r += SCAN_WORKERS * 32) co[r] = Pc[r] * fs;
     }
-  }
-  if (a.cnt_out && cs == 0) {
-    float* co = a.cnt_out + ((int64_t)b * h + hh) * (int64_t)M;
-    for (int r = tid; r < M; r += SCAN_THREADS) co[r] = Pc[r];
   }
 }
 
 bool rt_scan_supported(int M, int dh, int k) {
-  if (M < 1 || dh < 1 || k < 1 || k > 32) return false;
+  if (M < 1 || dh < 1 || k < 1 || k > SCAN_MAX_K) return false;
   return scan_layout(M, scan_chunk_len(k), k).total <= 227 * 1024;
 }
 

@@ -1,0 +1,84 @@
+"""Small, fixed workloads for profiling one kernel at a time (ncu / compute-sanitizer friendly sizes).
+
+    python -m sdmchat_b200.profile_cases scan     # one RunTimeSdm d768 layer forward, 8 x 2048 tokens (bf16)
+    python -m sdmchat_b200.profile_cases gemm     # the layer's projection GEMM alone, 16384 x 768 x 1548
+    python -m sdmchat_b200.profile_cases pk       # product-key addressing of 16384 tokens x 12 heads
+    python -m sdmchat_b200.profile_cases decode   # 32 streams x 12 layers FULL decode steps
+
+Each case runs its workload `--reps` times (default 2) after building it, and prints one line of CUDA-event
+timings; nothing else runs on the GPU, so `ncu -k regex:<kernel> -c N` captures exactly the launches of interest.
+"""
+import argparse
+import json
+
+import torch
+
+import sdmchat_b200 as S
+from sdmchat_b200 import _lib
+
+
+def _layer(dev):
+    torch.manual_seed(0)
+    m = S.RunTimeSdm(768, heads=12, n_sub=32, d_a=32, k=16, decays=S.readme_fades(12))
+    with torch.no_grad():
+        torch.nn.init.normal_(m.wo.weight, std=0.02)
+        torch.nn.init.normal_(m.wg.weight, std=0.5 / 768 ** 0.5)
+    return m.to(dev).to(torch.bfloat16)
+
+
+def _timed(fn, reps):
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(reps):
+        fn()
+    b.record(st)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["scan", "gemm", "pk", "decode"])
+    ap.add_argument("--reps", type=int, default=2)
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    with torch.no_grad():
+        if a.case == "scan":
+            m = _layer(dev)
+            x = (torch.randn(8, 2048, 768, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            ms = _timed(lambda: m(x), a.reps)
+            out = {"case": "scan", "tokens": 8 * 2048, "ms_per_layer_forward": ms}
+        elif a.case == "gemm":
+            x = torch.randn(16384, 768, device=dev, generator=g).to(torch.bfloat16)
+            w = torch.randn(1548, 768, device=dev, generator=g).to(torch.bfloat16)
+            y = torch.empty(16384, 1548, device=dev)
+            lib = _lib.lib()
+
+            def run():
+                _lib.check(lib.sdm_gemm(_lib.ptr(x), _lib.ptr(w), 16384, 768, 1548, _lib.SDM_BF16, _lib.ptr(y),
+                                        _lib.stream_ptr(dev)), "sdm_gemm")
+            ms = _timed(run, a.reps)
+            out = {"case": "gemm", "shape": [16384, 768, 1548], "ms": ms,
+                   "tflops": 2 * 16384 * 768 * 1548 / (ms / 1e3) / 1e12}
+        elif a.case == "pk":
+            z = torch.randn(16384, 12, 32, device=dev, generator=g)
+            k1 = torch.randn(12, 32, 16, device=dev, generator=g)
+            k2 = torch.randn(12, 32, 16, device=dev, generator=g)
+            ms = _timed(lambda: S.pk_address(z, k1, k2, 16), a.reps)
+            out = {"case": "pk", "addresses": 16384 * 12, "ms": ms}
+        else:
+            torch.manual_seed(0)
+            model = S.build_onesdm("onesdm_allsdm", 32768, dict(d=768, layers=12, mlp_f=2048, heads=12,
+                                                                 decays=S.readme_fades(12)))
+            model = model.to_bf16_stream().to(dev)
+            state = model.init_decode(32, dev)
+            ids = torch.randint(0, 32768, (32,), device=dev, generator=g)
+            ms = _timed(lambda: model.decode_step(ids, state), a.reps)
+            out = {"case": "decode", "streams": 32, "ms_per_step": ms}
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()
