@@ -6,12 +6,12 @@
 // so the state never travels through HBM (the reference's chunked form re-reads and re-writes it every chunk).
 // Columns are independent in the recurrence, so slices of one head never communicate.
 //
-// Schedule: micro-steps of up to 16 tokens.  Within a step every token reads in parallel (one warp per token,
-// lane per column): the exact state at the step start, faded lam^(t-t0), plus the writes of earlier tokens of the
-// same step to the slots it reads, found through a per-step slot list (with 16 tokens x k writes over M slots such
-// collisions are rare).  Then the step's writes go straight into the state, one job per distinct written slot,
-// jobs dealt round-robin to the warps; a job walks its slot's list (every write to that slot in this step, newest
-// first).  That is the reference's math (chunked form = token recurrence, :728-755) with a step of 16:
+// Schedule: micro-steps of up to 16 tokens.  Within a step every token reads in parallel (one warp per token): the
+// exact state at the step start, faded lam^(t-t0), plus the writes of earlier tokens of the same step to the slots
+// it reads, found through a per-step slot list (with 16 tokens x k writes over M slots such collisions are rare).
+// Then the step's writes go straight into the state, one job per distinct written slot, jobs dealt round-robin to
+// the warps; a job walks its slot's list (every write to that slot in this step, newest first).  That is the
+// reference's math (chunked form = token recurrence, :728-755) with a step of 16:
 //   read   num[t] = sum_i wr[t,i] * ( lam^(t-t0) * mem[sir[t,i]] + sum_{t0<=s<t, siw[s,j]=sir[t,i]}
 //                                                                      lam^(t-1-s) * ww[s,j] * v[s] )
 //   write  mem <- lam^U * mem + sum_{s, j} lam^(t0+U-1-s) * ww[s,j] * e_{siw[s,j]} v[s]^T
@@ -19,6 +19,11 @@
 // touching every row; writes add their term / sigma.  P is renormalised (one pass) when sigma would fall below
 // 2^-40.  Fade 1 keeps sigma = 1; fade 0 (and fades below 2^-100) keep only the last token's writes.  A BOS reset
 // (:229-233) starts a new step and empties the state.
+//
+// Lanes work in four groups of eight: a group covers one 32-column row with one 16-byte access per lane, so a
+// warp touches four rows per shared-memory instruction (each quarter-warp phase reads one 128-byte row: no bank
+// conflicts).  A token's k reads are taken four at a time and the four partial sums combined with two shuffles;
+// write jobs are taken four at a time, one per group.
 //
 // Warps 0-15 ("workers") read and write, synchronising among themselves with a named barrier between the two
 // phases; warp 16 ("builder") builds the NEXT step's slot lists and job list meanwhile (double-buffered) and
@@ -76,6 +81,13 @@ static int scan_chunk_len(int k) {
 }
 
 __device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(SCAN_WORKERS * 32) : "memory"); }
+
+__device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
+  acc.x = fmaf(w, v.x, acc.x);
+  acc.y = fmaf(w, v.y, acc.y);
+  acc.z = fmaf(w, v.z, acc.z);
+  acc.w = fmaf(w, v.w, acc.w);
+}
 
 // Inputs of one chunk held in registers between their load and their store to shared memory (worker warps).
 struct Prefetch {
@@ -143,18 +155,21 @@ __device__ __forceinline__ int step_len(int t0, int Lc, int ustep, const int* rs
 // head[r] = newest entry writing slot r (-1 if none), nxt[e] = next older entry of the same slot, ent_s / ent_w =
 // chunk position and weight of e, jobs[1..] = the distinct written slots in first-write order, jobs[0] = count.
 // Tokens are inserted 32/k at a time; writes of one group to the same slot are ordered with __match_any_sync.
-__device__ __forceinline__ void build_lists(int t0, int ue, int k, int M, const int* siw_s, const float* ww_s,
+template <int K>
+__device__ __forceinline__ void build_lists(int t0, int ue, int k_rt, int M, const int* siw_s, const float* ww_s,
                                             int* head, int* nxt, int* ent_s, float* ent_w, int* jobs) {
+  const int k = K > 0 ? K : k_rt;
   const int lane = threadIdx.x & 31;
   const unsigned FULL = 0xffffffffu;
   const int G = 32 / k;  // tokens per group
+  const int ql = lane / k, jl = lane % k;
   int njobs = 0;
   for (int g0 = 0; g0 < ue; g0 += G) {
-    const int q = g0 + lane / k, j = lane % k;
+    const int q = g0 + ql;
     const bool valid = lane < G * k && q < ue;
     const int e = g0 * k + lane;
     const int s = t0 + q;
-    const int r = valid ? siw_s[s * k + j] : M + lane;  // invalid lanes match nothing
+    const int r = valid ? siw_s[s * k + jl] : M + lane;  // invalid lanes match nothing
     const unsigned peers = __match_any_sync(FULL, r);
     const unsigned lower = peers & ((1u << lane) - 1u);
     const unsigned higher = peers & ~((2u << lane) - 1u);
@@ -162,7 +177,7 @@ __device__ __forceinline__ void build_lists(int t0, int ue, int k, int M, const 
     if (valid) {
       nxt[e] = lower ? g0 * k + (31 - __clz(lower)) : old_head;
       ent_s[e] = s;
-      ent_w[e] = ww_s[s * k + j];
+      ent_w[e] = ww_s[s * k + jl];
     }
     __syncwarp();
     if (valid && higher == 0) head[r] = e;
@@ -176,18 +191,23 @@ __device__ __forceinline__ void build_lists(int t0, int ue, int k, int M, const 
   __syncwarp();
 }
 
+template <int K>
 __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, int L, int n_slices) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float lampow[SCAN_U + 2];
-  const int M = a.M, k = a.k, dh = a.dh, T = a.T, h = a.h;
+  const int M = a.M, dh = a.dh, T = a.T, h = a.h;
+  const int k = K > 0 ? K : a.k;
+  constexpr int KR = K > 0 ? K : SCAN_MAX_K;  // unroll bound of the per-read loops
   const ScanSmem lay = scan_layout(M, L, k);
   float* P = reinterpret_cast<float*>(smem + lay.P);
+  float4* P4 = reinterpret_cast<float4*>(smem + lay.P);
   float* Pc = reinterpret_cast<float*>(smem + lay.Pc);
   int* siw_s = reinterpret_cast<int*>(smem + lay.siw);
   float* ww_s = reinterpret_cast<float*>(smem + lay.ww);
   int* sir_s = reinterpret_cast<int*>(smem + lay.sir);
   float* wr_s = reinterpret_cast<float*>(smem + lay.wr);
   float* Vs = reinterpret_cast<float*>(smem + lay.Vs);
+  const float4* Vs4 = reinterpret_cast<const float4*>(smem + lay.Vs);
   int* rst_s = reinterpret_cast<int*>(smem + lay.rst);
   int* head_b = reinterpret_cast<int*>(smem + lay.head);
   int* nxt_b = reinterpret_cast<int*>(smem + lay.nxt);
@@ -201,9 +221,9 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
   const int hh = bh % h;
   const int b = bh / h;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = lane >> 3, c4 = lane & 7;  // lane group (row) and its 4-column quad
   const bool builder = warp == SCAN_WORKERS;
-  const int col = cs * SCAN_CW + lane;
-  const bool col_ok = col < dh;
+  const int ncols = min(SCAN_CW, dh - cs * SCAN_CW);  // valid columns of this slice
   const float lam = a.decay[hh];
   const bool has_reset = a.reset != nullptr;
   const unsigned FULL = 0xffffffffu;
@@ -212,7 +232,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
   int ustep = SCAN_U;
   if (mode == 2 && lam < 0.0131f) ustep = max(1, min(SCAN_U, (int)floorf(100.f / -log2f(lam))));  // lam^U >= 2^-100
 
-  for (int i = tid; i < M * SCAN_CW; i += SCAN_THREADS) P[i] = 0.f;
+  for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_THREADS) P4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int i = tid; i < M; i += SCAN_THREADS) {
     Pc[i] = 0.f;
     head_b[i] = -1;
@@ -237,8 +257,9 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
     const int Lcn = c0n < T ? min(L, T - c0n) : 0;
     if (!builder && Lcn > 0) prefetch_load(pf, a, b, hh, cs, c0n, Lcn);  // lands while this chunk computes
     if (builder)
-      build_lists(0, step_len(0, Lc, ustep, rst_s, has_reset), k, M, siw_s, ww_s, head_b + buf * M,
-                  nxt_b + buf * SCAN_EB, ents_b + buf * SCAN_EB, entw_b + buf * SCAN_EB, jobs_b + buf * (SCAN_EB + 1));
+      build_lists<K>(0, step_len(0, Lc, ustep, rst_s, has_reset), k, M, siw_s, ww_s, head_b + buf * M,
+                     nxt_b + buf * SCAN_EB, ents_b + buf * SCAN_EB, entw_b + buf * SCAN_EB,
+                     jobs_b + buf * (SCAN_EB + 1));
     __syncthreads();
 
     for (int t0 = 0; t0 < Lc;) {
@@ -248,9 +269,9 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
         // the next step's lists, into the other buffer (its heads were cleared by the previous step's writes)
         if (t1 < Lc) {
           const int nb = buf ^ 1;
-          build_lists(t1, step_len(t1, Lc, ustep, rst_s, has_reset), k, M, siw_s, ww_s, head_b + nb * M,
-                      nxt_b + nb * SCAN_EB, ents_b + nb * SCAN_EB, entw_b + nb * SCAN_EB,
-                      jobs_b + nb * (SCAN_EB + 1));
+          build_lists<K>(t1, step_len(t1, Lc, ustep, rst_s, has_reset), k, M, siw_s, ww_s, head_b + nb * M,
+                         nxt_b + nb * SCAN_EB, ents_b + nb * SCAN_EB, entw_b + nb * SCAN_EB,
+                         jobs_b + nb * (SCAN_EB + 1));
         }
       } else {
         int* head = head_b + buf * M;
@@ -263,14 +284,17 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
         const bool renorm = !clear && mode == 2 && sigma * lampow[ue] < 9.094947e-13f;  // 2^-40
         if (clear || renorm) {
           const float f = clear ? 0.f : sigma;
-          for (int i = tid; i < M * SCAN_CW; i += SCAN_WORKERS * 32) P[i] *= f;
+          for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_WORKERS * 32) {
+            float4 v = P4[i];
+            P4[i] = make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
+          }
           for (int i = tid; i < M; i += SCAN_WORKERS * 32) Pc[i] *= f;
           if (clear && tid < SCAN_MAX_K) lastr_b[lbuf * SCAN_MAX_K + tid] = -1;
           sigma = 1.f;
           workers_sync();
         }
 
-        // reads: worker warp w takes token t0 + w
+        // reads: worker warp w takes token t0 + w; group g handles reads g, g+4, ...
         if (warp < ue) {
           const int tau = t0 + warp;
           const float fade = (mode == 2 ? sigma : 1.f) * lampow[warp];
@@ -282,16 +306,24 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
             pdi = Pc[ri];
             hd = head[ri];
           }
-          float pv[SCAN_MAX_K];
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < SCAN_MAX_K; ++i)
-            if (i < k) pv[i] = P[__shfl_sync(FULL, ri, i) * SCAN_CW + lane];
-          float acc = 0.f;
+          for (int q = 0; q < (KR + 3) / 4; ++q) {
+            const int ii = 4 * q + grp;
+            const int r = __shfl_sync(FULL, ri, ii & 31);
+            const float w = __shfl_sync(FULL, wi, ii & 31);
+            if (K > 0 ? (ii < K) : (ii < k)) fma4(acc, w, P4[r * (SCAN_CW / 4) + c4]);
+          }
 #pragma unroll
-          for (int i = 0; i < SCAN_MAX_K; ++i)
-            if (i < k) acc = fmaf(__shfl_sync(FULL, wi, i), pv[i], acc);
+          for (int o = 8; o < 32; o <<= 1) {
+            acc.x += __shfl_xor_sync(FULL, acc.x, o);
+            acc.y += __shfl_xor_sync(FULL, acc.y, o);
+            acc.z += __shfl_xor_sync(FULL, acc.z, o);
+            acc.w += __shfl_xor_sync(FULL, acc.w, o);
+          }
           const float dcar = warp_sum(wi * pdi);
-          float iv = 0.f, idn = 0.f;
+          float4 iv = make_float4(0.f, 0.f, 0.f, 0.f);
+          float idn = 0.f;
           unsigned mask = __ballot_sync(FULL, hd >= 0);
           while (mask) {
             const int i = __ffs(mask) - 1;
@@ -301,12 +333,24 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
               const int s = ent_s[e];
               if (s >= tau) continue;
               const float coef = w * ent_w[e] * lampow[tau - 1 - s];
-              iv = fmaf(coef, Vs[s * SCAN_CW + lane], iv);
+              fma4(iv, coef, Vs4[s * (SCAN_CW / 4) + c4]);
               idn += coef;
             }
           }
           const int64_t tok = (int64_t)b * T + c0 + tau;
-          if (col_ok) a.num[(tok * h + hh) * dh + col] = fmaf(fade, acc, iv);
+          if (grp == 0) {
+            float* dst = a.num + (tok * h + hh) * dh + cs * SCAN_CW + 4 * c4;
+            const float o0 = fmaf(fade, acc.x, iv.x), o1 = fmaf(fade, acc.y, iv.y);
+            const float o2 = fmaf(fade, acc.z, iv.z), o3 = fmaf(fade, acc.w, iv.w);
+            if (4 * c4 + 3 < ncols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+              *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
+            } else {
+              if (4 * c4 + 0 < ncols) dst[0] = o0;
+              if (4 * c4 + 1 < ncols) dst[1] = o1;
+              if (4 * c4 + 2 < ncols) dst[2] = o2;
+              if (4 * c4 + 3 < ncols) dst[3] = o3;
+            }
+          }
           if (cs == 0 && lane == 0) a.den[tok * h + hh] = fmaf(fade, dcar, idn);
         }
         workers_sync();
@@ -315,64 +359,64 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
         const int njobs = jobs[0];
         if (mode != 0) {
           const float inv = mode == 2 ? 1.f / (sigma * lampow[ue]) : 1.f;
-          for (int jb = warp; jb < njobs; jb += 2 * SCAN_WORKERS) {
-            // two jobs per pass for memory-level parallelism
-            const int jb2 = jb + SCAN_WORKERS;
-            const bool two = jb2 < njobs;
-            const int r0 = jobs[1 + jb];
-            const int r1 = two ? jobs[1 + jb2] : r0;
-            int e0 = head[r0];
-            int e1 = two ? head[r1] : -1;
-            float p0 = P[r0 * SCAN_CW + lane], pc0 = Pc[r0];
-            float p1 = two ? P[r1 * SCAN_CW + lane] : 0.f, pc1 = two ? Pc[r1] : 0.f;
-            while (e0 >= 0 || e1 >= 0) {
-              if (e0 >= 0) {
-                const int se = ent_s[e0];
-                const float f = ent_w[e0] * lampow[t1 - 1 - se] * inv;
-                p0 = fmaf(f, Vs[se * SCAN_CW + lane], p0);
-                pc0 += f;
-                e0 = nxt[e0];
-              }
-              if (e1 >= 0) {
-                const int se = ent_s[e1];
-                const float f = ent_w[e1] * lampow[t1 - 1 - se] * inv;
-                p1 = fmaf(f, Vs[se * SCAN_CW + lane], p1);
-                pc1 += f;
-                e1 = nxt[e1];
-              }
+          for (int jb = 4 * warp; jb < njobs; jb += 4 * SCAN_WORKERS) {
+            const int j = jb + grp;
+            const bool valid = j < njobs;
+            const int r = valid ? jobs[1 + j] : 0;
+            int e = valid ? head[r] : -1;
+            float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
+            float pc = 0.f;
+            if (valid) {
+              p = P4[r * (SCAN_CW / 4) + c4];
+              pc = Pc[r];
             }
-            P[r0 * SCAN_CW + lane] = p0;
-            if (two) P[r1 * SCAN_CW + lane] = p1;
+            while (e >= 0) {
+              const int se = ent_s[e];
+              const float f = ent_w[e] * lampow[t1 - 1 - se] * inv;
+              fma4(p, f, Vs4[se * (SCAN_CW / 4) + c4]);
+              pc += f;
+              e = nxt[e];
+            }
             __syncwarp();
-            if (lane == 0) {
-              Pc[r0] = pc0;
-              head[r0] = -1;
-              if (two) {
-                Pc[r1] = pc1;
-                head[r1] = -1;
+            if (valid) {
+              P4[r * (SCAN_CW / 4) + c4] = p;
+              if (c4 == 0) {
+                Pc[r] = pc;
+                head[r] = -1;
               }
             }
           }
           if (mode == 2) sigma *= lampow[ue];
         } else {
-          // fade 0: the state becomes the step's last token's writes alone.  Warp w < k sets new row w and clears
-          // old survivor row w unless it is among the new rows (the two sets of rows touched are disjoint).
+          // fade 0: the state becomes the step's last token's writes alone.  Row jj: set new row jj and clear
+          // old survivor row jj unless it is among the new rows (the two sets of rows touched are disjoint).
           const int sl = t1 - 1;
           const int* lold = lastr_b + lbuf * SCAN_MAX_K;
           int* lnew = lastr_b + (lbuf ^ 1) * SCAN_MAX_K;
           const int rn_l = lane < k ? siw_s[sl * k + lane] : -2;
-          for (int jj = warp; jj < k; jj += SCAN_WORKERS) {
-            const int rn = siw_s[sl * k + jj];
-            const float wn = ww_s[sl * k + jj];
-            P[rn * SCAN_CW + lane] = wn * Vs[sl * SCAN_CW + lane];
-            if (lane == 0) {
-              Pc[rn] = wn;
-              lnew[jj] = rn;
+          for (int j0 = 4 * warp; j0 < k; j0 += 4 * SCAN_WORKERS) {
+            const int jj = j0 + grp;
+            const bool valid = jj < k;
+            const int rn = valid ? siw_s[sl * k + jj] : 0;
+            const int ro = valid ? lold[jj] : -1;
+            bool old_in_new = false;
+#pragma unroll
+            for (int l = 0; l < SCAN_MAX_K; ++l) {
+              const int rl = __shfl_sync(FULL, rn_l, l);
+              old_in_new |= (rl == ro);
             }
-            const int ro = lold[jj];
-            if (ro >= 0 && __ballot_sync(FULL, rn_l == ro) == 0u) {
-              P[ro * SCAN_CW + lane] = 0.f;
-              if (lane == 0) Pc[ro] = 0.f;
+            if (valid) {
+              const float wn = ww_s[sl * k + jj];
+              const float4 v = Vs4[sl * (SCAN_CW / 4) + c4];
+              P4[rn * (SCAN_CW / 4) + c4] = make_float4(wn * v.x, wn * v.y, wn * v.z, wn * v.w);
+              if (c4 == 0) {
+                Pc[rn] = wn;
+                lnew[jj] = rn;
+              }
+              if (ro >= 0 && !old_in_new) {
+                P4[ro * (SCAN_CW / 4) + c4] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (c4 == 0) Pc[ro] = 0.f;
+              }
             }
           }
           for (int jb = warp; jb < njobs; jb += SCAN_WORKERS)
@@ -412,17 +456,26 @@ bool rt_scan_supported(int M, int dh, int k) {
   return scan_layout(M, scan_chunk_len(k), k).total <= 227 * 1024;
 }
 
+template <int K>
+static cudaError_t launch_scan_k(const ScanArgs& a, int L, size_t smem, int n_slices, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(rt_scan_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int64_t grid = (int64_t)a.B * a.h * n_slices;
+  LaunchScope scope_("rt_scan", st);
+  rt_scan_kernel<K><<<(unsigned)grid, SCAN_THREADS, smem, st>>>(a, L, n_slices);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st) {
   if (a.B == 0 || a.T == 0) return cudaSuccess;
   const int L = scan_chunk_len(a.k);
-  const ScanSmem lay = scan_layout(a.M, L, a.k);
-  cudaError_t e = cudaFuncSetAttribute(rt_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.total);
-  if (e != cudaSuccess) return e;
+  const size_t smem = scan_layout(a.M, L, a.k).total;
   const int n_slices = (a.dh + SCAN_CW - 1) / SCAN_CW;
-  const int64_t grid = (int64_t)a.B * a.h * n_slices;
-  LaunchScope scope_("rt_scan", st);
-  rt_scan_kernel<<<(unsigned)grid, SCAN_THREADS, lay.total, st>>>(a, L, n_slices);
-  return cudaGetLastError();
+  switch (a.k) {
+    case 16: return launch_scan_k<16>(a, L, smem, n_slices, st);
+    case 4: return launch_scan_k<4>(a, L, smem, n_slices, st);
+    default: return launch_scan_k<0>(a, L, smem, n_slices, st);
+  }
 }
 
 }  // namespace sdm
