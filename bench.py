@@ -341,7 +341,8 @@ def run_ours(a):
         ach = byts / (per_kernel[dom]["ms"] / 1e3) / 1e9
         roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(ach / pk["hbm_gbs"], 4), "traffic": None, "peak_source": f"{how} hbm_gbs"}
-    breakdown = {k: {"ms_per_step": round(v["ms"] / a.steps, 3), "launches_per_step": v["launches"] / a.steps}
+    breakdown = {k: {"ms_per_step": round(v["ms"] / a.steps, 3), "launches_per_step": v["launches"] / a.steps,
+                     "by_call_site_ms": {t: round(ms / a.steps, 3) for t, ms in v["tags"].items()}}
                  for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1]["ms"])}
 
     # decode (config 4): S streams per GPU, 2,048-token prompt prefilled, then carried-state greedy steps

@@ -284,12 +284,20 @@ sdm_status swiglu_t(const void* xv, const void* nw, const void* wg, const void* 
 
 constexpr int64_t HEAD_ROWS = 4096;  // rows of logits materialised at a time by the loss / argmax heads
 
-size_t head_ws(int64_t N, int d, int V, int dtype, void* base, void** hbuf, float** lg) {
+size_t head_ws(int64_t N, int d, int V, int dtype, void* base, void** hbuf, float** lg, float2** part,
+               float** tgt_logit) {
   Bump bp(base);
   const size_t es = dtype == SDM_BF16 ? 2 : 4;
   *hbuf = bp.take<char>(N * d * es);
+  // the fused tensor-core head needs per-(row, column tile) partials; the CUDA-core head a block of logits rows
   const int64_t R = N < HEAD_ROWS ? N : HEAD_ROWS;
-  *lg = bp.take<float>(R * V);
+  const size_t fused = (size_t)N * ceil_div(V, TC_BN) * sizeof(float2) + 256 + (size_t)N * sizeof(float) + 256;
+  const size_t chunk = (size_t)R * V * sizeof(float) + 256;
+  char* rest = bp.take<char>(fused > chunk ? fused : chunk);
+  *lg = reinterpret_cast<float*>(rest);
+  *part = reinterpret_cast<float2*>(rest);
+  *tgt_logit = rest ? reinterpret_cast<float*>(rest + (((size_t)N * ceil_div(V, TC_BN) * sizeof(float2) + 255) & ~(size_t)255))
+                    : nullptr;
   return bp.off;
 }
 
@@ -299,10 +307,12 @@ sdm_status head_t(int mode, const void* xv, const void* nf_w, const void* emb, c
                   cudaStream_t st) {
   void* hb;
   float* lg;
+  float2* part;
+  float* tl;
   const int dtype = sizeof(T) == 2 ? SDM_BF16 : SDM_F32;
-  const size_t need = head_ws(N, d, V, dtype, nullptr, &hb, &lg);
+  const size_t need = head_ws(N, d, V, dtype, nullptr, &hb, &lg, &part, &tl);
   if (ws_bytes < need || (need && !ws)) return SDM_ERR_WORKSPACE;
-  head_ws(N, d, V, dtype, ws, &hb, &lg);
+  head_ws(N, d, V, dtype, ws, &hb, &lg, &part, &tl);
   if (N == 0) return SDM_OK;
   const T* x = static_cast<const T*>(xv);
   T* h = static_cast<T*>(hb);
@@ -312,6 +322,20 @@ sdm_status head_t(int mode, const void* xv, const void* nf_w, const void* emb, c
   if (mode == 0) {
     SDM_TRY(launch_gemm<T, EpiStore<T>>(h, d, E, d, N, d, V, EpiStore<T>{static_cast<T*>(logits), V}, st));
     return SDM_OK;
+  }
+  if constexpr (sizeof(T) == 2) {
+    if (tc_gemm_supported(h, d, E, d, d, d)) {
+      // fused head: the logits never leave the SM (per-tile logsumexp / argmax partials only)
+      const int tiles_n = (int)ceil_div(V, TC_BN);
+      if (mode == 1) {
+        SDM_TRY(launch_gemm_tc<EpiCE>(h, d, E, d, N, d, V, EpiCE{tgt, part, tl}, st, d));
+        SDM_TRY(launch_ce_combine(part, tl, tgt, N, tiles_n, loss, st));
+      } else {
+        SDM_TRY(launch_gemm_tc<EpiArgmax>(h, d, E, d, N, d, V, EpiArgmax{part}, st, d));
+        SDM_TRY(launch_argmax_combine(part, N, tiles_n, ids, st));
+      }
+      return SDM_OK;
+    }
   }
   for (int64_t r0 = 0; r0 < N; r0 += HEAD_ROWS) {
     const int64_t R = (N - r0) < HEAD_ROWS ? (N - r0) : HEAD_ROWS;
@@ -536,8 +560,9 @@ sdm_status sdm_swiglu_block(const void* x, const void* norm_w, const void* w_gat
 
 size_t sdm_tied_head_workspace_size(int64_t N, int d, int V, int dtype) {
   void* a;
-  float* b;
-  return head_ws(N < 0 ? 0 : N, d, V, dtype, nullptr, &a, &b);
+  float *b, *t;
+  float2* c;
+  return head_ws(N < 0 ? 0 : N, d, V, dtype, nullptr, &a, &b, &c, &t);
 }
 
 static sdm_status head_dispatch(int mode, const void* x, const void* nf_w, const void* emb, const int32_t* tgt,

@@ -76,10 +76,6 @@ cudaError_t launch_gemm_simt(const TA* x, int64_t ldx, const TA* w, int64_t ldw,
   return cudaGetLastError();
 }
 
-template <typename Epi>
-cudaError_t launch_gemm_tc(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K, int n,
-                           Epi epi, cudaStream_t st, int kwrap);
-
 template <typename TA, typename Epi>
 cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int n, Epi epi,
                         cudaStream_t st, int kwrap) {

@@ -1,14 +1,18 @@
 // bfloat16 GEMM on the sm_100a tensor cores: y = x @ w^T with a fused epilogue (tcgen05.mma, TMA, TMEM).
 //
-// CTA tile 128 x 128, K step 64 (one 128-byte swizzle atom of bf16 per row).  Warp roles:
-//   warp 0      TMA producer: one elected lane streams A (x rows) and B (w rows) tiles into a 3-stage ring with
+// Persistent kernel, one CTA per SM, CTA tile 128 x 128, K step 64 (one 128-byte swizzle atom of bf16 per row).
+// Warp roles:
+//   warp 0      TMA producer: one lane streams A (x rows) and B (w rows) tiles into a 4-stage ring with
 //               cp.async.bulk.tensor, completing on the stage's `full` mbarrier.
-//   warp 1      MMA issuer: allocates the 128-column TMEM accumulator; one lane issues 4 tcgen05.mma (K = 16 each)
-//               per stage from shared-memory descriptors and releases the stage with tcgen05.commit on `empty`;
-//               after the last stage it commits the accumulator-full barrier.
+//   warp 1      MMA issuer: allocates two 128-column TMEM accumulators; one lane issues 4 tcgen05.mma (K = 16
+//               each) per stage from shared-memory descriptors, releases the stage with tcgen05.commit on `empty`
+//               and, after a tile's last stage, commits that accumulator's `acc_full` barrier.
 //   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time (warp w reads TMEM lanes 32*(w%4)..+31, i.e.
-//               accumulator rows), then the epilogue functor writes each element.
-// Two CTAs fit on an SM (96 KB ring each), so one CTA's epilogue overlaps the other's main loop.
+//               accumulator rows), then hands the accumulator back (`acc_empty`), so tile i's epilogue runs while
+//               tile i+1's MMAs fill the other accumulator.
+// Epilogues: element-wise ones (Epi::kRowMode false) go through a padded shared-memory transpose so a warp's global
+// accesses are 32 consecutive columns of one row; row-owned ones (kRowMode true: the tied-head loss / argmax)
+// reduce each thread's row of the tile in registers and write one partial per (row, column tile).
 // Every mbarrier wait is bounded (about 4 s of %globaltimer); a wait that gives up sets g_tc_timeout, every role
 // falls through to the common exit, and the TMEM columns are released.  No load here reads another GPU's memory
 // and none is issued to more than one CTA.
@@ -21,9 +25,12 @@ __device__ int g_tc_timeout;
 
 namespace tc {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3, THREADS = 192;
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4, THREADS = 192;
 constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr size_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+constexpr int STAGE_LD = 33;  // padded row of the epilogue transpose
+constexpr size_t RING_BYTES = STAGES * STAGE_BYTES;
+constexpr size_t SMEM_BYTES = RING_BYTES + 4 * 32 * STAGE_LD * 4 + 1024;
+constexpr uint32_t TMEM_COLS = 2 * BN;
 
 // Instruction descriptor of tcgen05.mma kind::f16: D float32, A and B bfloat16, both K-major, M = 128, N = BN.
 constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -41,6 +48,9 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 }
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -109,34 +119,39 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 template <typename Epi>
-__global__ void __launch_bounds__(THREADS, 2)
+__global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t rows,
                    int K, int n, Epi epi, int kwrap) {
   extern __shared__ __align__(1024) unsigned char dsmem[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_slot;
 
   unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
+  float* stage_all = reinterpret_cast<float*>(ring + RING_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int64_t m0 = (int64_t)blockIdx.y * BM;
   const int kt_count = (K + BK - 1) / BK;
+  const int tiles_n = (n + BN - 1) / BN;
+  const int64_t tiles = (int64_t)tiles_n * ((rows + BM - 1) / BM);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&acc_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
-                 "r"(BN)
+                 "r"(TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -147,62 +162,111 @@ __global__ void __launch_bounds__(THREADS, 2)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int kt = 0; kt < kt_count; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
-        if (!mbar_wait(&empty_bar[s], ph ^ 1u)) break;
-        unsigned char* a_dst = ring + s * STAGE_BYTES;
-        unsigned char* b_dst = a_dst + A_BYTES;
-        mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
-        tma_load_2d(&tmA, &full_bar[s], a_dst, kt * BK, (int)m0);
-        tma_load_2d(&tmB, &full_bar[s], b_dst, (kt * BK) % kwrap, n0);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int n0 = (int)(t % tiles_n) * BN;
+        const int m0 = (int)(t / tiles_n) * BM;
+        for (int kt = 0; kt < kt_count; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u)) {
+            ok = false;
+            break;
+          }
+          unsigned char* a_dst = ring + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+          tma_load_2d(&tmA, &full_bar[s], a_dst, kt * BK, m0);
+          tma_load_2d(&tmB, &full_bar[s], a_dst + A_BYTES, (kt * BK) % kwrap, n0);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      uint32_t it = 0, tl = 0;
       bool ok = true;
-      for (int kt = 0; kt < kt_count; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (uint32_t)(kt / STAGES) & 1u;
-        if (!mbar_wait(&full_bar[s], ph)) {
-          ok = false;
-          break;
-        }
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++tl) {
+        const uint32_t buf = tl & 1u, use = tl >> 1;
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_base = smem_u32(ring + s * STAGE_BYTES);
-        const uint32_t b_base = a_base + A_BYTES;
+        const uint32_t dt = tmem + buf * BN;
+        for (int kt = 0; kt < kt_count; ++kt, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&full_bar[s], ph)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_base = smem_u32(ring + s * STAGE_BYTES);
+          const uint32_t b_base = a_base + A_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          umma_bf16(tmem, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), (kt | kk) != 0);
-        umma_commit(&empty_bar[s]);
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16(dt, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), (kt | kk) != 0);
+          umma_commit(&empty_bar[s]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
       }
-      if (ok) umma_commit(&acc_bar);
     }
   } else {
     // epilogue warps 2..5: TMEM lane quarter = warp % 4
     const int q = warp & 3;
-    if (mbar_wait(&acc_bar, 0)) {
+    float* stage = stage_all + q * 32 * STAGE_LD;
+    uint32_t tl = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++tl) {
+      const uint32_t buf = tl & 1u, use = tl >> 1;
+      const int tn = (int)(t % tiles_n);
+      const int n0 = tn * BN;
+      const int64_t m0 = (t / tiles_n) * BM;
+      if (!mbar_wait(&acc_full[buf], use & 1u)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int64_t row = m0 + q * 32 + lane;
+      const int64_t row0 = m0 + q * 32;
+      if constexpr (Epi::kRowMode) {
+        typename Epi::RowState rs;
+        epi.row_begin(rs, row0 + lane, rows, n0);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
-        if (row < rows) {
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem + buf * BN + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
+          epi.row_chunk(rs, n0 + c0, n, r);
+        }
+        epi.row_end(rs, row0 + lane, rows, tn, tiles_n);
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem + buf * BN + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, r);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = n0 + c0 + j;
-            if (col < n) epi.apply(row, col, __uint_as_float(r[j]));
+          for (int j = 0; j < 32; ++j) stage[lane * STAGE_LD + j] = __uint_as_float(r[j]);
+          __syncwarp();
+          const int col = n0 + c0 + lane;
+          const bool col_ok = col < n;
+          const typename Epi::Col cc = col_ok ? epi.column(col) : typename Epi::Col{};
+          float in[32];
+          if constexpr (Epi::kHasInput) {
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr)  // all 32 loads in flight before the first use
+              in[rr] = (col_ok && row0 + rr < rows) ? epi.load_input(row0 + rr, col) : 0.f;
           }
+#pragma unroll 8
+          for (int rr = 0; rr < 32; ++rr) {
+            const int64_t row = row0 + rr;
+            if (row < rows && col_ok)
+              epi.store(row, col, stage[rr * STAGE_LD + lane], cc, Epi::kHasInput ? in[rr] : 0.f);
+          }
+          __syncwarp();
         }
       }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -235,6 +299,19 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+static int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : 148;
+  }
+  return cached[dev];
+}
+
 }  // namespace tc
 
 bool tc_gemm_supported(const void* x, int64_t ldx, const void* w, int64_t ldw, int K, int kwrap) {
@@ -255,7 +332,8 @@ cudaError_t launch_gemm_tc(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_
   auto kern = tc::gemm_tc_kernel<Epi>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)ceil_div(n, tc::BN), (unsigned)ceil_div(rows, tc::BM));
+  const int64_t tiles = ceil_div(n, tc::BN) * ceil_div(rows, tc::BM);
+  const int grid = (int)(tiles < tc::num_sms() ? tiles : tc::num_sms());
   LaunchScope scope_("gemm_tc", st);
   kern<<<grid, tc::THREADS, tc::SMEM_BYTES, st>>>(ma, mb, rows, K, n, epi, kwrap);
   return cudaGetLastError();
@@ -269,6 +347,8 @@ SDM_TC_INST(EpiProj)
 SDM_TC_INST(EpiStore<bf16_t>)
 SDM_TC_INST(EpiF32R<bf16_t>)
 SDM_TC_INST(EpiResid<bf16_t>)
+SDM_TC_INST(EpiCE)
+SDM_TC_INST(EpiArgmax)
 
 // Read and clear the bounded-wait timeout flag (set by any kernel whose wait gave up).
 cudaError_t read_and_clear_timeout(int* flag, cudaStream_t st) {

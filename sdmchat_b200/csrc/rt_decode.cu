@@ -174,6 +174,79 @@ __global__ void argmax_rows_kernel(const float* __restrict__ lg, int64_t rows, i
   }
 }
 
+// Cross-entropy from the fused head's per-tile partials: per row, logsumexp = M + log(sum_i s_i exp(m_i - M)) over
+// the column tiles, minus the target's logit; rows with target < 0 are skipped.  One warp per row, float64 total.
+__global__ void ce_combine_kernel(const float2* __restrict__ part, const float* __restrict__ tgt_logit,
+                                  const int32_t* __restrict__ targets, int64_t rows, int tiles_n, double* loss_sum) {
+  __shared__ double red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
+  double contrib = 0.0;
+  if (row < rows && targets[row] >= 0) {
+    const float2* pr = part + row * tiles_n;
+    float M = -INFINITY;
+    for (int i = lane; i < tiles_n; i += 32) M = fmaxf(M, pr[i].x);
+    M = warp_max(M);
+    float S = 0.f;
+    for (int i = lane; i < tiles_n; i += 32) {
+      const float2 p = pr[i];
+      if (p.x != -INFINITY) S += p.y * expf(p.x - M);
+    }
+    S = warp_sum(S);
+    contrib = (double)M + log((double)S) - (double)tgt_logit[row];
+  }
+  if (lane == 0) red[warp] = contrib;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < 8; ++w) t += red[w];
+    atomicAdd(loss_sum, t);
+  }
+}
+
+// Greedy id from the fused head's per-tile (best, column) partials; lowest column on ties.  One warp per row.
+__global__ void argmax_combine_kernel(const float2* __restrict__ part, int64_t rows, int tiles_n,
+                                      int32_t* __restrict__ ids) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
+  if (row >= rows) return;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = lane; i < tiles_n; i += 32) {
+    const float2 p = part[row * tiles_n + i];
+    const int idx = __float_as_int(p.y);
+    if (p.x > bv || (p.x == bv && idx < bi)) {
+      bv = p.x;
+      bi = idx;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) ids[row] = bi;
+}
+
+cudaError_t launch_ce_combine(const float2* part, const float* tgt_logit, const int32_t* targets, int64_t rows,
+                              int tiles_n, double* loss_sum, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  LaunchScope scope_("ce_combine", st);
+  ce_combine_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, st>>>(part, tgt_logit, targets, rows, tiles_n, loss_sum);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_combine(const float2* part, int64_t rows, int tiles_n, int32_t* ids, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  LaunchScope scope_("argmax_combine", st);
+  argmax_combine_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, st>>>(part, rows, tiles_n, ids);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_ce_rows(const float* logits, int64_t rows, int V, const int32_t* targets, double* loss_sum,
                            cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
