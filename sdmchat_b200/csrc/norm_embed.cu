@@ -99,6 +99,56 @@ __global__ void rt_finish_kernel(const float* __restrict__ num, const float* __r
   }
 }
 
+// The same finish for dh a multiple of 32: eight lanes per (token, head) row, each lane 4 consecutive columns per
+// 32-column step (16-byte loads), the row's sum of squares reduced over the eight lanes; a warp does four rows.
+template <typename T>
+__global__ void rt_finish_vec_kernel(const float* __restrict__ num, const float* __restrict__ den, int64_t N, int h,
+                                     int dh, int read_sum, float read_eps, int out_norm, float out_norm_eps,
+                                     const float* __restrict__ onorm_w, T* __restrict__ r, int split) {
+  const int64_t item = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+  const int g = threadIdx.x & 7;
+  const bool live = item < N * h;
+  const int64_t it = live ? item : 0;
+  const int hh = (int)(it % h);
+  const float4* nr = reinterpret_cast<const float4*>(num + it * dh);
+  const float dv = read_sum ? 0.f : den[it] + read_eps;
+  float4 vals[8];
+  float ss = 0.f;
+  const int steps = dh / 32;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    if (q < steps) {
+      float4 v = nr[q * 8 + g];
+      if (!read_sum) {
+        v.x = __fdiv_rn(v.x, dv);
+        v.y = __fdiv_rn(v.y, dv);
+        v.z = __fdiv_rn(v.z, dv);
+        v.w = __fdiv_rn(v.w, dv);
+      }
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+      vals[q] = v;
+    }
+  }
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+  if (!live) return;
+  const float rs = out_norm ? rsqrt_rn(__fdiv_rn(ss, (float)dh) + out_norm_eps) : 1.f;
+  const int64_t n = item / h;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    if (q < steps) {
+      const int c = q * 32 + g * 4;
+      float o[4] = {vals[q].x, vals[q].y, vals[q].z, vals[q].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (out_norm) o[e] = (o[e] * rs) * onorm_w[hh * dh + c + e];
+        store_split<T>(r, n, (int64_t)h * dh, (int64_t)hh * dh + c + e, o[e], split);
+      }
+    }
+  }
+}
+
 // TrainedSdm read (track4_onesdm_models.py:452-456): r[n, hh, :] = sum_j w[n, hh, j] * values[hh, si[n, hh, j], :]
 // (embedding_bag, mode "sum", accumulated in float32 in j order).  One warp per (token, head).
 template <typename T>
@@ -164,6 +214,11 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
                              cudaStream_t st) {
   if (N == 0) return cudaSuccess;
   LaunchScope scope_("rt_finish", st);
+  if (dh % 32 == 0 && dh <= 256) {
+    rt_finish_vec_kernel<T><<<(unsigned)ceil_div(N * h * 8, 256), 256, 0, st>>>(
+        num, den, N, h, dh, read_sum, read_eps, out_norm, out_norm_eps, onorm_w, r, split);
+    return cudaGetLastError();
+  }
   rt_finish_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(num, den, N, h, dh, read_sum, read_eps,
                                                                     out_norm, out_norm_eps, onorm_w, r, split);
   return cudaGetLastError();

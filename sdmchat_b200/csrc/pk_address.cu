@@ -114,8 +114,14 @@ __device__ __forceinline__ void normalize_half(const float* src, float (&zn)[HAL
 
 constexpr int PK_THREADS = 128;
 
+// Resident blocks per SM the register budget is sized for: 4 for lists up to 16 (128 registers, no spills), 2 for 32.
+template <int C>
+struct PkOcc {
+  static constexpr int value = C <= 16 ? 4 : 2;
+};
+
 template <int HALF, int C>
-__global__ void __launch_bounds__(PK_THREADS) pk_kernel(PkArgs a, int c1, int kk) {
+__global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs a, int c1, int kk) {
   extern __shared__ float pk_smem[];
   const int hh = blockIdx.y;
   const int tid = threadIdx.x;
@@ -126,8 +132,8 @@ __global__ void __launch_bounds__(PK_THREADS) pk_kernel(PkArgs a, int c1, int kk
   int* i1s = reinterpret_cast<int*>(v1s + C * PK_THREADS);
   float* v2s = reinterpret_cast<float*>(i1s + C * PK_THREADS);
   int* i2s = reinterpret_cast<int*>(v2s + C * PK_THREADS);
-  float* ov = reinterpret_cast<float*>(i2s + C * PK_THREADS);  // (32, PK_THREADS) emitted scores
-  int* oi = reinterpret_cast<int*>(ov + 32 * PK_THREADS);       // (32, PK_THREADS) emitted slot ids
+  float* ov = reinterpret_cast<float*>(i2s + C * PK_THREADS);  // (kk, PK_THREADS) emitted scores
+  int* oi = reinterpret_cast<int*>(ov + kk * PK_THREADS);       // (kk, PK_THREADS) emitted slot ids
 
   // F.normalize(keys, dim=-1) for this head
   for (int j = tid; j < 2 * n_sub; j += PK_THREADS) {
@@ -144,29 +150,30 @@ __global__ void __launch_bounds__(PK_THREADS) pk_kernel(PkArgs a, int c1, int kk
   const int64_t n = (int64_t)blockIdx.x * PK_THREADS + tid;
   if (n >= a.N) return;
   const float* zr = a.z + n * a.ldz + (int64_t)hh * a.d_a;
-  float tv1[C], tv2[C];
-  int ti1[C], ti2[C];
-  {
+  // the two halves one after the other through one register list (fewer live registers, more resident warps)
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    float tv[C];
+    int ti[C];
     float zn[HALF];
-    normalize_half<HALF>(zr, zn);
-    half_topc<HALF, C>(zn, kn1, n_sub, tv1, ti1);
-    normalize_half<HALF>(zr + HALF, zn);
-    half_topc<HALF, C>(zn, kn2, n_sub, tv2, ti2);
-  }
+    normalize_half<HALF>(zr + hf * HALF, zn);
+    half_topc<HALF, C>(zn, hf ? kn2 : kn1, n_sub, tv, ti);
+    float* vs = hf ? v2s : v1s;
+    int* is = hf ? i2s : i1s;
 #pragma unroll
-  for (int q = 0; q < C; ++q) {
-    v1s[q * PK_THREADS + tid] = tv1[q];
-    i1s[q * PK_THREADS + tid] = ti1[q];
-    v2s[q * PK_THREADS + tid] = tv2[q];
-    i2s[q * PK_THREADS + tid] = ti2[q];
+    for (int q = 0; q < C; ++q) {
+      vs[q * PK_THREADS + tid] = tv[q];
+      is[q * PK_THREADS + tid] = ti[q];
+    }
   }
   // frontier walk over the c1 x c1 grid: row a's next candidate is (a, fb[a])
   int fb[C];
   float fv[C];
+  const float v2_0 = v2s[tid];
 #pragma unroll
   for (int q = 0; q < C; ++q) {
     fb[q] = 0;
-    fv[q] = q < c1 ? (tv1[q] + tv2[0]) * 0.5f : -INFINITY;
+    fv[q] = q < c1 ? (v1s[q * PK_THREADS + tid] + v2_0) * 0.5f : -INFINITY;
   }
   for (int step = 0; step < kk; ++step) {
     int best = 0;
@@ -223,7 +230,7 @@ __global__ void __launch_bounds__(PK_THREADS) pk_kernel(PkArgs a, int c1, int kk
 
 template <int HALF, int C>
 static cudaError_t launch_pk_tc(const PkArgs& a, int c1, int kk, cudaStream_t st) {
-  const size_t smem = (size_t)2 * a.n_sub * HALF * 4 + (size_t)4 * C * PK_THREADS * 4 + (size_t)2 * 32 * PK_THREADS * 4;
+  const size_t smem = (size_t)2 * a.n_sub * HALF * 4 + (size_t)4 * C * PK_THREADS * 4 + (size_t)2 * kk * PK_THREADS * 4;
   auto kern = pk_kernel<HALF, C>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
