@@ -76,11 +76,113 @@ cudaError_t launch_gemm_simt(const TA* x, int64_t ldx, const TA* w, int64_t ldw,
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------------- skinny GEMM
+// Decode-sized products (at most 32 rows): the tile GEMMs would keep only a handful of SMs busy, so here every warp
+// owns output columns.  x is staged once per CTA in shared memory; a warp streams one weight row (16 bytes per lane
+// per step, coalesced), accumulates all rows' partial dot products in registers, and a 31-shuffle reduce-scatter
+// butterfly leaves row m's sum in lane m, which applies the epilogue.
+constexpr int SK_WARPS = 8;
+constexpr int SK_MAX_ROWS = 32;
+
+template <typename TA>
+struct Vec8 {
+  float v[8];
+};
+__device__ __forceinline__ Vec8<bf16_t> load8(const bf16_t* p) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  Vec8<bf16_t> r;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    r.v[2 * i] = f.x;
+    r.v[2 * i + 1] = f.y;
+  }
+  return r;
+}
+__device__ __forceinline__ Vec8<float> load8(const float* p) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  return {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
+}
+
+template <typename TA, typename Epi>
+__global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_kernel(const TA* __restrict__ x, int64_t ldx,
+                                                                   const TA* __restrict__ w, int64_t ldw, int rows,
+                                                                   int K, int n, Epi epi, int kwrap) {
+  extern __shared__ __align__(16) unsigned char sk_smem[];
+  TA* xs = reinterpret_cast<TA*>(sk_smem);  // (rows, K)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int vec_per_row = K / 8;
+  for (int i = tid; i < rows * vec_per_row; i += SK_WARPS * 32) {
+    const int r = i / vec_per_row, c = (i % vec_per_row) * 8;
+    if constexpr (sizeof(TA) == 2) {
+      *reinterpret_cast<uint4*>(xs + (int64_t)r * K + c) = *reinterpret_cast<const uint4*>(x + r * ldx + c);
+    } else {
+      reinterpret_cast<float4*>(xs + (int64_t)r * K + c)[0] = reinterpret_cast<const float4*>(x + r * ldx + c)[0];
+      reinterpret_cast<float4*>(xs + (int64_t)r * K + c)[1] = reinterpret_cast<const float4*>(x + r * ldx + c)[1];
+    }
+  }
+  __syncthreads();
+  for (int col = blockIdx.x * SK_WARPS + warp; col < n; col += gridDim.x * SK_WARPS) {
+    float acc[SK_MAX_ROWS];
+#pragma unroll
+    for (int m = 0; m < SK_MAX_ROWS; ++m) acc[m] = 0.f;
+    const TA* wr = w + (int64_t)col * ldw;
+    for (int k0 = lane * 8; k0 < K; k0 += 256) {
+      const Vec8<TA> wv = load8(wr + (k0 % kwrap));
+#pragma unroll
+      for (int m = 0; m < SK_MAX_ROWS; ++m) {
+        if (m < rows) {
+          const Vec8<TA> xv = load8(xs + (int64_t)m * K + k0);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[m] = fmaf(xv.v[e], wv.v[e], acc[m]);
+        }
+      }
+    }
+    // reduce-scatter: after the step of width o, this lane keeps the rows whose bit matches its lane bit
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < o; ++i) {
+        const float mine = upper ? acc[i + o] : acc[i];
+        const float other = upper ? acc[i] : acc[i + o];
+        acc[i] = mine + __shfl_xor_sync(0xffffffffu, other, o);
+      }
+    }
+    if (lane < rows) epi.apply(lane, col, acc[0]);
+  }
+}
+
+template <typename TA>
+static bool skinny_ok(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int kwrap) {
+  const size_t smem = (size_t)rows * K * sizeof(TA);
+  const uintptr_t ax = reinterpret_cast<uintptr_t>(x), aw = reinterpret_cast<uintptr_t>(w);
+  return rows >= 1 && rows <= SK_MAX_ROWS && K % 8 == 0 && kwrap % 8 == 0 && ldx % 8 == 0 && ldw % 8 == 0 &&
+         ax % 16 == 0 && aw % 16 == 0 && smem <= 160 * 1024;
+}
+
+template <typename TA, typename Epi>
+static cudaError_t launch_gemm_skinny(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int n,
+                                     Epi epi, cudaStream_t st, int kwrap) {
+  const size_t smem = (size_t)rows * K * sizeof(TA);
+  auto kern = gemm_skinny_kernel<TA, Epi>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int64_t grid = ceil_div(n, SK_WARPS);
+  if (grid > 148 * 2) grid = 148 * 2;
+  LaunchScope scope_("gemm_skinny", st);
+  kern<<<(unsigned)grid, SK_WARPS * 32, smem, st>>>(x, ldx, w, ldw, (int)rows, K, n, epi, kwrap);
+  return cudaGetLastError();
+}
+
 template <typename TA, typename Epi>
 cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int n, Epi epi,
                         cudaStream_t st, int kwrap) {
   if (kwrap <= 0) kwrap = K;
   if (K % kwrap) return cudaErrorInvalidValue;
+  if (rows == 0 || n == 0) return cudaSuccess;
+  if (skinny_ok(x, ldx, w, ldw, rows, K, kwrap)) return launch_gemm_skinny<TA, Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
   if constexpr (sizeof(TA) == 2) {
     if (tc_gemm_supported(x, ldx, w, ldw, K, kwrap))
       return launch_gemm_tc<Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);

@@ -248,10 +248,175 @@ static cudaError_t launch_pk_half(const PkArgs& a, int c1, int kk, cudaStream_t 
   return launch_pk_tc<HALF, 32>(a, c1, kk, st);
 }
 
+// ------------------------------------------------------------------------------------ warp-per-address variant
+// For launches with few addresses (decode: tens of tokens), one thread's serial sort chain is the whole latency.
+// Here a warp owns an address: lanes score sub-keys in parallel, each half's top-c1 is taken by c1 rounds of a warp
+// arg-max under the same total order (score desc, index asc), and the frontier walk's arg-max over rows is a warp
+// reduction (row a lives in lane a).  Same selections, same order, same soft weights as pk_kernel.
+constexpr int PKW_WARPS = 4;
+
+__device__ __forceinline__ void warp_best(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (better(ov, oi, v, i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
+template <int HALF>
+__global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c1, int kk) {
+  extern __shared__ float pkw_smem[];
+  const int hh = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_sub = a.n_sub;
+  float* kn1 = pkw_smem;                 // (n_sub, HALF)
+  float* kn2 = kn1 + n_sub * HALF;
+  float* wsm = kn2 + n_sub * HALF + warp * 4 * 32;  // per warp: v1[32], i1[32], v2[32], i2[32]
+  float* v1 = wsm;
+  int* i1 = reinterpret_cast<int*>(wsm + 32);
+  float* v2 = wsm + 64;
+  int* i2 = reinterpret_cast<int*>(wsm + 96);
+  for (int j = tid; j < 2 * n_sub; j += PKW_WARPS * 32) {
+    const float* src = (j < n_sub ? a.keys1 + ((int64_t)hh * n_sub + j) * HALF
+                                  : a.keys2 + ((int64_t)hh * n_sub + (j - n_sub)) * HALF);
+    float kv[HALF];
+    normalize_half<HALF>(src, kv);
+    float* dst = (j < n_sub ? kn1 + j * HALF : kn2 + (j - n_sub) * HALF);
+#pragma unroll
+    for (int dd = 0; dd < HALF; ++dd) dst[dd] = kv[dd];
+  }
+  __syncthreads();
+  const int64_t n = (int64_t)blockIdx.x * PKW_WARPS + warp;
+  if (n >= a.N) return;
+  const float* zr = a.z + n * a.ldz + (int64_t)hh * a.d_a;
+  // each half: lanes score sub-keys lane, lane+32, ...; c1 rounds of warp arg-max give the sorted top-c1
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    float zn[HALF];
+    normalize_half<HALF>(zr + hf * HALF, zn);
+    const float* kn = hf ? kn2 : kn1;
+    float sc[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int j = lane + 32 * q;
+      float s = -INFINITY;
+      if (j < n_sub) {
+        s = 0.f;
+#pragma unroll
+        for (int dd = 0; dd < HALF; ++dd) s = fmaf(zn[dd], kn[j * HALF + dd], s);
+        if (s != s) s = -INFINITY;
+      }
+      sc[q] = s;
+    }
+    float* vo = hf ? v2 : v1;
+    int* io = hf ? i2 : i1;
+    unsigned used = 0;  // this lane's candidates already taken
+    for (int r = 0; r < c1; ++r) {
+      // this lane's best remaining candidate, then the warp's
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = lane + 32 * q;
+        if (j < n_sub && !((used >> q) & 1u) && better(sc[q], j, bv, bi)) {
+          bv = sc[q];
+          bi = j;
+        }
+      }
+      warp_best(bv, bi);
+      if (lane == 0) {
+        vo[r] = bv;
+        io[r] = bi;
+      }
+      if ((bi & 31) == lane) used |= 1u << (bi >> 5);  // retire the winner
+    }
+    __syncwarp();
+  }
+  // frontier: lane a holds row a's next candidate (a, fb)
+  int fb = 0;
+  const float v1a = lane < c1 ? v1[lane] : -INFINITY;
+  const int i1a = lane < c1 ? i1[lane] : 0;
+  float fv = lane < c1 ? (v1a + v2[0]) * 0.5f : -INFINITY;
+  float out_v = 0.f;
+  int out_i = 0;
+  for (int step = 0; step < kk; ++step) {
+    float bv = fv;
+    int bflat = lane < c1 ? lane * c1 + fb : 0x7fffffff;
+    warp_best(bv, bflat);
+    const int ba = bflat / c1, bb = bflat - ba * c1;
+    const int slot = __shfl_sync(0xffffffffu, i1a, ba) * n_sub + i2[bb];
+    if (lane == step) {
+      out_v = bv;
+      out_i = slot;
+    }
+    if (lane == ba) {
+      fb = bb + 1;
+      fv = fb < c1 ? (v1a + v2[fb]) * 0.5f : -INFINITY;
+    }
+  }
+  // outputs and softmax(scale * score) (* gate): lane j holds the j-th pick
+  int64_t dst;
+  if (a.T_bh > 0) {
+    const int64_t bb = n / a.T_bh, t = n % a.T_bh;
+    dst = ((bb * a.h + hh) * a.T_bh + t) * kk;
+  } else {
+    dst = (n * a.h + hh) * kk;
+  }
+  const bool mine = lane < kk;
+  if (mine) {
+    a.si[dst + lane] = out_i;
+    if (a.sv) a.sv[dst + lane] = out_v;
+  }
+  if (a.w) {
+    const float scale = expf(a.log_scale[hh]);
+    const float x = mine ? out_v * scale : -INFINITY;
+    const float mx = warp_max(x);
+    const float e = mine ? expf(x - mx) : 0.f;
+    // the sum in pick order, as the thread-per-address kernel adds it
+    float sum = 0.f;
+    for (int j = 0; j < kk; ++j) sum += __shfl_sync(0xffffffffu, e, j);
+    if (mine) {
+      float wj = __fdiv_rn(e, sum);
+      if (a.gate) wj = wj * a.gate[n * a.ldgate + hh];
+      a.w[dst + lane] = wj;
+    }
+  }
+}
+
+template <int HALF>
+static cudaError_t launch_pk_warp(const PkArgs& a, int c1, int kk, cudaStream_t st) {
+  const size_t smem = (size_t)2 * a.n_sub * HALF * 4 + (size_t)PKW_WARPS * 4 * 32 * 4;
+  auto kern = pk_warp_kernel<HALF>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)ceil_div(a.N, PKW_WARPS), (unsigned)a.h);
+  LaunchScope scope_("pk_address", st);
+  kern<<<grid, PKW_WARPS * 32, smem, st>>>(a, c1, kk);
+  return cudaGetLastError();
+}
+
+// Launches with at most this many addresses use the warp-per-address kernel.
+constexpr int64_t PK_WARP_MAX_ADDRESSES = 8192;
+
 cudaError_t launch_pk_address(const PkArgs& a, cudaStream_t st) {
   if (a.N == 0) return cudaSuccess;
   const int c1 = a.k < a.n_sub ? a.k : a.n_sub;
   const int kk = a.k < c1 * c1 ? a.k : c1 * c1;
+  if (a.N * a.h <= PK_WARP_MAX_ADDRESSES && a.n_sub <= 128 && c1 <= 32 && kk <= 32) {
+    switch (a.d_a / 2) {
+      case 2: return launch_pk_warp<2>(a, c1, kk, st);
+      case 4: return launch_pk_warp<4>(a, c1, kk, st);
+      case 6: return launch_pk_warp<6>(a, c1, kk, st);
+      case 8: return launch_pk_warp<8>(a, c1, kk, st);
+      case 16: return launch_pk_warp<16>(a, c1, kk, st);
+      case 32: return launch_pk_warp<32>(a, c1, kk, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (a.d_a / 2) {
     case 2: return launch_pk_half<2>(a, c1, kk, st);
     case 4: return launch_pk_half<4>(a, c1, kk, st);

@@ -42,12 +42,23 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
       for (int r = 0; r < M; ++r) cnt[r] = 0.f;
   }
   const float scr = reset ? 1.f : sc;
-  // read k rows before the write
+  // read k rows before the write: all k loads issued before the first use
+  float rv[32], rc[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (i < k) {
+      const int r = min(max(sir[i], 0), M - 1);  // slot ids are clamped into the state (see rt_scan.cu)
+      rv[i] = mem[(int64_t)r * dh + c];
+      rc[i] = own_cnt ? cnt[r] : 0.f;
+    }
+  }
   float acc = 0.f, accd = 0.f;
-  for (int i = 0; i < k; ++i) {
-    const int r = min(max(sir[i], 0), M - 1);  // slot ids are clamped into the state (see rt_scan.cu)
-    acc = fmaf(wr[i], mem[(int64_t)r * dh + c], acc);
-    if (own_cnt) accd = fmaf(wr[i], cnt[r], accd);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (i < k) {
+      acc = fmaf(wr[i], rv[i], acc);
+      accd = fmaf(wr[i], rc[i], accd);
+    }
   }
   a.num[(int64_t)sh * dh + c] = acc * scr;
   if (own_cnt) a.den[sh] = accd * scr;
@@ -76,11 +87,25 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
     }
   }
   const float vc = v[c];
-  for (int j = 0; j < k; ++j) {
-    const int r = min(max(siw[j], 0), M - 1);
-    const float f = __fdiv_rn(ww[j], ns);
-    mem[(int64_t)r * dh + c] = fmaf(f, vc, mem[(int64_t)r * dh + c]);
-    if (own_cnt) cnt[r] += f;
+  // the k written rows are distinct (a top-k): load them all, then store them all.  With fade 0 every row that
+  // is not cleared above is already zero, so the written value is the write alone.
+  const bool keep_old = lam != 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < k) {
+      const int r = min(max(siw[j], 0), M - 1);
+      rv[j] = keep_old ? mem[(int64_t)r * dh + c] : 0.f;
+      rc[j] = (keep_old && own_cnt) ? cnt[r] : 0.f;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < k) {
+      const int r = min(max(siw[j], 0), M - 1);
+      const float f = __fdiv_rn(ww[j], ns);
+      mem[(int64_t)r * dh + c] = fmaf(f, vc, rv[j]);
+      if (own_cnt) cnt[r] = rc[j] + f;
+    }
   }
   if (own_cnt) {
     a.scale[sh] = ns;

@@ -197,14 +197,46 @@ class OneSdmLM(nn.Module):
                 x = self.sdms[i]._run(x, add_residual=True)[0]
         return self._head(x, "argmax")
 
-    def generate(self, prompt, steps):
+    def decode_graph(self, state):
+        """Capture one decode_step over `state` (all its streams) as a CUDA graph; returns step(ids) -> next ids.
+
+        The graph replays every kernel of the step with no host work in between (the step is otherwise bound by
+        ~100 launches and their Python/ctypes overhead).  Inputs are copied into a static buffer; the returned ids
+        tensor is the graph's static output (overwritten by the next call).  Warm-up runs on a saved copy of the
+        state, which is restored before capture, so building the graph does not advance any stream."""
+        S = state[0]["mem"].shape[0]
+        dev = state[0]["mem"].device
+        ids_in = torch.zeros(S, dtype=torch.int64, device=dev)
+        saved = [{k: v.clone() for k, v in st.items()} for st in state]
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.no_grad():
+            for _ in range(2):
+                self.decode_step(ids_in, state)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        for st, sv in zip(state, saved):
+            for k in st:
+                st[k].copy_(sv[k])
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph), torch.no_grad():
+            ids_out = self.decode_step(ids_in, state)
+
+        def step(ids):
+            ids_in.copy_(ids)
+            graph.replay()
+            return ids_out
+        step.graph = graph
+        return step
+
+    def generate(self, prompt, steps, use_graph=True):
         """Greedy decoding: prompt (S, T) -> (S, steps) generated ids (int64)."""
         state = self.init_decode(prompt.shape[0], prompt.device)
         nxt = self.prefill(prompt, state)
-        out = [nxt]
+        out = [nxt.clone()]
+        step = self.decode_graph(state) if (use_graph and steps > 2) else (lambda ids: self.decode_step(ids, state))
         for _ in range(steps - 1):
-            nxt = self.decode_step(nxt, state)
-            out.append(nxt)
+            nxt = step(nxt)
+            out.append(nxt.clone())
         return torch.stack(out, 1).long()
 
 

@@ -112,6 +112,24 @@ def test_full_d768_L12_T2048_properties(cuda_ok):
     assert abs(loss - want) / abs(want) < 1e-4
 
 
+def test_decode_graph_equals_eager(cuda_ok):
+    """The CUDA-graph decode step replays exactly the eager step: same ids, same carried state, bit for bit."""
+    rng = np.random.default_rng(5)
+    model = full_model(layers=2, seed=2)
+    idx = torch.from_numpy(zipf_ids(rng, (3, 64))).to(DEV)
+    with torch.no_grad():
+        st1, st2 = model.init_decode(3), model.init_decode(3)
+        a, b = model.prefill(idx, st1), model.prefill(idx, st2)
+        step = model.decode_graph(st2)
+        for _ in range(5):
+            a = model.decode_step(a, st1)
+            b = step(b).clone()
+            assert torch.equal(a, b)
+    for i in range(2):
+        for key in st1[i]:
+            assert torch.equal(st1[i][key], st2[i][key]), key
+
+
 def test_full_decode_matches_prefill(cuda_ok):
     """Greedy decode on the carried state = argmax of the chunked forward on the whole prefix."""
     rng = np.random.default_rng(4)
