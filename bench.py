@@ -116,10 +116,20 @@ def time_oracle(P, tokens, reps=1):
     return tokens / best
 
 
+def all_host_threads():
+    """Let the CPU baseline's BLAS use every host core (torchrun sets OMP_NUM_THREADS=1 for its workers)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        return threadpool_limits(limits=os.cpu_count() or 1)
+    except Exception:
+        return None
+
+
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    _limits = all_host_threads()  # noqa: F841 (kept alive for the whole run)
     P = oracle_params(a.layers)
     tokens = 64
     from oracle import sdm_oracle as O
@@ -371,6 +381,7 @@ def run_ours(a):
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        _limits = all_host_threads()  # noqa: F841
         P = oracle_params(a.layers)
         tok = 128
         v = time_oracle(P, tok)
