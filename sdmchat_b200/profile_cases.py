@@ -5,7 +5,7 @@
     python -m sdmchat_b200.profile_cases pk       # product-key addressing of 16384 tokens x 12 heads
     python -m sdmchat_b200.profile_cases decode   # 32 streams x 12 layers FULL decode steps
 
-Each case runs its workload `--reps` times (default 2) after building it, and prints one line of CUDA-event
+Each case runs its workload once untimed and then `--reps` times (default 2), and prints one line of CUDA-event
 timings; nothing else runs on the GPU, so `ncu -k regex:<kernel> -c N` captures exactly the launches of interest.
 """
 import argparse
@@ -27,6 +27,8 @@ def _layer(dev):
 
 
 def _timed(fn, reps):
+    fn()  # first call: module load and attribute setup stay out of the timing
+    torch.cuda.synchronize()
     st = torch.cuda.current_stream()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(st)
