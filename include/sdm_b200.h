@@ -112,10 +112,13 @@ sdm_status sdm_rt_forward(const sdm_rt_params* p, const void* x, int B, int T, c
 /* The chunk loop alone (RunTimeSdm._chunk over all chunks, M:215-241, 255-272) from prepared selections:
  * siw, sir (B, h, T, k) int32; ww, wr (B, h, T, k) float32; V (B*T rows, row stride ldv floats, head hh's dh
  * values at column hh*dh); decay (h).  num (B, T, h, dh), den (B, T, h) float32; mem_out/cnt_out optional.
- * The state stays resident in shared memory for the whole window; no workspace. */
+ * The state stays resident in shared memory for the whole window; the workspace (16-byte aligned,
+ * sdm_rt_scan_workspace_size bytes) holds the per-chunk slot lists. */
+size_t sdm_rt_scan_workspace_size(int B, int T, int heads, int k);
 sdm_status sdm_rt_scan(const int32_t* siw, const float* ww, const int32_t* sir, const float* wr, const float* V,
                        int64_t ldv, const float* decay, const uint8_t* reset, int B, int T, int heads, int n_sub,
-                       int dh, int k, float* num, float* den, float* mem_out, float* cnt_out, void* stream);
+                       int dh, int k, float* num, float* den, float* mem_out, float* cnt_out, void* workspace,
+                       size_t workspace_bytes, void* stream);
 
 /* Carried-state decode (new API; the reference has none, M:249-258): one token per stream through one
  * RunTimeSdm, the state read and then written in place.  x, out (S, d) in p->dtype (one token per stream).

@@ -52,7 +52,9 @@ _SIGS = {
     "sdm_rt_forward_workspace_size": (c_size_t, [ctypes.POINTER(RtParams), c_int, c_int]),
     "sdm_rt_forward": (c_int, [ctypes.POINTER(RtParams), P, c_int, c_int, P, c_int, P, P, P, P, P, P, P, P, P, P, P,
                                P, c_size_t, P]),
-    "sdm_rt_scan": (c_int, [P, P, P, P, P, c_int64, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P]),
+    "sdm_rt_scan_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "sdm_rt_scan": (c_int, [P, P, P, P, P, c_int64, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P,
+                            c_size_t, P]),
     "sdm_rt_decode_workspace_size": (c_size_t, [ctypes.POINTER(RtParams), c_int]),
     "sdm_rt_decode_step": (c_int, [ctypes.POINTER(RtParams), P, c_int, P, c_int, P, P, P, P, P, P, c_size_t, P]),
     "sdm_rt_decode_noalloc_scratch_bytes": (c_size_t, []),

@@ -60,9 +60,11 @@ struct RtWs {
   int32_t *siw, *sir;
   float *ww, *wr, *num, *den;
   void* rbuf;
+  unsigned char* rec;  // chunk records of the scan (forward only)
 };
 
-RtWs carve_rt(Bump& bp, const sdm_rt_params* p, int64_t N, bool own_sel, bool own_num) {
+// B, T: the window shape of a forward (its scan needs chunk records); 0 for a decode step.
+RtWs carve_rt(Bump& bp, const sdm_rt_params* p, int64_t N, bool own_sel, bool own_num, int B = 0, int T = 0) {
   const size_t es = p->dtype == SDM_BF16 ? 2 : 4;
   const int h = p->heads, d = p->d, kk = sel_k(p->k, p->n_sub);
   const int64_t C = 2LL * h * p->d_a + d + h;
@@ -80,6 +82,7 @@ RtWs carve_rt(Bump& bp, const sdm_rt_params* p, int64_t N, bool own_sel, bool ow
     w.den = bp.take<float>(N * h);
   }
   w.rbuf = bp.take<char>(N * d * es * (es == 2 ? 2 : 1));  // bf16: hi | lo halves of the float32 read
+  w.rec = bp.take<unsigned char>(rt_scan_workspace_bytes(B, T, h, kk));
   return w;
 }
 
@@ -134,10 +137,10 @@ sdm_status rt_forward_t(const sdm_rt_params* p, const void* xv, int B, int T_, c
   const bool own_sel = !(siw_o && ww_o && sir_o && wr_o);
   const bool own_num = !(num_o && den_o);
   Bump meas(nullptr);
-  carve_rt(meas, p, N, own_sel, own_num);
+  carve_rt(meas, p, N, own_sel, own_num, B, T_);
   if (ws_bytes < meas.off || (meas.off && !ws)) return SDM_ERR_WORKSPACE;
   Bump bp(ws);
-  RtWs w = carve_rt(bp, p, N, own_sel, own_num);
+  RtWs w = carve_rt(bp, p, N, own_sel, own_num, B, T_);
   int32_t* siw = own_sel ? w.siw : siw_o;
   int32_t* sir = own_sel ? w.sir : sir_o;
   float* ww = own_sel ? w.ww : ww_o;
@@ -172,6 +175,7 @@ sdm_status rt_forward_t(const sdm_rt_params* p, const void* xv, int B, int T_, c
   sa.den = den;
   sa.mem_out = mem_out;
   sa.cnt_out = cnt_out;
+  sa.rec = w.rec;
   SDM_TRY(launch_rt_scan(sa, st));
   OpTag tag_("rt_out");
   T* rbuf = static_cast<T*>(w.rbuf);
@@ -410,7 +414,7 @@ sdm_status sdm_rmsnorm(const void* x, const void* w, int64_t rows, int d, float 
 size_t sdm_rt_forward_workspace_size(const sdm_rt_params* p, int B, int T) {
   if (check_rt(p) != SDM_OK || B < 0 || T < 0) return 0;
   Bump meas(nullptr);
-  carve_rt(meas, p, (int64_t)B * T, true, true);
+  carve_rt(meas, p, (int64_t)B * T, true, true, B, T);
   return meas.off;
 }
 
@@ -429,12 +433,21 @@ sdm_status sdm_rt_forward(const sdm_rt_params* p, const void* x, int B, int T, c
                              num, den, workspace, workspace_bytes, S(stream));
 }
 
+size_t sdm_rt_scan_workspace_size(int B, int T, int heads, int k) {
+  if (B < 0 || T < 0 || heads < 1 || k < 1) return 0;
+  return rt_scan_workspace_bytes(B, T, heads, k);
+}
+
 sdm_status sdm_rt_scan(const int32_t* siw, const float* ww, const int32_t* sir, const float* wr, const float* V,
                        int64_t ldv, const float* decay, const uint8_t* reset, int B, int T, int heads, int n_sub,
-                       int dh, int k, float* num, float* den, float* mem_out, float* cnt_out, void* stream) {
+                       int dh, int k, float* num, float* den, float* mem_out, float* cnt_out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
   if (!siw || !ww || !sir || !wr || !V || !decay || !num || !den) return SDM_ERR_ARG;
   if (B < 0 || T < 0 || heads < 1 || n_sub < 1 || dh < 1 || k < 1 || ldv < (int64_t)heads * dh) return SDM_ERR_SHAPE;
   if (!rt_scan_supported(n_sub * n_sub, dh, k)) return SDM_ERR_SHAPE;
+  const size_t need = rt_scan_workspace_bytes(B, T, heads, k);
+  if (workspace_bytes < need || (need && !workspace)) return SDM_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return SDM_ERR_ARG;
   ScanArgs sa{};
   sa.siw = siw;
   sa.ww = ww;
@@ -454,6 +467,7 @@ sdm_status sdm_rt_scan(const int32_t* siw, const float* ww, const int32_t* sir, 
   sa.den = den;
   sa.mem_out = mem_out;
   sa.cnt_out = cnt_out;
+  sa.rec = static_cast<unsigned char*>(workspace);
   return to_status(launch_rt_scan(sa, S(stream)));
 }
 

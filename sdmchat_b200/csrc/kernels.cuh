@@ -239,7 +239,8 @@ struct PkArgs {
 };
 cudaError_t launch_pk_address(const PkArgs& a, cudaStream_t st);
 
-// The chunked write-then-read scan of RunTimeSdm (track4_onesdm_models.py:215-241, 255-272).
+// The chunked write-then-read scan of RunTimeSdm (track4_onesdm_models.py:215-241, 255-272): a parallel pass per
+// (row, head, chunk) that builds the chunk's slot lists and its intra-chunk reads, then the state scan.
 struct ScanArgs {
   const int32_t* siw; const float* ww; const int32_t* sir; const float* wr;  // (B, h, T, k)
   const float* V; int64_t ldv;                                             // (B*T, ldv), head hh at hh*dh
@@ -248,9 +249,11 @@ struct ScanArgs {
   float* num;   // (B*T, h, dh)
   float* den;   // (B*T, h)
   float* mem_out; float* cnt_out;
+  unsigned char* rec;  // chunk records, rt_scan_workspace_bytes(B, T, h, k) bytes
 };
 cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st);
 bool rt_scan_supported(int M, int dh, int k);
+size_t rt_scan_workspace_bytes(int B, int T, int h, int k);
 
 // Single-token decode on the lazily-decayed state.
 struct DecodeArgs {

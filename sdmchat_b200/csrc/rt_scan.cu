@@ -1,86 +1,435 @@
 // The run-time memory's write-then-read over a whole window (RunTimeSdm.forward's chunk loop,
-// track4_onesdm_models.py:215-241 and :255-272), with the per-head state resident in shared memory.
+// track4_onesdm_models.py:215-241 and :255-272, equal to the token recurrence of forward_sequential, :285-299).
 //
-// One CTA owns one (batch row b, head hh, slice of SCAN_CW value columns) for the WHOLE window: its slice of
-// mem (M x SCAN_CW float32) and the slot counts cnt (M) live in shared memory from the first token to the last,
-// so the state never travels through HBM (the reference's chunked form re-reads and re-writes it every chunk).
-// Columns are independent in the recurrence, so slices of one head never communicate.
+// Per token t of head hh (fade lam, k reads and k writes per token):
+//   read   num[t] = sum_i wr[t,i] * mem_t[sir[t,i]]            den[t] = sum_i wr[t,i] * cnt_t[sir[t,i]]
+//   write  mem_{t+1} = lam * mem_t + sum_j ww[t,j] e_{siw[t,j]} v[t]^T      (cnt likewise with 1 for v)
+// and a BOS reset at t empties the memory before t's read (:229-233).  Over a chunk [c0, c0 + Lc) this unrolls to
+//   num[t] = lam^(t-c0) sum_i wr[t,i] mem_c0[sir[t,i]]                                  (the state part)
+//          + sum_{c0<=s<t} lam^(t-1-s) sum_{i,j: sir[t,i]=siw[s,j]} wr[t,i] ww[s,j] v[s]    (the intra part)
+//   mem_{c0+Lc} = lam^Lc mem_c0 + sum_{s,j} lam^(c0+Lc-1-s) ww[s,j] e_{siw[s,j]} v[s]^T
+// The intra part and the slot lists of the state update depend on the chunk's own selections only, so they are
+// computed for every (row, head, chunk) at once by rt_lists_kernel; only the state part is sequential, and
+// rt_scan_kernel carries the state through the chunks of one (row, head) with all of a chunk's reads (and then
+// all of its writes) in parallel: two or three CTA barriers per 64 tokens.
 //
-// Schedule: micro-steps of up to 16 tokens.  Within a step every token reads in parallel (one warp per token): the
-// exact state at the step start, faded lam^(t-t0), plus the writes of earlier tokens of the same step to the slots
-// it reads, found through a per-step slot list (with 16 tokens x k writes over M slots such collisions are rare).
-// Then the step's writes go straight into the state, one job per distinct written slot, jobs dealt round-robin to
-// the warps; a job walks its slot's list (every write to that slot in this step, newest first).  That is the
-// reference's math (chunked form = token recurrence, :728-755) with a step of 16:
-//   read   num[t] = sum_i wr[t,i] * ( lam^(t-t0) * mem[sir[t,i]] + sum_{t0<=s<t, siw[s,j]=sir[t,i]}
-//                                                                      lam^(t-1-s) * ww[s,j] * v[s] )
-//   write  mem <- lam^U * mem + sum_{s, j} lam^(t0+U-1-s) * ww[s,j] * e_{siw[s,j]} v[s]^T
-// The fade is applied lazily: the state is held as sigma * P and a step multiplies sigma by lam^U instead of
-// touching every row; writes add their term / sigma.  P is renormalised (one pass) when sigma would fall below
-// 2^-40.  Fade 1 keeps sigma = 1; fade 0 (and fades below 2^-100) keep only the last token's writes.  A BOS reset
-// (:229-233) starts a new step and empties the state.
+// rt_lists_kernel, one CTA per (b, hh, chunk):
+//   * sorts the chunk's k * Lc write entries by slot (shared-memory counting sort, then each slot's short run
+//     sorted by entry index, so the order is deterministic);
+//   * intra part: one warp per token; each of its k reads walks its slot's run (entries of earlier tokens of
+//     the chunk, at or after the token's last reset) and adds coef * v[s] row by row; writes num and den;
+//   * the chunk record for the state scan: the distinct written slots ("jobs", ascending) with their entries
+//     (source token and coefficient ww * lam^(Lc-1-s)), restricted to entries after the chunk's last reset;
+//     plus rd_end (tokens before the first reset read the state) and the clear flag.
+//   Fade 0 (and fades below 2^-100): only the previous token's writes are visible, so the intra part compares
+//   token t's reads with token t-1's writes (t-1 may be the last token of the previous chunk) and the state scan
+//   only materialises the final state (the last token's writes).
 //
-// Lanes work in four groups of eight: a group covers one 32-column row with one 16-byte access per lane, so a
-// warp touches four rows per shared-memory instruction (each quarter-warp phase reads one 128-byte row: no bank
-// conflicts).  A token's k reads are taken four at a time and the four partial sums combined with two shuffles;
-// write jobs are taken four at a time, one per group.
-//
-// Warps 0-15 ("workers") read and write, synchronising among themselves with a named barrier between the two
-// phases; warp 16 ("builder") builds the NEXT step's slot lists and job list meanwhile (double-buffered) and
-// meets the workers only at the step boundary.  Chunk inputs (slot ids, weights, values of 128 tokens) are
-// prefetched into registers one chunk ahead.  No atomics touch float data and every sum runs in a fixed order, so
-// results are bit-reproducible.
+// rt_scan_kernel, one CTA per (b, hh, slice of SCAN_CW value columns): the slice of mem (M x SCAN_CW float32) and
+// cnt (M) stay in shared memory for the whole window.  Chunk inputs (record, read selections, value slice, the
+// intra num/den) are copied with cp.async one chunk ahead into a second buffer.  Per chunk: reads (warp per
+// token; lanes in four groups of eight, each group one 32-column row per 16-byte access) add the faded state
+// part to num; then the jobs update the state (a group per slot, entries in record order).  The fade is lazy:
+// the state is sigma * P, a chunk multiplies sigma by lam^Lc and writes add coef / sigma; when sigma would drop
+// below 2^-40 the chunk instead scales P in one pass.  All sums run in a fixed order: results are bit-reproducible.
 #include "kernels.cuh"
 
 namespace sdm {
 
-constexpr int SCAN_CW = 32;                            // value columns per CTA
-constexpr int SCAN_WORKERS = 16;                       // warps that read and write
-constexpr int SCAN_THREADS = (SCAN_WORKERS + 1) * 32;  // + the list-builder warp
-constexpr int SCAN_U = 16;                             // tokens per micro-step (max)
-constexpr int SCAN_MAX_ENTRIES = 2048;                 // L * k of one prefetched chunk
-constexpr int SCAN_MAX_L = 128;
+constexpr int CH_MAX_E = 1024;  // write entries (tokens x k) of one chunk
+constexpr int CH_MAX_L = 64;    // tokens of one chunk
 constexpr int SCAN_MAX_K = 32;
-constexpr int SCAN_EB = SCAN_U * SCAN_MAX_K;           // entries (and jobs) per list buffer
-constexpr int PF_E = SCAN_MAX_ENTRIES / (SCAN_WORKERS * 32);
-constexpr int PF_V = SCAN_MAX_L * SCAN_CW / (SCAN_WORKERS * 32);
+constexpr int LIST_THREADS = 256;
+constexpr int LIST_WARPS = LIST_THREADS / 32;
+constexpr int LIST_MAX_DH = 256;
+constexpr int SCAN_CW = 32;  // value columns per scan CTA
+constexpr int SCAN_WARPS = 16;
+constexpr int SCAN_THREADS = SCAN_WARPS * 32;
+constexpr float kTinyFade = 7.8886e-31f;  // 2^-100: fades below are treated as 0
+constexpr float kRenorm = 9.094947e-13f;  // 2^-40
 
-struct ScanSmem {
-  size_t P, Pc, siw, ww, sir, wr, Vs, rst, head, nxt, ent_s, ent_w, jobs, lastr, total;
+__host__ __device__ inline int chunk_len(int k) {
+  const int L = CH_MAX_E / k;
+  return L > CH_MAX_L ? CH_MAX_L : L;
+}
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+// One chunk's record: header {njobs, nent, rd_end, clear}, jobs (slot << 16 | first entry; jobs[njobs] closes the
+// last run), entry source tokens (u16) and coefficients (f32).
+struct RecLayout {
+  int E;
+  size_t jobs, tau, coef, bytes;
 };
+__host__ __device__ inline RecLayout rec_layout(int k) {
+  RecLayout r;
+  r.E = chunk_len(k) * k;
+  size_t o = 16;
+  r.jobs = o;
+  o += align16((size_t)(r.E + 1) * 4);
+  r.tau = o;
+  o += align16((size_t)r.E * 2);
+  r.coef = o;
+  o += align16((size_t)r.E * 4);
+  r.bytes = o;
+  return r;
+}
 
-__host__ __device__ inline ScanSmem scan_layout(int M, int L, int k) {
-  ScanSmem s;
+__device__ __forceinline__ int fade_mode(float lam) { return lam < kTinyFade ? 0 : (lam == 1.f ? 1 : 2); }
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// rows x w 4-byte elements from src (row stride `stride` elements) to dst (row pitch `pitch` elements), issued by
+// threads [0, nt) as 16-byte copies when everything is 16-byte aligned, else as 4-byte copies.
+__device__ __forceinline__ void copy_rows_async(void* dst, const void* src, int rows, int w, int pitch,
+                                                int64_t stride, int tid, int nt) {
+  const uint32_t* s = static_cast<const uint32_t*>(src);
+  uint32_t* d = static_cast<uint32_t*>(dst);
+  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (w & 3) == 0 && (pitch & 3) == 0 &&
+                   (stride & 3) == 0;
+  if (vec) {
+    const int nv = w >> 2;
+    for (int i = tid; i < rows * nv; i += nt) {
+      const int r = i / nv, q = i - r * nv;
+      cp_async16(d + (int64_t)r * pitch + 4 * q, s + r * stride + 4 * q);
+    }
+  } else {
+    for (int i = tid; i < rows * w; i += nt) {
+      const int r = i / w, q = i - r * w;
+      cp_async4(d + (int64_t)r * pitch + q, s + r * stride + q);
+    }
+  }
+}
+
+// Exclusive prefix sum of in[0, n) into out[0, n) by all LIST_THREADS threads (in and out distinct); returns the
+// total.  Ends with a barrier.
+__device__ int block_exclusive_scan(const int* in, int* out, int n, int* wtot) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (n + LIST_THREADS - 1) / LIST_THREADS;
+  const int s0 = tid * per, s1 = min(n, s0 + per);
+  int sum = 0;
+  for (int i = s0; i < s1; ++i) sum += in[i];
+  int x = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wtot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int t = lane < LIST_WARPS ? wtot[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane < LIST_WARPS) wtot[lane] = t;
+  }
+  __syncthreads();
+  int base = (warp ? wtot[warp - 1] : 0) + x - sum;
+  for (int i = s0; i < s1; ++i) {
+    out[i] = base;
+    base += in[i];
+  }
+  const int total = wtot[LIST_WARPS - 1];
+  __syncthreads();
+  return total;
+}
+
+// ------------------------------------------------------------------------------------------------- list kernel
+struct ListSmem {
+  size_t siw, ww, sir, wr, V, cnt, off, pfx, sorted, rst, wsl, lampow, prev_si, prev_w, prev_v, rec, misc, total;
+};
+__host__ __device__ inline ListSmem list_layout(int M, int k, int dh) {
+  const int L = chunk_len(k), E = L * k;
+  ListSmem s;
   size_t o = 0;
   auto take = [&](size_t bytes) {
-    size_t r = o;
-    o += (bytes + 15) & ~(size_t)15;
+    const size_t r = o;
+    o += align16(bytes);
     return r;
   };
-  s.P = take((size_t)M * SCAN_CW * 4);
-  s.Pc = take((size_t)M * 4);
-  s.siw = take((size_t)L * k * 4);
-  s.ww = take((size_t)L * k * 4);
-  s.sir = take((size_t)L * k * 4);
-  s.wr = take((size_t)L * k * 4);
-  s.Vs = take((size_t)L * SCAN_CW * 4);
+  s.siw = take((size_t)E * 4);
+  s.ww = take((size_t)E * 4);
+  s.sir = take((size_t)E * 4);
+  s.wr = take((size_t)E * 4);
+  s.V = take((size_t)L * dh * 4);
+  s.cnt = take((size_t)M * 4);
+  s.off = take((size_t)M * 4);
+  s.pfx = take((size_t)M * 4);
+  s.sorted = take((size_t)E * 2);
   s.rst = take((size_t)L * 4);
-  s.head = take((size_t)2 * M * 4);
-  s.nxt = take((size_t)2 * SCAN_EB * 4);
-  s.ent_s = take((size_t)2 * SCAN_EB * 4);
-  s.ent_w = take((size_t)2 * SCAN_EB * 4);
-  s.jobs = take((size_t)2 * (SCAN_EB + 1) * 4);
-  s.lastr = take((size_t)2 * SCAN_MAX_K * 4);
+  s.wsl = take((size_t)L * 4);
+  s.lampow = take((size_t)(L + 1) * 4);
+  s.prev_si = take((size_t)SCAN_MAX_K * 4);
+  s.prev_w = take((size_t)SCAN_MAX_K * 4);
+  s.prev_v = take((size_t)dh * 4);
+  s.rec = take(rec_layout(k).bytes);
+  s.misc = take(64);
   s.total = o;
   return s;
 }
 
-static int scan_chunk_len(int k) {
-  int L = SCAN_MAX_ENTRIES / k;
-  return L > SCAN_MAX_L ? SCAN_MAX_L : L;
+template <int K>
+__global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int nch) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int k = K > 0 ? K : a.k;
+  const int M = a.M, dh = a.dh, h = a.h, T = a.T;
+  const int L = chunk_len(k);
+  const ListSmem lay = list_layout(M, k, dh);
+  const RecLayout rl = rec_layout(k);
+  int* siw_s = reinterpret_cast<int*>(smem + lay.siw);
+  float* ww_s = reinterpret_cast<float*>(smem + lay.ww);
+  int* sir_s = reinterpret_cast<int*>(smem + lay.sir);
+  float* wr_s = reinterpret_cast<float*>(smem + lay.wr);
+  float* V_s = reinterpret_cast<float*>(smem + lay.V);
+  int* cnt = reinterpret_cast<int*>(smem + lay.cnt);
+  int* off = reinterpret_cast<int*>(smem + lay.off);
+  int* pfx = reinterpret_cast<int*>(smem + lay.pfx);
+  uint16_t* sorted = reinterpret_cast<uint16_t*>(smem + lay.sorted);
+  int* rst_s = reinterpret_cast<int*>(smem + lay.rst);
+  int* wsl = reinterpret_cast<int*>(smem + lay.wsl);
+  float* lampow = reinterpret_cast<float*>(smem + lay.lampow);
+  int* prev_si = reinterpret_cast<int*>(smem + lay.prev_si);
+  float* prev_w = reinterpret_cast<float*>(smem + lay.prev_w);
+  float* prev_v = reinterpret_cast<float*>(smem + lay.prev_v);
+  unsigned char* rec_s = smem + lay.rec;
+  int* misc = reinterpret_cast<int*>(smem + lay.misc);  // [0..8) scan totals, [8..12) chunk flags
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned FULL = 0xffffffffu;
+  const int c = blockIdx.x % nch;
+  const int bh = blockIdx.x / nch;  // b * h + hh
+  const int hh = bh % h, b = bh / h;
+  const int c0 = c * L, Lc = min(L, T - c0), E = Lc * k;
+  const float lam = a.decay[hh];
+  const int mode = fade_mode(lam);
+  const bool last_chunk = c == nch - 1;
+  const int64_t sel0 = ((int64_t)bh * T + c0) * k;
+  const int64_t tok0 = (int64_t)b * T + c0;
+
+  for (int e = tid; e < E; e += LIST_THREADS) {
+    siw_s[e] = min(max(a.siw[sel0 + e], 0), M - 1);  // ids outside [0, M) never come from the address kernel
+    ww_s[e] = a.ww[sel0 + e];
+    sir_s[e] = min(max(a.sir[sel0 + e], 0), M - 1);
+    wr_s[e] = a.wr[sel0 + e];
+  }
+  for (int i = tid; i < Lc * dh; i += LIST_THREADS) {
+    const int t = i / dh, col = i - t * dh;
+    V_s[i] = a.V[(tok0 + t) * a.ldv + (int64_t)hh * dh + col];
+  }
+  if (tid < L) rst_s[tid] = (a.reset && tid < Lc) ? (int)a.reset[tok0 + tid] : 0;
+  if (tid <= L) lampow[tid] = mode == 0 ? (tid == 0 ? 1.f : 0.f) : powf(lam, (float)tid);
+  if (mode == 0 && c0 > 0) {
+    if (tid < k) {
+      prev_si[tid] = min(max(a.siw[sel0 - k + tid], 0), M - 1);
+      prev_w[tid] = a.ww[sel0 - k + tid];
+    }
+    for (int col = tid; col < dh; col += LIST_THREADS) prev_v[col] = a.V[(tok0 - 1) * a.ldv + (int64_t)hh * dh + col];
+  }
+  __syncthreads();
+  // resets of the chunk (L <= 64): wsl[t] = last reset position <= t (-1: none), rd_end = first reset position
+  if (warp == 0) {
+    const unsigned lo = __ballot_sync(FULL, rst_s[lane] != 0);
+    const unsigned hi = __ballot_sync(FULL, L > 32 && rst_s[min(32 + lane, L - 1)] != 0 && 32 + lane < L);
+    const unsigned long long m = ((unsigned long long)hi << 32) | lo;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int t = lane + 32 * q;
+      if (t < L) {
+        const unsigned long long below = m & ((2ull << t) - 1ull);  // t <= 63: 2ull << 63 wraps to 0, -1 = all ones
+        wsl[t] = below ? 63 - __clzll((long long)below) : -1;
+      }
+    }
+    if (lane == 0) {
+      misc[8] = m ? __ffsll((long long)m) - 1 : Lc;    // rd_end
+      misc[9] = m ? 1 : 0;                              // clear
+      misc[10] = m ? 63 - __clzll((long long)m) : 0;   // first entry token of the state update
+    }
+  }
+  __syncthreads();
+
+  const bool need_sort = mode != 0 || last_chunk;
+  if (need_sort) {
+    for (int r = tid; r < M; r += LIST_THREADS) cnt[r] = 0;
+    __syncthreads();
+    int pos[CH_MAX_E / LIST_THREADS];
+#pragma unroll
+    for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
+      const int e = tid + q * LIST_THREADS;
+      if (e < E) pos[q] = atomicAdd(&cnt[siw_s[e]], 1);
+    }
+    __syncthreads();
+    block_exclusive_scan(cnt, off, M, misc);
+#pragma unroll
+    for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
+      const int e = tid + q * LIST_THREADS;
+      if (e < E) sorted[off[siw_s[e]] + pos[q]] = (uint16_t)e;
+    }
+    __syncthreads();
+    for (int r = tid; r < M; r += LIST_THREADS) {  // each slot's run by entry index (runs are short)
+      const int n = cnt[r], s0 = off[r];
+      for (int i = 1; i < n; ++i) {
+        const uint16_t x = sorted[s0 + i];
+        int j = i - 1;
+        while (j >= 0 && sorted[s0 + j] > x) {
+          sorted[s0 + j + 1] = sorted[s0 + j];
+          --j;
+        }
+        sorted[s0 + j + 1] = x;
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- intra-chunk reads
+  for (int t = warp; t < Lc; t += LIST_WARPS) {
+    float acc[LIST_MAX_DH / 32];
+#pragma unroll
+    for (int q = 0; q < LIST_MAX_DH / 32; ++q) acc[q] = 0.f;
+    float dsum = 0.f;
+    const int ri = lane < k ? sir_s[t * k + lane] : -1;
+    const float wi = lane < k ? wr_s[t * k + lane] : 0.f;
+    if (mode == 0) {
+      // only token t-1's writes are visible (none after a reset at t, none before the first token)
+      const bool has_src = !rst_s[t] && (t > 0 || c0 > 0);
+      if (has_src) {
+        const int* ssi = t > 0 ? siw_s + (t - 1) * k : prev_si;
+        const float* sw = t > 0 ? ww_s + (t - 1) * k : prev_w;
+        const float* sv = t > 0 ? V_s + (t - 1) * dh : prev_v;
+        float m = 0.f;
+        for (int j = 0; j < k; ++j)
+          if (ri == ssi[j]) m += sw[j];
+        dsum = warp_sum(wi * m);
+#pragma unroll
+        for (int q = 0; q < LIST_MAX_DH / 32; ++q) {
+          const int col = lane + 32 * q;
+          if (col < dh) acc[q] = dsum * sv[col];
+        }
+      }
+    } else {
+      const int lo = max(wsl[t], 0);
+      const int st = ri >= 0 ? off[ri] : 0, n = ri >= 0 ? cnt[ri] : 0;
+      unsigned act = __ballot_sync(FULL, n > 0);
+      while (act) {
+        const int i = __ffs(act) - 1;
+        act &= act - 1u;
+        const int sti = __shfl_sync(FULL, st, i), ni = __shfl_sync(FULL, n, i);
+        const float wii = __shfl_sync(FULL, wi, i);
+        for (int x = sti; x < sti + ni; ++x) {
+          const int e = sorted[x];
+          const int s = e / k;
+          if (s >= t) break;
+          if (s < lo) continue;
+          const float cf = wii * ww_s[e] * lampow[t - 1 - s];
+          dsum += cf;
+#pragma unroll
+          for (int q = 0; q < LIST_MAX_DH / 32; ++q) {
+            const int col = lane + 32 * q;
+            if (col < dh) acc[q] = fmaf(cf, V_s[s * dh + col], acc[q]);
+          }
+        }
+      }
+    }
+    const int64_t tok = tok0 + t;
+    float* dst = a.num + (tok * h + hh) * dh;
+#pragma unroll
+    for (int q = 0; q < LIST_MAX_DH / 32; ++q) {
+      const int col = lane + 32 * q;
+      if (col < dh) dst[col] = acc[q];
+    }
+    if (lane == 0) a.den[tok * h + hh] = dsum;
+  }
+  if (!need_sort) return;
+  __syncthreads();
+
+  // ---- the chunk record: entries from token p_first on, grouped by slot
+  const int p_first = mode == 0 ? Lc - 1 : misc[10];
+  for (int r = tid; r < M; r += LIST_THREADS) {
+    const int n = cnt[r], s0 = off[r];
+    int skip = 0;
+    while (skip < n && (int)sorted[s0 + skip] / k < p_first) ++skip;
+    const int vc = n - skip;
+    off[r] = s0 + skip;
+    cnt[r] = vc | (vc > 0 ? 1 << 16 : 0);
+  }
+  __syncthreads();
+  const int tot = block_exclusive_scan(cnt, pfx, M, misc);
+  const int njobs = tot >> 16, nent = tot & 0xFFFF;
+  uint32_t* jobs_s = reinterpret_cast<uint32_t*>(rec_s + rl.jobs);
+  uint16_t* tau_s = reinterpret_cast<uint16_t*>(rec_s + rl.tau);
+  float* coef_s = reinterpret_cast<float*>(rec_s + rl.coef);
+  for (int r = tid; r < M; r += LIST_THREADS) {
+    const int vc = cnt[r] & 0xFFFF;
+    if (vc) {
+      const int jx = pfx[r] >> 16, eo = pfx[r] & 0xFFFF, s0 = off[r];
+      jobs_s[jx] = ((uint32_t)r << 16) | (uint32_t)eo;
+      for (int i = 0; i < vc; ++i) {
+        const int e = sorted[s0 + i];
+        const int s = e / k;
+        tau_s[eo + i] = (uint16_t)s;
+        coef_s[eo + i] = ww_s[e] * lampow[Lc - 1 - s];
+      }
+    }
+  }
+  if (tid == 0) {
+    jobs_s[njobs] = (0xFFFFu << 16) | (uint32_t)nent;
+    int* hdr = reinterpret_cast<int*>(rec_s);
+    hdr[0] = njobs;
+    hdr[1] = nent;
+    hdr[2] = misc[8];
+    hdr[3] = misc[9];
+  }
+  __syncthreads();
+  // copy out the used parts (16-byte stores)
+  unsigned char* rec = a.rec + ((int64_t)bh * nch + c) * rl.bytes;
+  const int n_head = (int)((rl.jobs + align16((size_t)(njobs + 1) * 4)) / 16);
+  const int n_tau = (int)(align16((size_t)nent * 2) / 16), n_coef = (int)(align16((size_t)nent * 4) / 16);
+  for (int i = tid; i < n_head + n_tau + n_coef; i += LIST_THREADS) {
+    size_t o;
+    if (i < n_head) o = (size_t)i * 16;
+    else if (i < n_head + n_tau) o = rl.tau + (size_t)(i - n_head) * 16;
+    else o = rl.coef + (size_t)(i - n_head - n_tau) * 16;
+    *reinterpret_cast<uint4*>(rec + o) = *reinterpret_cast<const uint4*>(rec_s + o);
+  }
 }
 
-__device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(SCAN_WORKERS * 32) : "memory"); }
+// ------------------------------------------------------------------------------------------------- state scan
+struct ScanBuf {
+  size_t rec, sir, wr, V, numi, deni, bytes;
+};
+__host__ __device__ inline ScanBuf scan_buf_layout(int k) {
+  const int L = chunk_len(k), E = L * k;
+  ScanBuf s;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t r = o;
+    o += align16(bytes);
+    return r;
+  };
+  s.rec = take(rec_layout(k).bytes);
+  s.sir = take((size_t)E * 4);
+  s.wr = take((size_t)E * 4);
+  s.V = take((size_t)L * SCAN_CW * 4);
+  s.numi = take((size_t)L * SCAN_CW * 4);
+  s.deni = take((size_t)L * 4);
+  s.bytes = o;
+  return s;
+}
+__host__ __device__ inline size_t scan_smem_bytes(int M, int k) {
+  return align16((size_t)M * SCAN_CW * 4) + align16((size_t)M * 4) + 2 * scan_buf_layout(k).bytes +
+         align16((size_t)(CH_MAX_L + 1) * 4);
+}
 
 __device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
   acc.x = fmaf(w, v.x, acc.x);
@@ -89,392 +438,241 @@ __device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
   acc.w = fmaf(w, v.w, acc.w);
 }
 
-// Inputs of one chunk held in registers between their load and their store to shared memory (worker warps).
-struct Prefetch {
-  int siw[PF_E], sir[PF_E];
-  float ww[PF_E], wr[PF_E], v[PF_V];
-  int rst;
-};
-
-__device__ __forceinline__ void prefetch_load(Prefetch& pf, const ScanArgs& a, int b, int hh, int cs, int c0,
-                                              int Lc) {
-  const int tid = threadIdx.x, k = a.k, nk = Lc * k;
-  const int64_t base = (((int64_t)b * a.h + hh) * a.T + c0) * k;
-#pragma unroll
-  for (int q = 0; q < PF_E; ++q) {
-    const int e = tid + q * SCAN_WORKERS * 32;
-    if (e < nk) {
-      pf.siw[q] = a.siw[base + e];
-      pf.ww[q] = a.ww[base + e];
-      pf.sir[q] = a.sir[base + e];
-      pf.wr[q] = a.wr[base + e];
-    }
+// Issue the cp.async copies of chunk c's inputs into buffer `buf` (all threads).
+__device__ __forceinline__ void scan_issue(const ScanArgs& a, unsigned char* buf, const ScanBuf& sb,
+                                           const RecLayout& rl, int nch, int c, int b, int hh, int cs, int ncols,
+                                           bool want_reads) {
+  const int tid = threadIdx.x, k = a.k, h = a.h, dh = a.dh, T = a.T;
+  const int L = chunk_len(k), c0 = c * L, Lc = min(L, T - c0), E = Lc * k;
+  const int64_t bh = (int64_t)b * h + hh;
+  const int64_t tok0 = (int64_t)b * T + c0;
+  copy_rows_async(buf + sb.rec, a.rec + (bh * nch + c) * rl.bytes, 1, (int)(rl.bytes / 4), 0, 0, tid,
+                  SCAN_THREADS);
+  copy_rows_async(buf + sb.V, a.V + tok0 * a.ldv + (int64_t)hh * dh + cs * SCAN_CW, Lc, ncols, SCAN_CW, a.ldv, tid,
+                  SCAN_THREADS);
+  if (want_reads) {
+    const int64_t sel0 = (bh * T + c0) * k;
+    copy_rows_async(buf + sb.sir, a.sir + sel0, 1, E, 0, 0, tid, SCAN_THREADS);
+    copy_rows_async(buf + sb.wr, a.wr + sel0, 1, E, 0, 0, tid, SCAN_THREADS);
+    copy_rows_async(buf + sb.numi, a.num + (tok0 * h + hh) * dh + cs * SCAN_CW, Lc, ncols, SCAN_CW,
+                    (int64_t)h * dh, tid, SCAN_THREADS);
+    if (cs == 0) copy_rows_async(buf + sb.deni, a.den + tok0 * h + hh, Lc, 1, 1, h, tid, SCAN_THREADS);
   }
-#pragma unroll
-  for (int q = 0; q < PF_V; ++q) {
-    const int i = tid + q * SCAN_WORKERS * 32;
-    const int s = i / SCAN_CW, c = i % SCAN_CW, gc = cs * SCAN_CW + c;
-    pf.v[q] = (s < Lc && gc < a.dh) ? a.V[((int64_t)b * a.T + c0 + s) * a.ldv + (int64_t)hh * a.dh + gc] : 0.f;
-  }
-  pf.rst = (a.reset && tid < Lc) ? (int)a.reset[(int64_t)b * a.T + c0 + tid] : 0;
-}
-
-__device__ __forceinline__ void prefetch_store(const Prefetch& pf, int M, int k, int Lc, int* siw_s, float* ww_s,
-                                               int* sir_s, float* wr_s, float* Vs, int* rst_s) {
-  const int tid = threadIdx.x, nk = Lc * k;
-#pragma unroll
-  for (int q = 0; q < PF_E; ++q) {
-    const int e = tid + q * SCAN_WORKERS * 32;
-    if (e < nk) {
-      // slot ids outside [0, M) (never produced by the address kernel) are clamped so no access leaves the state
-      siw_s[e] = min(max(pf.siw[q], 0), M - 1);
-      ww_s[e] = pf.ww[q];
-      sir_s[e] = min(max(pf.sir[q], 0), M - 1);
-      wr_s[e] = pf.wr[q];
-    }
-  }
-#pragma unroll
-  for (int q = 0; q < PF_V; ++q) {
-    const int i = tid + q * SCAN_WORKERS * 32;
-    if (i < Lc * SCAN_CW) Vs[i] = pf.v[q];
-  }
-  if (tid < Lc) rst_s[tid] = pf.rst;
-}
-
-// Length of the micro-step starting at chunk position t0: at most ustep tokens, within the chunk, and cut before
-// any BOS reset after t0 (a reset always starts a step).
-__device__ __forceinline__ int step_len(int t0, int Lc, int ustep, const int* rst_s, bool has_reset) {
-  int ue = min(ustep, Lc - t0);
-  if (has_reset)
-    for (int q = 1; q < ue; ++q)
-      if (rst_s[t0 + q]) return q;
-  return ue;
-}
-
-// The builder warp's lists for the step [t0, t0 + ue).  Entry e = q*k + j is write j of token t0 + q.
-// head[r] = newest entry writing slot r (-1 if none), nxt[e] = next older entry of the same slot, ent_s / ent_w =
-// chunk position and weight of e, jobs[1..] = the distinct written slots in first-write order, jobs[0] = count.
-// Tokens are inserted 32/k at a time; writes of one group to the same slot are ordered with __match_any_sync.
-template <int K>
-__device__ __forceinline__ void build_lists(int t0, int ue, int k_rt, int M, const int* siw_s, const float* ww_s,
-                                            int* head, int* nxt, int* ent_s, float* ent_w, int* jobs) {
-  const int k = K > 0 ? K : k_rt;
-  const int lane = threadIdx.x & 31;
-  const unsigned FULL = 0xffffffffu;
-  const int G = 32 / k;  // tokens per group
-  const int ql = lane / k, jl = lane % k;
-  int njobs = 0;
-  for (int g0 = 0; g0 < ue; g0 += G) {
-    const int q = g0 + ql;
-    const bool valid = lane < G * k && q < ue;
-    const int e = g0 * k + lane;
-    const int s = t0 + q;
-    const int r = valid ? siw_s[s * k + jl] : M + lane;  // invalid lanes match nothing
-    const unsigned peers = __match_any_sync(FULL, r);
-    const unsigned lower = peers & ((1u << lane) - 1u);
-    const unsigned higher = peers & ~((2u << lane) - 1u);
-    const int old_head = valid ? head[r] : -1;
-    if (valid) {
-      nxt[e] = lower ? g0 * k + (31 - __clz(lower)) : old_head;
-      ent_s[e] = s;
-      ent_w[e] = ww_s[s * k + jl];
-    }
-    __syncwarp();
-    if (valid && higher == 0) head[r] = e;
-    const bool newjob = valid && old_head < 0 && lower == 0;
-    const unsigned jm = __ballot_sync(FULL, newjob);
-    if (newjob) jobs[1 + njobs + __popc(jm & ((1u << lane) - 1u))] = r;
-    njobs += __popc(jm);
-    __syncwarp();
-  }
-  if (lane == 0) jobs[0] = njobs;
-  __syncwarp();
+  cp_async_commit();
 }
 
 template <int K>
-__global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, int L, int n_slices) {
+__global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, int nch, int n_slices) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ float lampow[SCAN_U + 2];
-  const int M = a.M, dh = a.dh, T = a.T, h = a.h;
   const int k = K > 0 ? K : a.k;
-  constexpr int KR = K > 0 ? K : SCAN_MAX_K;  // unroll bound of the per-read loops
-  const ScanSmem lay = scan_layout(M, L, k);
-  float* P = reinterpret_cast<float*>(smem + lay.P);
-  float4* P4 = reinterpret_cast<float4*>(smem + lay.P);
-  float* Pc = reinterpret_cast<float*>(smem + lay.Pc);
-  int* siw_s = reinterpret_cast<int*>(smem + lay.siw);
-  float* ww_s = reinterpret_cast<float*>(smem + lay.ww);
-  int* sir_s = reinterpret_cast<int*>(smem + lay.sir);
-  float* wr_s = reinterpret_cast<float*>(smem + lay.wr);
-  float* Vs = reinterpret_cast<float*>(smem + lay.Vs);
-  const float4* Vs4 = reinterpret_cast<const float4*>(smem + lay.Vs);
-  int* rst_s = reinterpret_cast<int*>(smem + lay.rst);
-  int* head_b = reinterpret_cast<int*>(smem + lay.head);
-  int* nxt_b = reinterpret_cast<int*>(smem + lay.nxt);
-  int* ents_b = reinterpret_cast<int*>(smem + lay.ent_s);
-  float* entw_b = reinterpret_cast<float*>(smem + lay.ent_w);
-  int* jobs_b = reinterpret_cast<int*>(smem + lay.jobs);
-  int* lastr_b = reinterpret_cast<int*>(smem + lay.lastr);
+  constexpr int KR = K > 0 ? K : SCAN_MAX_K;
+  const int M = a.M, dh = a.dh, h = a.h, T = a.T;
+  const int L = chunk_len(k);
+  const RecLayout rl = rec_layout(k);
+  const ScanBuf sb = scan_buf_layout(k);
+  float4* P4 = reinterpret_cast<float4*>(smem);
+  float* P = reinterpret_cast<float*>(smem);
+  float* Pc = reinterpret_cast<float*>(smem + align16((size_t)M * SCAN_CW * 4));
+  unsigned char* bufs = smem + align16((size_t)M * SCAN_CW * 4) + align16((size_t)M * 4);
+  float* lampow = reinterpret_cast<float*>(bufs + 2 * sb.bytes);
 
   const int cs = blockIdx.x % n_slices;
   const int bh = blockIdx.x / n_slices;
-  const int hh = bh % h;
-  const int b = bh / h;
+  const int hh = bh % h, b = bh / h;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int grp = lane >> 3, c4 = lane & 7;  // lane group (row) and its 4-column quad
-  const bool builder = warp == SCAN_WORKERS;
-  const int ncols = min(SCAN_CW, dh - cs * SCAN_CW);  // valid columns of this slice
-  const float lam = a.decay[hh];
-  const bool has_reset = a.reset != nullptr;
+  const int grp = lane >> 3, c4 = lane & 7;
   const unsigned FULL = 0xffffffffu;
-  // fade mode: 0 = only the last token's writes survive (lam = 0 or below 2^-100), 1 = no fade, 2 = lazy scale
-  const int mode = (lam < 7.8886e-31f) ? 0 : (lam == 1.f ? 1 : 2);
-  int ustep = SCAN_U;
-  if (mode == 2 && lam < 0.0131f) ustep = max(1, min(SCAN_U, (int)floorf(100.f / -log2f(lam))));  // lam^U >= 2^-100
+  const int ncols = min(SCAN_CW, dh - cs * SCAN_CW);
+  const float lam = a.decay[hh];
+  const int mode = fade_mode(lam);
+  // fade 0: the intra pass already produced every read; only the final state (the last token's writes) is left
+  if (mode == 0 && !a.mem_out && !a.cnt_out) return;
+  const int c_begin = mode == 0 ? nch - 1 : 0;
+  const bool reads = mode != 0;
 
   for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_THREADS) P4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int i = tid; i < M; i += SCAN_THREADS) {
-    Pc[i] = 0.f;
-    head_b[i] = -1;
-    head_b[M + i] = -1;
+  for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] = 0.f;
+  if (ncols < SCAN_CW) {  // columns past dh stay zero in both buffers (never copied, never stored)
+    for (int i = tid; i < 2 * L * SCAN_CW; i += SCAN_THREADS) {
+      const int bb = i / (L * SCAN_CW), j = i - bb * L * SCAN_CW;
+      reinterpret_cast<float*>(bufs + bb * sb.bytes + sb.V)[j] = 0.f;
+      reinterpret_cast<float*>(bufs + bb * sb.bytes + sb.numi)[j] = 0.f;
+    }
   }
-  if (tid <= SCAN_U) lampow[tid] = mode == 0 ? (tid == 0 ? 1.f : 0.f) : powf(lam, (float)tid);
-  if (tid < 2 * SCAN_MAX_K) lastr_b[tid] = -1;
-  float sigma = 1.f;  // state = sigma * P (mode 2)
-  Prefetch pf;
-  if (!builder) {
-    const int Lc0 = min(L, T);
-    prefetch_load(pf, a, b, hh, cs, 0, Lc0);
-    prefetch_store(pf, M, k, Lc0, siw_s, ww_s, sir_s, wr_s, Vs, rst_s);
-  }
+  if (tid <= L) lampow[tid] = mode == 0 ? (tid == 0 ? 1.f : 0.f) : powf(lam, (float)tid);
   __syncthreads();
-  int buf = 0;   // list buffer of the current step
-  int lbuf = 0;  // survivor-row buffer (fade 0)
+  scan_issue(a, bufs, sb, rl, nch, c_begin, b, hh, cs, ncols, reads);
 
-  for (int c0 = 0; c0 < T; c0 += L) {
-    const int Lc = min(L, T - c0);
-    const int c0n = c0 + L;
-    const int Lcn = c0n < T ? min(L, T - c0n) : 0;
-    if (!builder && Lcn > 0) prefetch_load(pf, a, b, hh, cs, c0n, Lcn);  // lands while this chunk computes
-    if (builder)
-      build_lists<K>(0, step_len(0, Lc, ustep, rst_s, has_reset), k, M, siw_s, ww_s, head_b + buf * M,
-                     nxt_b + buf * SCAN_EB, ents_b + buf * SCAN_EB, entw_b + buf * SCAN_EB,
-                     jobs_b + buf * (SCAN_EB + 1));
+  float sigma = 1.f;  // state = sigma * P
+  int buf = 0;
+  for (int c = c_begin; c < nch; ++c, buf ^= 1) {
+    cp_async_wait_all();
+    __syncthreads();
+    if (c + 1 < nch) scan_issue(a, bufs + (buf ^ 1) * sb.bytes, sb, rl, nch, c + 1, b, hh, cs, ncols, reads);
+    unsigned char* cur = bufs + buf * sb.bytes;
+    const int* hdr = reinterpret_cast<const int*>(cur + sb.rec);
+    const int njobs = hdr[0], rd_end = hdr[2], clear = hdr[3];
+    const int c0 = c * L, Lc = min(L, T - c0);
+    const float4* V4 = reinterpret_cast<const float4*>(cur + sb.V);
+
+    if (reads) {
+      const int* sir_b = reinterpret_cast<const int*>(cur + sb.sir);
+      const float* wr_b = reinterpret_cast<const float*>(cur + sb.wr);
+      const float4* numi4 = reinterpret_cast<const float4*>(cur + sb.numi);
+      const float* deni = reinterpret_cast<const float*>(cur + sb.deni);
+      for (int t = warp; t < rd_end; t += SCAN_WARPS) {
+        int ri = 0;
+        float wi = 0.f, pdi = 0.f;
+        if (lane < k) {
+          ri = min(max(sir_b[t * k + lane], 0), M - 1);
+          wi = wr_b[t * k + lane];
+          pdi = Pc[ri];
+        }
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < (KR + 3) / 4; ++q) {
+          const int ii = 4 * q + grp;
+          const int r = __shfl_sync(FULL, ri, ii & 31);
+          const float w = __shfl_sync(FULL, wi, ii & 31);
+          if (K > 0 ? (ii < K) : (ii < k)) fma4(acc, w, P4[r * (SCAN_CW / 4) + c4]);
+        }
+#pragma unroll
+        for (int o = 8; o < 32; o <<= 1) {
+          acc.x += __shfl_xor_sync(FULL, acc.x, o);
+          acc.y += __shfl_xor_sync(FULL, acc.y, o);
+          acc.z += __shfl_xor_sync(FULL, acc.z, o);
+          acc.w += __shfl_xor_sync(FULL, acc.w, o);
+        }
+        const float dcar = warp_sum(wi * pdi);
+        const float fade = (mode == 2 ? sigma : 1.f) * lampow[t];
+        const int64_t tok = (int64_t)b * T + c0 + t;
+        if (grp == 0) {
+          const float4 ni = numi4[t * (SCAN_CW / 4) + c4];
+          const float o0 = fmaf(fade, acc.x, ni.x), o1 = fmaf(fade, acc.y, ni.y);
+          const float o2 = fmaf(fade, acc.z, ni.z), o3 = fmaf(fade, acc.w, ni.w);
+          float* dst = a.num + (tok * h + hh) * dh + cs * SCAN_CW + 4 * c4;
+          if (4 * c4 + 3 < ncols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
+          } else {
+            if (4 * c4 + 0 < ncols) dst[0] = o0;
+            if (4 * c4 + 1 < ncols) dst[1] = o1;
+            if (4 * c4 + 2 < ncols) dst[2] = o2;
+            if (4 * c4 + 3 < ncols) dst[3] = o3;
+          }
+        }
+        if (cs == 0 && lane == 0) a.den[tok * h + hh] = fmaf(fade, dcar, deni[t]);
+      }
+    }
     __syncthreads();
 
-    for (int t0 = 0; t0 < Lc;) {
-      const int ue = step_len(t0, Lc, ustep, rst_s, has_reset);
-      const int t1 = t0 + ue;
-      if (builder) {
-        // the next step's lists, into the other buffer (its heads were cleared by the previous step's writes)
-        if (t1 < Lc) {
-          const int nb = buf ^ 1;
-          build_lists<K>(t1, step_len(t1, Lc, ustep, rst_s, has_reset), k, M, siw_s, ww_s, head_b + nb * M,
-                         nxt_b + nb * SCAN_EB, ents_b + nb * SCAN_EB, entw_b + nb * SCAN_EB,
-                         jobs_b + nb * (SCAN_EB + 1));
-        }
+    // the state after the chunk: a reset (or fade 0) empties it first, a tiny scale is folded into it
+    float inv = 1.f;
+    bool pass = false;
+    float f = 0.f;
+    if (mode == 0) {
+      sigma = 1.f;  // only the last chunk runs, on the zero state
+    } else if (clear) {
+      pass = true;
+      sigma = 1.f;
+    } else if (mode == 2) {
+      const float s2 = sigma * lampow[Lc];
+      if (s2 < kRenorm) {
+        pass = true;
+        f = s2;
+        sigma = 1.f;
       } else {
-        int* head = head_b + buf * M;
-        const int* nxt = nxt_b + buf * SCAN_EB;
-        const int* ent_s = ents_b + buf * SCAN_EB;
-        const float* ent_w = entw_b + buf * SCAN_EB;
-        const int* jobs = jobs_b + buf * (SCAN_EB + 1);
-        // a BOS empties the memory before its token reads; a tiny scale is folded into the state
-        const bool clear = has_reset && rst_s[t0] != 0;
-        const bool renorm = !clear && mode == 2 && sigma * lampow[ue] < 9.094947e-13f;  // 2^-40
-        if (clear || renorm) {
-          const float f = clear ? 0.f : sigma;
-          for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_WORKERS * 32) {
-            float4 v = P4[i];
-            P4[i] = make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
-          }
-          for (int i = tid; i < M; i += SCAN_WORKERS * 32) Pc[i] *= f;
-          if (clear && tid < SCAN_MAX_K) lastr_b[lbuf * SCAN_MAX_K + tid] = -1;
-          sigma = 1.f;
-          workers_sync();
-        }
-
-        // reads: worker warp w takes token t0 + w; group g handles reads g, g+4, ...
-        if (warp < ue) {
-          const int tau = t0 + warp;
-          const float fade = (mode == 2 ? sigma : 1.f) * lampow[warp];
-          int ri = 0, hd = -1;
-          float wi = 0.f, pdi = 0.f;
-          if (lane < k) {
-            ri = sir_s[tau * k + lane];
-            wi = wr_s[tau * k + lane];
-            pdi = Pc[ri];
-            hd = head[ri];
-          }
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int q = 0; q < (KR + 3) / 4; ++q) {
-            const int ii = 4 * q + grp;
-            const int r = __shfl_sync(FULL, ri, ii & 31);
-            const float w = __shfl_sync(FULL, wi, ii & 31);
-            if (K > 0 ? (ii < K) : (ii < k)) fma4(acc, w, P4[r * (SCAN_CW / 4) + c4]);
-          }
-#pragma unroll
-          for (int o = 8; o < 32; o <<= 1) {
-            acc.x += __shfl_xor_sync(FULL, acc.x, o);
-            acc.y += __shfl_xor_sync(FULL, acc.y, o);
-            acc.z += __shfl_xor_sync(FULL, acc.z, o);
-            acc.w += __shfl_xor_sync(FULL, acc.w, o);
-          }
-          const float dcar = warp_sum(wi * pdi);
-          float4 iv = make_float4(0.f, 0.f, 0.f, 0.f);
-          float idn = 0.f;
-          unsigned mask = __ballot_sync(FULL, hd >= 0);
-          while (mask) {
-            const int i = __ffs(mask) - 1;
-            mask &= mask - 1u;
-            const float w = __shfl_sync(FULL, wi, i);
-            for (int e = __shfl_sync(FULL, hd, i); e >= 0; e = nxt[e]) {
-              const int s = ent_s[e];
-              if (s >= tau) continue;
-              const float coef = w * ent_w[e] * lampow[tau - 1 - s];
-              fma4(iv, coef, Vs4[s * (SCAN_CW / 4) + c4]);
-              idn += coef;
-            }
-          }
-          const int64_t tok = (int64_t)b * T + c0 + tau;
-          if (grp == 0) {
-            float* dst = a.num + (tok * h + hh) * dh + cs * SCAN_CW + 4 * c4;
-            const float o0 = fmaf(fade, acc.x, iv.x), o1 = fmaf(fade, acc.y, iv.y);
-            const float o2 = fmaf(fade, acc.z, iv.z), o3 = fmaf(fade, acc.w, iv.w);
-            if (4 * c4 + 3 < ncols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-              *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
-            } else {
-              if (4 * c4 + 0 < ncols) dst[0] = o0;
-              if (4 * c4 + 1 < ncols) dst[1] = o1;
-              if (4 * c4 + 2 < ncols) dst[2] = o2;
-              if (4 * c4 + 3 < ncols) dst[3] = o3;
-            }
-          }
-          if (cs == 0 && lane == 0) a.den[tok * h + hh] = fmaf(fade, dcar, idn);
-        }
-        workers_sync();
-
-        // writes
-        const int njobs = jobs[0];
-        if (mode != 0) {
-          const float inv = mode == 2 ? 1.f / (sigma * lampow[ue]) : 1.f;
-          for (int jb = 4 * warp; jb < njobs; jb += 4 * SCAN_WORKERS) {
-            const int j = jb + grp;
-            const bool valid = j < njobs;
-            const int r = valid ? jobs[1 + j] : 0;
-            int e = valid ? head[r] : -1;
-            float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
-            float pc = 0.f;
-            if (valid) {
-              p = P4[r * (SCAN_CW / 4) + c4];
-              pc = Pc[r];
-            }
-            while (e >= 0) {
-              const int se = ent_s[e];
-              const float f = ent_w[e] * lampow[t1 - 1 - se] * inv;
-              fma4(p, f, Vs4[se * (SCAN_CW / 4) + c4]);
-              pc += f;
-              e = nxt[e];
-            }
-            __syncwarp();
-            if (valid) {
-              P4[r * (SCAN_CW / 4) + c4] = p;
-              if (c4 == 0) {
-                Pc[r] = pc;
-                head[r] = -1;
-              }
-            }
-          }
-          if (mode == 2) sigma *= lampow[ue];
-        } else {
-          // fade 0: the state becomes the step's last token's writes alone.  Row jj: set new row jj and clear
-          // old survivor row jj unless it is among the new rows (the two sets of rows touched are disjoint).
-          const int sl = t1 - 1;
-          const int* lold = lastr_b + lbuf * SCAN_MAX_K;
-          int* lnew = lastr_b + (lbuf ^ 1) * SCAN_MAX_K;
-          const int rn_l = lane < k ? siw_s[sl * k + lane] : -2;
-          for (int j0 = 4 * warp; j0 < k; j0 += 4 * SCAN_WORKERS) {
-            const int jj = j0 + grp;
-            const bool valid = jj < k;
-            const int rn = valid ? siw_s[sl * k + jj] : 0;
-            const int ro = valid ? lold[jj] : -1;
-            bool old_in_new = false;
-#pragma unroll
-            for (int l = 0; l < SCAN_MAX_K; ++l) {
-              const int rl = __shfl_sync(FULL, rn_l, l);
-              old_in_new |= (rl == ro);
-            }
-            if (valid) {
-              const float wn = ww_s[sl * k + jj];
-              const float4 v = Vs4[sl * (SCAN_CW / 4) + c4];
-              P4[rn * (SCAN_CW / 4) + c4] = make_float4(wn * v.x, wn * v.y, wn * v.z, wn * v.w);
-              if (c4 == 0) {
-                Pc[rn] = wn;
-                lnew[jj] = rn;
-              }
-              if (ro >= 0 && !old_in_new) {
-                P4[ro * (SCAN_CW / 4) + c4] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (c4 == 0) Pc[ro] = 0.f;
-              }
-            }
-          }
-          for (int jb = warp; jb < njobs; jb += SCAN_WORKERS)
-            if (lane == 0) head[jobs[1 + jb]] = -1;
-          lbuf ^= 1;
-        }
+        sigma = s2;
+        inv = 1.f / s2;
       }
-      buf ^= 1;
-      t0 = t1;
+    }
+    if (pass) {
+      for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_THREADS) {
+        const float4 v = P4[i];
+        P4[i] = make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
+      }
+      for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] *= f;
       __syncthreads();
     }
-    // the next chunk's inputs
-    if (Lcn > 0) {
-      if (!builder) prefetch_store(pf, M, k, Lcn, siw_s, ww_s, sir_s, wr_s, Vs, rst_s);
-      __syncthreads();
+    const uint32_t* jobs = reinterpret_cast<const uint32_t*>(cur + sb.rec + rl.jobs);
+    const uint16_t* tau = reinterpret_cast<const uint16_t*>(cur + sb.rec + rl.tau);
+    const float* coef = reinterpret_cast<const float*>(cur + sb.rec + rl.coef);
+    for (int jb = 4 * warp; jb < njobs; jb += 4 * SCAN_WARPS) {
+      const int j = jb + grp;
+      const bool valid = j < njobs;
+      const uint32_t j0 = valid ? jobs[j] : 0u, j1 = valid ? jobs[j + 1] : 0u;
+      const int r = (int)(j0 >> 16), st = (int)(j0 & 0xFFFFu), en = valid ? (int)(j1 & 0xFFFFu) : st;
+      float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
+      float pc = 0.f;
+      if (valid) {
+        p = P4[r * (SCAN_CW / 4) + c4];
+        pc = Pc[r];
+      }
+      for (int e = st; e < en; ++e) {
+        const float fe = coef[e] * inv;
+        fma4(p, fe, V4[tau[e] * (SCAN_CW / 4) + c4]);
+        pc += fe;
+      }
+      if (valid) {
+        P4[r * (SCAN_CW / 4) + c4] = p;
+        if (c4 == 0) Pc[r] = pc;
+      }
     }
   }
+  __syncthreads();
   // the final state, unscaled
-  if (!builder) {
-    const float fs = mode == 2 ? sigma : 1.f;
-    if (a.mem_out) {
-      float* mo = a.mem_out + ((int64_t)b * h + hh) * (int64_t)M * dh;
-      for (int i = tid; i < M * SCAN_CW; i += SCAN_WORKERS * 32) {
-        const int r = i / SCAN_CW, c = i % SCAN_CW, gc = cs * SCAN_CW + c;
-        if (gc < dh) mo[(int64_t)r * dh + gc] = P[i] * fs;
-      }
+  const float fs = sigma;
+  if (a.mem_out) {
+    float* mo = a.mem_out + ((int64_t)b * h + hh) * (int64_t)M * dh;
+    for (int i = tid; i < M * SCAN_CW; i += SCAN_THREADS) {
+      const int r = i / SCAN_CW, cc = i % SCAN_CW, gc = cs * SCAN_CW + cc;
+      if (gc < dh) mo[(int64_t)r * dh + gc] = P[i] * fs;
     }
-    if (a.cnt_out && cs == 0) {
-      float* co = a.cnt_out + ((int64_t)b * h + hh) * (int64_t)M;
-      for (int r = tid; r < M; r += SCAN_WORKERS * 32) co[r] = Pc[r] * fs;
-    }
+  }
+  if (a.cnt_out && cs == 0) {
+    float* co = a.cnt_out + ((int64_t)b * h + hh) * (int64_t)M;
+    for (int r = tid; r < M; r += SCAN_THREADS) co[r] = Pc[r] * fs;
   }
 }
 
 bool rt_scan_supported(int M, int dh, int k) {
-  if (M < 1 || dh < 1 || k < 1 || k > SCAN_MAX_K) return false;
-  return scan_layout(M, scan_chunk_len(k), k).total <= 227 * 1024;
+  if (M < 1 || M > 65535 || dh < 1 || dh > LIST_MAX_DH || k < 1 || k > SCAN_MAX_K) return false;
+  return scan_smem_bytes(M, k) <= 227 * 1024 && list_layout(M, k, dh).total <= 227 * 1024;
+}
+
+size_t rt_scan_workspace_bytes(int B, int T, int h, int k) {
+  if (B <= 0 || T <= 0 || h <= 0 || k <= 0) return 0;
+  const int L = chunk_len(k);
+  return (size_t)B * h * ((T + L - 1) / L) * rec_layout(k).bytes;
 }
 
 template <int K>
-static cudaError_t launch_scan_k(const ScanArgs& a, int L, size_t smem, int n_slices, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(rt_scan_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+static cudaError_t launch_scan_k(const ScanArgs& a, int nch, int n_slices, cudaStream_t st) {
+  const size_t lsm = list_layout(a.M, a.k, a.dh).total;
+  cudaError_t e = cudaFuncSetAttribute(rt_lists_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsm);
   if (e != cudaSuccess) return e;
-  const int64_t grid = (int64_t)a.B * a.h * n_slices;
+  const size_t ssm = scan_smem_bytes(a.M, a.k);
+  e = cudaFuncSetAttribute(rt_scan_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm);
+  if (e != cudaSuccess) return e;
+  {
+    LaunchScope scope_("rt_lists", st);
+    rt_lists_kernel<K><<<(unsigned)((int64_t)a.B * a.h * nch), LIST_THREADS, lsm, st>>>(a, nch);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   LaunchScope scope_("rt_scan", st);
-  rt_scan_kernel<K><<<(unsigned)grid, SCAN_THREADS, smem, st>>>(a, L, n_slices);
+  rt_scan_kernel<K><<<(unsigned)((int64_t)a.B * a.h * n_slices), SCAN_THREADS, ssm, st>>>(a, nch, n_slices);
   return cudaGetLastError();
 }
 
 cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st) {
   if (a.B == 0 || a.T == 0) return cudaSuccess;
-  const int L = scan_chunk_len(a.k);
-  const size_t smem = scan_layout(a.M, L, a.k).total;
+  if (!a.rec || !rt_scan_supported(a.M, a.dh, a.k)) return cudaErrorInvalidValue;
+  const int nch = (a.T + chunk_len(a.k) - 1) / chunk_len(a.k);
   const int n_slices = (a.dh + SCAN_CW - 1) / SCAN_CW;
   switch (a.k) {
-    case 16: return launch_scan_k<16>(a, L, smem, n_slices, st);
-    case 4: return launch_scan_k<4>(a, L, smem, n_slices, st);
-    default: return launch_scan_k<0>(a, L, smem, n_slices, st);
+    case 16: return launch_scan_k<16>(a, nch, n_slices, st);
+    case 4: return launch_scan_k<4>(a, nch, n_slices, st);
+    default: return launch_scan_k<0>(a, nch, n_slices, st);
   }
 }
 
