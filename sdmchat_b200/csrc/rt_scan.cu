@@ -16,22 +16,25 @@
 // rt_lists_kernel, one CTA per (b, hh, chunk):
 //   * sorts the chunk's k * Lc write entries by slot (shared-memory counting sort, then each slot's short run
 //     sorted by entry index, so the order is deterministic);
-//   * intra part: one warp per token; each of its k reads walks its slot's run (entries of earlier tokens of
-//     the chunk, at or after the token's last reset) and adds coef * v[s] row by row; writes num and den;
+//   * intra part: eight lanes per token (each owning dh/8 columns); each of the token's k reads walks its slot's
+//     run (entries of earlier tokens of the chunk, at or after the token's last reset) and adds coef * v[s];
+//     writes num and den;
 //   * the chunk record for the state scan: the distinct written slots ("jobs", ascending) with their entries
-//     (source token and coefficient ww * lam^(Lc-1-s)), restricted to entries after the chunk's last reset;
-//     plus rd_end (tokens before the first reset read the state) and the clear flag.
+//     (source token and coefficient ww * lam^(Lc-1-s)), restricted to entries after the chunk's last reset, and
+//     the chunk header {njobs, nent, rd_end, clear}: tokens before the first reset (rd_end) read the state, a
+//     reset anywhere in the chunk clears it before the writes.
 //   Fade 0 (and fades below 2^-100): only the previous token's writes are visible, so the intra part compares
 //   token t's reads with token t-1's writes (t-1 may be the last token of the previous chunk) and the state scan
 //   only materialises the final state (the last token's writes).
 //
 // rt_scan_kernel, one CTA per (b, hh, slice of SCAN_CW value columns): the slice of mem (M x SCAN_CW float32) and
 // cnt (M) stay in shared memory for the whole window.  Chunk inputs (record, read selections, value slice, the
-// intra num/den) are copied with cp.async one chunk ahead into a second buffer.  Per chunk: reads (warp per
-// token; lanes in four groups of eight, each group one 32-column row per 16-byte access) add the faded state
-// part to num; then the jobs update the state (a group per slot, entries in record order).  The fade is lazy:
-// the state is sigma * P, a chunk multiplies sigma by lam^Lc and writes add coef / sigma; when sigma would drop
-// below 2^-40 the chunk instead scales P in one pass.  All sums run in a fixed order: results are bit-reproducible.
+// intra num/den) are copied with cp.async one chunk ahead into a second buffer; chunk headers are loaded two
+// chunks ahead so every copy has its exact size.  Per chunk: reads (eight lanes per token, one 32-column row per
+// 16-byte access, four read ids per 16-byte load) add the faded state part to num; then the jobs update the state
+// (eight lanes per slot: the sum of the slot's entries, then one read-modify-write).  The fade is lazy: the state
+// is sigma * P, a chunk multiplies sigma by lam^Lc and writes add coef / sigma; when sigma would drop below 2^-40
+// the chunk instead scales P in one pass.  All sums run in a fixed order: results are bit-reproducible.
 #include "kernels.cuh"
 
 namespace sdm {
@@ -54,24 +57,22 @@ __host__ __device__ inline int chunk_len(int k) {
 }
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
 
-// One chunk's record: header {njobs, nent, rd_end, clear}, jobs (slot << 16 | first entry; jobs[njobs] closes the
-// last run), entry source tokens (u16) and coefficients (f32).
+// One chunk's record: jobs (slot << 16 | first entry; jobs[njobs] closes the last run), then entries
+// {source token, coefficient bits}.  Headers {njobs, nent, rd_end, clear} are kept apart, one int4 per chunk.
 struct RecLayout {
   int E;
-  size_t jobs, tau, coef, bytes;
+  size_t ents, bytes;
 };
 __host__ __device__ inline RecLayout rec_layout(int k) {
   RecLayout r;
   r.E = chunk_len(k) * k;
-  size_t o = 16;
-  r.jobs = o;
-  o += align16((size_t)(r.E + 1) * 4);
-  r.tau = o;
-  o += align16((size_t)r.E * 2);
-  r.coef = o;
-  o += align16((size_t)r.E * 4);
-  r.bytes = o;
+  r.ents = align16((size_t)(r.E + 1) * 4);
+  r.bytes = r.ents + align16((size_t)r.E * 8);
   return r;
+}
+__host__ __device__ inline size_t rec_region_bytes(int B, int T, int h, int k) {
+  const int L = chunk_len(k);
+  return (size_t)B * h * ((T + L - 1) / L) * rec_layout(k).bytes;
 }
 
 __device__ __forceinline__ int fade_mode(float lam) { return lam < kTinyFade ? 0 : (lam == 1.f ? 1 : 2); }
@@ -108,6 +109,13 @@ __device__ __forceinline__ void copy_rows_async(void* dst, const void* src, int 
       cp_async4(d + (int64_t)r * pitch + q, s + r * stride + q);
     }
   }
+}
+
+__device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
+  acc.x = fmaf(w, v.x, acc.x);
+  acc.y = fmaf(w, v.y, acc.y);
+  acc.z = fmaf(w, v.z, acc.z);
+  acc.w = fmaf(w, v.w, acc.w);
 }
 
 // Exclusive prefix sum of in[0, n) into out[0, n) by all LIST_THREADS threads (in and out distinct); returns the
@@ -148,7 +156,7 @@ __device__ int block_exclusive_scan(const int* in, int* out, int n, int* wtot) {
 
 // ------------------------------------------------------------------------------------------------- list kernel
 struct ListSmem {
-  size_t siw, ww, sir, wr, V, cnt, off, pfx, sorted, rst, wsl, lampow, prev_si, prev_w, prev_v, rec, misc, total;
+  size_t siw, ww, sir, wr, V, cnt, off, pfx, sorted, ent, rst, wsl, lampow, prev_si, prev_w, prev_v, rec, misc, total;
 };
 __host__ __device__ inline ListSmem list_layout(int M, int k, int dh) {
   const int L = chunk_len(k), E = L * k;
@@ -166,25 +174,30 @@ __host__ __device__ inline ListSmem list_layout(int M, int k, int dh) {
   s.V = take((size_t)L * dh * 4);
   s.cnt = take((size_t)M * 4);
   s.off = take((size_t)M * 4);
-  s.pfx = take((size_t)M * 4);
   s.sorted = take((size_t)E * 2);
+  s.ent = take((size_t)E * 8);
   s.rst = take((size_t)L * 4);
   s.wsl = take((size_t)L * 4);
   s.lampow = take((size_t)(L + 1) * 4);
   s.prev_si = take((size_t)SCAN_MAX_K * 4);
   s.prev_w = take((size_t)SCAN_MAX_K * 4);
   s.prev_v = take((size_t)dh * 4);
-  s.rec = take(rec_layout(k).bytes);
   s.misc = take(64);
+  // the record phase runs after the intra reads: its prefix sums reuse the write ids (dead once the entries are
+  // built) and its staging reuses the values when they are large enough
+  s.pfx = (size_t)E * 4 >= (size_t)M * 4 ? s.siw : take((size_t)M * 4);
+  s.rec = (size_t)L * dh * 4 >= rec_layout(k).bytes ? s.V : take(rec_layout(k).bytes);
   s.total = o;
   return s;
 }
 
-template <int K>
+// K: compile-time k (0: runtime).  DH: compile-time head width, a multiple of 32 (0: runtime, any width).
+template <int K, int DH>
 __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int nch) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int k = K > 0 ? K : a.k;
-  const int M = a.M, dh = a.dh, h = a.h, T = a.T;
+  const int dh = DH > 0 ? DH : a.dh;
+  const int M = a.M, h = a.h, T = a.T;
   const int L = chunk_len(k);
   const ListSmem lay = list_layout(M, k, dh);
   const RecLayout rl = rec_layout(k);
@@ -197,6 +210,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   int* off = reinterpret_cast<int*>(smem + lay.off);
   int* pfx = reinterpret_cast<int*>(smem + lay.pfx);
   uint16_t* sorted = reinterpret_cast<uint16_t*>(smem + lay.sorted);
+  int2* ent = reinterpret_cast<int2*>(smem + lay.ent);  // sorted entries: {source token, ww bits}
   int* rst_s = reinterpret_cast<int*>(smem + lay.rst);
   int* wsl = reinterpret_cast<int*>(smem + lay.wsl);
   float* lampow = reinterpret_cast<float*>(smem + lay.lampow);
@@ -204,7 +218,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   float* prev_w = reinterpret_cast<float*>(smem + lay.prev_w);
   float* prev_v = reinterpret_cast<float*>(smem + lay.prev_v);
   unsigned char* rec_s = smem + lay.rec;
-  int* misc = reinterpret_cast<int*>(smem + lay.misc);  // [0..8) scan totals, [8..12) chunk flags
+  int* misc = reinterpret_cast<int*>(smem + lay.misc);  // [0..8) scan totals, [8..11) chunk flags
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const unsigned FULL = 0xffffffffu;
@@ -217,6 +231,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   const bool last_chunk = c == nch - 1;
   const int64_t sel0 = ((int64_t)bh * T + c0) * k;
   const int64_t tok0 = (int64_t)b * T + c0;
+  const float* Vh = a.V + (int64_t)hh * dh;
 
   for (int e = tid; e < E; e += LIST_THREADS) {
     siw_s[e] = min(max(a.siw[sel0 + e], 0), M - 1);  // ids outside [0, M) never come from the address kernel
@@ -224,9 +239,17 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
     sir_s[e] = min(max(a.sir[sel0 + e], 0), M - 1);
     wr_s[e] = a.wr[sel0 + e];
   }
-  for (int i = tid; i < Lc * dh; i += LIST_THREADS) {
-    const int t = i / dh, col = i - t * dh;
-    V_s[i] = a.V[(tok0 + t) * a.ldv + (int64_t)hh * dh + col];
+  if (DH > 0 && (a.ldv & 3) == 0 && (reinterpret_cast<uintptr_t>(Vh) & 15) == 0) {
+    float4* V4 = reinterpret_cast<float4*>(V_s);
+    for (int i = tid; i < Lc * (dh / 4); i += LIST_THREADS) {
+      const int t = i / (dh / 4), q = i - t * (dh / 4);
+      V4[i] = *reinterpret_cast<const float4*>(Vh + (tok0 + t) * a.ldv + 4 * q);
+    }
+  } else {
+    for (int i = tid; i < Lc * dh; i += LIST_THREADS) {
+      const int t = i / dh, col = i - t * dh;
+      V_s[i] = Vh[(tok0 + t) * a.ldv + col];
+    }
   }
   if (tid < L) rst_s[tid] = (a.reset && tid < Lc) ? (int)a.reset[tok0 + tid] : 0;
   if (tid <= L) lampow[tid] = mode == 0 ? (tid == 0 ? 1.f : 0.f) : powf(lam, (float)tid);
@@ -235,19 +258,19 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
       prev_si[tid] = min(max(a.siw[sel0 - k + tid], 0), M - 1);
       prev_w[tid] = a.ww[sel0 - k + tid];
     }
-    for (int col = tid; col < dh; col += LIST_THREADS) prev_v[col] = a.V[(tok0 - 1) * a.ldv + (int64_t)hh * dh + col];
+    for (int col = tid; col < dh; col += LIST_THREADS) prev_v[col] = Vh[(tok0 - 1) * a.ldv + col];
   }
   __syncthreads();
-  // resets of the chunk (L <= 64): wsl[t] = last reset position <= t (-1: none), rd_end = first reset position
+  // resets of the chunk (32 <= L <= 64): wsl[t] = last reset position <= t (-1: none), rd_end = first reset
   if (warp == 0) {
     const unsigned lo = __ballot_sync(FULL, rst_s[lane] != 0);
-    const unsigned hi = __ballot_sync(FULL, L > 32 && rst_s[min(32 + lane, L - 1)] != 0 && 32 + lane < L);
+    const unsigned hi = __ballot_sync(FULL, 32 + lane < L && rst_s[min(32 + lane, L - 1)] != 0);
     const unsigned long long m = ((unsigned long long)hi << 32) | lo;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int t = lane + 32 * q;
       if (t < L) {
-        const unsigned long long below = m & ((2ull << t) - 1ull);  // t <= 63: 2ull << 63 wraps to 0, -1 = all ones
+        const unsigned long long below = m & ((2ull << t) - 1ull);  // t = 63: 2ull << 63 wraps to 0, -1 = all ones
         wsl[t] = below ? 63 - __clzll((long long)below) : -1;
       }
     }
@@ -290,34 +313,89 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
       }
     }
     __syncthreads();
+    for (int x = tid; x < E; x += LIST_THREADS) {
+      const int e = sorted[x];
+      ent[x] = make_int2(e / k, __float_as_int(ww_s[e]));
+    }
+    __syncthreads();
   }
 
   // ---- intra-chunk reads
-  for (int t = warp; t < Lc; t += LIST_WARPS) {
-    float acc[LIST_MAX_DH / 32];
-#pragma unroll
-    for (int q = 0; q < LIST_MAX_DH / 32; ++q) acc[q] = 0.f;
-    float dsum = 0.f;
-    const int ri = lane < k ? sir_s[t * k + lane] : -1;
-    const float wi = lane < k ? wr_s[t * k + lane] : 0.f;
-    if (mode == 0) {
-      // only token t-1's writes are visible (none after a reset at t, none before the first token)
+  if (mode == 0) {
+    // only token t-1's writes are visible (none after a reset at t, none before the first token): warp per token
+    for (int t = warp; t < Lc; t += LIST_WARPS) {
+      const int ri = lane < k ? sir_s[t * k + lane] : -1;
+      const float wi = lane < k ? wr_s[t * k + lane] : 0.f;
       const bool has_src = !rst_s[t] && (t > 0 || c0 > 0);
+      const float* sv = t > 0 ? V_s + (t - 1) * dh : prev_v;
+      float dsum = 0.f;
       if (has_src) {
         const int* ssi = t > 0 ? siw_s + (t - 1) * k : prev_si;
         const float* sw = t > 0 ? ww_s + (t - 1) * k : prev_w;
-        const float* sv = t > 0 ? V_s + (t - 1) * dh : prev_v;
         float m = 0.f;
         for (int j = 0; j < k; ++j)
           if (ri == ssi[j]) m += sw[j];
         dsum = warp_sum(wi * m);
+      }
+      const int64_t tok = tok0 + t;
+      float* dst = a.num + (tok * h + hh) * dh;
+      for (int col = lane; col < dh; col += 32) dst[col] = has_src ? dsum * sv[col] : 0.f;
+      if (lane == 0) a.den[tok * h + hh] = dsum;
+    }
+  } else if constexpr (DH > 0) {
+    // eight lanes per token: lane gl owns the float4 columns gl, gl + 8, ... of the head
+    constexpr int NQ = DH / 32;
+    const int grp = lane >> 3, gl = lane & 7;
+    const float4* V4 = reinterpret_cast<const float4*>(V_s);
+    const bool vst = (reinterpret_cast<uintptr_t>(a.num) & 15) == 0;
+    for (int tb = warp * 4; tb < Lc; tb += LIST_WARPS * 4) {
+      const int t = tb + grp;
+      if (t >= Lc) continue;
+      float4 acc[NQ];
 #pragma unroll
-        for (int q = 0; q < LIST_MAX_DH / 32; ++q) {
-          const int col = lane + 32 * q;
-          if (col < dh) acc[q] = dsum * sv[col];
+      for (int q = 0; q < NQ; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      float dsum = 0.f;
+      const int lo = max(wsl[t], 0);
+      for (int i = 0; i < k; ++i) {
+        const int r = sir_s[t * k + i];
+        const float w = wr_s[t * k + i];
+        const int st = off[r], en = st + cnt[r];
+        for (int x = st; x < en; ++x) {
+          const int2 q2 = ent[x];
+          const int s = q2.x;
+          if (s >= t) break;
+          if (s < lo) continue;
+          const float cf = w * __int_as_float(q2.y) * lampow[t - 1 - s];
+          dsum += cf;
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) fma4(acc[q], cf, V4[s * (DH / 4) + gl + 8 * q]);
         }
       }
-    } else {
+      const int64_t tok = tok0 + t;
+      float* dst = a.num + (tok * h + hh) * DH;
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        if (vst) {
+          reinterpret_cast<float4*>(dst)[gl + 8 * q] = acc[q];
+        } else {
+          float* d1 = dst + 4 * (gl + 8 * q);
+          d1[0] = acc[q].x;
+          d1[1] = acc[q].y;
+          d1[2] = acc[q].z;
+          d1[3] = acc[q].w;
+        }
+      }
+      if (gl == 0) a.den[tok * h + hh] = dsum;
+    }
+  } else {
+    // any head width: warp per token, lanes over columns
+    for (int t = warp; t < Lc; t += LIST_WARPS) {
+      float acc[LIST_MAX_DH / 32];
+#pragma unroll
+      for (int q = 0; q < LIST_MAX_DH / 32; ++q) acc[q] = 0.f;
+      float dsum = 0.f;
+      const int ri = lane < k ? sir_s[t * k + lane] : -1;
+      const float wi = lane < k ? wr_s[t * k + lane] : 0.f;
       const int lo = max(wsl[t], 0);
       const int st = ri >= 0 ? off[ri] : 0, n = ri >= 0 ? cnt[ri] : 0;
       unsigned act = __ballot_sync(FULL, n > 0);
@@ -327,11 +405,11 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
         const int sti = __shfl_sync(FULL, st, i), ni = __shfl_sync(FULL, n, i);
         const float wii = __shfl_sync(FULL, wi, i);
         for (int x = sti; x < sti + ni; ++x) {
-          const int e = sorted[x];
-          const int s = e / k;
+          const int2 q2 = ent[x];
+          const int s = q2.x;
           if (s >= t) break;
           if (s < lo) continue;
-          const float cf = wii * ww_s[e] * lampow[t - 1 - s];
+          const float cf = wii * __int_as_float(q2.y) * lampow[t - 1 - s];
           dsum += cf;
 #pragma unroll
           for (int q = 0; q < LIST_MAX_DH / 32; ++q) {
@@ -340,15 +418,15 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
           }
         }
       }
-    }
-    const int64_t tok = tok0 + t;
-    float* dst = a.num + (tok * h + hh) * dh;
+      const int64_t tok = tok0 + t;
+      float* dst = a.num + (tok * h + hh) * dh;
 #pragma unroll
-    for (int q = 0; q < LIST_MAX_DH / 32; ++q) {
-      const int col = lane + 32 * q;
-      if (col < dh) dst[col] = acc[q];
+      for (int q = 0; q < LIST_MAX_DH / 32; ++q) {
+        const int col = lane + 32 * q;
+        if (col < dh) dst[col] = acc[q];
+      }
+      if (lane == 0) a.den[tok * h + hh] = dsum;
     }
-    if (lane == 0) a.den[tok * h + hh] = dsum;
   }
   if (!need_sort) return;
   __syncthreads();
@@ -358,7 +436,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   for (int r = tid; r < M; r += LIST_THREADS) {
     const int n = cnt[r], s0 = off[r];
     int skip = 0;
-    while (skip < n && (int)sorted[s0 + skip] / k < p_first) ++skip;
+    while (skip < n && ent[s0 + skip].x < p_first) ++skip;
     const int vc = n - skip;
     off[r] = s0 + skip;
     cnt[r] = vc | (vc > 0 ? 1 << 16 : 0);
@@ -366,40 +444,31 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   __syncthreads();
   const int tot = block_exclusive_scan(cnt, pfx, M, misc);
   const int njobs = tot >> 16, nent = tot & 0xFFFF;
-  uint32_t* jobs_s = reinterpret_cast<uint32_t*>(rec_s + rl.jobs);
-  uint16_t* tau_s = reinterpret_cast<uint16_t*>(rec_s + rl.tau);
-  float* coef_s = reinterpret_cast<float*>(rec_s + rl.coef);
+  uint32_t* jobs_s = reinterpret_cast<uint32_t*>(rec_s);
+  int2* ents_s = reinterpret_cast<int2*>(rec_s + rl.ents);
   for (int r = tid; r < M; r += LIST_THREADS) {
     const int vc = cnt[r] & 0xFFFF;
     if (vc) {
       const int jx = pfx[r] >> 16, eo = pfx[r] & 0xFFFF, s0 = off[r];
       jobs_s[jx] = ((uint32_t)r << 16) | (uint32_t)eo;
       for (int i = 0; i < vc; ++i) {
-        const int e = sorted[s0 + i];
-        const int s = e / k;
-        tau_s[eo + i] = (uint16_t)s;
-        coef_s[eo + i] = ww_s[e] * lampow[Lc - 1 - s];
+        const int2 q2 = ent[s0 + i];
+        ents_s[eo + i] = make_int2(q2.x, __float_as_int(__int_as_float(q2.y) * lampow[Lc - 1 - q2.x]));
       }
     }
   }
   if (tid == 0) {
     jobs_s[njobs] = (0xFFFFu << 16) | (uint32_t)nent;
-    int* hdr = reinterpret_cast<int*>(rec_s);
-    hdr[0] = njobs;
-    hdr[1] = nent;
-    hdr[2] = misc[8];
-    hdr[3] = misc[9];
+    reinterpret_cast<int4*>(a.rec + rec_region_bytes(a.B, T, h, k))[(int64_t)bh * nch + c] =
+        make_int4(njobs, nent, misc[8], misc[9]);
   }
   __syncthreads();
   // copy out the used parts (16-byte stores)
   unsigned char* rec = a.rec + ((int64_t)bh * nch + c) * rl.bytes;
-  const int n_head = (int)((rl.jobs + align16((size_t)(njobs + 1) * 4)) / 16);
-  const int n_tau = (int)(align16((size_t)nent * 2) / 16), n_coef = (int)(align16((size_t)nent * 4) / 16);
-  for (int i = tid; i < n_head + n_tau + n_coef; i += LIST_THREADS) {
-    size_t o;
-    if (i < n_head) o = (size_t)i * 16;
-    else if (i < n_head + n_tau) o = rl.tau + (size_t)(i - n_head) * 16;
-    else o = rl.coef + (size_t)(i - n_head - n_tau) * 16;
+  const int n_jobs16 = (int)(align16((size_t)(njobs + 1) * 4) / 16);
+  const int n_ent16 = (int)(align16((size_t)nent * 8) / 16);
+  for (int i = tid; i < n_jobs16 + n_ent16; i += LIST_THREADS) {
+    const size_t o = i < n_jobs16 ? (size_t)i * 16 : rl.ents + (size_t)(i - n_jobs16) * 16;
     *reinterpret_cast<uint4*>(rec + o) = *reinterpret_cast<const uint4*>(rec_s + o);
   }
 }
@@ -431,33 +500,30 @@ __host__ __device__ inline size_t scan_smem_bytes(int M, int k) {
          align16((size_t)(CH_MAX_L + 1) * 4);
 }
 
-__device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
-  acc.x = fmaf(w, v.x, acc.x);
-  acc.y = fmaf(w, v.y, acc.y);
-  acc.z = fmaf(w, v.z, acc.z);
-  acc.w = fmaf(w, v.w, acc.w);
-}
-
-// Issue the cp.async copies of chunk c's inputs into buffer `buf` (all threads).
+// Issue the cp.async copies of chunk c's inputs (header hd) into buffer `buf` (all threads).
 __device__ __forceinline__ void scan_issue(const ScanArgs& a, unsigned char* buf, const ScanBuf& sb,
-                                           const RecLayout& rl, int nch, int c, int b, int hh, int cs, int ncols,
-                                           bool want_reads) {
+                                           const RecLayout& rl, int nch, int c, int4 hd, int b, int hh, int cs,
+                                           int ncols, bool want_reads) {
   const int tid = threadIdx.x, k = a.k, h = a.h, dh = a.dh, T = a.T;
   const int L = chunk_len(k), c0 = c * L, Lc = min(L, T - c0), E = Lc * k;
   const int64_t bh = (int64_t)b * h + hh;
   const int64_t tok0 = (int64_t)b * T + c0;
-  copy_rows_async(buf + sb.rec, a.rec + (bh * nch + c) * rl.bytes, 1, (int)(rl.bytes / 4), 0, 0, tid,
+  const unsigned char* rec = a.rec + (bh * nch + c) * rl.bytes;
+  copy_rows_async(buf + sb.rec, rec, 1, (int)(align16((size_t)(hd.x + 1) * 4) / 4), 0, 0, tid, SCAN_THREADS);
+  copy_rows_async(buf + sb.rec + rl.ents, rec + rl.ents, 1, (int)(align16((size_t)hd.y * 8) / 4), 0, 0, tid,
                   SCAN_THREADS);
   copy_rows_async(buf + sb.V, a.V + tok0 * a.ldv + (int64_t)hh * dh + cs * SCAN_CW, Lc, ncols, SCAN_CW, a.ldv, tid,
                   SCAN_THREADS);
-  if (want_reads) {
+  if (want_reads && hd.z > 0) {
     const int64_t sel0 = (bh * T + c0) * k;
-    copy_rows_async(buf + sb.sir, a.sir + sel0, 1, E, 0, 0, tid, SCAN_THREADS);
-    copy_rows_async(buf + sb.wr, a.wr + sel0, 1, E, 0, 0, tid, SCAN_THREADS);
-    copy_rows_async(buf + sb.numi, a.num + (tok0 * h + hh) * dh + cs * SCAN_CW, Lc, ncols, SCAN_CW,
+    const int nr = hd.z;  // tokens before the first reset read the state
+    copy_rows_async(buf + sb.sir, a.sir + sel0, 1, nr * k, 0, 0, tid, SCAN_THREADS);
+    copy_rows_async(buf + sb.wr, a.wr + sel0, 1, nr * k, 0, 0, tid, SCAN_THREADS);
+    copy_rows_async(buf + sb.numi, a.num + (tok0 * h + hh) * dh + cs * SCAN_CW, nr, ncols, SCAN_CW,
                     (int64_t)h * dh, tid, SCAN_THREADS);
-    if (cs == 0) copy_rows_async(buf + sb.deni, a.den + tok0 * h + hh, Lc, 1, 1, h, tid, SCAN_THREADS);
+    if (cs == 0) copy_rows_async(buf + sb.deni, a.den + tok0 * h + hh, nr, 1, 1, h, tid, SCAN_THREADS);
   }
+  (void)E;
   cp_async_commit();
 }
 
@@ -466,6 +532,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
   extern __shared__ __align__(16) unsigned char smem[];
   const int k = K > 0 ? K : a.k;
   constexpr int KR = K > 0 ? K : SCAN_MAX_K;
+  constexpr bool kVecReads = K > 0 && K % 4 == 0;
   const int M = a.M, dh = a.dh, h = a.h, T = a.T;
   const int L = chunk_len(k);
   const RecLayout rl = rec_layout(k);
@@ -489,6 +556,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
   if (mode == 0 && !a.mem_out && !a.cnt_out) return;
   const int c_begin = mode == 0 ? nch - 1 : 0;
   const bool reads = mode != 0;
+  const int4* hdrs = reinterpret_cast<const int4*>(a.rec + rec_region_bytes(a.B, T, h, k)) + (int64_t)bh * nch;
 
   for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_THREADS) P4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] = 0.f;
@@ -500,18 +568,20 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
     }
   }
   if (tid <= L) lampow[tid] = mode == 0 ? (tid == 0 ? 1.f : 0.f) : powf(lam, (float)tid);
+  int4 hd = hdrs[c_begin];                                              // this chunk's header
+  int4 hd1 = c_begin + 1 < nch ? hdrs[c_begin + 1] : make_int4(0, 0, 0, 0);  // the next one's
   __syncthreads();
-  scan_issue(a, bufs, sb, rl, nch, c_begin, b, hh, cs, ncols, reads);
+  scan_issue(a, bufs, sb, rl, nch, c_begin, hd, b, hh, cs, ncols, reads);
 
   float sigma = 1.f;  // state = sigma * P
   int buf = 0;
   for (int c = c_begin; c < nch; ++c, buf ^= 1) {
     cp_async_wait_all();
     __syncthreads();
-    if (c + 1 < nch) scan_issue(a, bufs + (buf ^ 1) * sb.bytes, sb, rl, nch, c + 1, b, hh, cs, ncols, reads);
+    if (c + 1 < nch) scan_issue(a, bufs + (buf ^ 1) * sb.bytes, sb, rl, nch, c + 1, hd1, b, hh, cs, ncols, reads);
+    const int4 hd2 = c + 2 < nch ? hdrs[c + 2] : make_int4(0, 0, 0, 0);  // used two iterations on
     unsigned char* cur = bufs + buf * sb.bytes;
-    const int* hdr = reinterpret_cast<const int*>(cur + sb.rec);
-    const int njobs = hdr[0], rd_end = hdr[2], clear = hdr[3];
+    const int njobs = hd.x, rd_end = hd.z, clear = hd.w;
     const int c0 = c * L, Lc = min(L, T - c0);
     const float4* V4 = reinterpret_cast<const float4*>(cur + sb.V);
 
@@ -520,33 +590,33 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
       const float* wr_b = reinterpret_cast<const float*>(cur + sb.wr);
       const float4* numi4 = reinterpret_cast<const float4*>(cur + sb.numi);
       const float* deni = reinterpret_cast<const float*>(cur + sb.deni);
-      for (int t = warp; t < rd_end; t += SCAN_WARPS) {
-        int ri = 0;
-        float wi = 0.f, pdi = 0.f;
-        if (lane < k) {
-          ri = min(max(sir_b[t * k + lane], 0), M - 1);
-          wi = wr_b[t * k + lane];
-          pdi = Pc[ri];
-        }
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float sg = mode == 2 ? sigma : 1.f;
+      if constexpr (kVecReads) {
+        // eight lanes per token, four tokens per warp; read ids and weights four at a time
+        for (int tb = 4 * warp; tb < rd_end; tb += 4 * SCAN_WARPS) {
+          const int t = tb + grp;
+          if (t >= rd_end) continue;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          float dc = 0.f;
+          const int4* s4 = reinterpret_cast<const int4*>(sir_b + t * K);
+          const float4* w4 = reinterpret_cast<const float4*>(wr_b + t * K);
 #pragma unroll
-        for (int q = 0; q < (KR + 3) / 4; ++q) {
-          const int ii = 4 * q + grp;
-          const int r = __shfl_sync(FULL, ri, ii & 31);
-          const float w = __shfl_sync(FULL, wi, ii & 31);
-          if (K > 0 ? (ii < K) : (ii < k)) fma4(acc, w, P4[r * (SCAN_CW / 4) + c4]);
-        }
-#pragma unroll
-        for (int o = 8; o < 32; o <<= 1) {
-          acc.x += __shfl_xor_sync(FULL, acc.x, o);
-          acc.y += __shfl_xor_sync(FULL, acc.y, o);
-          acc.z += __shfl_xor_sync(FULL, acc.z, o);
-          acc.w += __shfl_xor_sync(FULL, acc.w, o);
-        }
-        const float dcar = warp_sum(wi * pdi);
-        const float fade = (mode == 2 ? sigma : 1.f) * lampow[t];
-        const int64_t tok = (int64_t)b * T + c0 + t;
-        if (grp == 0) {
+          for (int q = 0; q < K / 4; ++q) {
+            const int4 rr = s4[q];
+            const float4 wv = w4[q];
+            const int r0 = min(max(rr.x, 0), M - 1), r1 = min(max(rr.y, 0), M - 1);
+            const int r2 = min(max(rr.z, 0), M - 1), r3 = min(max(rr.w, 0), M - 1);
+            fma4(acc, wv.x, P4[r0 * (SCAN_CW / 4) + c4]);
+            fma4(acc, wv.y, P4[r1 * (SCAN_CW / 4) + c4]);
+            fma4(acc, wv.z, P4[r2 * (SCAN_CW / 4) + c4]);
+            fma4(acc, wv.w, P4[r3 * (SCAN_CW / 4) + c4]);
+            dc = fmaf(wv.x, Pc[r0], dc);
+            dc = fmaf(wv.y, Pc[r1], dc);
+            dc = fmaf(wv.z, Pc[r2], dc);
+            dc = fmaf(wv.w, Pc[r3], dc);
+          }
+          const float fade = sg * lampow[t];
+          const int64_t tok = (int64_t)b * T + c0 + t;
           const float4 ni = numi4[t * (SCAN_CW / 4) + c4];
           const float o0 = fmaf(fade, acc.x, ni.x), o1 = fmaf(fade, acc.y, ni.y);
           const float o2 = fmaf(fade, acc.z, ni.z), o3 = fmaf(fade, acc.w, ni.w);
@@ -559,8 +629,48 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
             if (4 * c4 + 2 < ncols) dst[2] = o2;
             if (4 * c4 + 3 < ncols) dst[3] = o3;
           }
+          if (cs == 0 && c4 == 0) a.den[tok * h + hh] = fmaf(fade, dc, deni[t]);
         }
-        if (cs == 0 && lane == 0) a.den[tok * h + hh] = fmaf(fade, dcar, deni[t]);
+      } else {
+        // any k: warp per token, the four lane groups take reads g, g + 4, ...
+        for (int t = warp; t < rd_end; t += SCAN_WARPS) {
+          int ri = 0;
+          float wi = 0.f, pdi = 0.f;
+          if (lane < k) {
+            ri = min(max(sir_b[t * k + lane], 0), M - 1);
+            wi = wr_b[t * k + lane];
+            pdi = Pc[ri];
+          }
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int q = 0; q < (KR + 3) / 4; ++q) {
+            const int ii = 4 * q + grp;
+            const int r = __shfl_sync(FULL, ri, ii & 31);
+            const float w = __shfl_sync(FULL, wi, ii & 31);
+            if (ii < k) fma4(acc, w, P4[r * (SCAN_CW / 4) + c4]);
+          }
+#pragma unroll
+          for (int o = 8; o < 32; o <<= 1) {
+            acc.x += __shfl_xor_sync(FULL, acc.x, o);
+            acc.y += __shfl_xor_sync(FULL, acc.y, o);
+            acc.z += __shfl_xor_sync(FULL, acc.z, o);
+            acc.w += __shfl_xor_sync(FULL, acc.w, o);
+          }
+          const float dcar = warp_sum(wi * pdi);
+          const float fade = sg * lampow[t];
+          const int64_t tok = (int64_t)b * T + c0 + t;
+          if (grp == 0) {
+            const float4 ni = numi4[t * (SCAN_CW / 4) + c4];
+            const float o0 = fmaf(fade, acc.x, ni.x), o1 = fmaf(fade, acc.y, ni.y);
+            const float o2 = fmaf(fade, acc.z, ni.z), o3 = fmaf(fade, acc.w, ni.w);
+            float* dst = a.num + (tok * h + hh) * dh + cs * SCAN_CW + 4 * c4;
+            if (4 * c4 + 0 < ncols) dst[0] = o0;
+            if (4 * c4 + 1 < ncols) dst[1] = o1;
+            if (4 * c4 + 2 < ncols) dst[2] = o2;
+            if (4 * c4 + 3 < ncols) dst[3] = o3;
+          }
+          if (cs == 0 && lane == 0) a.den[tok * h + hh] = fmaf(fade, dcar, deni[t]);
+        }
       }
     }
     __syncthreads();
@@ -593,30 +703,30 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
       for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] *= f;
       __syncthreads();
     }
-    const uint32_t* jobs = reinterpret_cast<const uint32_t*>(cur + sb.rec + rl.jobs);
-    const uint16_t* tau = reinterpret_cast<const uint16_t*>(cur + sb.rec + rl.tau);
-    const float* coef = reinterpret_cast<const float*>(cur + sb.rec + rl.coef);
+    // writes: eight lanes per written slot, four slots per warp
+    const uint32_t* jobs = reinterpret_cast<const uint32_t*>(cur + sb.rec);
+    const int2* ents = reinterpret_cast<const int2*>(cur + sb.rec + rl.ents);
     for (int jb = 4 * warp; jb < njobs; jb += 4 * SCAN_WARPS) {
       const int j = jb + grp;
-      const bool valid = j < njobs;
-      const uint32_t j0 = valid ? jobs[j] : 0u, j1 = valid ? jobs[j + 1] : 0u;
-      const int r = (int)(j0 >> 16), st = (int)(j0 & 0xFFFFu), en = valid ? (int)(j1 & 0xFFFFu) : st;
-      float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
-      float pc = 0.f;
-      if (valid) {
-        p = P4[r * (SCAN_CW / 4) + c4];
-        pc = Pc[r];
-      }
+      if (j >= njobs) continue;
+      const uint32_t j0 = jobs[j], j1 = jobs[j + 1];
+      const int r = (int)(j0 >> 16), st = (int)(j0 & 0xFFFFu), en = (int)(j1 & 0xFFFFu);
+      float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
+      float dc = 0.f;
+#pragma unroll 2
       for (int e = st; e < en; ++e) {
-        const float fe = coef[e] * inv;
-        fma4(p, fe, V4[tau[e] * (SCAN_CW / 4) + c4]);
-        pc += fe;
+        const int2 q2 = ents[e];
+        const float cf = __int_as_float(q2.y);
+        fma4(d, cf, V4[q2.x * (SCAN_CW / 4) + c4]);
+        dc += cf;
       }
-      if (valid) {
-        P4[r * (SCAN_CW / 4) + c4] = p;
-        if (c4 == 0) Pc[r] = pc;
-      }
+      float4 p = P4[r * (SCAN_CW / 4) + c4];
+      fma4(p, inv, d);
+      P4[r * (SCAN_CW / 4) + c4] = p;
+      if (c4 == 0) Pc[r] = fmaf(inv, dc, Pc[r]);
     }
+    hd = hd1;
+    hd1 = hd2;
   }
   __syncthreads();
   // the final state, unscaled
@@ -642,20 +752,21 @@ bool rt_scan_supported(int M, int dh, int k) {
 size_t rt_scan_workspace_bytes(int B, int T, int h, int k) {
   if (B <= 0 || T <= 0 || h <= 0 || k <= 0) return 0;
   const int L = chunk_len(k);
-  return (size_t)B * h * ((T + L - 1) / L) * rec_layout(k).bytes;
+  return rec_region_bytes(B, T, h, k) + (size_t)B * h * ((T + L - 1) / L) * 16;  // records + headers
 }
 
-template <int K>
+template <int K, int DH>
 static cudaError_t launch_scan_k(const ScanArgs& a, int nch, int n_slices, cudaStream_t st) {
   const size_t lsm = list_layout(a.M, a.k, a.dh).total;
-  cudaError_t e = cudaFuncSetAttribute(rt_lists_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsm);
+  cudaError_t e =
+      cudaFuncSetAttribute(rt_lists_kernel<K, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsm);
   if (e != cudaSuccess) return e;
   const size_t ssm = scan_smem_bytes(a.M, a.k);
   e = cudaFuncSetAttribute(rt_scan_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm);
   if (e != cudaSuccess) return e;
   {
     LaunchScope scope_("rt_lists", st);
-    rt_lists_kernel<K><<<(unsigned)((int64_t)a.B * a.h * nch), LIST_THREADS, lsm, st>>>(a, nch);
+    rt_lists_kernel<K, DH><<<(unsigned)((int64_t)a.B * a.h * nch), LIST_THREADS, lsm, st>>>(a, nch);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -669,10 +780,11 @@ cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st) {
   if (!a.rec || !rt_scan_supported(a.M, a.dh, a.k)) return cudaErrorInvalidValue;
   const int nch = (a.T + chunk_len(a.k) - 1) / chunk_len(a.k);
   const int n_slices = (a.dh + SCAN_CW - 1) / SCAN_CW;
+  if (a.k == 16 && a.dh == 64) return launch_scan_k<16, 64>(a, nch, n_slices, st);
   switch (a.k) {
-    case 16: return launch_scan_k<16>(a, nch, n_slices, st);
-    case 4: return launch_scan_k<4>(a, nch, n_slices, st);
-    default: return launch_scan_k<0>(a, nch, n_slices, st);
+    case 16: return launch_scan_k<16, 0>(a, nch, n_slices, st);
+    case 4: return launch_scan_k<4, 0>(a, nch, n_slices, st);
+    default: return launch_scan_k<0, 0>(a, nch, n_slices, st);
   }
 }
 
