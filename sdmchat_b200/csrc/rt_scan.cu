@@ -14,12 +14,14 @@
 // all of its writes) in parallel: two or three CTA barriers per 64 tokens.
 //
 // rt_lists_kernel, one CTA per (b, hh, chunk):
-//   * sorts the chunk's k * Lc write entries by slot (shared-memory counting sort, then each slot's short run
-//     sorted by entry index, so the order is deterministic);
+//   * groups the chunk's k * Lc write entries by slot, in token order within a slot (a bit per (slot, token) in
+//     shared memory: an entry's rank in its run is the number of earlier tokens that wrote the slot), so the
+//     order is deterministic;
 //   * intra part: eight lanes per token (each owning dh/8 columns); each of the token's k reads walks its slot's
 //     run (entries of earlier tokens of the chunk, at or after the token's last reset) and adds coef * v[s];
 //     writes num and den;
-//   * the chunk record for the state scan: the distinct written slots ("jobs", ascending) with their entries
+//   * the chunk record for the state scan: the distinct written slots ("jobs", runs of kLongRun or more entries
+//     first so the long runs of repeated tokens start together) with their entries
 //     (source token and coefficient ww * lam^(Lc-1-s)), restricted to entries after the chunk's last reset, and
 //     the chunk header {njobs, nent, rd_end, clear}: tokens before the first reset (rd_end) read the state, a
 //     reset anywhere in the chunk clears it before the writes.
@@ -57,8 +59,10 @@ __host__ __device__ inline int chunk_len(int k) {
 }
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
 
-// One chunk's record: jobs (slot << 16 | first entry; jobs[njobs] closes the last run), then entries
-// {source token, coefficient bits}.  Headers {njobs, nent, rd_end, clear} are kept apart, one int4 per chunk.
+// One chunk's record: jobs {slot, first entry | entry count << 16}, runs of kLongRun or more entries first, then
+// entries {source token, coefficient bits} grouped by slot.  Headers {njobs, nent, rd_end, clear} are kept apart,
+// one int4 per chunk.
+constexpr int kLongRun = 4;
 struct RecLayout {
   int E;
   size_t ents, bytes;
@@ -66,8 +70,8 @@ struct RecLayout {
 __host__ __device__ inline RecLayout rec_layout(int k) {
   RecLayout r;
   r.E = chunk_len(k) * k;
-  r.ents = align16((size_t)(r.E + 1) * 4);
-  r.bytes = r.ents + align16((size_t)r.E * 8);
+  r.ents = align16((size_t)r.E * 8);
+  r.bytes = 2 * r.ents;
   return r;
 }
 __host__ __device__ inline size_t rec_region_bytes(int B, int T, int h, int k) {
@@ -118,14 +122,15 @@ __device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
   acc.w = fmaf(w, v.w, acc.w);
 }
 
-// Exclusive prefix sum of in[0, n) into out[0, n) by all LIST_THREADS threads (in and out distinct); returns the
-// total.  Ends with a barrier.
-__device__ int block_exclusive_scan(const int* in, int* out, int n, int* wtot) {
+// Exclusive prefix sum of in(0) .. in(n-1) into out[0, n) by all LIST_THREADS threads (out must not be what in()
+// reads); returns the total.  Ends with a barrier.
+template <typename In>
+__device__ __forceinline__ int block_exclusive_scan(In in, int* out, int n, int* wtot) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int per = (n + LIST_THREADS - 1) / LIST_THREADS;
   const int s0 = tid * per, s1 = min(n, s0 + per);
   int sum = 0;
-  for (int i = s0; i < s1; ++i) sum += in[i];
+  for (int i = s0; i < s1; ++i) sum += in(i);
   int x = sum;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -147,7 +152,7 @@ __device__ int block_exclusive_scan(const int* in, int* out, int n, int* wtot) {
   int base = (warp ? wtot[warp - 1] : 0) + x - sum;
   for (int i = s0; i < s1; ++i) {
     out[i] = base;
-    base += in[i];
+    base += in(i);
   }
   const int total = wtot[LIST_WARPS - 1];
   __syncthreads();
@@ -156,7 +161,7 @@ __device__ int block_exclusive_scan(const int* in, int* out, int n, int* wtot) {
 
 // ------------------------------------------------------------------------------------------------- list kernel
 struct ListSmem {
-  size_t siw, ww, sir, wr, V, cnt, off, pfx, sorted, ent, rst, wsl, lampow, prev_si, prev_w, prev_v, rec, misc, total;
+  size_t siw, ww, sir, wr, V, run, pfx, tmask, ent, rst, wsl, lampow, prev_si, prev_w, prev_v, rec, misc, total;
 };
 __host__ __device__ inline ListSmem list_layout(int M, int k, int dh) {
   const int L = chunk_len(k), E = L * k;
@@ -172,9 +177,8 @@ __host__ __device__ inline ListSmem list_layout(int M, int k, int dh) {
   s.sir = take((size_t)E * 4);
   s.wr = take((size_t)E * 4);
   s.V = take((size_t)L * dh * 4);
-  s.cnt = take((size_t)M * 4);
-  s.off = take((size_t)M * 4);
-  s.sorted = take((size_t)E * 2);
+  s.run = take((size_t)M * 4);
+  s.tmask = take((size_t)M * 8);
   s.ent = take((size_t)E * 8);
   s.rst = take((size_t)L * 4);
   s.wsl = take((size_t)L * 4);
@@ -206,11 +210,11 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   int* sir_s = reinterpret_cast<int*>(smem + lay.sir);
   float* wr_s = reinterpret_cast<float*>(smem + lay.wr);
   float* V_s = reinterpret_cast<float*>(smem + lay.V);
-  int* cnt = reinterpret_cast<int*>(smem + lay.cnt);
-  int* off = reinterpret_cast<int*>(smem + lay.off);
+  int* run = reinterpret_cast<int*>(smem + lay.run);  // slot r's entries: ent[run & 0xFFFF], run >> 16 of them
   int* pfx = reinterpret_cast<int*>(smem + lay.pfx);
-  uint16_t* sorted = reinterpret_cast<uint16_t*>(smem + lay.sorted);
-  int2* ent = reinterpret_cast<int2*>(smem + lay.ent);  // sorted entries: {source token, ww bits}
+  unsigned long long* tmask = reinterpret_cast<unsigned long long*>(smem + lay.tmask);  // tokens writing a slot
+  int* cntt = reinterpret_cast<int*>(smem + lay.tmask);  // per-slot counts where tmask is not in use
+  int2* ent = reinterpret_cast<int2*>(smem + lay.ent);  // entries by slot, then token: {source token, ww bits}
   int* rst_s = reinterpret_cast<int*>(smem + lay.rst);
   int* wsl = reinterpret_cast<int*>(smem + lay.wsl);
   float* lampow = reinterpret_cast<float*>(smem + lay.lampow);
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   float* prev_w = reinterpret_cast<float*>(smem + lay.prev_w);
   float* prev_v = reinterpret_cast<float*>(smem + lay.prev_v);
   unsigned char* rec_s = smem + lay.rec;
-  int* misc = reinterpret_cast<int*>(smem + lay.misc);  // [0..8) scan totals, [8..11) chunk flags
+  int* misc = reinterpret_cast<int*>(smem + lay.misc);  // [0..8) scan totals, [8..11) chunk flags, [11] repeat
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const unsigned FULL = 0xffffffffu;
@@ -284,40 +288,69 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
 
   const bool need_sort = mode != 0 || last_chunk;
   if (need_sort) {
-    for (int r = tid; r < M; r += LIST_THREADS) cnt[r] = 0;
+    // Group the entries by slot, in token order within a slot.  A token writes distinct slots, so the rank of an
+    // entry in its slot's run is the number of earlier tokens of the chunk that wrote the slot: one bit per token.
+    for (int r = tid; r < M; r += LIST_THREADS) tmask[r] = 0ull;
+    if (tid == 0) misc[11] = 0;
     __syncthreads();
-    int pos[CH_MAX_E / LIST_THREADS];
 #pragma unroll
     for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
       const int e = tid + q * LIST_THREADS;
-      if (e < E) pos[q] = atomicAdd(&cnt[siw_s[e]], 1);
-    }
-    __syncthreads();
-    block_exclusive_scan(cnt, off, M, misc);
-#pragma unroll
-    for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
-      const int e = tid + q * LIST_THREADS;
-      if (e < E) sorted[off[siw_s[e]] + pos[q]] = (uint16_t)e;
-    }
-    __syncthreads();
-    for (int r = tid; r < M; r += LIST_THREADS) {  // each slot's run by entry index (runs are short)
-      const int n = cnt[r], s0 = off[r];
-      for (int i = 1; i < n; ++i) {
-        const uint16_t x = sorted[s0 + i];
-        int j = i - 1;
-        while (j >= 0 && sorted[s0 + j] > x) {
-          sorted[s0 + j + 1] = sorted[s0 + j];
-          --j;
-        }
-        sorted[s0 + j + 1] = x;
+      if (e < E) {
+        const int t = e / k;
+        const unsigned long long old = atomicOr(&tmask[siw_s[e]], 1ull << t);
+        if ((old >> t) & 1ull) misc[11] = 1;
       }
     }
     __syncthreads();
-    for (int x = tid; x < E; x += LIST_THREADS) {
-      const int e = sorted[x];
-      ent[x] = make_int2(e / k, __float_as_int(ww_s[e]));
+    if (misc[11] == 0) {
+      block_exclusive_scan([=](int r) { return __popcll(tmask[r]); }, run, M, misc);
+#pragma unroll
+      for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
+        const int e = tid + q * LIST_THREADS;
+        if (e < E) {
+          const int r = siw_s[e], t = e / k;
+          ent[run[r] + __popcll(tmask[r] & ((1ull << t) - 1ull))] = make_int2(t, __float_as_int(ww_s[e]));
+        }
+      }
+      __syncthreads();
+      for (int r = tid; r < M; r += LIST_THREADS) run[r] |= __popcll(tmask[r]) << 16;
+      __syncthreads();
+    } else {
+      // a token wrote one slot twice (ids from outside the address kernel): counting sort, then each run by entry
+      for (int r = tid; r < M; r += LIST_THREADS) cntt[r] = 0;
+      __syncthreads();
+      int pos[CH_MAX_E / LIST_THREADS];
+#pragma unroll
+      for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
+        const int e = tid + q * LIST_THREADS;
+        if (e < E) pos[q] = atomicAdd(&cntt[siw_s[e]], 1);
+      }
+      __syncthreads();
+      block_exclusive_scan([=](int r) { return cntt[r]; }, run, M, misc);
+#pragma unroll
+      for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
+        const int e = tid + q * LIST_THREADS;
+        if (e < E) ent[run[siw_s[e]] + pos[q]] = make_int2(e, __float_as_int(ww_s[e]));
+      }
+      __syncthreads();
+      for (int r = tid; r < M; r += LIST_THREADS) {
+        const int n = cntt[r], s0 = run[r];
+        run[r] = s0 | (n << 16);
+        for (int i = 1; i < n; ++i) {
+          const int2 x = ent[s0 + i];
+          int j = i - 1;
+          while (j >= 0 && ent[s0 + j].x > x.x) {
+            ent[s0 + j + 1] = ent[s0 + j];
+            --j;
+          }
+          ent[s0 + j + 1] = x;
+        }
+      }
+      __syncthreads();
+      for (int x = tid; x < E; x += LIST_THREADS) ent[x].x /= k;
+      __syncthreads();
     }
-    __syncthreads();
   }
 
   // ---- intra-chunk reads
@@ -359,7 +392,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
       for (int i = 0; i < k; ++i) {
         const int r = sir_s[t * k + i];
         const float w = wr_s[t * k + i];
-        const int st = off[r], en = st + cnt[r];
+        const int st = run[r] & 0xFFFF, en = st + (run[r] >> 16);
         for (int x = st; x < en; ++x) {
           const int2 q2 = ent[x];
           const int s = q2.x;
@@ -397,7 +430,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
       const int ri = lane < k ? sir_s[t * k + lane] : -1;
       const float wi = lane < k ? wr_s[t * k + lane] : 0.f;
       const int lo = max(wsl[t], 0);
-      const int st = ri >= 0 ? off[ri] : 0, n = ri >= 0 ? cnt[ri] : 0;
+      const int st = ri >= 0 ? run[ri] & 0xFFFF : 0, n = ri >= 0 ? run[ri] >> 16 : 0;
       unsigned act = __ballot_sync(FULL, n > 0);
       while (act) {
         const int i = __ffs(act) - 1;
@@ -434,23 +467,24 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   // ---- the chunk record: entries from token p_first on, grouped by slot
   const int p_first = mode == 0 ? Lc - 1 : misc[10];
   for (int r = tid; r < M; r += LIST_THREADS) {
-    const int n = cnt[r], s0 = off[r];
+    const int n = run[r] >> 16, s0 = run[r] & 0xFFFF;
     int skip = 0;
     while (skip < n && ent[s0 + skip].x < p_first) ++skip;
     const int vc = n - skip;
-    off[r] = s0 + skip;
-    cnt[r] = vc | (vc > 0 ? 1 << 16 : 0);
+    run[r] = s0 + skip;
+    // packed counts for one prefix sum: entries (bits 0-10), jobs (11-21), long jobs (22-)
+    cntt[r] = vc | (vc > 0 ? 1 << 11 : 0) | (vc >= kLongRun ? 1 << 22 : 0);
   }
   __syncthreads();
-  const int tot = block_exclusive_scan(cnt, pfx, M, misc);
-  const int njobs = tot >> 16, nent = tot & 0xFFFF;
-  uint32_t* jobs_s = reinterpret_cast<uint32_t*>(rec_s);
+  const int tot = block_exclusive_scan([=](int r) { return cntt[r]; }, pfx, M, misc);
+  const int nent = tot & 0x7FF, njobs = (tot >> 11) & 0x7FF, nlong = tot >> 22;
+  int2* jobs_s = reinterpret_cast<int2*>(rec_s);
   int2* ents_s = reinterpret_cast<int2*>(rec_s + rl.ents);
   for (int r = tid; r < M; r += LIST_THREADS) {
-    const int vc = cnt[r] & 0xFFFF;
+    const int vc = cntt[r] & 0x7FF;
     if (vc) {
-      const int jx = pfx[r] >> 16, eo = pfx[r] & 0xFFFF, s0 = off[r];
-      jobs_s[jx] = ((uint32_t)r << 16) | (uint32_t)eo;
+      const int p = pfx[r], eo = p & 0x7FF, pj = (p >> 11) & 0x7FF, pl = p >> 22, s0 = run[r];
+      jobs_s[vc >= kLongRun ? pl : nlong + pj - pl] = make_int2(r, eo | (vc << 16));
       for (int i = 0; i < vc; ++i) {
         const int2 q2 = ent[s0 + i];
         ents_s[eo + i] = make_int2(q2.x, __float_as_int(__int_as_float(q2.y) * lampow[Lc - 1 - q2.x]));
@@ -458,14 +492,13 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
     }
   }
   if (tid == 0) {
-    jobs_s[njobs] = (0xFFFFu << 16) | (uint32_t)nent;
     reinterpret_cast<int4*>(a.rec + rec_region_bytes(a.B, T, h, k))[(int64_t)bh * nch + c] =
         make_int4(njobs, nent, misc[8], misc[9]);
   }
   __syncthreads();
   // copy out the used parts (16-byte stores)
   unsigned char* rec = a.rec + ((int64_t)bh * nch + c) * rl.bytes;
-  const int n_jobs16 = (int)(align16((size_t)(njobs + 1) * 4) / 16);
+  const int n_jobs16 = (int)(align16((size_t)njobs * 8) / 16);
   const int n_ent16 = (int)(align16((size_t)nent * 8) / 16);
   for (int i = tid; i < n_jobs16 + n_ent16; i += LIST_THREADS) {
     const size_t o = i < n_jobs16 ? (size_t)i * 16 : rl.ents + (size_t)(i - n_jobs16) * 16;
@@ -509,7 +542,7 @@ __device__ __forceinline__ void scan_issue(const ScanArgs& a, unsigned char* buf
   const int64_t bh = (int64_t)b * h + hh;
   const int64_t tok0 = (int64_t)b * T + c0;
   const unsigned char* rec = a.rec + (bh * nch + c) * rl.bytes;
-  copy_rows_async(buf + sb.rec, rec, 1, (int)(align16((size_t)(hd.x + 1) * 4) / 4), 0, 0, tid, SCAN_THREADS);
+  copy_rows_async(buf + sb.rec, rec, 1, (int)(align16((size_t)hd.x * 8) / 4), 0, 0, tid, SCAN_THREADS);
   copy_rows_async(buf + sb.rec + rl.ents, rec + rl.ents, 1, (int)(align16((size_t)hd.y * 8) / 4), 0, 0, tid,
                   SCAN_THREADS);
   copy_rows_async(buf + sb.V, a.V + tok0 * a.ldv + (int64_t)hh * dh + cs * SCAN_CW, Lc, ncols, SCAN_CW, a.ldv, tid,
@@ -704,13 +737,13 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
       __syncthreads();
     }
     // writes: eight lanes per written slot, four slots per warp
-    const uint32_t* jobs = reinterpret_cast<const uint32_t*>(cur + sb.rec);
+    const int2* jobs = reinterpret_cast<const int2*>(cur + sb.rec);
     const int2* ents = reinterpret_cast<const int2*>(cur + sb.rec + rl.ents);
     for (int jb = 4 * warp; jb < njobs; jb += 4 * SCAN_WARPS) {
       const int j = jb + grp;
       if (j >= njobs) continue;
-      const uint32_t j0 = jobs[j], j1 = jobs[j + 1];
-      const int r = (int)(j0 >> 16), st = (int)(j0 & 0xFFFFu), en = (int)(j1 & 0xFFFFu);
+      const int2 jj = jobs[j];
+      const int r = jj.x, st = jj.y & 0xFFFF, en = st + (jj.y >> 16);
       float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
       float dc = 0.f;
 #pragma unroll 2

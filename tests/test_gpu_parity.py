@@ -221,3 +221,46 @@ def test_gemm_bf16_against_fp32_reference(cuda_ok):
         ref = x.double() @ w.double().T
         err = (y.double() - ref).abs().max() / ref.abs().max()
         assert err < 1e-5, (rows, K, n, float(err))
+
+
+@pytest.mark.parametrize("dup", [False, True])
+def test_scan_abi_against_token_recurrence(cuda_ok, dup):
+    """sdm_rt_scan from prepared selections = the oracle's token recurrence (M:285-299), through the C-ABI: every
+    fade mode (0, 0.8, 0.99, 1), BOS resets (one at a chunk start), a ragged last chunk (T = 150), k = 4 and 16;
+    with dup, tokens write one slot twice (only possible with ids from outside the address kernel)."""
+    from sdmchat_b200 import _lib
+    lib = _lib.lib()
+    rng = np.random.default_rng(7 + dup)
+    for k, dh in ((4, 24), (16, 64)):
+        B, h, T, n_sub = 2, 4, 150, 8
+        M = n_sub * n_sub
+        siw = np.stack([rng.choice(M, k, replace=False) for _ in range(B * h * T)]).reshape(B, h, T, k)
+        if dup:
+            siw[..., 1] = siw[..., 0]
+        sir = np.stack([rng.choice(M, k, replace=False) for _ in range(B * h * T)]).reshape(B, h, T, k)
+        siw, sir = siw.astype(np.int32), sir.astype(np.int32)
+        ww = rng.random((B, h, T, k)).astype(np.float32)
+        wr = rng.random((B, h, T, k)).astype(np.float32)
+        V = rng.standard_normal((B, h, T, dh)).astype(np.float32)
+        lam = np.array([0.0, 0.8, 0.99, 1.0], np.float32)
+        reset = rng.random((B, T)) < 0.03
+        reset[0, 64] = True
+        want_num, want_den, want_mem, want_cnt = O.rt_scan_sequential(
+            dict(siw=siw, ww=ww, sir=sir, wr=wr, V=V), lam, M, reset)
+        Vt = t(V.transpose(0, 2, 1, 3).reshape(B * T, h * dh))
+        num = torch.empty(B, T, h, dh, device=DEV)
+        den = torch.empty(B, T, h, device=DEV)
+        mem = torch.empty(B, h, M, dh, device=DEV)
+        cnt = torch.empty(B, h, M, device=DEV)
+        ws = torch.empty(lib.sdm_rt_scan_workspace_size(B, T, h, k), dtype=torch.uint8, device=DEV)
+        args = [t(siw), t(ww), t(sir), t(wr), Vt]  # kept alive until the call has run
+        lam_d, reset_d = t(lam), t(reset.astype(np.uint8))
+        st = lib.sdm_rt_scan(*map(_lib.ptr, args), h * dh, _lib.ptr(lam_d), _lib.ptr(reset_d),
+                             B, T, h, n_sub, dh, k, _lib.ptr(num), _lib.ptr(den), _lib.ptr(mem), _lib.ptr(cnt),
+                             _lib.ptr(ws), ws.numel(), _lib.stream_ptr(torch.device(DEV)))
+        _lib.check(st, "sdm_rt_scan")
+        torch.cuda.synchronize()
+        assert rel(num.cpu().numpy().transpose(0, 2, 1, 3), want_num) < 1e-5
+        assert rel(den.cpu().numpy().transpose(0, 2, 1), want_den.reshape(B, h, T)) < 1e-5
+        assert rel(mem.cpu().numpy(), want_mem) < 1e-5
+        assert rel(cnt.cpu().numpy(), want_cnt) < 1e-5
