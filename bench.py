@@ -228,10 +228,24 @@ def gemm_flops(tag, rows, layers):
     return per_row.get(tag, 0) * rows
 
 
-def scan_bytes(rows_tokens):
-    """Compulsory HBM bytes of the scan per launch: per (token, head) it reads k (slot id, weight) pairs for the
-    write and the read (16 * 16 B), the value row (64 float32) and writes num (64 float32) + den."""
-    return rows_tokens * HEADS * (16 * 16 + 64 * 4 + 64 * 4 + 4)
+def kernel_bytes(kernel, tag, tokens):
+    """Algorithmic HBM bytes of one launch of a memory-bound kernel of the step: its inputs read once and its
+    outputs written once, per (token, head) of the call site (k slot ids + weights are 8 B per pair)."""
+    dh, k, ts_h, ts_dh, ts_k = D // HEADS, 16, 4, D // 4, 32
+    per = {
+        # product-key addressing: z (d_a float32) [+ gate] in, k (id, weight) pairs out
+        ("pk_address", "rt_address"): HEADS * (32 * 4 + 4 + k * 8),
+        ("pk_address", "ts"): ts_h * (32 * 4 + ts_k * 8),
+        # chunk lists + intra reads: write/read selections and the value row in; num, den and the chunk record out
+        ("rt_lists", ""): HEADS * (4 * k * 4 + dh * 4 + dh * 4 + 4 + 2 * k * 8),
+        # state scan: read selections, value row, intra num/den and the chunk record in; num, den out
+        ("rt_scan", ""): HEADS * (2 * k * 4 + dh * 4 + dh * 4 + 4 + 2 * k * 8 + dh * 4 + 4),
+        # TrainedSdm gather: k (id, weight) pairs in, the bf16 hi/lo read out (the value table is L2-resident)
+        ("ts_gather", "ts"): ts_h * (ts_k * 8 + ts_dh * 4),
+        # finish: num, den in; bf16 hi/lo read out
+        ("rt_finish", "rt_out"): HEADS * (dh * 4 + 4) + D * 4,
+    }
+    return per.get((kernel, tag), 0) * tokens
 
 
 def run_ours(a):
@@ -346,11 +360,11 @@ def run_ours(a):
                 "peak_source": f"{how} bf16_tflops_sustained",
                 "avg_launch_ms": round(per_kernel[dom]["ms"] / launches_dom, 4)}
     else:
-        n_scan = per_kernel[dom]["launches"]
-        byts = scan_bytes(rows_tokens) * n_scan
+        byts = sum(kernel_bytes(k, tag, rows_tokens) * n for k, tag, n, ms in groups if k == dom)
         ach = byts / (per_kernel[dom]["ms"] / 1e3) / 1e9
         roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(ach / pk["hbm_gbs"], 4), "traffic": None, "peak_source": f"{how} hbm_gbs"}
+                "frac": round(ach / pk["hbm_gbs"], 4), "traffic": None, "peak_source": f"{how} hbm_gbs",
+                "avg_launch_ms": round(per_kernel[dom]["ms"] / per_kernel[dom]["launches"], 4)}
     breakdown = {k: {"ms_per_step": round(v["ms"] / a.steps, 3), "launches_per_step": v["launches"] / a.steps,
                      "by_call_site_ms": {t: round(ms / a.steps, 3) for t, ms in v["tags"].items()}}
                  for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1]["ms"])}

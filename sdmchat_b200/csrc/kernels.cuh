@@ -5,105 +5,189 @@
 namespace sdm {
 
 // ------------------------------------------------------------------------------------------- GEMM epilogues
-// Each epilogue receives one accumulator element (row, col, acc) of y = x @ w^T and writes it.  `rows` and `n`
-// bound the valid region; the GEMM kernels never call apply() outside it.
+// Each epilogue receives accumulator elements of y = x @ w^T and writes them; `rows` and `n` bound the valid region.
+// Two call shapes:
+//   apply(row, col, acc)              one element (the CUDA-core GEMMs);
+//   prefetch(pre, rl0, rows, col, n)  + store4(pre, it, row, col, acc4, n): the tensor-core GEMM's epilogue thread
+//     owns columns col .. col+3 of rows rl0 + 4*it (it < 8); prefetch fetches what those need from global memory
+//     (biases, the residual input) before the accumulator is ready, store4 writes the four values (16-byte or
+//     8-byte stores when aligned; a column tail past n is written element by element).
+struct NoPre {};
 
-// Element-wise epilogues share one shape: column(col) returns what depends on the column only (hoisted out of the
-// row loop by the tensor-core GEMM), load_input(row, col) fetches a per-element input when kHasInput (issued for 32
-// rows at once before any is used), store(...) writes; apply(row, col, acc) composes them (the CUDA-core GEMM).
-struct NoCol {};
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+__device__ __forceinline__ bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
+__device__ __forceinline__ float f4get(const float4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+__device__ __forceinline__ uint2 pack_bf16x4(float4 v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+__device__ __forceinline__ float4 unpack_bf16x4(uint2 u) {
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+// Four consecutive values of T at d (m = how many of them are valid, 1..4+).
+__device__ __forceinline__ void store4_to(float* d, float4 v, int m) {
+  if (m >= 4 && aligned16(d)) {
+    *reinterpret_cast<float4*>(d) = v;
+  } else {
+    for (int i = 0; i < 4 && i < m; ++i) d[i] = f4get(v, i);
+  }
+}
+__device__ __forceinline__ void store4_to(bf16_t* d, float4 v, int m) {
+  if (m >= 4 && aligned8(d)) {
+    *reinterpret_cast<uint2*>(d) = pack_bf16x4(v);
+  } else {
+    for (int i = 0; i < 4 && i < m; ++i) d[i] = __float2bfloat16_rn(f4get(v, i));
+  }
+}
+__device__ __forceinline__ float4 load4_from(const float* s, int m) {
+  if (m >= 4 && aligned16(s)) return *reinterpret_cast<const float4*>(s);
+  float t[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int i = 0; i < 4 && i < m; ++i) t[i] = s[i];
+  return make_float4(t[0], t[1], t[2], t[3]);
+}
+__device__ __forceinline__ float4 load4_from(const bf16_t* s, int m) {
+  if (m >= 4 && aligned8(s)) return unpack_bf16x4(*reinterpret_cast<const uint2*>(s));
+  float t[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int i = 0; i < 4 && i < m; ++i) t[i] = __bfloat162float(s[i]);
+  return make_float4(t[0], t[1], t[2], t[3]);
+}
+
+// Four values of T as loaded from memory (bf16: 8 bytes), for prefetched inputs held in registers.
+template <typename T>
+struct Pack4;
+template <>
+struct Pack4<float> {
+  using type = float4;
+  __device__ __forceinline__ static float4 load(const float* s, int m) { return load4_from(s, m); }
+  __device__ __forceinline__ static float4 zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ static float4 unpack(float4 v) { return v; }
+};
+template <>
+struct Pack4<bf16_t> {
+  using type = uint2;
+  __device__ __forceinline__ static uint2 load(const bf16_t* s, int m) {
+    if (m >= 4 && aligned8(s)) return *reinterpret_cast<const uint2*>(s);
+    return pack_bf16x4(load4_from(s, m));  // exact: the values are bf16 already
+  }
+  __device__ __forceinline__ static uint2 zero() { return make_uint2(0u, 0u); }
+  __device__ __forceinline__ static float4 unpack(uint2 u) { return unpack_bf16x4(u); }
+};
 
 // y (float32) = acc
 struct EpiF32 {
-  static constexpr bool kRowMode = false, kHasInput = false;
+  static constexpr bool kRowMode = false;
   float* y;
   int64_t ldy;
-  using Col = NoCol;
-  __device__ __forceinline__ Col column(int) const { return {}; }
-  __device__ __forceinline__ float load_input(int64_t, int) const { return 0.f; }
-  __device__ __forceinline__ void store(int64_t row, int col, float acc, const Col&, float) const {
-    y[row * ldy + col] = acc;
+  using Pre = NoPre;
+  __device__ __forceinline__ void apply(int64_t row, int col, float acc) const { y[row * ldy + col] = acc; }
+  __device__ __forceinline__ void prefetch(Pre&, int64_t, int64_t, int, int) const {}
+  __device__ __forceinline__ void store4(const Pre&, int, int64_t row, int col, float4 v, int n) const {
+    store4_to(y + row * ldy + col, v, n - col);
   }
-  __device__ __forceinline__ void apply(int64_t row, int col, float acc) const { store(row, col, acc, {}, 0.f); }
 };
 // y (float32) = acc rounded to the precision of T (logits of a bf16 head, then reduced in float32)
 template <typename T>
 struct EpiF32R {
-  static constexpr bool kRowMode = false, kHasInput = false;
+  static constexpr bool kRowMode = false;
   float* y;
   int64_t ldy;
-  using Col = NoCol;
-  __device__ __forceinline__ Col column(int) const { return {}; }
-  __device__ __forceinline__ float load_input(int64_t, int) const { return 0.f; }
-  __device__ __forceinline__ void store(int64_t row, int col, float acc, const Col&, float) const {
-    y[row * ldy + col] = round_to<T>(acc);
+  using Pre = NoPre;
+  __device__ __forceinline__ void apply(int64_t row, int col, float acc) const { y[row * ldy + col] = round_to<T>(acc); }
+  __device__ __forceinline__ void prefetch(Pre&, int64_t, int64_t, int, int) const {}
+  __device__ __forceinline__ void store4(const Pre&, int, int64_t row, int col, float4 v, int n) const {
+    store4_to(y + row * ldy + col, make_float4(round_to<T>(v.x), round_to<T>(v.y), round_to<T>(v.z), round_to<T>(v.w)),
+              n - col);
   }
-  __device__ __forceinline__ void apply(int64_t row, int col, float acc) const { store(row, col, acc, {}, 0.f); }
 };
 // y (T) = round(acc)
 template <typename T>
 struct EpiStore {
-  static constexpr bool kRowMode = false, kHasInput = false;
+  static constexpr bool kRowMode = false;
   T* y;
   int64_t ldy;
-  using Col = NoCol;
-  __device__ __forceinline__ Col column(int) const { return {}; }
-  __device__ __forceinline__ float load_input(int64_t, int) const { return 0.f; }
-  __device__ __forceinline__ void store(int64_t row, int col, float acc, const Col&, float) const {
-    y[row * ldy + col] = from_f32<T>(acc);
+  using Pre = NoPre;
+  __device__ __forceinline__ void apply(int64_t row, int col, float acc) const { y[row * ldy + col] = from_f32<T>(acc); }
+  __device__ __forceinline__ void prefetch(Pre&, int64_t, int64_t, int, int) const {}
+  __device__ __forceinline__ void store4(const Pre&, int, int64_t row, int col, float4 v, int n) const {
+    store4_to(y + row * ldy + col, v, n - col);
   }
-  __device__ __forceinline__ void apply(int64_t row, int col, float acc) const { store(row, col, acc, {}, 0.f); }
 };
 // RunTimeSdm.prepare's projection (track4_onesdm_models.py:199-205): columns [0, 2*h*d_a) are the write key and
 // the read query, each + addr_b; [2*h*d_a, 2*h*d_a + d) the value; the last h columns the write gate
 // sigmoid(acc + b).  Everything is stored float32 in one (rows, ldy) buffer.
 struct EpiProj {
-  static constexpr bool kRowMode = false, kHasInput = false;
+  static constexpr bool kRowMode = false;
   float* y;
   int64_t ldy;
   const float* addr_b;  // (h*d_a)
   const float* gate_b;  // (h)
   int hda;              // h*d_a
   int gate_from;        // 2*h*d_a + d
-  struct Col {
-    float bias;
-    bool sig;
-  };
-  __device__ __forceinline__ Col column(int col) const {
-    if (col < 2 * hda) return {addr_b[col < hda ? col : col - hda], false};
-    if (col < gate_from) return {0.f, false};
-    return {gate_b[col - gate_from], true};
+  __device__ __forceinline__ float bias(int col) const {
+    if (col < 2 * hda) return addr_b[col < hda ? col : col - hda];
+    return col < gate_from ? 0.f : gate_b[col - gate_from];
   }
-  __device__ __forceinline__ float load_input(int64_t, int) const { return 0.f; }
-  __device__ __forceinline__ void store(int64_t row, int col, float acc, const Col& c, float) const {
-    float v = acc + c.bias;
-    if (c.sig) v = 1.f / (1.f + expf(-v));
-    y[row * ldy + col] = v;
+  __device__ __forceinline__ static float finish(float acc, float b, bool sig) {
+    const float v = acc + b;
+    return sig ? 1.f / (1.f + expf(-v)) : v;
   }
   __device__ __forceinline__ void apply(int64_t row, int col, float acc) const {
-    store(row, col, acc, column(col), 0.f);
+    y[row * ldy + col] = finish(acc, bias(col), col >= gate_from);
+  }
+  struct Pre {
+    float4 b;
+  };
+  __device__ __forceinline__ void prefetch(Pre& p, int64_t, int64_t, int col, int n) const {
+    float t[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) t[i] = col + i < n ? bias(col + i) : 0.f;
+    p.b = make_float4(t[0], t[1], t[2], t[3]);
+  }
+  __device__ __forceinline__ void store4(const Pre& p, int, int64_t row, int col, float4 v, int n) const {
+    float4 o = make_float4(v.x + p.b.x, v.y + p.b.y, v.z + p.b.z, v.w + p.b.w);
+    if (col + 3 >= gate_from) gate4(o, col);  // only the last h columns take the sigmoid
+    store4_to(y + row * ldy + col, o, n - col);
+  }
+  __device__ __noinline__ void gate4(float4& o, int col) const {
+    if (col >= gate_from) o.x = 1.f / (1.f + expf(-o.x));
+    if (col + 1 >= gate_from) o.y = 1.f / (1.f + expf(-o.y));
+    if (col + 2 >= gate_from) o.z = 1.f / (1.f + expf(-o.z));
+    if (col + 3 >= gate_from) o.w = 1.f / (1.f + expf(-o.w));
   }
 };
 // Residual add of a module output (OneSdmLM.residual, track4_onesdm_models.py:540-547): the module output is
 // rounded to T (its `.to(x.dtype)`), then x + out is rounded to T.  x == nullptr: y = round(acc).
 template <typename T>
 struct EpiResid {
-  static constexpr bool kRowMode = false, kHasInput = true;
+  static constexpr bool kRowMode = false;
   const T* x;
   T* y;
   int64_t ld;
-  using Col = NoCol;
-  __device__ __forceinline__ Col column(int) const { return {}; }
-  __device__ __forceinline__ float load_input(int64_t row, int col) const {
-    return x ? to_f32(x[row * ld + col]) : 0.f;
-  }
-  __device__ __forceinline__ void store(int64_t row, int col, float acc, const Col&, float in) const {
-    float o = round_to<T>(acc);
-    if (x) o = in + o;
-    y[row * ld + col] = from_f32<T>(o);
+  __device__ __forceinline__ float out1(float acc, float in) const {
+    const float o = round_to<T>(acc);
+    return x ? in + o : o;
   }
   __device__ __forceinline__ void apply(int64_t row, int col, float acc) const {
-    store(row, col, acc, {}, load_input(row, col));
+    y[row * ld + col] = from_f32<T>(out1(acc, x ? to_f32(x[row * ld + col]) : 0.f));
+  }
+  struct Pre {
+    typename Pack4<T>::type in[8];  // the residual input, packed as stored
+  };
+  __device__ __forceinline__ void prefetch(Pre& p, int64_t rl0, int64_t rows, int col, int n) const {
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int64_t row = rl0 + 4 * it;
+      p.in[it] = (x && row < rows && col < n) ? Pack4<T>::load(x + row * ld + col, n - col) : Pack4<T>::zero();
+    }
+  }
+  __device__ __forceinline__ void store4(const Pre& p, int it, int64_t row, int col, float4 v, int n) const {
+    const float4 in = Pack4<T>::unpack(p.in[it]);
+    store4_to(y + row * ld + col, make_float4(out1(v.x, in.x), out1(v.y, in.y), out1(v.z, in.z), out1(v.w, in.w)),
+              n - col);
   }
 };
 
@@ -187,7 +271,7 @@ struct EpiArgmax {
 template <typename Epi>
 cudaError_t launch_gemm_tc(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K, int n,
                            Epi epi, cudaStream_t st, int kwrap);
-constexpr int TC_BN = 128;  // column tile of the tensor-core GEMM (partials per row = ceil(n / TC_BN))
+constexpr int TC_BN = 128;  // columns per row-mode partial of the tensor-core GEMM (partials per row = ceil(n / 128))
 cudaError_t launch_ce_combine(const float2* part, const float* tgt_logit, const int32_t* targets, int64_t rows,
                               int tiles_n, double* loss_sum, cudaStream_t st);
 cudaError_t launch_argmax_combine(const float2* part, int64_t rows, int tiles_n, int32_t* ids, cudaStream_t st);

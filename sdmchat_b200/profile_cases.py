@@ -4,6 +4,7 @@
     python -m sdmchat_b200.profile_cases gemm     # the layer's projection GEMM alone, 16384 x 768 x 1548
     python -m sdmchat_b200.profile_cases pk       # product-key addressing of 16384 tokens x 12 heads
     python -m sdmchat_b200.profile_cases decode   # 32 streams x 12 layers FULL decode steps
+    python -m sdmchat_b200.profile_cases lm       # FULL d768 L12 forward + CE sum, 4 x 2048 Zipf(1.1) tokens
 
 Each case runs its workload once untimed and then `--reps` times (default 2), and prints one line of CUDA-event
 timings; nothing else runs on the GPU, so `ncu -k regex:<kernel> -c N` captures exactly the launches of interest.
@@ -26,6 +27,20 @@ def _layer(dev):
     return m.to(dev).to(torch.bfloat16)
 
 
+def _full_model(dev):
+    """The benchmark's FULL d768 L12 model: seed-0 init with the zero-initialised output maps perturbed."""
+    torch.manual_seed(0)
+    model = S.build_onesdm("onesdm_allsdm", 32768, dict(d=768, layers=12, mlp_f=2048, heads=12,
+                                                         decays=S.readme_fades(12)))
+    with torch.no_grad():
+        for m in model.mems:
+            torch.nn.init.normal_(m.wo.weight, std=0.02)
+            torch.nn.init.normal_(m.wg.weight, std=0.5 / 768 ** 0.5)
+        for s in model.sdms:
+            torch.nn.init.normal_(s.values, std=0.02)
+    return model.to_bf16_stream().to(dev)
+
+
 def _timed(fn, reps):
     fn()  # first call: module load and attribute setup stay out of the timing
     torch.cuda.synchronize()
@@ -41,7 +56,7 @@ def _timed(fn, reps):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["scan", "gemm", "pk", "decode"])
+    ap.add_argument("case", choices=["scan", "gemm", "pk", "decode", "lm"])
     ap.add_argument("--reps", type=int, default=2)
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
@@ -70,11 +85,17 @@ def main():
             k2 = torch.randn(12, 32, 16, device=dev, generator=g)
             ms = _timed(lambda: S.pk_address(z, k1, k2, 16), a.reps)
             out = {"case": "pk", "addresses": 16384 * 12, "ms": ms}
+        elif a.case == "lm":
+            import numpy as np
+            model = _full_model(dev)
+            rng = np.random.default_rng(1000)
+            ids_np = np.minimum(rng.zipf(1.1, size=(4, 2049)) - 1, 32767)
+            ids = torch.from_numpy(ids_np[:, :-1].astype(np.int32)).to(dev)
+            tgt = torch.from_numpy(ids_np[:, 1:].astype(np.int32)).to(dev)
+            ms = _timed(lambda: model.loss_sum(ids, tgt), a.reps)
+            out = {"case": "lm", "tokens": 4 * 2048, "ms_per_forward": ms, "tok_per_s": 8192 / (ms / 1e3)}
         else:
-            torch.manual_seed(0)
-            model = S.build_onesdm("onesdm_allsdm", 32768, dict(d=768, layers=12, mlp_f=2048, heads=12,
-                                                                 decays=S.readme_fades(12)))
-            model = model.to_bf16_stream().to(dev)
+            model = _full_model(dev)
             state = model.init_decode(32, dev)
             ids = torch.randint(0, 32768, (32,), device=dev, generator=g)
             ms = _timed(lambda: model.decode_step(ids, state), a.reps)
