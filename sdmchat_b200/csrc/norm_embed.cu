@@ -62,6 +62,19 @@ __device__ __forceinline__ void store_split(T* r, int64_t n, int64_t d, int64_t 
   }
 }
 
+// Four consecutive columns c..c+3 (c a multiple of 4) of store_split: 8-byte bf16 stores (16-byte float32) when the
+// destination is aligned.
+template <typename T>
+__device__ __forceinline__ void store_split4(T* r, int64_t n, int64_t d, int64_t c, float4 v, int split) {
+  if (split) {
+    const float4 hi = make_float4(round_to<T>(v.x), round_to<T>(v.y), round_to<T>(v.z), round_to<T>(v.w));
+    store4_to(r + n * 2 * d + c, hi, 4);
+    store4_to(r + n * 2 * d + d + c, make_float4(v.x - hi.x, v.y - hi.y, v.z - hi.z, v.w - hi.w), 4);
+  } else {
+    store4_to(r + n * d + c, v, 4);
+  }
+}
+
 // RunTimeSdm.finish up to wo (track4_onesdm_models.py:243-246): mean (or sum) read, per-head RMS out-norm with
 // onorm_w.  num (N, h, dh), den (N, h) float32 -> r (N, h*dh) in T.  One warp per (token, head).
 template <typename T>
@@ -139,12 +152,12 @@ __global__ void rt_finish_vec_kernel(const float* __restrict__ num, const float*
   for (int q = 0; q < 8; ++q) {
     if (q < steps) {
       const int c = q * 32 + g * 4;
-      float o[4] = {vals[q].x, vals[q].y, vals[q].z, vals[q].w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if (out_norm) o[e] = (o[e] * rs) * onorm_w[hh * dh + c + e];
-        store_split<T>(r, n, (int64_t)h * dh, (int64_t)hh * dh + c + e, o[e], split);
+      float4 o = vals[q];
+      if (out_norm) {
+        const float4 wv = *reinterpret_cast<const float4*>(onorm_w + hh * dh + c);
+        o = make_float4((o.x * rs) * wv.x, (o.y * rs) * wv.y, (o.z * rs) * wv.z, (o.w * rs) * wv.w);
       }
+      store_split4<T>(r, n, (int64_t)h * dh, (int64_t)hh * dh + c, o, split);
     }
   }
 }
@@ -183,6 +196,46 @@ __global__ void ts_gather_kernel(const int32_t* __restrict__ si, const float* __
   }
 }
 
+// The same read for bf16 values with dh a multiple of 8 (at most 256) and k <= 32: lane l owns columns 8l..8l+7 and
+// loads them as one 16-byte access per gathered row; the k (slot, weight) pairs are loaded once and broadcast.
+__global__ void ts_gather_vec_kernel(const int32_t* __restrict__ si, const float* __restrict__ w,
+                                     const bf16_t* __restrict__ values, int64_t N, int h, int M, int dh, int k,
+                                     bf16_t* __restrict__ r, int split) {
+  const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (item >= N * h) return;
+  const int hh = (int)(item % h);
+  const int my_s = lane < k ? si[item * k + lane] : 0;
+  const float my_w = lane < k ? w[item * k + lane] : 0.f;
+  const bool active = 8 * lane < dh;
+  const bf16_t* base = values + (int64_t)hh * M * dh + 8 * lane;
+  float acc[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+#pragma unroll 4
+  for (int j = 0; j < k; ++j) {
+    const int slot = __shfl_sync(0xffffffffu, my_s, j);
+    const float wj = __shfl_sync(0xffffffffu, my_w, j);
+    if (active) {
+      const uint4 u = *reinterpret_cast<const uint4*>(base + (int64_t)slot * dh);
+      const float4 a = unpack_bf16x4(make_uint2(u.x, u.y)), b = unpack_bf16x4(make_uint2(u.z, u.w));
+      acc[0] = fmaf(wj, a.x, acc[0]);
+      acc[1] = fmaf(wj, a.y, acc[1]);
+      acc[2] = fmaf(wj, a.z, acc[2]);
+      acc[3] = fmaf(wj, a.w, acc[3]);
+      acc[4] = fmaf(wj, b.x, acc[4]);
+      acc[5] = fmaf(wj, b.y, acc[5]);
+      acc[6] = fmaf(wj, b.z, acc[6]);
+      acc[7] = fmaf(wj, b.w, acc[7]);
+    }
+  }
+  if (active) {
+    const int64_t n = item / h, c = (int64_t)hh * dh + 8 * lane;
+    store_split4<bf16_t>(r, n, (int64_t)h * dh, c, make_float4(acc[0], acc[1], acc[2], acc[3]), split);
+    store_split4<bf16_t>(r, n, (int64_t)h * dh, c + 4, make_float4(acc[4], acc[5], acc[6], acc[7]), split);
+  }
+}
+
 // ------------------------------------------------------------------------------------------------- launchers
 template <typename T>
 cudaError_t launch_rmsnorm(const T* x, const T* w, int64_t rows, int d, float eps, T* y, cudaStream_t st) {
@@ -214,7 +267,8 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
                              cudaStream_t st) {
   if (N == 0) return cudaSuccess;
   LaunchScope scope_("rt_finish", st);
-  if (dh % 32 == 0 && dh <= 256) {
+  const bool al = ((reinterpret_cast<uintptr_t>(num) | reinterpret_cast<uintptr_t>(onorm_w)) & 15) == 0;
+  if (dh % 32 == 0 && dh <= 256 && al) {
     rt_finish_vec_kernel<T><<<(unsigned)ceil_div(N * h * 8, 256), 256, 0, st>>>(
         num, den, N, h, dh, read_sum, read_eps, out_norm, out_norm_eps, onorm_w, r, split);
     return cudaGetLastError();
@@ -228,6 +282,12 @@ cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values,
                              int k, T* r, int split, cudaStream_t st) {
   if (N == 0) return cudaSuccess;
   LaunchScope scope_("ts_gather", st);
+  if constexpr (sizeof(T) == 2) {
+    if (dh % 8 == 0 && dh <= 256 && k <= 32 && (reinterpret_cast<uintptr_t>(values) & 15) == 0) {
+      ts_gather_vec_kernel<<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r, split);
+      return cudaGetLastError();
+    }
+  }
   ts_gather_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r, split);
   return cudaGetLastError();
 }

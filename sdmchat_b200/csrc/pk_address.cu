@@ -166,7 +166,8 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
       is[q * PK_THREADS + tid] = ti[q];
     }
   }
-  // frontier walk over the c1 x c1 grid: row a's next candidate is (a, fb[a])
+  // frontier walk over the c1 x c1 grid: row a's next candidate is (a, fb[a]); each step takes the best row by a
+  // tree arg-max (depth log2 C) under (score desc, (a, b) asc) -- the key a << 6 | b orders like a * c1 + b
   int fb[C];
   float fv[C];
   const float v2_0 = v2s[tid];
@@ -176,19 +177,24 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
     fv[q] = q < c1 ? (v1s[q * PK_THREADS + tid] + v2_0) * 0.5f : -INFINITY;
   }
   for (int step = 0; step < kk; ++step) {
-    int best = 0;
-    float bv = fv[0];
-    int bflat = fb[0];
+    float bv[C];
+    int bk[C];
 #pragma unroll
-    for (int q = 1; q < C; ++q) {
-      const int flat = q * c1 + fb[q];
-      const bool take = q <= step && (fv[q] > bv || (fv[q] == bv && flat < bflat));
-      best = take ? q : best;
-      bv = take ? fv[q] : bv;
-      bflat = take ? flat : bflat;
+    for (int q = 0; q < C; ++q) {
+      bv[q] = fv[q];
+      bk[q] = q < c1 ? (q << 6) | fb[q] : 0x7fffffff;
     }
-    const int b = bflat - best * c1;
-    ov[step * PK_THREADS + tid] = bv;
+#pragma unroll
+    for (int w = C / 2; w >= 1; w >>= 1) {
+#pragma unroll
+      for (int q = 0; q < w; ++q) {
+        const bool take = better(bv[q + w], bk[q + w], bv[q], bk[q]);
+        bv[q] = take ? bv[q + w] : bv[q];
+        bk[q] = take ? bk[q + w] : bk[q];
+      }
+    }
+    const int best = bk[0] >> 6, b = bk[0] & 63;
+    ov[step * PK_THREADS + tid] = bv[0];
     oi[step * PK_THREADS + tid] = i1s[best * PK_THREADS + tid] * n_sub + i2s[b * PK_THREADS + tid];
     const int nb = b + 1;
     const float nv = nb < c1 ? (v1s[best * PK_THREADS + tid] + v2s[min(nb, C - 1) * PK_THREADS + tid]) * 0.5f
@@ -201,7 +207,7 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
       }
     }
   }
-  // outputs and softmax(scale * score) (* gate)
+  // outputs and softmax(scale * score) (* gate); exp(scale * s - max) is kept in place of the score
   int64_t dst;
   if (a.T_bh > 0) {
     const int64_t bb = n / a.T_bh, t = n % a.T_bh;
@@ -209,21 +215,37 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
   } else {
     dst = (n * a.h + hh) * kk;
   }
-  float scale = 0.f, mx = -INFINITY, sum = 0.f, g = 1.f;
-  if (a.w) {
-    scale = expf(a.log_scale[hh]);
-    for (int j = 0; j < kk; ++j) mx = fmaxf(mx, ov[j * PK_THREADS + tid] * scale);
-    for (int j = 0; j < kk; ++j) sum += expf(ov[j * PK_THREADS + tid] * scale - mx);
-    if (a.gate) g = a.gate[n * a.ldgate + hh];
+  const bool vec = (kk & 3) == 0 && ((reinterpret_cast<uintptr_t>(a.si + dst) | (a.w ? reinterpret_cast<uintptr_t>(a.w + dst) : 0) |
+                                      (a.sv ? reinterpret_cast<uintptr_t>(a.sv + dst) : 0)) & 15) == 0;
+  if (a.sv) {
+    for (int j = 0; j < kk; ++j) a.sv[dst + j] = ov[j * PK_THREADS + tid];
   }
-  for (int j = 0; j < kk; ++j) {
-    const float s = ov[j * PK_THREADS + tid];
-    a.si[dst + j] = oi[j * PK_THREADS + tid];
-    if (a.sv) a.sv[dst + j] = s;
-    if (a.w) {
-      float wj = __fdiv_rn(expf(s * scale - mx), sum);
-      if (a.gate) wj = wj * g;
-      a.w[dst + j] = wj;
+  if (vec) {
+    for (int j = 0; j < kk; j += 4)
+      *reinterpret_cast<int4*>(a.si + dst + j) = make_int4(oi[j * PK_THREADS + tid], oi[(j + 1) * PK_THREADS + tid],
+                                                           oi[(j + 2) * PK_THREADS + tid], oi[(j + 3) * PK_THREADS + tid]);
+  } else {
+    for (int j = 0; j < kk; ++j) a.si[dst + j] = oi[j * PK_THREADS + tid];
+  }
+  if (a.w) {
+    const float scale = expf(a.log_scale[hh]);
+    float mx = -INFINITY, sum = 0.f;
+    for (int j = 0; j < kk; ++j) mx = fmaxf(mx, ov[j * PK_THREADS + tid] * scale);
+    for (int j = 0; j < kk; ++j) {
+      const float e = expf(ov[j * PK_THREADS + tid] * scale - mx);
+      ov[j * PK_THREADS + tid] = e;
+      sum += e;
+    }
+    const float g = a.gate ? a.gate[n * a.ldgate + hh] : 1.f;
+    auto wt = [&](int j) {
+      const float wj = __fdiv_rn(ov[j * PK_THREADS + tid], sum);
+      return a.gate ? wj * g : wj;
+    };
+    if (vec) {
+      for (int j = 0; j < kk; j += 4)
+        *reinterpret_cast<float4*>(a.w + dst + j) = make_float4(wt(j), wt(j + 1), wt(j + 2), wt(j + 3));
+    } else {
+      for (int j = 0; j < kk; ++j) a.w[dst + j] = wt(j);
     }
   }
 }
