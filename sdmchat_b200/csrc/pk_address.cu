@@ -2,7 +2,7 @@
 //
 // One thread owns one (token, head) address.  The address halves are L2-normalised, scored against the head's
 // normalised sub-keys (kept in shared memory), and each half's top-c1 is found with a register bitonic network
-// under the total order (score descending, sub-key index ascending).  The c1 x c1 cartesian combine is never
+// over 64-bit keys that encode the total order (score descending, sub-key index ascending).  The c1 x c1 cartesian combine is never
 // built: a frontier walk over the two sorted lists emits the top-kk combined scores in (score descending,
 // flat index a*c1+b ascending) order, which is the order a stable top-k of the reference's flattened `comb`
 // gives.  Only exactly equal scores can order differently from aten::topk, whose tie order is unspecified.
@@ -14,19 +14,26 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
   return va > vb || (va == vb && ia < ib);
 }
 
-template <int C>
-__device__ __forceinline__ void cswap(float (&v)[C], int (&ix)[C], int i, int j, bool sw) {
-  float tv = v[i];
-  int ti = ix[i];
-  v[i] = sw ? v[j] : tv;
-  ix[i] = sw ? ix[j] : ti;
-  v[j] = sw ? tv : v[j];
-  ix[j] = sw ? ti : ix[j];
+// (score, tie) as one 64-bit key whose unsigned order is the selection order: score descending, tie ascending.
+// High word: the order-preserving bit image of the float score; low word: 0xFFFFFFFF - tie.  One 64-bit compare
+// then orders both at once, exactly, and a compare-exchange is that compare plus four selects.
+typedef unsigned long long KT;
+__device__ __forceinline__ KT kmax(KT a, KT b) { return a > b ? a : b; }
+__device__ __forceinline__ KT kmin(KT a, KT b) { return a > b ? b : a; }
+__device__ __forceinline__ KT pk_key(float s, uint32_t tie) {
+  const uint32_t b = __float_as_uint(s + 0.f);  // -0 -> +0: equal scores share one image
+  const uint32_t m = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((KT)m << 32) | (KT)(0xFFFFFFFFu - tie);
 }
+__device__ __forceinline__ float pk_key_score(KT k) {
+  const uint32_t m = (uint32_t)(k >> 32);
+  return __uint_as_float((m & 0x80000000u) ? (m & 0x7FFFFFFFu) : ~m);
+}
+__device__ __forceinline__ uint32_t pk_key_tie(KT k) { return 0xFFFFFFFFu - (uint32_t)k; }
 
-// Sort C (power of two) elements descending under `better`.
+// Sort C (power of two) keys descending: a bitonic network of max/min pairs (directions fixed at compile time).
 template <int C>
-__device__ __forceinline__ void bitonic_sort_desc(float (&v)[C], int (&ix)[C]) {
+__device__ __forceinline__ void bitonic_sort_desc(KT (&k)[C]) {
 #pragma unroll
   for (int size = 2; size <= C; size <<= 1) {
 #pragma unroll
@@ -35,9 +42,10 @@ __device__ __forceinline__ void bitonic_sort_desc(float (&v)[C], int (&ix)[C]) {
       for (int i = 0; i < C; ++i) {
         const int j = i ^ stride;
         if (j > i) {
+          const KT hi = kmax(k[i], k[j]), lo = kmin(k[i], k[j]);
           const bool desc = (i & size) == 0;
-          const bool sw = desc ? better(v[j], ix[j], v[i], ix[i]) : better(v[i], ix[i], v[j], ix[j]);
-          cswap<C>(v, ix, i, j, sw);
+          k[i] = desc ? hi : lo;
+          k[j] = desc ? lo : hi;
         }
       }
     }
@@ -46,32 +54,29 @@ __device__ __forceinline__ void bitonic_sort_desc(float (&v)[C], int (&ix)[C]) {
 
 // t <- top-C of (t U g), both sorted descending; result sorted descending.
 template <int C>
-__device__ __forceinline__ void merge_top(float (&t)[C], int (&ti)[C], const float (&g)[C], const int (&gi)[C]) {
+__device__ __forceinline__ void merge_top(KT (&t)[C], const KT (&g)[C]) {
 #pragma unroll
-  for (int q = 0; q < C; ++q) {
-    const float gv = g[C - 1 - q];
-    const int gx = gi[C - 1 - q];
-    const bool take = better(gv, gx, t[q], ti[q]);
-    t[q] = take ? gv : t[q];
-    ti[q] = take ? gx : ti[q];
-  }
+  for (int q = 0; q < C; ++q) t[q] = kmax(t[q], g[C - 1 - q]);
 #pragma unroll
   for (int stride = C >> 1; stride > 0; stride >>= 1) {
 #pragma unroll
     for (int i = 0; i < C; ++i) {
       const int j = i ^ stride;
-      if (j > i) cswap<C>(t, ti, i, j, better(t[j], ti[j], t[i], ti[i]));
+      if (j > i) {
+        const KT hi = kmax(t[i], t[j]), lo = kmin(t[i], t[j]);
+        t[i] = hi;
+        t[j] = lo;
+      }
     }
   }
 }
 
-// Top-C of the n_sub cosine scores of one normalised half against the sub-keys kn (n_sub, HALF) in shared memory.
+// Top-C keys of the n_sub cosine scores of one normalised half against the sub-keys kn (n_sub, HALF) in shared
+// memory; a NaN score orders last and padding entries (j >= n_sub) after every real one.
 template <int HALF, int C>
-__device__ __forceinline__ void half_topc(const float (&zn)[HALF], const float* kn, int n_sub, float (&tv)[C],
-                                          int (&ti)[C]) {
+__device__ __forceinline__ void half_topc(const float (&zn)[HALF], const float* kn, int n_sub, KT (&tk)[C]) {
   for (int g0 = 0; g0 < n_sub; g0 += C) {
-    float gv[C];
-    int gi[C];
+    KT gk[C];
 #pragma unroll
     for (int q = 0; q < C; ++q) {
       const int j = g0 + q;
@@ -81,20 +86,16 @@ __device__ __forceinline__ void half_topc(const float (&zn)[HALF], const float* 
         s = 0.f;
 #pragma unroll
         for (int dd = 0; dd < HALF; ++dd) s = fmaf(zn[dd], kr[dd], s);
-        if (s != s) s = -INFINITY;  // a NaN address orders last, so a padding entry can never be selected
+        if (s != s) s = -INFINITY;
       }
-      gv[q] = s;
-      gi[q] = j < n_sub ? j : 0x7fffffff;
+      gk[q] = pk_key(s, j < n_sub ? (uint32_t)j : 0xFFFFFFFFu);
     }
-    bitonic_sort_desc<C>(gv, gi);
+    bitonic_sort_desc<C>(gk);
     if (g0 == 0) {
 #pragma unroll
-      for (int q = 0; q < C; ++q) {
-        tv[q] = gv[q];
-        ti[q] = gi[q];
-      }
+      for (int q = 0; q < C; ++q) tk[q] = gk[q];
     } else {
-      merge_top<C>(tv, ti, gv, gi);
+      merge_top<C>(tk, gk);
     }
   }
 }
@@ -114,7 +115,7 @@ __device__ __forceinline__ void normalize_half(const float* src, float (&zn)[HAL
 
 constexpr int PK_THREADS = 128;
 
-// Resident blocks per SM the register budget is sized for: 4 for lists up to 16 (128 registers, no spills), 2 for 32.
+// Resident blocks per SM the register budget is sized for: 4 for lists up to 16, 2 for 32.
 template <int C>
 struct PkOcc {
   static constexpr int value = C <= 16 ? 4 : 2;
@@ -153,59 +154,45 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
   // the two halves one after the other through one register list (fewer live registers, more resident warps)
 #pragma unroll 1
   for (int hf = 0; hf < 2; ++hf) {
-    float tv[C];
-    int ti[C];
+    KT tk[C];
     float zn[HALF];
     normalize_half<HALF>(zr + hf * HALF, zn);
-    half_topc<HALF, C>(zn, hf ? kn2 : kn1, n_sub, tv, ti);
+    half_topc<HALF, C>(zn, hf ? kn2 : kn1, n_sub, tk);
     float* vs = hf ? v2s : v1s;
     int* is = hf ? i2s : i1s;
 #pragma unroll
     for (int q = 0; q < C; ++q) {
-      vs[q * PK_THREADS + tid] = tv[q];
-      is[q * PK_THREADS + tid] = ti[q];
+      vs[q * PK_THREADS + tid] = pk_key_score(tk[q]);
+      is[q * PK_THREADS + tid] = (int)pk_key_tie(tk[q]);
     }
   }
-  // frontier walk over the c1 x c1 grid: row a's next candidate is (a, fb[a]); each step takes the best row by a
-  // tree arg-max (depth log2 C) under (score desc, (a, b) asc) -- the key a << 6 | b orders like a * c1 + b
-  int fb[C];
-  float fv[C];
+  // frontier walk over the c1 x c1 grid: row r's next candidate is (r, b_r), held as the key of its combined
+  // score with tie r << 6 | b_r (which orders like the flat index r * c1 + b_r); each step takes the largest key
+  // by a max tree and advances the winning row.
+  KT kq[C];
   const float v2_0 = v2s[tid];
+  const KT kminv = pk_key(-INFINITY, 0xFFFFFFFFu);
 #pragma unroll
-  for (int q = 0; q < C; ++q) {
-    fb[q] = 0;
-    fv[q] = q < c1 ? (v1s[q * PK_THREADS + tid] + v2_0) * 0.5f : -INFINITY;
-  }
+  for (int q = 0; q < C; ++q) kq[q] = q < c1 ? pk_key((v1s[q * PK_THREADS + tid] + v2_0) * 0.5f, (uint32_t)(q << 6)) : kminv;
   for (int step = 0; step < kk; ++step) {
-    float bv[C];
-    int bk[C];
+    KT t[C];
 #pragma unroll
-    for (int q = 0; q < C; ++q) {
-      bv[q] = fv[q];
-      bk[q] = q < c1 ? (q << 6) | fb[q] : 0x7fffffff;
-    }
+    for (int q = 0; q < C; ++q) t[q] = kq[q];
 #pragma unroll
     for (int w = C / 2; w >= 1; w >>= 1) {
 #pragma unroll
-      for (int q = 0; q < w; ++q) {
-        const bool take = better(bv[q + w], bk[q + w], bv[q], bk[q]);
-        bv[q] = take ? bv[q + w] : bv[q];
-        bk[q] = take ? bk[q + w] : bk[q];
-      }
+      for (int q = 0; q < w; ++q) t[q] = kmax(t[q], t[q + w]);
     }
-    const int best = bk[0] >> 6, b = bk[0] & 63;
-    ov[step * PK_THREADS + tid] = bv[0];
-    oi[step * PK_THREADS + tid] = i1s[best * PK_THREADS + tid] * n_sub + i2s[b * PK_THREADS + tid];
+    const uint32_t tie = pk_key_tie(t[0]);
+    const int r = (int)(tie >> 6), b = (int)(tie & 63u);
+    ov[step * PK_THREADS + tid] = pk_key_score(t[0]);
+    oi[step * PK_THREADS + tid] = i1s[r * PK_THREADS + tid] * n_sub + i2s[b * PK_THREADS + tid];
     const int nb = b + 1;
-    const float nv = nb < c1 ? (v1s[best * PK_THREADS + tid] + v2s[min(nb, C - 1) * PK_THREADS + tid]) * 0.5f
-                             : -INFINITY;
+    const KT nk = nb < c1 ? pk_key((v1s[r * PK_THREADS + tid] + v2s[min(nb, C - 1) * PK_THREADS + tid]) * 0.5f,
+                                       (uint32_t)((r << 6) | nb))
+                              : kminv;
 #pragma unroll
-    for (int q = 0; q < C; ++q) {
-      if (q == best) {
-        fb[q] = nb;
-        fv[q] = nv;
-      }
-    }
+    for (int q = 0; q < C; ++q) kq[q] = q == r ? nk : kq[q];
   }
   // outputs and softmax(scale * score) (* gate); exp(scale * s - max) is kept in place of the score
   int64_t dst;
