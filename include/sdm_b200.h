@@ -55,7 +55,8 @@ sdm_status sdm_profile_begin(void);
 int sdm_profile_end(void);
 sdm_status sdm_profile_group(int i, char* kernel, char* tag, int name_len, int* launches, double* total_ms);
 /* Synchronises `stream`, then reports SDM_ERR_TIMEOUT if any bounded device-side wait (the tensor-core GEMM's
- * mbarrier waits give up after about 4 s) gave up since the previous call, and clears the flag. */
+ * mbarrier waits and the scan's chunk-copy waits give up after about 4 s) gave up since the previous call, and
+ * clears the flags. */
 sdm_status sdm_device_status(void* stream);
 
 /* ---------------------------------------------------------------------------------------- product-key address

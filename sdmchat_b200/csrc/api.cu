@@ -359,9 +359,10 @@ extern "C" {
 int sdm_abi_version(void) { return 1; }
 
 sdm_status sdm_device_status(void* stream) {
-  int flag = 0;
-  if (read_and_clear_timeout(&flag, S(stream)) != cudaSuccess) return SDM_ERR_CUDA;
-  return flag ? SDM_ERR_TIMEOUT : SDM_OK;
+  int gemm = 0, scan = 0;
+  if (read_and_clear_timeout(&gemm, S(stream)) != cudaSuccess) return SDM_ERR_CUDA;
+  if (read_and_clear_scan_timeout(&scan, S(stream)) != cudaSuccess) return SDM_ERR_CUDA;
+  return (gemm || scan) ? SDM_ERR_TIMEOUT : SDM_OK;
 }
 
 const char* sdm_status_string(sdm_status s) {

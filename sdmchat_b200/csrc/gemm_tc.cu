@@ -15,15 +15,14 @@
 // four consecutive columns (16-byte stores; eight lanes cover a 128-byte row segment).  Row-owned epilogues
 // (kRowMode: the tied-head loss / argmax) reduce each thread's row of its 128 columns in registers and write one
 // partial per (row, 128-column block).
-// Every mbarrier wait is bounded (about 4 s of %globaltimer); a wait that gives up sets g_tc_timeout, every role
+// Every mbarrier wait is bounded (about 4 s of %globaltimer); a wait that gives up sets the module's timeout flag, every role
 // falls through to the common exit, and the TMEM columns are released.  No load here reads another GPU's memory
 // and none is issued to more than one CTA.
 #include <cuda.h>
 #include "kernels.cuh"
+#include "tma.cuh"
 
 namespace sdm {
-
-__device__ int g_tc_timeout;
 
 namespace tc {
 
@@ -44,55 +43,7 @@ struct Cfg {
       (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Wait for the phase with the given parity to complete; false (and the timeout flag set) after ~4 s.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > 4000000000ull) {
-      atomicExch(&g_tc_timeout, 1);
-      return false;
-    }
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
+using namespace sdm::tma;
 
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -156,9 +107,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], EPI_WARPS);  // one arrival per epilogue warp
     }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    mbar_init_fence();
+    prefetch_map(&tmA);
+    prefetch_map(&tmB);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
@@ -187,8 +138,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           unsigned char* a_dst = ring + s * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
-          tma_load_2d(&tmA, &full_bar[s], a_dst, kt * BK, m0);
-          tma_load_2d(&tmB, &full_bar[s], a_dst + A_BYTES, (kt * BK) % kwrap, n0);
+          load_2d(&tmA, &full_bar[s], a_dst, kt * BK, m0);
+          load_2d(&tmB, &full_bar[s], a_dst + A_BYTES, (kt * BK) % kwrap, n0);
         }
       }
     }
@@ -285,33 +236,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
-// 2-D bf16 tensor map over a row-major (outer, inner) matrix with row stride ld elements; box (box_outer, 64).
+// 2-D bf16 tensor map over a row-major (outer, inner) matrix with row stride ld elements; box (64, box_outer),
+// 128-byte swizzle (the UMMA K-major operand layout).
 static bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_outer) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {ld * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, box_outer};
-  cuuint32_t es[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return make_tensor_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, inner, outer, ld * 2, (uint32_t)BK, box_outer,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 static int num_sms() {
@@ -329,11 +258,39 @@ static int num_sms() {
 
 }  // namespace tc
 
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+bool make_tensor_map_2d(CUtensorMap* m, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                        uint64_t ld_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, dtype, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool tc_gemm_supported(const void* x, int64_t ldx, const void* w, int64_t ldw, int K, int kwrap) {
   const uintptr_t ax = reinterpret_cast<uintptr_t>(x), aw = reinterpret_cast<uintptr_t>(w);
   const bool wrap_ok = kwrap == K || (kwrap % tc::BK) == 0;  // a wrapped B restarts on a K-step boundary
   return K >= 16 && (K % 8) == 0 && wrap_ok && (ax % 16) == 0 && (aw % 16) == 0 && (ldx % 8) == 0 &&
-         (ldw % 8) == 0 && tc::encode_fn() != nullptr;
+         (ldw % 8) == 0 && encode_fn() != nullptr;
 }
 
 template <typename Epi, int BN>
@@ -382,14 +339,7 @@ SDM_TC_INST(EpiResid<bf16_t>)
 SDM_TC_INST(EpiCE)
 SDM_TC_INST(EpiArgmax)
 
-// Read and clear the bounded-wait timeout flag (set by any kernel whose wait gave up).
-cudaError_t read_and_clear_timeout(int* flag, cudaStream_t st) {
-  int zero = 0;
-  cudaError_t e = cudaMemcpyFromSymbolAsync(flag, g_tc_timeout, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
-  if (e != cudaSuccess) return e;
-  e = cudaStreamSynchronize(st);
-  if (e != cudaSuccess) return e;
-  return cudaMemcpyToSymbol(g_tc_timeout, &zero, sizeof(int));
-}
+// Read and clear the bounded-wait timeout flag of the GEMM module.
+cudaError_t read_and_clear_timeout(int* flag, cudaStream_t st) { return tma::read_and_clear_wait_timeout(flag, st); }
 
 }  // namespace sdm

@@ -338,6 +338,7 @@ struct ScanArgs {
 cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st);
 bool rt_scan_supported(int M, int dh, int k);
 size_t rt_scan_workspace_bytes(int B, int T, int h, int k);
+cudaError_t read_and_clear_scan_timeout(int* flag, cudaStream_t st);
 
 // Single-token decode on the lazily-decayed state.
 struct DecodeArgs {

@@ -32,12 +32,14 @@
 // rt_scan_kernel, one CTA per (b, hh, slice of SCAN_CW value columns): the slice of mem (M x SCAN_CW float32) and
 // cnt (M) stay in shared memory for the whole window.  Chunk inputs (record, read selections, value slice, the
 // intra num/den) are copied with cp.async one chunk ahead into a second buffer; chunk headers are loaded two
-// chunks ahead so every copy has its exact size.  Per chunk: reads (eight lanes per token, one 32-column row per
-// 16-byte access, four read ids per 16-byte load) add the faded state part to num; then the jobs update the state
-// (eight lanes per slot: the sum of the slot's entries, then one read-modify-write).  The fade is lazy: the state
-// is sigma * P, a chunk multiplies sigma by lam^Lc and writes add coef / sigma; when sigma would drop below 2^-40
-// the chunk instead scales P in one pass.  All sums run in a fixed order: results are bit-reproducible.
+// chunks ahead so every copy has its exact size.  32 warps per CTA.  Per chunk: reads (two eight-lane groups per
+// token, each taking half of its k reads; a lane group covers one 32-column row per 16-byte access, four read ids
+// per 16-byte load) add the faded state part to num; then the jobs update the state (eight lanes per slot: the sum
+// of the slot's entries, then one read-modify-write).  The fade is lazy: the state is sigma * P, a chunk multiplies
+// sigma by lam^Lc and writes add coef / sigma; when sigma would drop below 2^-40 the chunk instead scales P in one
+// pass.  All sums run in a fixed order: results are bit-reproducible.
 #include "kernels.cuh"
+#include "tma.cuh"
 
 namespace sdm {
 
@@ -48,7 +50,7 @@ constexpr int LIST_THREADS = 256;
 constexpr int LIST_WARPS = LIST_THREADS / 32;
 constexpr int LIST_MAX_DH = 256;
 constexpr int SCAN_CW = 32;  // value columns per scan CTA
-constexpr int SCAN_WARPS = 16;
+constexpr int SCAN_WARPS = 32;
 constexpr int SCAN_THREADS = SCAN_WARPS * 32;
 constexpr float kTinyFade = 7.8886e-31f;  // 2^-100: fades below are treated as 0
 constexpr float kRenorm = 9.094947e-13f;  // 2^-40
@@ -114,6 +116,22 @@ __device__ __forceinline__ void copy_rows_async(void* dst, const void* src, int 
     }
   }
 }
+
+// n contiguous 4-byte words, 16-byte copies when both ends are aligned.
+__device__ __forceinline__ void copy_words_async(void* dst, const void* src, int n, int tid, int nt) {
+  const uint32_t* s = static_cast<const uint32_t*>(src);
+  uint32_t* d = static_cast<uint32_t*>(dst);
+  int done = 0;
+  if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15) == 0) {
+    const int nv = n >> 2;
+    for (int i = tid; i < nv; i += nt) cp_async16(d + 4 * i, s + 4 * i);
+    done = nv << 2;
+  }
+  for (int i = done + tid; i < n; i += nt) cp_async4(d + i, s + i);
+}
+// rows of SCAN_CW words (w of them valid) with row stride `stride` words into rows of SCAN_CW words.
+__device__ __forceinline__ void copy_rows32_async(void* dst, const void* src, int rows, int w, int64_t stride,
+                                                  int tid, int nt);
 
 __device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
   acc.x = fmaf(w, v.x, acc.x);
@@ -214,7 +232,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   int* pfx = reinterpret_cast<int*>(smem + lay.pfx);
   unsigned long long* tmask = reinterpret_cast<unsigned long long*>(smem + lay.tmask);  // tokens writing a slot
   int* cntt = reinterpret_cast<int*>(smem + lay.tmask);  // per-slot counts where tmask is not in use
-  int2* ent = reinterpret_cast<int2*>(smem + lay.ent);  // entries by slot, then token: {source token, ww bits}
+  int2* ent = reinterpret_cast<int2*>(smem + lay.ent);  // entries by slot, then token: {slot << 16 | token, ww bits}
   int* rst_s = reinterpret_cast<int*>(smem + lay.rst);
   int* wsl = reinterpret_cast<int*>(smem + lay.wsl);
   float* lampow = reinterpret_cast<float*>(smem + lay.lampow);
@@ -237,11 +255,26 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   const int64_t tok0 = (int64_t)b * T + c0;
   const float* Vh = a.V + (int64_t)hh * dh;
 
-  for (int e = tid; e < E; e += LIST_THREADS) {
-    siw_s[e] = min(max(a.siw[sel0 + e], 0), M - 1);  // ids outside [0, M) never come from the address kernel
-    ww_s[e] = a.ww[sel0 + e];
-    sir_s[e] = min(max(a.sir[sel0 + e], 0), M - 1);
-    wr_s[e] = a.wr[sel0 + e];
+  // ids outside [0, M) never come from the address kernel; they are clamped so no access leaves the state
+  if ((E & 3) == 0 && ((reinterpret_cast<uintptr_t>(a.siw + sel0) | reinterpret_cast<uintptr_t>(a.ww + sel0) |
+                        reinterpret_cast<uintptr_t>(a.sir + sel0) | reinterpret_cast<uintptr_t>(a.wr + sel0)) & 15) == 0) {
+    for (int e4 = tid; e4 < E / 4; e4 += LIST_THREADS) {
+      const int4 sw = reinterpret_cast<const int4*>(a.siw + sel0)[e4];
+      const int4 sr = reinterpret_cast<const int4*>(a.sir + sel0)[e4];
+      reinterpret_cast<int4*>(siw_s)[e4] = make_int4(min(max(sw.x, 0), M - 1), min(max(sw.y, 0), M - 1),
+                                                     min(max(sw.z, 0), M - 1), min(max(sw.w, 0), M - 1));
+      reinterpret_cast<int4*>(sir_s)[e4] = make_int4(min(max(sr.x, 0), M - 1), min(max(sr.y, 0), M - 1),
+                                                     min(max(sr.z, 0), M - 1), min(max(sr.w, 0), M - 1));
+      reinterpret_cast<float4*>(ww_s)[e4] = reinterpret_cast<const float4*>(a.ww + sel0)[e4];
+      reinterpret_cast<float4*>(wr_s)[e4] = reinterpret_cast<const float4*>(a.wr + sel0)[e4];
+    }
+  } else {
+    for (int e = tid; e < E; e += LIST_THREADS) {
+      siw_s[e] = min(max(a.siw[sel0 + e], 0), M - 1);
+      ww_s[e] = a.ww[sel0 + e];
+      sir_s[e] = min(max(a.sir[sel0 + e], 0), M - 1);
+      wr_s[e] = a.wr[sel0 + e];
+    }
   }
   if (DH > 0 && (a.ldv & 3) == 0 && (reinterpret_cast<uintptr_t>(Vh) & 15) == 0) {
     float4* V4 = reinterpret_cast<float4*>(V_s);
@@ -310,7 +343,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
         const int e = tid + q * LIST_THREADS;
         if (e < E) {
           const int r = siw_s[e], t = e / k;
-          ent[run[r] + __popcll(tmask[r] & ((1ull << t) - 1ull))] = make_int2(t, __float_as_int(ww_s[e]));
+          ent[run[r] + __popcll(tmask[r] & ((1ull << t) - 1ull))] = make_int2((r << 16) | t, __float_as_int(ww_s[e]));
         }
       }
       __syncthreads();
@@ -348,7 +381,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
         }
       }
       __syncthreads();
-      for (int x = tid; x < E; x += LIST_THREADS) ent[x].x /= k;
+      for (int x = tid; x < E; x += LIST_THREADS) ent[x].x = (siw_s[ent[x].x] << 16) | (ent[x].x / k);
       __syncthreads();
     }
   }
@@ -381,21 +414,41 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
     const int grp = lane >> 3, gl = lane & 7;
     const float4* V4 = reinterpret_cast<const float4*>(V_s);
     const bool vst = (reinterpret_cast<uintptr_t>(a.num) & 15) == 0;
-    for (int tb = warp * 4; tb < Lc; tb += LIST_WARPS * 4) {
+    for (int tb = warp * 4; tb < Lc; tb += LIST_WARPS * 4) {  // uniform per warp: every lane takes the shuffles
       const int t = tb + grp;
-      if (t >= Lc) continue;
+      const bool tv = t < Lc;  // a group past the chunk's end walks empty runs and stores nothing
       float4 acc[NQ];
 #pragma unroll
       for (int q = 0; q < NQ; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
       float dsum = 0.f;
-      const int lo = max(wsl[t], 0);
+      const int lo = tv ? max(wsl[t], 0) : 0;
+      // lane gl of the token's group holds reads gl, gl + 8, ...: slot run (start | count << 16) and weight
+      constexpr int NR = (K > 0 ? K : SCAN_MAX_K) / 8 > 0 ? (K > 0 ? K : SCAN_MAX_K) / 8 : 1;
+      int rr[NR];
+      float rw[NR];
+#pragma unroll
+      for (int m = 0; m < NR; ++m) {
+        const int i = gl + 8 * m;
+        rr[m] = (tv && i < k) ? run[sir_s[t * k + i]] : 0;
+        rw[m] = (tv && i < k) ? wr_s[t * k + i] : 0.f;
+      }
       for (int i = 0; i < k; ++i) {
-        const int r = sir_s[t * k + i];
-        const float w = wr_s[t * k + i];
-        const int st = run[r] & 0xFFFF, en = st + (run[r] >> 16);
+        int ri = rr[0];
+        float wi = rw[0];
+#pragma unroll
+        for (int m = 1; m < NR; ++m)
+          if ((i >> 3) == m) {
+            ri = rr[m];
+            wi = rw[m];
+          }
+        const int rs = __shfl_sync(FULL, ri, (lane & 24) | (i & 7));
+        const float w = __shfl_sync(FULL, wi, (lane & 24) | (i & 7));
+        const int st = rs & 0xFFFF, en = st + (rs >> 16);
+        int2 nq = st < en ? ent[st] : make_int2(0xFFFF, 0);
         for (int x = st; x < en; ++x) {
-          const int2 q2 = ent[x];
-          const int s = q2.x;
+          const int2 q2 = nq;
+          if (x + 1 < en) nq = ent[x + 1];
+          const int s = q2.x & 0xFFFF;
           if (s >= t) break;
           if (s < lo) continue;
           const float cf = w * __int_as_float(q2.y) * lampow[t - 1 - s];
@@ -404,6 +457,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
           for (int q = 0; q < NQ; ++q) fma4(acc[q], cf, V4[s * (DH / 4) + gl + 8 * q]);
         }
       }
+      if (!tv) continue;
       const int64_t tok = tok0 + t;
       float* dst = a.num + (tok * h + hh) * DH;
 #pragma unroll
@@ -439,7 +493,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
         const float wii = __shfl_sync(FULL, wi, i);
         for (int x = sti; x < sti + ni; ++x) {
           const int2 q2 = ent[x];
-          const int s = q2.x;
+          const int s = q2.x & 0xFFFF;
           if (s >= t) break;
           if (s < lo) continue;
           const float cf = wii * __int_as_float(q2.y) * lampow[t - 1 - s];
@@ -469,7 +523,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   for (int r = tid; r < M; r += LIST_THREADS) {
     const int n = run[r] >> 16, s0 = run[r] & 0xFFFF;
     int skip = 0;
-    while (skip < n && ent[s0 + skip].x < p_first) ++skip;
+    while (skip < n && (ent[s0 + skip].x & 0xFFFF) < p_first) ++skip;
     const int vc = n - skip;
     run[r] = s0 + skip;
     // packed counts for one prefix sum: entries (bits 0-10), jobs (11-21), long jobs (22-)
@@ -483,13 +537,15 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   for (int r = tid; r < M; r += LIST_THREADS) {
     const int vc = cntt[r] & 0x7FF;
     if (vc) {
-      const int p = pfx[r], eo = p & 0x7FF, pj = (p >> 11) & 0x7FF, pl = p >> 22, s0 = run[r];
+      const int p = pfx[r], eo = p & 0x7FF, pj = (p >> 11) & 0x7FF, pl = p >> 22;
       jobs_s[vc >= kLongRun ? pl : nlong + pj - pl] = make_int2(r, eo | (vc << 16));
-      for (int i = 0; i < vc; ++i) {
-        const int2 q2 = ent[s0 + i];
-        ents_s[eo + i] = make_int2(q2.x, __float_as_int(__int_as_float(q2.y) * lampow[Lc - 1 - q2.x]));
-      }
     }
+  }
+  for (int x = tid; x < E; x += LIST_THREADS) {  // entry x of slot r's run goes to r's output block
+    const int2 q2 = ent[x];
+    const int r = (int)((unsigned)q2.x >> 16), t = q2.x & 0xFFFF, first = run[r];
+    if (x >= first)
+      ents_s[(pfx[r] & 0x7FF) + (x - first)] = make_int2(t, __float_as_int(__int_as_float(q2.y) * lampow[Lc - 1 - t]));
   }
   if (tid == 0) {
     reinterpret_cast<int4*>(a.rec + rec_region_bytes(a.B, T, h, k))[(int64_t)bh * nch + c] =
@@ -508,29 +564,33 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
 
 // ------------------------------------------------------------------------------------------------- state scan
 struct ScanBuf {
-  size_t rec, sir, wr, V, numi, deni, bytes;
+  size_t hdr, rec, sir, wr, V, numi, deni, bytes;
 };
 __host__ __device__ inline ScanBuf scan_buf_layout(int k) {
   const int L = chunk_len(k), E = L * k;
   ScanBuf s;
   size_t o = 0;
-  auto take = [&](size_t bytes) {
+  auto take = [&](size_t bytes) {  // 128-byte aligned: tensor-copy destinations
     const size_t r = o;
-    o += align16(bytes);
+    o += (bytes + 127) & ~(size_t)127;
     return r;
   };
+  s.hdr = take(16);
   s.rec = take(rec_layout(k).bytes);
   s.sir = take((size_t)E * 4);
   s.wr = take((size_t)E * 4);
   s.V = take((size_t)L * SCAN_CW * 4);
   s.numi = take((size_t)L * SCAN_CW * 4);
-  s.deni = take((size_t)L * 4);
+  s.deni = take((size_t)L * 4 * 4);  // TMA mode: a 4-head-wide box per token (the head's column at hh % 4)
   s.bytes = o;
   return s;
 }
+// P | Pc | two chunk buffers (128-byte aligned) | lampow, plus 128 bytes to align the dynamic region's base.
+__host__ __device__ inline size_t scan_bufs_offset(int M) {
+  return ((align16((size_t)M * SCAN_CW * 4) + align16((size_t)M * 4)) + 127) & ~(size_t)127;
+}
 __host__ __device__ inline size_t scan_smem_bytes(int M, int k) {
-  return align16((size_t)M * SCAN_CW * 4) + align16((size_t)M * 4) + 2 * scan_buf_layout(k).bytes +
-         align16((size_t)(CH_MAX_L + 1) * 4);
+  return 128 + scan_bufs_offset(M) + 2 * scan_buf_layout(k).bytes + align16((size_t)(CH_MAX_L + 1) * 4);
 }
 
 // Issue the cp.async copies of chunk c's inputs (header hd) into buffer `buf` (all threads).
@@ -542,30 +602,82 @@ __device__ __forceinline__ void scan_issue(const ScanArgs& a, unsigned char* buf
   const int64_t bh = (int64_t)b * h + hh;
   const int64_t tok0 = (int64_t)b * T + c0;
   const unsigned char* rec = a.rec + (bh * nch + c) * rl.bytes;
-  copy_rows_async(buf + sb.rec, rec, 1, (int)(align16((size_t)hd.x * 8) / 4), 0, 0, tid, SCAN_THREADS);
-  copy_rows_async(buf + sb.rec + rl.ents, rec + rl.ents, 1, (int)(align16((size_t)hd.y * 8) / 4), 0, 0, tid,
-                  SCAN_THREADS);
-  copy_rows_async(buf + sb.V, a.V + tok0 * a.ldv + (int64_t)hh * dh + cs * SCAN_CW, Lc, ncols, SCAN_CW, a.ldv, tid,
-                  SCAN_THREADS);
+  copy_words_async(buf + sb.rec, rec, 2 * hd.x, tid, SCAN_THREADS);
+  copy_words_async(buf + sb.rec + rl.ents, rec + rl.ents, 2 * hd.y, tid, SCAN_THREADS);
+  copy_rows32_async(buf + sb.V, a.V + tok0 * a.ldv + (int64_t)hh * dh + cs * SCAN_CW, Lc, ncols, a.ldv, tid,
+                    SCAN_THREADS);
   if (want_reads && hd.z > 0) {
     const int64_t sel0 = (bh * T + c0) * k;
     const int nr = hd.z;  // tokens before the first reset read the state
-    copy_rows_async(buf + sb.sir, a.sir + sel0, 1, nr * k, 0, 0, tid, SCAN_THREADS);
-    copy_rows_async(buf + sb.wr, a.wr + sel0, 1, nr * k, 0, 0, tid, SCAN_THREADS);
-    copy_rows_async(buf + sb.numi, a.num + (tok0 * h + hh) * dh + cs * SCAN_CW, nr, ncols, SCAN_CW,
-                    (int64_t)h * dh, tid, SCAN_THREADS);
-    if (cs == 0) copy_rows_async(buf + sb.deni, a.den + tok0 * h + hh, nr, 1, 1, h, tid, SCAN_THREADS);
+    copy_words_async(buf + sb.sir, a.sir + sel0, nr * k, tid, SCAN_THREADS);
+    copy_words_async(buf + sb.wr, a.wr + sel0, nr * k, tid, SCAN_THREADS);
+    copy_rows32_async(buf + sb.numi, a.num + (tok0 * h + hh) * dh + cs * SCAN_CW, nr, ncols, (int64_t)h * dh, tid,
+                      SCAN_THREADS);
+    if (cs == 0) {
+      float* dd = reinterpret_cast<float*>(buf + sb.deni);
+      for (int i = tid; i < nr; i += SCAN_THREADS) cp_async4(dd + i, a.den + (tok0 + i) * h + hh);
+    }
   }
   (void)E;
   cp_async_commit();
 }
 
+__device__ __forceinline__ void copy_rows32_async(void* dst, const void* src, int rows, int w, int64_t stride,
+                                                  int tid, int nt) {
+  const uint32_t* s = static_cast<const uint32_t*>(src);
+  uint32_t* d = static_cast<uint32_t*>(dst);
+  if (w == SCAN_CW && (reinterpret_cast<uintptr_t>(s) & 15) == 0 && (stride & 3) == 0) {
+    for (int i = tid; i < rows * (SCAN_CW / 4); i += nt) {
+      const int r = i / (SCAN_CW / 4), q = i % (SCAN_CW / 4);
+      cp_async16(d + r * SCAN_CW + 4 * q, s + r * stride + 4 * q);
+    }
+  } else {
+    copy_rows_async(dst, src, rows, w, SCAN_CW, stride, tid, nt);
+  }
+}
+
+// Issue chunk c's inputs (header hd) into buffer `buf` with TMA, completing on `bar` (one thread).  Record parts and
+// read selections are 1-D bulk copies of their exact (16-byte rounded) sizes; the value slice, intra num slice and
+// the 4-head den box are 2-D tensor copies of L token rows.
+__device__ __forceinline__ void scan_issue_tma(const ScanArgs& a, unsigned char* buf, uint64_t* bar,
+                                               const ScanBuf& sb, const RecLayout& rl, int nch, int c, int4 hd,
+                                               int b, int hh, int cs, bool want_reads, const CUtensorMap* mV,
+                                               const CUtensorMap* mN, const CUtensorMap* mD) {
+  const int k = a.k, h = a.h, dh = a.dh, T = a.T;
+  const int L = chunk_len(k), c0 = c * L;
+  const int64_t bh = (int64_t)b * h + hh;
+  const unsigned char* rec = a.rec + (bh * nch + c) * rl.bytes;
+  const uint32_t jb = (uint32_t)align16((size_t)hd.x * 8), eb = (uint32_t)align16((size_t)hd.y * 8);
+  const int nr = want_reads ? hd.z : 0;
+  const uint32_t selb = (uint32_t)nr * k * 4, slab = (uint32_t)L * SCAN_CW * 4;
+  uint32_t total = 16 + jb + eb + slab;
+  if (nr > 0) total += 2 * selb + slab + (cs == 0 ? (uint32_t)L * 16 : 0u);
+  tma::mbar_arrive_expect_tx(bar, total);
+  tma::load_1d(buf + sb.hdr, reinterpret_cast<const int4*>(a.rec + rec_region_bytes(a.B, T, h, k)) + bh * nch + c,
+               16, bar);
+  if (jb) tma::load_1d(buf + sb.rec, rec, jb, bar);
+  if (eb) tma::load_1d(buf + sb.rec + rl.ents, rec + rl.ents, eb, bar);
+  const int x = hh * dh + cs * SCAN_CW, y = b * T + c0;
+  tma::load_2d(mV, bar, buf + sb.V, x, y);
+  if (nr > 0) {
+    const int64_t sel0 = (bh * T + c0) * k;
+    tma::load_1d(buf + sb.sir, a.sir + sel0, selb, bar);
+    tma::load_1d(buf + sb.wr, a.wr + sel0, selb, bar);
+    tma::load_2d(mN, bar, buf + sb.numi, x, y);
+    if (cs == 0) tma::load_2d(mD, bar, buf + sb.deni, hh & ~3, y);
+  }
+}
+
 template <int K>
-__global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, int nch, int n_slices) {
-  extern __shared__ __align__(16) unsigned char smem[];
+__global__ void __launch_bounds__(SCAN_THREADS, 1)
+    rt_scan_kernel(ScanArgs a, int nch, int n_slices, const __grid_constant__ CUtensorMap mapV,
+                   const __grid_constant__ CUtensorMap mapN, const __grid_constant__ CUtensorMap mapD, int use_tma) {
+  __shared__ __align__(8) uint64_t full_bar[2];
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
   const int k = K > 0 ? K : a.k;
   constexpr int KR = K > 0 ? K : SCAN_MAX_K;
-  constexpr bool kVecReads = K > 0 && K % 4 == 0;
+  constexpr bool kVecReads = K > 0 && K % 8 == 0;
   const int M = a.M, dh = a.dh, h = a.h, T = a.T;
   const int L = chunk_len(k);
   const RecLayout rl = rec_layout(k);
@@ -573,7 +685,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
   float4* P4 = reinterpret_cast<float4*>(smem);
   float* P = reinterpret_cast<float*>(smem);
   float* Pc = reinterpret_cast<float*>(smem + align16((size_t)M * SCAN_CW * 4));
-  unsigned char* bufs = smem + align16((size_t)M * SCAN_CW * 4) + align16((size_t)M * 4);
+  unsigned char* bufs = smem + scan_bufs_offset(M);
   float* lampow = reinterpret_cast<float*>(bufs + 2 * sb.bytes);
 
   const int cs = blockIdx.x % n_slices;
@@ -601,19 +713,49 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
     }
   }
   if (tid <= L) lampow[tid] = mode == 0 ? (tid == 0 ? 1.f : 0.f) : powf(lam, (float)tid);
-  int4 hd = hdrs[c_begin];                                              // this chunk's header
-  int4 hd1 = c_begin + 1 < nch ? hdrs[c_begin + 1] : make_int4(0, 0, 0, 0);  // the next one's
-  __syncthreads();
-  scan_issue(a, bufs, sb, rl, nch, c_begin, hd, b, hh, cs, ncols, reads);
+  int4 hd = make_int4(0, 0, 0, 0), hd1 = hd;  // cp.async mode: this chunk's header and the next one's
+  int4 hn = hd;                                // TMA mode (thread 0): the header of the next chunk to issue
+  if (use_tma) {
+    if (tid == 0) {
+      tma::mbar_init(&full_bar[0], 1);
+      tma::mbar_init(&full_bar[1], 1);
+      tma::mbar_init_fence();
+      tma::prefetch_map(&mapV);
+      tma::prefetch_map(&mapN);
+      tma::prefetch_map(&mapD);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      scan_issue_tma(a, bufs, &full_bar[0], sb, rl, nch, c_begin, hdrs[c_begin], b, hh, cs, reads, &mapV, &mapN,
+                     &mapD);
+      if (c_begin + 1 < nch) hn = hdrs[c_begin + 1];
+    }
+  } else {
+    hd = hdrs[c_begin];
+    hd1 = c_begin + 1 < nch ? hdrs[c_begin + 1] : make_int4(0, 0, 0, 0);
+    __syncthreads();
+    scan_issue(a, bufs, sb, rl, nch, c_begin, hd, b, hh, cs, ncols, reads);
+  }
 
   float sigma = 1.f;  // state = sigma * P
   int buf = 0;
   for (int c = c_begin; c < nch; ++c, buf ^= 1) {
-    cp_async_wait_all();
-    __syncthreads();
-    if (c + 1 < nch) scan_issue(a, bufs + (buf ^ 1) * sb.bytes, sb, rl, nch, c + 1, hd1, b, hh, cs, ncols, reads);
-    const int4 hd2 = c + 2 < nch ? hdrs[c + 2] : make_int4(0, 0, 0, 0);  // used two iterations on
     unsigned char* cur = bufs + buf * sb.bytes;
+    int4 hd2 = make_int4(0, 0, 0, 0);
+    if (use_tma) {
+      // every thread waits for this chunk's copies (bounded); a wait that gave up ends the CTA on all threads
+      const bool ok = tma::mbar_wait(&full_bar[buf], (uint32_t)((c - c_begin) >> 1) & 1u);
+      if (__syncthreads_or(!ok)) {
+        if (ok == false) tma::mbar_wait(&full_bar[buf], (uint32_t)((c - c_begin) >> 1) & 1u);  // drain, bounded
+        return;
+      }
+      hd = *reinterpret_cast<const int4*>(cur + sb.hdr);
+    } else {
+      cp_async_wait_all();
+      __syncthreads();
+      if (c + 1 < nch) scan_issue(a, bufs + (buf ^ 1) * sb.bytes, sb, rl, nch, c + 1, hd1, b, hh, cs, ncols, reads);
+      hd2 = c + 2 < nch ? hdrs[c + 2] : make_int4(0, 0, 0, 0);  // used two iterations on
+    }
     const int njobs = hd.x, rd_end = hd.z, clear = hd.w;
     const int c0 = c * L, Lc = min(L, T - c0);
     const float4* V4 = reinterpret_cast<const float4*>(cur + sb.V);
@@ -623,46 +765,60 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
       const float* wr_b = reinterpret_cast<const float*>(cur + sb.wr);
       const float4* numi4 = reinterpret_cast<const float4*>(cur + sb.numi);
       const float* deni = reinterpret_cast<const float*>(cur + sb.deni);
+      const int dstr = use_tma ? 4 : 1, doff = use_tma ? (hh & 3) : 0;  // den of token t at deni[t * dstr + doff]
       const float sg = mode == 2 ? sigma : 1.f;
       if constexpr (kVecReads) {
-        // eight lanes per token, four tokens per warp; read ids and weights four at a time
-        for (int tb = 4 * warp; tb < rd_end; tb += 4 * SCAN_WARPS) {
-          const int t = tb + grp;
-          if (t >= rd_end) continue;
+        // two eight-lane groups per token (reads [0, K/2) and [K/2, K)), two tokens per warp; read ids and weights
+        // four at a time; the halves are combined with one shuffle (the loop is warp-uniform, so every lane takes it)
+        const int half = grp & 1;
+        for (int tb = 2 * warp; tb < rd_end; tb += 2 * SCAN_WARPS) {
+          const int t = tb + (grp >> 1);
+          const bool tv = t < rd_end;
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
           float dc = 0.f;
-          const int4* s4 = reinterpret_cast<const int4*>(sir_b + t * K);
-          const float4* w4 = reinterpret_cast<const float4*>(wr_b + t * K);
+          if (tv) {
+            const int4* s4 = reinterpret_cast<const int4*>(sir_b + t * K + half * (K / 2));
+            const float4* w4 = reinterpret_cast<const float4*>(wr_b + t * K + half * (K / 2));
 #pragma unroll
-          for (int q = 0; q < K / 4; ++q) {
-            const int4 rr = s4[q];
-            const float4 wv = w4[q];
-            const int r0 = min(max(rr.x, 0), M - 1), r1 = min(max(rr.y, 0), M - 1);
-            const int r2 = min(max(rr.z, 0), M - 1), r3 = min(max(rr.w, 0), M - 1);
-            fma4(acc, wv.x, P4[r0 * (SCAN_CW / 4) + c4]);
-            fma4(acc, wv.y, P4[r1 * (SCAN_CW / 4) + c4]);
-            fma4(acc, wv.z, P4[r2 * (SCAN_CW / 4) + c4]);
-            fma4(acc, wv.w, P4[r3 * (SCAN_CW / 4) + c4]);
-            dc = fmaf(wv.x, Pc[r0], dc);
-            dc = fmaf(wv.y, Pc[r1], dc);
-            dc = fmaf(wv.z, Pc[r2], dc);
-            dc = fmaf(wv.w, Pc[r3], dc);
+            for (int q = 0; q < K / 8; ++q) {
+              const int4 rr = s4[q];
+              const float4 wv = w4[q];
+              const int r0 = min(max(rr.x, 0), M - 1), r1 = min(max(rr.y, 0), M - 1);
+              const int r2 = min(max(rr.z, 0), M - 1), r3 = min(max(rr.w, 0), M - 1);
+              fma4(acc, wv.x, P4[r0 * (SCAN_CW / 4) + c4]);
+              fma4(acc, wv.y, P4[r1 * (SCAN_CW / 4) + c4]);
+              fma4(acc, wv.z, P4[r2 * (SCAN_CW / 4) + c4]);
+              fma4(acc, wv.w, P4[r3 * (SCAN_CW / 4) + c4]);
+              dc = fmaf(wv.x, Pc[r0], dc);
+              dc = fmaf(wv.y, Pc[r1], dc);
+              dc = fmaf(wv.z, Pc[r2], dc);
+              dc = fmaf(wv.w, Pc[r3], dc);
+            }
           }
+          acc.x += __shfl_xor_sync(FULL, acc.x, 8);
+          acc.y += __shfl_xor_sync(FULL, acc.y, 8);
+          acc.z += __shfl_xor_sync(FULL, acc.z, 8);
+          acc.w += __shfl_xor_sync(FULL, acc.w, 8);
+          dc += __shfl_xor_sync(FULL, dc, 8);
+          if (!tv) continue;
           const float fade = sg * lampow[t];
           const int64_t tok = (int64_t)b * T + c0 + t;
-          const float4 ni = numi4[t * (SCAN_CW / 4) + c4];
-          const float o0 = fmaf(fade, acc.x, ni.x), o1 = fmaf(fade, acc.y, ni.y);
-          const float o2 = fmaf(fade, acc.z, ni.z), o3 = fmaf(fade, acc.w, ni.w);
-          float* dst = a.num + (tok * h + hh) * dh + cs * SCAN_CW + 4 * c4;
-          if (4 * c4 + 3 < ncols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-            *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
-          } else {
-            if (4 * c4 + 0 < ncols) dst[0] = o0;
-            if (4 * c4 + 1 < ncols) dst[1] = o1;
-            if (4 * c4 + 2 < ncols) dst[2] = o2;
-            if (4 * c4 + 3 < ncols) dst[3] = o3;
+          if (half == 0) {
+            const float4 ni = numi4[t * (SCAN_CW / 4) + c4];
+            const float o0 = fmaf(fade, acc.x, ni.x), o1 = fmaf(fade, acc.y, ni.y);
+            const float o2 = fmaf(fade, acc.z, ni.z), o3 = fmaf(fade, acc.w, ni.w);
+            float* dst = a.num + (tok * h + hh) * dh + cs * SCAN_CW + 4 * c4;
+            if (4 * c4 + 3 < ncols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+              *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
+            } else {
+              if (4 * c4 + 0 < ncols) dst[0] = o0;
+              if (4 * c4 + 1 < ncols) dst[1] = o1;
+              if (4 * c4 + 2 < ncols) dst[2] = o2;
+              if (4 * c4 + 3 < ncols) dst[3] = o3;
+            }
+          } else if (cs == 0 && c4 == 0) {
+            a.den[tok * h + hh] = fmaf(fade, dc, deni[t * dstr + doff]);
           }
-          if (cs == 0 && c4 == 0) a.den[tok * h + hh] = fmaf(fade, dc, deni[t]);
         }
       } else {
         // any k: warp per token, the four lane groups take reads g, g + 4, ...
@@ -702,7 +858,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
             if (4 * c4 + 2 < ncols) dst[2] = o2;
             if (4 * c4 + 3 < ncols) dst[3] = o3;
           }
-          if (cs == 0 && lane == 0) a.den[tok * h + hh] = fmaf(fade, dcar, deni[t]);
+          if (cs == 0 && lane == 0) a.den[tok * h + hh] = fmaf(fade, dcar, deni[t * dstr + doff]);
         }
       }
     }
@@ -736,10 +892,22 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1) rt_scan_kernel(ScanArgs a, in
       for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] *= f;
       __syncthreads();
     }
-    // writes: eight lanes per written slot, four slots per warp
+    // writes: eight lanes per written slot, four slots per warp.  In TMA mode warp 0 instead issues the next
+    // chunk's copies (each TMA instruction holds its thread for hundreds of cycles); their buffer has been free
+    // since this chunk's first barrier.
     const int2* jobs = reinterpret_cast<const int2*>(cur + sb.rec);
     const int2* ents = reinterpret_cast<const int2*>(cur + sb.rec + rl.ents);
-    for (int jb = 4 * warp; jb < njobs; jb += 4 * SCAN_WARPS) {
+    const int wwarp = use_tma ? warp - 1 : warp, nww = use_tma ? SCAN_WARPS - 1 : SCAN_WARPS;
+    if (use_tma && warp == 0) {
+      if (lane == 0 && c + 1 < nch) {
+        tma::fence_proxy_async();
+        scan_issue_tma(a, bufs + (buf ^ 1) * sb.bytes, &full_bar[buf ^ 1], sb, rl, nch, c + 1, hn, b, hh, cs, reads,
+                       &mapV, &mapN, &mapD);
+        if (c + 2 < nch) hn = hdrs[c + 2];
+      }
+      __syncwarp();
+    }
+    for (int jb = 4 * wwarp; wwarp >= 0 && jb < njobs; jb += 4 * nww) {
       const int j = jb + grp;
       if (j >= njobs) continue;
       const int2 jj = jobs[j];
@@ -788,6 +956,31 @@ size_t rt_scan_workspace_bytes(int B, int T, int h, int k) {
   return rec_region_bytes(B, T, h, k) + (size_t)B * h * ((T + L - 1) / L) * 16;  // records + headers
 }
 
+struct ScanMaps {
+  CUtensorMap v, num, den;
+  int use_tma;
+};
+
+// TMA staging of the scan's chunk inputs: value and num slices of 32 columns (dh a multiple of 32), 1-D selection
+// copies (k a multiple of 4), the 4-head den box (h a multiple of 4); else cp.async.
+static ScanMaps scan_maps(const ScanArgs& a) {
+  ScanMaps m{};
+  const int L = chunk_len(a.k);
+  const uint64_t rows = (uint64_t)a.B * a.T;
+  const bool shape_ok = a.dh % SCAN_CW == 0 && a.k % 4 == 0 && a.h % 4 == 0 && (a.ldv % 4) == 0 &&
+                        ((reinterpret_cast<uintptr_t>(a.sir) | reinterpret_cast<uintptr_t>(a.wr) |
+                          reinterpret_cast<uintptr_t>(a.V) | reinterpret_cast<uintptr_t>(a.num) |
+                          reinterpret_cast<uintptr_t>(a.den)) & 15) == 0;
+  m.use_tma = shape_ok &&
+              make_tensor_map_2d(&m.v, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.V, (uint64_t)a.h * a.dh, rows,
+                                 (uint64_t)a.ldv * 4, SCAN_CW, L, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+              make_tensor_map_2d(&m.num, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.num, (uint64_t)a.h * a.dh, rows,
+                                 (uint64_t)a.h * a.dh * 4, SCAN_CW, L, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+              make_tensor_map_2d(&m.den, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.den, (uint64_t)a.h, rows,
+                                 (uint64_t)a.h * 4, 4, L, CU_TENSOR_MAP_SWIZZLE_NONE);
+  return m;
+}
+
 template <int K, int DH>
 static cudaError_t launch_scan_k(const ScanArgs& a, int nch, int n_slices, cudaStream_t st) {
   const size_t lsm = list_layout(a.M, a.k, a.dh).total;
@@ -803,8 +996,10 @@ static cudaError_t launch_scan_k(const ScanArgs& a, int nch, int n_slices, cudaS
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
+  const ScanMaps m = scan_maps(a);
   LaunchScope scope_("rt_scan", st);
-  rt_scan_kernel<K><<<(unsigned)((int64_t)a.B * a.h * n_slices), SCAN_THREADS, ssm, st>>>(a, nch, n_slices);
+  rt_scan_kernel<K><<<(unsigned)((int64_t)a.B * a.h * n_slices), SCAN_THREADS, ssm, st>>>(a, nch, n_slices, m.v,
+                                                                                         m.num, m.den, m.use_tma);
   return cudaGetLastError();
 }
 
@@ -819,6 +1014,11 @@ cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st) {
     case 4: return launch_scan_k<4, 0>(a, nch, n_slices, st);
     default: return launch_scan_k<0, 0>(a, nch, n_slices, st);
   }
+}
+
+// Read and clear the bounded-wait timeout flag of the scan module.
+cudaError_t read_and_clear_scan_timeout(int* flag, cudaStream_t st) {
+  return tma::read_and_clear_wait_timeout(flag, st);
 }
 
 }  // namespace sdm
