@@ -233,8 +233,9 @@ def kernel_bytes(kernel, tag, tokens):
     outputs written once, per (token, head) of the call site (k slot ids + weights are 8 B per pair)."""
     dh, k, ts_h, ts_dh, ts_k = D // HEADS, 16, 4, D // 4, 32
     per = {
-        # product-key addressing: z (d_a float32) [+ gate] in, k (id, weight) pairs out
-        ("pk_address", "rt_address"): HEADS * (32 * 4 + 4 + k * 8),
+        # product-key addressing: z (d_a float32) [+ gate] in, k (id, weight) pairs out; one RunTimeSdm launch
+        # covers the write keys (gated) and the read queries
+        ("pk_address", "rt_address"): HEADS * (2 * (32 * 4 + k * 8) + 4),
         ("pk_address", "ts"): ts_h * (32 * 4 + ts_k * 8),
         # chunk lists + intra reads: write/read selections and the value row in; num, den and the chunk record out
         ("rt_lists", ""): HEADS * (4 * k * 4 + dh * 4 + dh * 4 + 4 + 2 * k * 8),

@@ -111,18 +111,16 @@ cudaError_t rt_prepare(const sdm_rt_params* p, const T* x, int64_t N, int T_bh, 
   pa.T_bh = T_bh;
   pa.log_scale = p->log_scale;
   pa.ldgate = C;
-  // write addresses (keys), gated
+  // write addresses (keys, gated) and read addresses (queries) in one launch
   pa.z = proj;
   pa.w = ww;
   pa.si = siw;
   pa.gate = p->write_gate ? proj + 2LL * h * p->d_a + d : nullptr;
-  e = launch_pk_address(pa, st);
-  if (e != cudaSuccess) return e;
-  // read addresses (queries)
-  pa.z = proj + (int64_t)h * p->d_a;
-  pa.w = wr;
-  pa.si = sir;
-  pa.gate = nullptr;
+  pa.pairs = 2;
+  pa.z2 = proj + (int64_t)h * p->d_a;
+  pa.w2 = wr;
+  pa.si2 = sir;
+  pa.gate2 = nullptr;
   return launch_pk_address(pa, st);
 }
 

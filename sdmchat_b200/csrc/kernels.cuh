@@ -320,6 +320,14 @@ struct PkArgs {
   const float* log_scale;  // (h), needed when w != nullptr
   const float* gate;    // gate of token n, head hh at gate[n * ldgate + hh] (or nullptr)
   int64_t ldgate;
+  // pairs == 2: a second address set against the same sub-keys in the same launch (RunTimeSdm's write keys and
+  // read queries): z2 / sv2 / w2 / si2 / gate2 play the roles of z / sv / w / si / gate
+  int pairs;
+  const float* z2;
+  float* sv2;
+  float* w2;
+  int32_t* si2;
+  const float* gate2;
 };
 cudaError_t launch_pk_address(const PkArgs& a, cudaStream_t st);
 

@@ -112,47 +112,57 @@ __global__ void rt_finish_kernel(const float* __restrict__ num, const float* __r
   }
 }
 
-// The same finish for dh a multiple of 32: eight lanes per (token, head) row, each lane 4 consecutive columns per
-// 32-column step (16-byte loads), the row's sum of squares reduced over the eight lanes; a warp does four rows.
-template <typename T>
-__global__ void rt_finish_vec_kernel(const float* __restrict__ num, const float* __restrict__ den, int64_t N, int h,
-                                     int dh, int read_sum, float read_eps, int out_norm, float out_norm_eps,
-                                     const float* __restrict__ onorm_w, T* __restrict__ r, int split) {
-  const int64_t item = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+// The same finish for dh = 32 * STEPS: eight lanes per (token, head) row, each lane 4 consecutive columns per
+// 32-column step (16-byte loads), the row's sum of squares reduced over the eight lanes.  A lane group takes
+// FIN_ROWS consecutive rows and issues all their loads before the first use, so the loads overlap.
+constexpr int FIN_ROWS = 4;
+template <typename T, int STEPS>
+__global__ void __launch_bounds__(256) rt_finish_vec_kernel(const float* __restrict__ num, const float* __restrict__ den,
+                                                            int64_t N, int h, int read_sum, float read_eps,
+                                                            int out_norm, float out_norm_eps,
+                                                            const float* __restrict__ onorm_w, T* __restrict__ r,
+                                                            int split) {
+  constexpr int dh = 32 * STEPS;
+  const int64_t item0 = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3) * FIN_ROWS;
   const int g = threadIdx.x & 7;
-  const bool live = item < N * h;
-  const int64_t it = live ? item : 0;
-  const int hh = (int)(it % h);
-  const float4* nr = reinterpret_cast<const float4*>(num + it * dh);
-  const float dv = read_sum ? 0.f : den[it] + read_eps;
-  float4 vals[8];
-  float ss = 0.f;
-  const int steps = dh / 32;
+  const int64_t items = N * h;
+  float4 vals[FIN_ROWS][STEPS];
+  float dv[FIN_ROWS];
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    if (q < steps) {
-      float4 v = nr[q * 8 + g];
+  for (int i = 0; i < FIN_ROWS; ++i) {
+    const int64_t it = item0 + i < items ? item0 + i : items - 1;
+    const float4* nr = reinterpret_cast<const float4*>(num + it * dh);
+#pragma unroll
+    for (int q = 0; q < STEPS; ++q) vals[i][q] = nr[q * 8 + g];
+    dv[i] = read_sum ? 0.f : den[it] + read_eps;
+  }
+#pragma unroll
+  for (int i = 0; i < FIN_ROWS; ++i) {
+    float ss = 0.f;
+#pragma unroll
+    for (int q = 0; q < STEPS; ++q) {
+      float4 v = vals[i][q];
       if (!read_sum) {
-        v.x = __fdiv_rn(v.x, dv);
-        v.y = __fdiv_rn(v.y, dv);
-        v.z = __fdiv_rn(v.z, dv);
-        v.w = __fdiv_rn(v.w, dv);
+        v.x = __fdiv_rn(v.x, dv[i]);
+        v.y = __fdiv_rn(v.y, dv[i]);
+        v.z = __fdiv_rn(v.z, dv[i]);
+        v.w = __fdiv_rn(v.w, dv[i]);
       }
       ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-      vals[q] = v;
+      vals[i][q] = v;
     }
-  }
-  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-  if (!live) return;
-  const float rs = out_norm ? rsqrt_rn(__fdiv_rn(ss, (float)dh) + out_norm_eps) : 1.f;
-  const int64_t n = item / h;
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    const int64_t item = item0 + i;
+    if (item >= items) continue;
+    const int hh = (int)(item % h);
+    const float rs = out_norm ? rsqrt_rn(__fdiv_rn(ss, (float)dh) + out_norm_eps) : 1.f;
+    const int64_t n = item / h;
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    if (q < steps) {
+    for (int q = 0; q < STEPS; ++q) {
       const int c = q * 32 + g * 4;
-      float4 o = vals[q];
+      float4 o = vals[i][q];
       if (out_norm) {
         const float4 wv = *reinterpret_cast<const float4*>(onorm_w + hh * dh + c);
         o = make_float4((o.x * rs) * wv.x, (o.y * rs) * wv.y, (o.z * rs) * wv.z, (o.w * rs) * wv.w);
@@ -217,7 +227,7 @@ __global__ void ts_gather_vec_kernel(const int32_t* __restrict__ si, const float
     const int slot = __shfl_sync(0xffffffffu, my_s, j);
     const float wj = __shfl_sync(0xffffffffu, my_w, j);
     if (active) {
-      const uint4 u = *reinterpret_cast<const uint4*>(base + (int64_t)slot * dh);
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)slot * dh));  // read-only: L1 reuse
       const float4 a = unpack_bf16x4(make_uint2(u.x, u.y)), b = unpack_bf16x4(make_uint2(u.z, u.w));
       acc[0] = fmaf(wj, a.x, acc[0]);
       acc[1] = fmaf(wj, a.y, acc[1]);
@@ -268,9 +278,17 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
   if (N == 0) return cudaSuccess;
   LaunchScope scope_("rt_finish", st);
   const bool al = ((reinterpret_cast<uintptr_t>(num) | reinterpret_cast<uintptr_t>(onorm_w)) & 15) == 0;
-  if (dh % 32 == 0 && dh <= 256 && al) {
-    rt_finish_vec_kernel<T><<<(unsigned)ceil_div(N * h * 8, 256), 256, 0, st>>>(
-        num, den, N, h, dh, read_sum, read_eps, out_norm, out_norm_eps, onorm_w, r, split);
+  if (al && (dh == 64 || dh == 32 || dh == 128)) {
+    const unsigned grid = (unsigned)ceil_div(ceil_div(N * h, FIN_ROWS) * 8, 256);
+    if (dh == 64)
+      rt_finish_vec_kernel<T, 2><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm, out_norm_eps,
+                                                      onorm_w, r, split);
+    else if (dh == 32)
+      rt_finish_vec_kernel<T, 1><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm, out_norm_eps,
+                                                      onorm_w, r, split);
+    else
+      rt_finish_vec_kernel<T, 4><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm, out_norm_eps,
+                                                      onorm_w, r, split);
     return cudaGetLastError();
   }
   rt_finish_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(num, den, N, h, dh, read_sum, read_eps,

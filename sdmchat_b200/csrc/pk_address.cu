@@ -124,7 +124,12 @@ struct PkOcc {
 template <int HALF, int C>
 __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs a, int c1, int kk) {
   extern __shared__ float pk_smem[];
-  const int hh = blockIdx.y;
+  const int hh = blockIdx.y % a.h, pr = blockIdx.y / a.h;  // pr: which address set of a paired launch
+  const float* const zb = pr ? a.z2 : a.z;
+  float* const svb = pr ? a.sv2 : a.sv;
+  float* const wb = pr ? a.w2 : a.w;
+  int32_t* const sib = pr ? a.si2 : a.si;
+  const float* const gb = pr ? a.gate2 : a.gate;
   const int tid = threadIdx.x;
   const int n_sub = a.n_sub;
   float* kn1 = pk_smem;                    // (n_sub, HALF)
@@ -150,7 +155,7 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
 
   const int64_t n = (int64_t)blockIdx.x * PK_THREADS + tid;
   if (n >= a.N) return;
-  const float* zr = a.z + n * a.ldz + (int64_t)hh * a.d_a;
+  const float* zr = zb + n * a.ldz + (int64_t)hh * a.d_a;
   // the two halves one after the other through one register list (fewer live registers, more resident warps)
 #pragma unroll 1
   for (int hf = 0; hf < 2; ++hf) {
@@ -202,19 +207,19 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
   } else {
     dst = (n * a.h + hh) * kk;
   }
-  const bool vec = (kk & 3) == 0 && ((reinterpret_cast<uintptr_t>(a.si + dst) | (a.w ? reinterpret_cast<uintptr_t>(a.w + dst) : 0) |
-                                      (a.sv ? reinterpret_cast<uintptr_t>(a.sv + dst) : 0)) & 15) == 0;
-  if (a.sv) {
-    for (int j = 0; j < kk; ++j) a.sv[dst + j] = ov[j * PK_THREADS + tid];
+  const bool vec = (kk & 3) == 0 && ((reinterpret_cast<uintptr_t>(sib + dst) | (wb ? reinterpret_cast<uintptr_t>(wb + dst) : 0) |
+                                      (svb ? reinterpret_cast<uintptr_t>(svb + dst) : 0)) & 15) == 0;
+  if (svb) {
+    for (int j = 0; j < kk; ++j) svb[dst + j] = ov[j * PK_THREADS + tid];
   }
   if (vec) {
     for (int j = 0; j < kk; j += 4)
-      *reinterpret_cast<int4*>(a.si + dst + j) = make_int4(oi[j * PK_THREADS + tid], oi[(j + 1) * PK_THREADS + tid],
+      *reinterpret_cast<int4*>(sib + dst + j) = make_int4(oi[j * PK_THREADS + tid], oi[(j + 1) * PK_THREADS + tid],
                                                            oi[(j + 2) * PK_THREADS + tid], oi[(j + 3) * PK_THREADS + tid]);
   } else {
-    for (int j = 0; j < kk; ++j) a.si[dst + j] = oi[j * PK_THREADS + tid];
+    for (int j = 0; j < kk; ++j) sib[dst + j] = oi[j * PK_THREADS + tid];
   }
-  if (a.w) {
+  if (wb) {
     const float scale = expf(a.log_scale[hh]);
     float mx = -INFINITY, sum = 0.f;
     for (int j = 0; j < kk; ++j) mx = fmaxf(mx, ov[j * PK_THREADS + tid] * scale);
@@ -223,16 +228,16 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
       ov[j * PK_THREADS + tid] = e;
       sum += e;
     }
-    const float g = a.gate ? a.gate[n * a.ldgate + hh] : 1.f;
+    const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
     auto wt = [&](int j) {
       const float wj = __fdiv_rn(ov[j * PK_THREADS + tid], sum);
-      return a.gate ? wj * g : wj;
+      return gb ? wj * g : wj;
     };
     if (vec) {
       for (int j = 0; j < kk; j += 4)
-        *reinterpret_cast<float4*>(a.w + dst + j) = make_float4(wt(j), wt(j + 1), wt(j + 2), wt(j + 3));
+        *reinterpret_cast<float4*>(wb + dst + j) = make_float4(wt(j), wt(j + 1), wt(j + 2), wt(j + 3));
     } else {
-      for (int j = 0; j < kk; ++j) a.w[dst + j] = wt(j);
+      for (int j = 0; j < kk; ++j) wb[dst + j] = wt(j);
     }
   }
 }
@@ -243,7 +248,7 @@ static cudaError_t launch_pk_tc(const PkArgs& a, int c1, int kk, cudaStream_t st
   auto kern = pk_kernel<HALF, C>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)ceil_div(a.N, PK_THREADS), (unsigned)a.h);
+  dim3 grid((unsigned)ceil_div(a.N, PK_THREADS), (unsigned)(a.h * (a.pairs > 1 ? 2 : 1)));
   LaunchScope scope_("pk_address", st);
   kern<<<grid, PK_THREADS, smem, st>>>(a, c1, kk);
   return cudaGetLastError();
@@ -279,7 +284,12 @@ __device__ __forceinline__ void warp_best(float& v, int& i) {
 template <int HALF>
 __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c1, int kk) {
   extern __shared__ float pkw_smem[];
-  const int hh = blockIdx.y;
+  const int hh = blockIdx.y % a.h, pr = blockIdx.y / a.h;  // pr: which address set of a paired launch
+  const float* const zb = pr ? a.z2 : a.z;
+  float* const svb = pr ? a.sv2 : a.sv;
+  float* const wb = pr ? a.w2 : a.w;
+  int32_t* const sib = pr ? a.si2 : a.si;
+  const float* const gb = pr ? a.gate2 : a.gate;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n_sub = a.n_sub;
   float* kn1 = pkw_smem;                 // (n_sub, HALF)
@@ -301,7 +311,7 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
   __syncthreads();
   const int64_t n = (int64_t)blockIdx.x * PKW_WARPS + warp;
   if (n >= a.N) return;
-  const float* zr = a.z + n * a.ldz + (int64_t)hh * a.d_a;
+  const float* zr = zb + n * a.ldz + (int64_t)hh * a.d_a;
   // each half: lanes score sub-keys lane, lane+32, ...; c1 rounds of warp arg-max give the sorted top-c1
 #pragma unroll 1
   for (int hf = 0; hf < 2; ++hf) {
@@ -377,10 +387,10 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
   }
   const bool mine = lane < kk;
   if (mine) {
-    a.si[dst + lane] = out_i;
-    if (a.sv) a.sv[dst + lane] = out_v;
+    sib[dst + lane] = out_i;
+    if (svb) svb[dst + lane] = out_v;
   }
-  if (a.w) {
+  if (wb) {
     const float scale = expf(a.log_scale[hh]);
     const float x = mine ? out_v * scale : -INFINITY;
     const float mx = warp_max(x);
@@ -390,8 +400,8 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
     for (int j = 0; j < kk; ++j) sum += __shfl_sync(0xffffffffu, e, j);
     if (mine) {
       float wj = __fdiv_rn(e, sum);
-      if (a.gate) wj = wj * a.gate[n * a.ldgate + hh];
-      a.w[dst + lane] = wj;
+      if (gb) wj = wj * gb[n * a.ldgate + hh];
+      wb[dst + lane] = wj;
     }
   }
 }
@@ -402,7 +412,7 @@ static cudaError_t launch_pk_warp(const PkArgs& a, int c1, int kk, cudaStream_t 
   auto kern = pk_warp_kernel<HALF>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)ceil_div(a.N, PKW_WARPS), (unsigned)a.h);
+  dim3 grid((unsigned)ceil_div(a.N, PKW_WARPS), (unsigned)(a.h * (a.pairs > 1 ? 2 : 1)));
   LaunchScope scope_("pk_address", st);
   kern<<<grid, PKW_WARPS * 32, smem, st>>>(a, c1, kk);
   return cudaGetLastError();
@@ -415,7 +425,7 @@ cudaError_t launch_pk_address(const PkArgs& a, cudaStream_t st) {
   if (a.N == 0) return cudaSuccess;
   const int c1 = a.k < a.n_sub ? a.k : a.n_sub;
   const int kk = a.k < c1 * c1 ? a.k : c1 * c1;
-  if (a.N * a.h <= PK_WARP_MAX_ADDRESSES && a.n_sub <= 128 && c1 <= 32 && kk <= 32) {
+  if (a.N * a.h * (a.pairs > 1 ? 2 : 1) <= PK_WARP_MAX_ADDRESSES && a.n_sub <= 128 && c1 <= 32 && kk <= 32) {
     switch (a.d_a / 2) {
       case 2: return launch_pk_warp<2>(a, c1, kk, st);
       case 4: return launch_pk_warp<4>(a, c1, kk, st);
