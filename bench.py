@@ -228,6 +228,19 @@ def gemm_flops(tag, rows, layers):
     return per_row.get(tag, 0) * rows
 
 
+# DRAM bytes (read + write) per token of one launch, from the ncu capture summarised in
+# profiles/{pk_kernel,rt_lists_rt_scan,ts_gather_rt_finish}_lm_d768_L12_B4_T2048.md (8,192 tokens, layer 6),
+# scaled by tokens: the bench's 65,536-token launches are too large to capture with every metric.
+NCU_DRAM_PER_TOKEN = {
+    ("pk_address", "rt_address"): (26591744 + 33536) / 8192,
+    ("pk_address", "ts"): 4334080 / 8192,
+    ("rt_lists", ""): (51309056 + 4100608) / 8192,
+    ("rt_scan", ""): (64075264 + 2735616) / 8192,
+    ("ts_gather", "ts"): 15511808 / 8192,
+    ("rt_finish", "rt_out"): (25603840 + 92160) / 8192,
+}
+
+
 def kernel_bytes(kernel, tag, tokens):
     """Algorithmic HBM bytes of one launch of a memory-bound kernel of the step: its inputs read once and its
     outputs written once, per (token, head) of the call site (k slot ids + weights are 8 B per pair)."""
@@ -363,9 +376,16 @@ def run_ours(a):
     else:
         byts = sum(kernel_bytes(k, tag, rows_tokens) * n for k, tag, n, ms in groups if k == dom)
         ach = byts / (per_kernel[dom]["ms"] / 1e3) / 1e9
+        nl = per_kernel[dom]["launches"]
+        traffic = None
+        if all((k, tag) in NCU_DRAM_PER_TOKEN for k, tag, n, ms in groups if k == dom):
+            traffic = round(sum(NCU_DRAM_PER_TOKEN[(k, tag)] * rows_tokens * n
+                                for k, tag, n, ms in groups if k == dom) / nl)
         roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(ach / pk["hbm_gbs"], 4), "traffic": None, "peak_source": f"{how} hbm_gbs",
-                "avg_launch_ms": round(per_kernel[dom]["ms"] / per_kernel[dom]["launches"], 4)}
+                "frac": round(ach / pk["hbm_gbs"], 4), "traffic": traffic,
+                "traffic_source": "ncu dram bytes per token of a 8,192-token capture, scaled to the launch",
+                "algorithmic_bytes_per_launch": round(byts / nl), "peak_source": f"{how} hbm_gbs",
+                "avg_launch_ms": round(per_kernel[dom]["ms"] / nl, 4)}
     breakdown = {k: {"ms_per_step": round(v["ms"] / a.steps, 3), "launches_per_step": v["launches"] / a.steps,
                      "by_call_site_ms": {t: round(ms / a.steps, 3) for t, ms in v["tags"].items()}}
                  for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1]["ms"])}
