@@ -100,6 +100,114 @@ __device__ __forceinline__ void half_topc(const float (&zn)[HALF], const float* 
   }
 }
 
+// Fast path (n_sub <= 32): 32-bit keys = the score's order-preserving image with its low 5 bits replaced by
+// 31 - index, so one unsigned min and one max make a compare-exchange.  Their order can differ from the exact one
+// only between two keys with equal high 27 bits (scores within ~2^-18 relative, or exactly tied); such a pair
+// among the top C, or at the boundary to the best key left out, is detected and the half is re-sorted exactly.
+constexpr int FK_IB = 5;
+constexpr uint32_t FK_MASK = (1u << FK_IB) - 1u;
+__device__ __forceinline__ uint32_t fast_key(float s, uint32_t j) {
+  const uint32_t b = __float_as_uint(s + 0.f);
+  const uint32_t m = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (m & ~FK_MASK) | (FK_MASK - j);
+}
+template <int C>
+__device__ __forceinline__ void bitonic_sort_desc32(uint32_t (&k)[C]) {
+#pragma unroll
+  for (int size = 2; size <= C; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < C; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint32_t hi = max(k[i], k[j]), lo = min(k[i], k[j]);
+          const bool desc = (i & size) == 0;
+          k[i] = desc ? hi : lo;
+          k[j] = desc ? lo : hi;
+        }
+      }
+    }
+  }
+}
+// t <- top-C of (t U g); disc <- max(disc, the best key left out).
+template <int C>
+__device__ __forceinline__ void merge_top32(uint32_t (&t)[C], const uint32_t (&g)[C], uint32_t& disc) {
+#pragma unroll
+  for (int q = 0; q < C; ++q) {
+    const uint32_t a = t[q], b = g[C - 1 - q];
+    t[q] = max(a, b);
+    disc = max(disc, min(a, b));
+  }
+#pragma unroll
+  for (int stride = C >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int j = i ^ stride;
+      if (j > i) {
+        const uint32_t hi = max(t[i], t[j]), lo = min(t[i], t[j]);
+        t[i] = hi;
+        t[j] = lo;
+      }
+    }
+  }
+}
+// Top-C of one half with 32-bit keys; the exact scores go to sc[j * PK_STRIDE].  False when the result may
+// differ from the exact order (the caller then sorts the stored scores with 64-bit keys).
+template <int HALF, int C, int PK_STRIDE>
+__device__ __forceinline__ bool half_topc_fast(const float (&zn)[HALF], const float* kn, int n_sub, float* sc,
+                                               uint32_t (&tk)[C]) {
+  uint32_t disc = 0u;
+  for (int g0 = 0; g0 < n_sub; g0 += C) {
+    uint32_t gk[C];
+#pragma unroll
+    for (int q = 0; q < C; ++q) {
+      const int j = g0 + q;
+      uint32_t key = 0u;  // padding: below every real key
+      if (j < n_sub) {
+        const float* kr = kn + j * HALF;
+        float s = 0.f;
+#pragma unroll
+        for (int dd = 0; dd < HALF; ++dd) s = fmaf(zn[dd], kr[dd], s);
+        if (s != s) s = -INFINITY;
+        sc[j * PK_STRIDE] = s;
+        key = fast_key(s, (uint32_t)j);
+      }
+      gk[q] = key;
+    }
+    bitonic_sort_desc32<C>(gk);
+    if (g0 == 0) {
+#pragma unroll
+      for (int q = 0; q < C; ++q) tk[q] = gk[q];
+    } else {
+      merge_top32<C>(tk, gk, disc);
+    }
+  }
+  bool amb = disc != 0u && tk[C - 1] != 0u && (disc >> FK_IB) == (tk[C - 1] >> FK_IB);
+#pragma unroll
+  for (int q = 0; q + 1 < C; ++q) amb |= tk[q + 1] != 0u && (tk[q] >> FK_IB) == (tk[q + 1] >> FK_IB);
+  return !amb;
+}
+// The exact top-C (64-bit keys) of scores already stored at sc[j * PK_STRIDE].
+template <int C, int PK_STRIDE>
+__device__ __noinline__ void half_topc_stored(const float* sc, int n_sub, KT (&tk)[C]) {
+  for (int g0 = 0; g0 < n_sub; g0 += C) {
+    KT gk[C];
+#pragma unroll
+    for (int q = 0; q < C; ++q) {
+      const int j = g0 + q;
+      gk[q] = j < n_sub ? pk_key(sc[j * PK_STRIDE], (uint32_t)j) : pk_key(-INFINITY, 0xFFFFFFFFu);
+    }
+    bitonic_sort_desc<C>(gk);
+    if (g0 == 0) {
+#pragma unroll
+      for (int q = 0; q < C; ++q) tk[q] = gk[q];
+    } else {
+      merge_top<C>(tk, gk);
+    }
+  }
+}
+
 template <int HALF>
 __device__ __forceinline__ void normalize_half(const float* src, float (&zn)[HALF]) {
   float ss = 0.f;
@@ -159,16 +267,42 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
   // the two halves one after the other through one register list (fewer live registers, more resident warps)
 #pragma unroll 1
   for (int hf = 0; hf < 2; ++hf) {
-    KT tk[C];
     float zn[HALF];
     normalize_half<HALF>(zr + hf * HALF, zn);
-    half_topc<HALF, C>(zn, hf ? kn2 : kn1, n_sub, tk);
     float* vs = hf ? v2s : v1s;
     int* is = hf ? i2s : i1s;
+    bool done = false;
+    if constexpr (C <= 16) {
+      if (n_sub <= 32) {
+        float* sc = ov + tid;  // this thread's scores (the emitted-score rows are free until the walk)
+        uint32_t tf[C];
+        if (half_topc_fast<HALF, C, PK_THREADS>(zn, hf ? kn2 : kn1, n_sub, sc, tf)) {
 #pragma unroll
-    for (int q = 0; q < C; ++q) {
-      vs[q * PK_THREADS + tid] = pk_key_score(tk[q]);
-      is[q * PK_THREADS + tid] = (int)pk_key_tie(tk[q]);
+          for (int q = 0; q < C; ++q) {
+            const uint32_t j = FK_MASK - (tf[q] & FK_MASK);
+            vs[q * PK_THREADS + tid] = tf[q] ? sc[j * PK_THREADS] : -INFINITY;
+            is[q * PK_THREADS + tid] = tf[q] ? (int)j : -1;
+          }
+        } else {
+          KT tk[C];
+          half_topc_stored<C, PK_THREADS>(sc, n_sub, tk);
+#pragma unroll
+          for (int q = 0; q < C; ++q) {
+            vs[q * PK_THREADS + tid] = pk_key_score(tk[q]);
+            is[q * PK_THREADS + tid] = (int)pk_key_tie(tk[q]);
+          }
+        }
+        done = true;
+      }
+    }
+    if (!done) {
+      KT tk[C];
+      half_topc<HALF, C>(zn, hf ? kn2 : kn1, n_sub, tk);
+#pragma unroll
+      for (int q = 0; q < C; ++q) {
+        vs[q * PK_THREADS + tid] = pk_key_score(tk[q]);
+        is[q * PK_THREADS + tid] = (int)pk_key_tie(tk[q]);
+      }
     }
   }
   // frontier walk over the c1 x c1 grid: row r's next candidate is (r, b_r), held as the key of its combined
@@ -244,7 +378,9 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
 
 template <int HALF, int C>
 static cudaError_t launch_pk_tc(const PkArgs& a, int c1, int kk, cudaStream_t st) {
-  const size_t smem = (size_t)2 * a.n_sub * HALF * 4 + (size_t)4 * C * PK_THREADS * 4 + (size_t)2 * kk * PK_THREADS * 4;
+  const size_t emit_rows = (size_t)(2 * kk > a.n_sub ? 2 * kk : a.n_sub);  // emitted (score, id) rows; the fast
+  // path first keeps a half's n_sub scores there
+  const size_t smem = (size_t)2 * a.n_sub * HALF * 4 + (size_t)4 * C * PK_THREADS * 4 + emit_rows * PK_THREADS * 4;
   auto kern = pk_kernel<HALF, C>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

@@ -68,6 +68,27 @@ def test_pk_address_matches_oracle_bitwise_order(cuda_ok):
         assert (si == si_o).all(-1)[live & gaps].all()
 
 
+def test_pk_address_exact_ties_follow_index_order(cuda_ok):
+    """Duplicated sub-keys give exactly equal scores (in the kernel and in the oracle alike); the selection then
+    breaks ties by sub-key index and the combine by flat index, as the oracle does.  Equal scores also make the
+    kernel's 32-bit fast path give up, so this covers its exact fallback."""
+    rng = np.random.default_rng(11)
+    for n_sub, k in ((32, 16), (16, 8)):
+        z = rng.standard_normal((2000, 2, 32)).astype(np.float32)
+        k1 = rng.standard_normal((2, n_sub, 16)).astype(np.float32)
+        k2 = rng.standard_normal((2, n_sub, 16)).astype(np.float32)
+        k1[:, 1::2] = k1[:, 0::2]  # every sub-key twice: every half score appears twice
+        k2[:, 3::4] = k2[:, 0::4]
+        sv_o, si_o, margin = O.pk_address(z, k1, k2, k, return_margin=True)
+        sv, si = S.pk_address(t(z), t(k1), t(k2), k)
+        sv, si = sv.cpu().numpy(), si.cpu().numpy()
+        d = np.abs(np.diff(sv_o, axis=-1))
+        clean = ((d == 0) | (d > 1e-6)).all(-1) & (margin > 1e-6)  # ties exact, every other gap wide
+        assert clean.mean() > 0.2
+        assert (si == si_o).all(-1)[clean].all(), (n_sub, k)
+        np.testing.assert_allclose(sv, sv_o, atol=1e-6)
+
+
 RT_CASES = ["rt_config1", "rt_small_plain", "rt_small_learned", "rt_small_sumread", "rt_small_nogate",
             "rt_small_bos", "rt_prevtok"]
 
