@@ -411,6 +411,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
   } else if constexpr (DH > 0) {
     // eight lanes per token: lane gl owns the float4 columns gl, gl + 8, ... of the head
     constexpr int NQ = DH / 32;
+    const bool masks = misc[11] == 0;  // the per-slot token masks hold every entry (no token repeated a slot)
     const int grp = lane >> 3, gl = lane & 7;
     const float4* V4 = reinterpret_cast<const float4*>(V_s);
     const bool vst = (reinterpret_cast<uintptr_t>(a.num) & 15) == 0;
@@ -422,39 +423,63 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
       for (int q = 0; q < NQ; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
       float dsum = 0.f;
       const int lo = tv ? max(wsl[t], 0) : 0;
-      // lane gl of the token's group holds reads gl, gl + 8, ...: slot run (start | count << 16) and weight
+      // lane gl of the token's group holds reads gl, gl + 8, ...: slot run (start | count << 16), the slot's
+      // token mask and the read weight
       constexpr int NR = (K > 0 ? K : SCAN_MAX_K) / 8 > 0 ? (K > 0 ? K : SCAN_MAX_K) / 8 : 1;
       int rr[NR];
+      unsigned long long rm[NR];
       float rw[NR];
 #pragma unroll
       for (int m = 0; m < NR; ++m) {
         const int i = gl + 8 * m;
-        rr[m] = (tv && i < k) ? run[sir_s[t * k + i]] : 0;
-        rw[m] = (tv && i < k) ? wr_s[t * k + i] : 0.f;
+        const int r = (tv && i < k) ? sir_s[t * k + i] : -1;
+        rr[m] = r >= 0 ? run[r] : 0;
+        rm[m] = (r >= 0 && masks) ? tmask[r] : 0ull;
+        rw[m] = r >= 0 ? wr_s[t * k + i] : 0.f;
       }
+      // sources of token t: tokens lo .. t-1 of the chunk
+      const unsigned long long win = tv ? (((1ull << t) - 1ull) & ~((1ull << lo) - 1ull)) : 0ull;
       for (int i = 0; i < k; ++i) {
         int ri = rr[0];
+        unsigned long long mi = rm[0];
         float wi = rw[0];
 #pragma unroll
         for (int m = 1; m < NR; ++m)
           if ((i >> 3) == m) {
             ri = rr[m];
+            mi = rm[m];
             wi = rw[m];
           }
-        const int rs = __shfl_sync(FULL, ri, (lane & 24) | (i & 7));
-        const float w = __shfl_sync(FULL, wi, (lane & 24) | (i & 7));
+        const int src = (lane & 24) | (i & 7);
+        const int rs = __shfl_sync(FULL, ri, src);
+        const float w = __shfl_sync(FULL, wi, src);
         const int st = rs & 0xFFFF, en = st + (rs >> 16);
-        int2 nq = st < en ? ent[st] : make_int2(0xFFFF, 0);
-        for (int x = st; x < en; ++x) {
-          const int2 q2 = nq;
-          if (x + 1 < en) nq = ent[x + 1];
-          const int s = q2.x & 0xFFFF;
-          if (s >= t) break;
-          if (s < lo) continue;
-          const float cf = w * __int_as_float(q2.y) * lampow[t - 1 - s];
-          dsum += cf;
+        if (masks) {
+          // the slot's entries are in token order, so token s's entry sits at st + (earlier tokens in the mask)
+          const unsigned long long tm = ((unsigned long long)__shfl_sync(FULL, (unsigned)(mi >> 32), src) << 32) |
+                                        __shfl_sync(FULL, (unsigned)mi, src);
+          unsigned long long mm = tm & win;
+          while (mm) {
+            const int s = __ffsll((long long)mm) - 1;
+            mm &= mm - 1ull;
+            const int2 q2 = ent[st + __popcll(tm & ((1ull << s) - 1ull))];
+            const float cf = w * __int_as_float(q2.y) * lampow[t - 1 - s];
+            dsum += cf;
 #pragma unroll
-          for (int q = 0; q < NQ; ++q) fma4(acc[q], cf, V4[s * (DH / 4) + gl + 8 * q]);
+            for (int q = 0; q < NQ; ++q) fma4(acc[q], cf, V4[s * (DH / 4) + gl + 8 * q]);
+          }
+        } else {
+          // a token wrote one slot twice: walk the run (entries in token, then write order)
+          for (int x = st; x < en; ++x) {
+            const int2 q2 = ent[x];
+            const int s = q2.x & 0xFFFF;
+            if (s >= t) break;
+            if (s < lo) continue;
+            const float cf = w * __int_as_float(q2.y) * lampow[t - 1 - s];
+            dsum += cf;
+#pragma unroll
+            for (int q = 0; q < NQ; ++q) fma4(acc[q], cf, V4[s * (DH / 4) + gl + 8 * q]);
+          }
         }
       }
       if (!tv) continue;
