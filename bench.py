@@ -16,7 +16,8 @@ Every step's working set (activations, 0.4 GB per layer) is larger than the 126 
 
 The JSON line adds: e2e (the same step through the public API from pinned host ids, H2D + D2H inside the timed
 region), decode (config 4: 32 streams per GPU carried-state greedy decode after a 2,048-token prefill), roofline of
-the dominant kernel (measured live with CUDA events around every launch of the timed region), cpu_baseline (the CPU
+the dominant kernel (measured live with CUDA events around every launch of a profiled pass of the same K steps on
+one row stream, right after the timed region), cpu_baseline (the CPU
 oracle port of the reference algorithm, bounded sample, rank 0 at N = 1), clocks sampled during the timed region.
 """
 import argparse
@@ -241,6 +242,9 @@ NCU_DRAM_PER_TOKEN = {
 }
 
 
+ROW_STREAMS = 2  # rows split over two CUDA streams in the timed steps (OneSdmLM.loss_sum row_streams)
+
+
 def kernel_bytes(kernel, tag, tokens):
     """Algorithmic HBM bytes of one launch of a memory-bound kernel of the step: its inputs read once and its
     outputs written once, per (token, head) of the call site (k slot ids + weights are 8 B per pair)."""
@@ -290,10 +294,10 @@ def run_ours(a):
     tgt = tgt_host.to(dev)
     loss_buf = torch.zeros(2, dtype=torch.float64, device=dev)  # (loss sum, token count)
 
-    def step(idx, tg):
+    def step(idx, tg, row_streams=ROW_STREAMS):
         loss_buf.zero_()
         with torch.no_grad():
-            model.loss_sum(idx, tg, out=loss_buf[:1])
+            model.loss_sum(idx, tg, out=loss_buf[:1], row_streams=row_streams)
         loss_buf[1] = float(B * T)
         if world > 1:
             dist.all_reduce(loss_buf)
@@ -319,16 +323,22 @@ def run_ours(a):
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = lib.sdm_kernel_launch_count()
-    lib.sdm_profile_begin()
     e0.record(st)
     for _ in range(a.steps):
         step(ids, tgt)
     e1.record(st)
     torch.cuda.synchronize()
-    groups = _lib.profile_groups()
     launches = lib.sdm_kernel_launch_count() - n0
     barrier()
     clk = clocks.stop()
+    # per-kernel CUDA events around every launch, in a pass of the same K steps on one row stream (with two
+    # streams the per-launch events cost ~10 % and overlapping launches would share their time)
+    lib.sdm_profile_begin()
+    for _ in range(a.steps):
+        step(ids, tgt, row_streams=1)
+    torch.cuda.synchronize()
+    groups = _lib.profile_groups()
+    barrier()
     t_dev = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     loss_mean = float(loss_buf[0].item() / loss_buf[1].item())
     tokens = world * B * T * a.steps
@@ -354,7 +364,7 @@ def run_ours(a):
     e2e = {"value": round(tokens / t_e2e, 1), "unit": "tokens/s",
            "h2d_bytes_per_step": int(ids_host.numel() * 4 + tgt_host.numel() * 4), "d2h_bytes_per_step": 16}
 
-    # roofline of the dominant kernel, from the events recorded around every launch of the timed region
+    # roofline of the dominant kernel, from the events recorded around every launch of the profiled pass
     pk, how = peaks()
     per_kernel = {}
     for k, tag, n, ms in groups:
@@ -433,8 +443,9 @@ def run_ours(a):
                "config": {"workload": f"FULL onesdm_allsdm d768 L{a.layers} h12x64 M1024 k16, TrainedSdm n_sub72 "
                                       f"k32, V32768, {B} rows x {T} tokens per GPU",
                           "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world} (batch shards)",
-                          "l2": "per-step working set > 126 MB L2 (no flush)"},
+                          "row_streams": ROW_STREAMS, "l2": "per-step working set > 126 MB L2 (no flush)"},
                "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu,
+               "profiled_pass": f"{a.steps} steps, one row stream, CUDA events around every launch (roofline, kernels)",
                "clocks": clk, "decode": decode, "loss_mean": round(loss_mean, 5), "kernels": breakdown}
         print(json.dumps(out), flush=True)
     if world > 1:

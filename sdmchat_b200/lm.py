@@ -146,10 +146,33 @@ class OneSdmLM(nn.Module):
         """OneSdmLM.forward (M:554-555): logits (B, T, V) = nf(residual(idx)) @ E^T, in the stream dtype."""
         return self._head(self.residual(idx, sequential), "logits")
 
-    def loss_sum(self, idx, targets, out=None):
+    def loss_sum(self, idx, targets, out=None, row_streams=1):
         """Sum over positions of the tied-head cross-entropy against `targets` (B, T) (entries < 0 skipped), as a
-        float64 device scalar accumulated into `out` if given; the logits are never materialised whole."""
-        return self._head(self.residual(idx), "ce", targets, out)
+        float64 device scalar accumulated into `out` if given; the logits are never materialised whole.
+
+        row_streams > 1 splits the rows (independent sequences) into that many groups, each run on its own CUDA
+        stream after the current one, so one group's kernels fill the other's partial waves; the current stream
+        waits for all of them.  The sum is the same up to the order of its float64 additions."""
+        B = idx.shape[0]
+        if row_streams <= 1 or B < row_streams:
+            return self._head(self.residual(idx), "ce", targets, out)
+        if out is None:
+            out = torch.zeros(1, dtype=torch.float64, device=idx.device)
+        main = torch.cuda.current_stream(idx.device)
+        key = (idx.device.index, row_streams)
+        cache = self.__dict__.setdefault("_row_stream_cache", {})
+        if key not in cache:  # created once: a new stream per call would cost host time and hardware queues
+            cache[key] = [torch.cuda.Stream(idx.device) for _ in range(row_streams)]
+        side = cache[key]
+        bounds = [B * i // row_streams for i in range(row_streams + 1)]
+        for s in side:
+            s.wait_stream(main)
+        for s, r0, r1 in zip(side, bounds[:-1], bounds[1:]):
+            with torch.cuda.stream(s):
+                self._head(self.residual(idx[r0:r1]), "ce", targets[r0:r1], out)
+        for s in side:
+            main.wait_stream(s)
+        return out
 
     def memory_parameters(self):
         return {n for n, _ in self.named_parameters() if n.startswith("mems.")}

@@ -143,3 +143,16 @@ def test_full_decode_matches_prefill(cuda_ok):
     clear = (top[..., 0] - top[..., 1]) > 1e-2
     assert (lg.argmax(-1) == gen)[clear].all()
     assert clear.float().mean() > 0.5
+
+
+def test_loss_sum_row_streams_equal(cuda_ok):
+    """Rows split over two CUDA streams give the same CE sum (up to the order of float64 additions)."""
+    rng = np.random.default_rng(6)
+    model = full_model(layers=2, seed=3)
+    idx = torch.from_numpy(zipf_ids(rng, (4, 512))).to(DEV)
+    tgt = torch.roll(idx, -1, 1)
+    with torch.no_grad():
+        a = float(model.loss_sum(idx, tgt).item())
+        b = float(model.loss_sum(idx, tgt, row_streams=2).item())
+        c = float(model.loss_sum(idx, tgt, row_streams=2).item())
+    assert abs(a - b) <= 1e-12 * abs(a) and abs(b - c) <= 1e-12 * abs(a)
