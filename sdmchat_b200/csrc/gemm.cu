@@ -78,11 +78,14 @@ cudaError_t launch_gemm_simt(const TA* x, int64_t ldx, const TA* w, int64_t ldw,
 
 // ---------------------------------------------------------------------------------------------- skinny GEMM
 // Decode-sized products (at most 32 rows): the tile GEMMs would keep only a handful of SMs busy, so here every warp
-// owns output columns.  x is staged once per CTA in shared memory; a warp streams one weight row (16 bytes per lane
+// owns one output column.  The rows are staged once per CTA in shared memory as float32, K_eff = kwrap columns at a
+// time (up to SK_KC): with a K wrap (x = [hi | lo] against one w) the copies are added as they are staged, which is
+// exact for a bf16 hi/lo split and leaves one product per weight.  A warp streams its weight row (16 bytes per lane
 // per step, coalesced), accumulates all rows' partial dot products in registers, and a 31-shuffle reduce-scatter
 // butterfly leaves row m's sum in lane m, which applies the epilogue.
 constexpr int SK_WARPS = 8;
 constexpr int SK_MAX_ROWS = 32;
+constexpr int SK_KC = 1024;  // staged columns per pass (32 rows x 1024 x 4 B = 128 KB)
 
 template <typename TA>
 struct Vec8 {
@@ -110,67 +113,82 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_kernel(const TA* __
                                                                    const TA* __restrict__ w, int64_t ldw, int rows,
                                                                    int K, int n, Epi epi, int kwrap) {
   extern __shared__ __align__(16) unsigned char sk_smem[];
-  TA* xs = reinterpret_cast<TA*>(sk_smem);  // (rows, K)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int vec_per_row = K / 8;
-  for (int i = tid; i < rows * vec_per_row; i += SK_WARPS * 32) {
-    const int r = i / vec_per_row, c = (i % vec_per_row) * 8;
-    if constexpr (sizeof(TA) == 2) {
-      *reinterpret_cast<uint4*>(xs + (int64_t)r * K + c) = *reinterpret_cast<const uint4*>(x + r * ldx + c);
-    } else {
-      reinterpret_cast<float4*>(xs + (int64_t)r * K + c)[0] = reinterpret_cast<const float4*>(x + r * ldx + c)[0];
-      reinterpret_cast<float4*>(xs + (int64_t)r * K + c)[1] = reinterpret_cast<const float4*>(x + r * ldx + c)[1];
+  const int col = blockIdx.x * SK_WARPS + warp;
+  const int copies = K / kwrap;
+  float* xs = reinterpret_cast<float*>(sk_smem);  // (rows, kc) float32
+  float acc[SK_MAX_ROWS];
+#pragma unroll
+  for (int m = 0; m < SK_MAX_ROWS; ++m) acc[m] = 0.f;
+  const TA* wr = w + (int64_t)(col < n ? col : 0) * ldw;
+  for (int k0 = 0; k0 < kwrap; k0 += SK_KC) {
+    const int kc = min(SK_KC, kwrap - k0);
+    const int vpr = kc / 8;  // 8-column vectors per row
+    __syncthreads();          // the previous pass's reads of xs are done
+    for (int i = tid; i < rows * vpr; i += SK_WARPS * 32) {
+      const int r = i / vpr, c = (i - r * vpr) * 8;
+      Vec8<TA> v = load8(x + (int64_t)r * ldx + k0 + c);
+      for (int cp = 1; cp < copies; ++cp) {
+        const Vec8<TA> u = load8(x + (int64_t)r * ldx + (int64_t)cp * kwrap + k0 + c);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v.v[e] += u.v[e];
+      }
+      float4* d = reinterpret_cast<float4*>(xs + (int64_t)r * kc + c);
+      d[0] = make_float4(v.v[0], v.v[1], v.v[2], v.v[3]);
+      d[1] = make_float4(v.v[4], v.v[5], v.v[6], v.v[7]);
     }
-  }
-  __syncthreads();
-  for (int col = blockIdx.x * SK_WARPS + warp; col < n; col += gridDim.x * SK_WARPS) {
-    float acc[SK_MAX_ROWS];
+    __syncthreads();
+    if (col < n) {
+      for (int kk = lane * 8; kk < kc; kk += 256) {
+        const Vec8<TA> wv = load8(wr + k0 + kk);
 #pragma unroll
-    for (int m = 0; m < SK_MAX_ROWS; ++m) acc[m] = 0.f;
-    const TA* wr = w + (int64_t)col * ldw;
-    for (int k0 = lane * 8; k0 < K; k0 += 256) {
-      const Vec8<TA> wv = load8(wr + (k0 % kwrap));
-#pragma unroll
-      for (int m = 0; m < SK_MAX_ROWS; ++m) {
-        if (m < rows) {
-          const Vec8<TA> xv = load8(xs + (int64_t)m * K + k0);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[m] = fmaf(xv.v[e], wv.v[e], acc[m]);
+        for (int m = 0; m < SK_MAX_ROWS; ++m) {
+          if (m < rows) {
+            const float4 a = *reinterpret_cast<const float4*>(xs + (int64_t)m * kc + kk);
+            const float4 b = *reinterpret_cast<const float4*>(xs + (int64_t)m * kc + kk + 4);
+            acc[m] = fmaf(a.x, wv.v[0], acc[m]);
+            acc[m] = fmaf(a.y, wv.v[1], acc[m]);
+            acc[m] = fmaf(a.z, wv.v[2], acc[m]);
+            acc[m] = fmaf(a.w, wv.v[3], acc[m]);
+            acc[m] = fmaf(b.x, wv.v[4], acc[m]);
+            acc[m] = fmaf(b.y, wv.v[5], acc[m]);
+            acc[m] = fmaf(b.z, wv.v[6], acc[m]);
+            acc[m] = fmaf(b.w, wv.v[7], acc[m]);
+          }
         }
       }
     }
-    // reduce-scatter: after the step of width o, this lane keeps the rows whose bit matches its lane bit
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const bool upper = (lane & o) != 0;
-#pragma unroll
-      for (int i = 0; i < o; ++i) {
-        const float mine = upper ? acc[i + o] : acc[i];
-        const float other = upper ? acc[i] : acc[i + o];
-        acc[i] = mine + __shfl_xor_sync(0xffffffffu, other, o);
-      }
-    }
-    if (lane < rows) epi.apply(lane, col, acc[0]);
   }
+  if (col >= n) return;
+  // reduce-scatter: after the step of width o, this lane keeps the rows whose bit matches its lane bit
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float mine = upper ? acc[i + o] : acc[i];
+      const float other = upper ? acc[i] : acc[i + o];
+      acc[i] = mine + __shfl_xor_sync(0xffffffffu, other, o);
+    }
+  }
+  if (lane < rows) epi.apply(lane, col, acc[0]);
 }
 
 template <typename TA>
 static bool skinny_ok(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int kwrap) {
-  const size_t smem = (size_t)rows * K * sizeof(TA);
   const uintptr_t ax = reinterpret_cast<uintptr_t>(x), aw = reinterpret_cast<uintptr_t>(w);
   return rows >= 1 && rows <= SK_MAX_ROWS && K % 8 == 0 && kwrap % 8 == 0 && ldx % 8 == 0 && ldw % 8 == 0 &&
-         ax % 16 == 0 && aw % 16 == 0 && smem <= 160 * 1024;
+         ax % 16 == 0 && aw % 16 == 0;
 }
 
 template <typename TA, typename Epi>
 static cudaError_t launch_gemm_skinny(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int n,
                                      Epi epi, cudaStream_t st, int kwrap) {
-  const size_t smem = (size_t)rows * K * sizeof(TA);
+  const size_t smem = (size_t)rows * (kwrap < SK_KC ? kwrap : SK_KC) * sizeof(float);
   auto kern = gemm_skinny_kernel<TA, Epi>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  int64_t grid = ceil_div(n, SK_WARPS);
-  if (grid > 148 * 2) grid = 148 * 2;
+  const int64_t grid = ceil_div(n, SK_WARPS);
   LaunchScope scope_("gemm_skinny", st);
   kern<<<(unsigned)grid, SK_WARPS * 32, smem, st>>>(x, ldx, w, ldw, (int)rows, K, n, epi, kwrap);
   return cudaGetLastError();

@@ -114,9 +114,9 @@ __global__ void rt_finish_kernel(const float* __restrict__ num, const float* __r
 
 // The same finish for dh = 32 * STEPS: eight lanes per (token, head) row, each lane 4 consecutive columns per
 // 32-column step (16-byte loads), the row's sum of squares reduced over the eight lanes.  A lane group takes
-// FIN_ROWS consecutive rows and issues all their loads before the first use, so the loads overlap.
-constexpr int FIN_ROWS = 4;
-template <typename T, int STEPS>
+// FIN_ROWS consecutive rows (4 for large launches, 1 for decode-sized ones) and issues all their loads before the
+// first use, so the loads overlap.
+template <typename T, int STEPS, int FIN_ROWS>
 __global__ void __launch_bounds__(256) rt_finish_vec_kernel(const float* __restrict__ num, const float* __restrict__ den,
                                                             int64_t N, int h, int read_sum, float read_eps,
                                                             int out_norm, float out_norm_eps,
@@ -279,16 +279,22 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
   LaunchScope scope_("rt_finish", st);
   const bool al = ((reinterpret_cast<uintptr_t>(num) | reinterpret_cast<uintptr_t>(onorm_w)) & 15) == 0;
   if (al && (dh == 64 || dh == 32 || dh == 128)) {
-    const unsigned grid = (unsigned)ceil_div(ceil_div(N * h, FIN_ROWS) * 8, 256);
+    // rows per lane group: 4 while that still leaves at least two waves of 148 SMs x 8 blocks, else 1
+    const bool big = N * h >= (int64_t)148 * 8 * 32 * 4 * 2;
+    const int rows_per = big ? 4 : 1;
+    const unsigned grid = (unsigned)ceil_div(ceil_div(N * h, rows_per) * 8, 256);
+#define SDM_FIN(STEPS)                                                                                          \
+  (big ? rt_finish_vec_kernel<T, STEPS, 4><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm,   \
+                                                                 out_norm_eps, onorm_w, r, split)                \
+       : rt_finish_vec_kernel<T, STEPS, 1><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm,   \
+                                                                 out_norm_eps, onorm_w, r, split))
     if (dh == 64)
-      rt_finish_vec_kernel<T, 2><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm, out_norm_eps,
-                                                      onorm_w, r, split);
+      SDM_FIN(2);
     else if (dh == 32)
-      rt_finish_vec_kernel<T, 1><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm, out_norm_eps,
-                                                      onorm_w, r, split);
+      SDM_FIN(1);
     else
-      rt_finish_vec_kernel<T, 4><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm, out_norm_eps,
-                                                      onorm_w, r, split);
+      SDM_FIN(4);
+#undef SDM_FIN
     return cudaGetLastError();
   }
   rt_finish_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(num, den, N, h, dh, read_sum, read_eps,
