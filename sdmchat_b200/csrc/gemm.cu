@@ -1,6 +1,6 @@
 // y = x @ w^T with a fused epilogue.  float32 operands run on CUDA cores (the SDM_F32 precision mode: exact
-// float32 products, float32 accumulation in k order); bfloat16 operands run on the tcgen05 tensor cores
-// (gemm_tc.cu) whenever the shape allows it.
+// float32 products, float32 accumulation in k order); bfloat16 operands run on the tensor cores: tcgen05
+// (gemm_tc.cu) for tile-sized row counts, mma.sync below for decode-sized ones (at most 32 rows).
 #include "kernels.cuh"
 
 namespace sdm {
@@ -194,12 +194,99 @@ static cudaError_t launch_gemm_skinny(const TA* x, int64_t ldx, const TA* w, int
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------------------------- small-M tensor-core GEMM
+// Decode-sized bf16 products (at most 32 rows) on the tensor cores with mma.sync m16n8k16 (bf16 operands, float32
+// accumulation: the products and accumulation precision of the tcgen05 path).  A CTA owns 8 output columns; its 8
+// warps split the K range in 64-wide blocks (a K wrap, x = [hi | lo] against one w, is just more blocks reading the
+// same weights), each warp covering all rows as two 16-row tiles; the 8 partial 32 x 8 tiles are summed in shared
+// memory in warp order, so results are deterministic.  Inside a 64-block thread t of a quad holds 16 consecutive k
+// of its A rows and B column (two 16-byte loads each) and feeds them to four k-steps: slots (2t, 2t+1, 2t+8, 2t+9)
+// of step s carry its values 4s .. 4s+3 -- the same permutation of k for A and B, so the dot products are unchanged.
+constexpr int SMT_WARPS = 8;
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t u4w(const uint4& u, int i) {
+  return i == 0 ? u.x : (i == 1 ? u.y : (i == 2 ? u.z : u.w));
+}
+
+template <typename Epi>
+__global__ void __launch_bounds__(SMT_WARPS * 32) gemm_small_tc_kernel(const bf16_t* __restrict__ x, int64_t ldx,
+                                                                      const bf16_t* __restrict__ w, int64_t ldw,
+                                                                      int rows, int K, int n, Epi epi, int kwrap) {
+  __shared__ float part[SMT_WARPS][32][9];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int n0 = blockIdx.x * 8;
+  const int nb = n0 + g;  // this thread's B column
+  const bf16_t* wrow = w + (int64_t)(nb < n ? nb : n - 1) * ldw;
+  float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  for (int kb = warp; kb < K / 64; kb += SMT_WARPS) {
+    const int k = kb * 64 + 16 * t, kw = k % kwrap;
+    const uint4 b0 = nb < n ? *reinterpret_cast<const uint4*>(wrow + kw) : z4;
+    const uint4 b1 = nb < n ? *reinterpret_cast<const uint4*>(wrow + kw + 8) : z4;
+    uint4 a[2][2][2];  // [row tile][row g | g + 8][k 0-7 | 8-15]
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int rh = 0; rh < 2; ++rh) {
+        const int row = mt * 16 + rh * 8 + g;
+        const bf16_t* xr = x + (int64_t)row * ldx + k;
+        a[mt][rh][0] = row < rows ? *reinterpret_cast<const uint4*>(xr) : z4;
+        a[mt][rh][1] = row < rows ? *reinterpret_cast<const uint4*>(xr + 8) : z4;
+      }
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const int h = s4 >> 1, wi = (s4 & 1) * 2;  // values 4*s4 .. 4*s4+3 are words wi, wi+1 of chunk h
+      const uint32_t bw0 = u4w(h ? b1 : b0, wi), bw1 = u4w(h ? b1 : b0, wi + 1);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+        mma_bf16_16816(c[mt], u4w(a[mt][0][h], wi), u4w(a[mt][1][h], wi), u4w(a[mt][0][h], wi + 1),
+                       u4w(a[mt][1][h], wi + 1), bw0, bw1);
+    }
+  }
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    part[warp][mt * 16 + g][2 * t] = c[mt][0];
+    part[warp][mt * 16 + g][2 * t + 1] = c[mt][1];
+    part[warp][mt * 16 + g + 8][2 * t] = c[mt][2];
+    part[warp][mt * 16 + g + 8][2 * t + 1] = c[mt][3];
+  }
+  __syncthreads();
+  const int row = tid >> 3, cc = tid & 7, col = n0 + cc;
+  float v = 0.f;
+#pragma unroll
+  for (int q = 0; q < SMT_WARPS; ++q) v += part[q][row][cc];
+  if (row < rows && col < n) epi.apply(row, col, v);
+}
+
+static bool small_tc_ok(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K, int kwrap) {
+  const uintptr_t ax = reinterpret_cast<uintptr_t>(x), aw = reinterpret_cast<uintptr_t>(w);
+  return rows >= 1 && rows <= 32 && K % 64 == 0 && kwrap % 64 == 0 && ldx % 8 == 0 && ldw % 8 == 0 &&
+         ax % 16 == 0 && aw % 16 == 0;
+}
+
 template <typename TA, typename Epi>
 cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int n, Epi epi,
                         cudaStream_t st, int kwrap) {
   if (kwrap <= 0) kwrap = K;
   if (K % kwrap) return cudaErrorInvalidValue;
   if (rows == 0 || n == 0) return cudaSuccess;
+  if constexpr (sizeof(TA) == 2) {
+    if (small_tc_ok(x, ldx, w, ldw, rows, K, kwrap)) {
+      LaunchScope scope_("gemm_small_tc", st);
+      gemm_small_tc_kernel<Epi><<<(unsigned)ceil_div(n, 8), SMT_WARPS * 32, 0, st>>>(x, ldx, w, ldw, (int)rows, K, n,
+                                                                                     epi, kwrap);
+      return cudaGetLastError();
+    }
+  }
   if (skinny_ok(x, ldx, w, ldw, rows, K, kwrap)) return launch_gemm_skinny<TA, Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
   if constexpr (sizeof(TA) == 2) {
     if (tc_gemm_supported(x, ldx, w, ldw, K, kwrap))

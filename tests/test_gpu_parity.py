@@ -232,7 +232,9 @@ def test_bf16_lm_decode_equals_prefix_forward(cuda_ok):
 
 def test_gemm_bf16_against_fp32_reference(cuda_ok):
     torch.manual_seed(0)
-    for rows, K, n in ((128, 64, 128), (1000, 768, 1548), (333, 256, 96), (4096, 2048, 768), (7, 768, 32768)):
+    # (7 | 1 | 32 rows: the decode-sized tensor-core kernel; 5 x 72: the CUDA-core skinny kernel; rest: tcgen05)
+    for rows, K, n in ((128, 64, 128), (1000, 768, 1548), (333, 256, 96), (4096, 2048, 768), (7, 768, 32768),
+                       (1, 768, 1548), (32, 1536, 768), (17, 2048, 100), (5, 72, 40)):
         x = torch.randn(rows, K, device=DEV).bfloat16()
         w = torch.randn(n, K, device=DEV).bfloat16()
         y = torch.empty(rows, n, device=DEV)
