@@ -400,24 +400,47 @@ static cudaError_t launch_pk_half(const PkArgs& a, int c1, int kk, cudaStream_t 
 
 // ------------------------------------------------------------------------------------ warp-per-address variant
 // For launches with few addresses (decode: tens of tokens), one thread's serial sort chain is the whole latency.
-// Here a warp owns an address: lanes score sub-keys in parallel, each half's top-c1 is taken by c1 rounds of a warp
-// arg-max under the same total order (score desc, index asc), and the frontier walk's arg-max over rows is a warp
-// reduction (row a lives in lane a).  Same selections, same order, same soft weights as pk_kernel.
+// Here a warp owns an address and both stages are warp-wide bitonic sorts of the same 64-bit (score, tie) keys as
+// the thread kernel (so the selections and their order are identical): (1) each half's n_sub scores, lane l holding
+// sub-keys l*S .. l*S+S-1 (S = 1, 2 or 4 slots per lane), give the sorted top-c1; (2) the combined candidates
+// (a, b) with (a+1)(b+1) <= kk -- a superset of the top-kk, since every pair (a', b') <= (a, b) ranks before
+// (a, b) -- are sorted by (combined score desc, flat index a*c1+b asc) and the first kk are the selection.
 constexpr int PKW_WARPS = 4;
 
-__device__ __forceinline__ void warp_best(float& v, int& i) {
+// Descending bitonic sort of the warp's 32*S keys, element e = lane*S + s in v[s].
+template <int S>
+__device__ __forceinline__ void warp_sort_desc(KT (&v)[S]) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
-    if (better(ov, oi, v, i)) {
-      v = ov;
-      i = oi;
+  for (int size = 2; size <= 32 * S; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride >= S) {  // partner in another lane, same slot
+        const int lm = stride / S;
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          const int e = lane * S + q;
+          const KT o = __shfl_xor_sync(0xffffffffu, v[q], lm);
+          const bool keep_max = ((lane & lm) == 0) == ((e & size) == 0);
+          v[q] = keep_max ? (v[q] > o ? v[q] : o) : (v[q] > o ? o : v[q]);
+        }
+      } else {  // partner in this lane
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          const int q2 = q ^ stride;
+          if (q2 > q) {
+            const bool desc = ((lane * S + q) & size) == 0;
+            const KT hi = v[q] > v[q2] ? v[q] : v[q2], lo = v[q] > v[q2] ? v[q2] : v[q];
+            v[q] = desc ? hi : lo;
+            v[q2] = desc ? lo : hi;
+          }
+        }
+      }
     }
   }
 }
 
-template <int HALF>
+template <int HALF, int S>
 __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c1, int kk) {
   extern __shared__ float pkw_smem[];
   const int hh = blockIdx.y % a.h, pr = blockIdx.y / a.h;  // pr: which address set of a paired launch
@@ -435,6 +458,8 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
   int* i1 = reinterpret_cast<int*>(wsm + 32);
   float* v2 = wsm + 64;
   int* i2 = reinterpret_cast<int*>(wsm + 96);
+  int* cand = reinterpret_cast<int*>(pkw_smem + 2 * n_sub * HALF + PKW_WARPS * 4 * 32);  // (a << 8 | b) pairs
+  int* ncand = cand + 32 * S;
   for (int j = tid; j < 2 * n_sub; j += PKW_WARPS * 32) {
     const float* src = (j < n_sub ? a.keys1 + ((int64_t)hh * n_sub + j) * HALF
                                   : a.keys2 + ((int64_t)hh * n_sub + (j - n_sub)) * HALF);
@@ -444,76 +469,60 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
 #pragma unroll
     for (int dd = 0; dd < HALF; ++dd) dst[dd] = kv[dd];
   }
+  if (tid == 0) {  // the candidate pairs, in (a, b) order
+    int nc = 0;
+    for (int ra = 0; ra < c1; ++ra)
+      for (int rb = 0; rb < c1 && (ra + 1) * (rb + 1) <= kk; ++rb) cand[nc++] = (ra << 8) | rb;
+    *ncand = nc;
+  }
   __syncthreads();
   const int64_t n = (int64_t)blockIdx.x * PKW_WARPS + warp;
   if (n >= a.N) return;
   const float* zr = zb + n * a.ldz + (int64_t)hh * a.d_a;
-  // each half: lanes score sub-keys lane, lane+32, ...; c1 rounds of warp arg-max give the sorted top-c1
 #pragma unroll 1
   for (int hf = 0; hf < 2; ++hf) {
     float zn[HALF];
     normalize_half<HALF>(zr + hf * HALF, zn);
     const float* kn = hf ? kn2 : kn1;
-    float sc[4];
+    KT key[S];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int j = lane + 32 * q;
-      float s = -INFINITY;
+    for (int q = 0; q < S; ++q) {
+      const int j = lane * S + q;
+      key[q] = 0ull;  // padding: below every real key
       if (j < n_sub) {
-        s = 0.f;
+        float sc = 0.f;
 #pragma unroll
-        for (int dd = 0; dd < HALF; ++dd) s = fmaf(zn[dd], kn[j * HALF + dd], s);
-        if (s != s) s = -INFINITY;
+        for (int dd = 0; dd < HALF; ++dd) sc = fmaf(zn[dd], kn[j * HALF + dd], sc);
+        if (sc != sc) sc = -INFINITY;
+        key[q] = pk_key(sc, (uint32_t)j);
       }
-      sc[q] = s;
     }
+    warp_sort_desc<S>(key);
     float* vo = hf ? v2 : v1;
     int* io = hf ? i2 : i1;
-    unsigned used = 0;  // this lane's candidates already taken
-    for (int r = 0; r < c1; ++r) {
-      // this lane's best remaining candidate, then the warp's
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int j = lane + 32 * q;
-        if (j < n_sub && !((used >> q) & 1u) && better(sc[q], j, bv, bi)) {
-          bv = sc[q];
-          bi = j;
-        }
+    for (int q = 0; q < S; ++q) {
+      const int e = lane * S + q;
+      if (e < c1) {
+        vo[e] = pk_key_score(key[q]);
+        io[e] = (int)pk_key_tie(key[q]);
       }
-      warp_best(bv, bi);
-      if (lane == 0) {
-        vo[r] = bv;
-        io[r] = bi;
-      }
-      if ((bi & 31) == lane) used |= 1u << (bi >> 5);  // retire the winner
     }
     __syncwarp();
   }
-  // frontier: lane a holds row a's next candidate (a, fb)
-  int fb = 0;
-  const float v1a = lane < c1 ? v1[lane] : -INFINITY;
-  const int i1a = lane < c1 ? i1[lane] : 0;
-  float fv = lane < c1 ? (v1a + v2[0]) * 0.5f : -INFINITY;
-  float out_v = 0.f;
-  int out_i = 0;
-  for (int step = 0; step < kk; ++step) {
-    float bv = fv;
-    int bflat = lane < c1 ? lane * c1 + fb : 0x7fffffff;
-    warp_best(bv, bflat);
-    const int ba = bflat / c1, bb = bflat - ba * c1;
-    const int slot = __shfl_sync(0xffffffffu, i1a, ba) * n_sub + i2[bb];
-    if (lane == step) {
-      out_v = bv;
-      out_i = slot;
-    }
-    if (lane == ba) {
-      fb = bb + 1;
-      fv = fb < c1 ? (v1a + v2[fb]) * 0.5f : -INFINITY;
+  // the combined candidates, sorted: the first kk elements are the selection in order
+  const int nc = *ncand;
+  KT ck[S];
+#pragma unroll
+  for (int q = 0; q < S; ++q) {
+    const int e = lane * S + q;
+    ck[q] = 0ull;
+    if (e < nc) {
+      const int ab = cand[e], ra = ab >> 8, rb = ab & 255;
+      ck[q] = pk_key((v1[ra] + v2[rb]) * 0.5f, (uint32_t)(ra * c1 + rb));
     }
   }
-  // outputs and softmax(scale * score) (* gate): lane j holds the j-th pick
+  warp_sort_desc<S>(ck);
   int64_t dst;
   if (a.T_bh > 0) {
     const int64_t bb = n / a.T_bh, t = n % a.T_bh;
@@ -521,37 +530,72 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
   } else {
     dst = (n * a.h + hh) * kk;
   }
-  const bool mine = lane < kk;
-  if (mine) {
-    sib[dst + lane] = out_i;
-    if (svb) svb[dst + lane] = out_v;
+  float sv[S], ex[S];
+  const float scale = wb ? expf(a.log_scale[hh]) : 0.f;
+  const float mx = pk_key_score(__shfl_sync(0xffffffffu, ck[0], 0)) * scale;  // the first pick is the largest
+#pragma unroll
+  for (int q = 0; q < S; ++q) {
+    const int e = lane * S + q;
+    sv[q] = pk_key_score(ck[q]);
+    ex[q] = e < kk ? expf(sv[q] * scale - mx) : 0.f;
+    if (e < kk) {
+      const int flat = (int)pk_key_tie(ck[q]), ra = flat / c1, rb = flat - ra * c1;
+      sib[dst + e] = i1[ra] * n_sub + i2[rb];
+      if (svb) svb[dst + e] = sv[q];
+    }
   }
   if (wb) {
-    const float scale = expf(a.log_scale[hh]);
-    const float x = mine ? out_v * scale : -INFINITY;
-    const float mx = warp_max(x);
-    const float e = mine ? expf(x - mx) : 0.f;
     // the sum in pick order, as the thread-per-address kernel adds it
     float sum = 0.f;
-    for (int j = 0; j < kk; ++j) sum += __shfl_sync(0xffffffffu, e, j);
-    if (mine) {
-      float wj = __fdiv_rn(e, sum);
-      if (gb) wj = wj * gb[n * a.ldgate + hh];
-      wb[dst + lane] = wj;
+    for (int j = 0; j < kk; ++j) {
+      float ej = ex[0];
+#pragma unroll
+      for (int q = 1; q < S; ++q)
+        if ((j % S) == q) ej = ex[q];
+      sum += __shfl_sync(0xffffffffu, ej, j / S);
+    }
+    const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
+#pragma unroll
+    for (int q = 0; q < S; ++q) {
+      const int e = lane * S + q;
+      if (e < kk) {
+        float wj = __fdiv_rn(ex[q], sum);
+        if (gb) wj = wj * g;
+        wb[dst + e] = wj;
+      }
     }
   }
 }
 
-template <int HALF>
-static cudaError_t launch_pk_warp(const PkArgs& a, int c1, int kk, cudaStream_t st) {
-  const size_t smem = (size_t)2 * a.n_sub * HALF * 4 + (size_t)PKW_WARPS * 4 * 32 * 4;
-  auto kern = pk_warp_kernel<HALF>;
+template <int HALF, int S>
+static cudaError_t launch_pk_warp_s(const PkArgs& a, int c1, int kk, cudaStream_t st) {
+  const size_t smem = (size_t)2 * a.n_sub * HALF * 4 + (size_t)PKW_WARPS * 4 * 32 * 4 + (size_t)(32 * S + 1) * 4;
+  auto kern = pk_warp_kernel<HALF, S>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)ceil_div(a.N, PKW_WARPS), (unsigned)(a.h * (a.pairs > 1 ? 2 : 1)));
   LaunchScope scope_("pk_address", st);
   kern<<<grid, PKW_WARPS * 32, smem, st>>>(a, c1, kk);
   return cudaGetLastError();
+}
+
+// Slots per lane: enough for the n_sub scores of a half and for the candidate pairs.
+static int pk_warp_slots(int n_sub, int c1, int kk) {
+  int nc = 0;
+  for (int ra = 0; ra < c1; ++ra)
+    for (int rb = 0; rb < c1 && (ra + 1) * (rb + 1) <= kk; ++rb) ++nc;
+  const int need = n_sub > nc ? n_sub : nc;
+  return need <= 32 ? 1 : (need <= 64 ? 2 : (need <= 128 ? 4 : 0));
+}
+
+template <int HALF>
+static cudaError_t launch_pk_warp(const PkArgs& a, int c1, int kk, cudaStream_t st) {
+  switch (pk_warp_slots(a.n_sub, c1, kk)) {
+    case 1: return launch_pk_warp_s<HALF, 1>(a, c1, kk, st);
+    case 2: return launch_pk_warp_s<HALF, 2>(a, c1, kk, st);
+    case 4: return launch_pk_warp_s<HALF, 4>(a, c1, kk, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 // Launches with at most this many addresses use the warp-per-address kernel.

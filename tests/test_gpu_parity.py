@@ -68,6 +68,22 @@ def test_pk_address_matches_oracle_bitwise_order(cuda_ok):
         assert (si == si_o).all(-1)[live & gaps].all()
 
 
+def test_pk_address_warp_kernel_equals_thread_kernel(cuda_ok):
+    """Small launches (decode) take the warp-per-address kernel, large ones the thread-per-address kernel: both
+    give bit-identical slots, scores and weights on the same addresses (including exact ties)."""
+    rng = np.random.default_rng(13)
+    for n_sub, k, d_a in ((32, 16, 32), (72, 32, 32), (16, 8, 32), (9, 5, 12)):
+        z = rng.standard_normal((4000, 3, d_a)).astype(np.float32)
+        z[7] = 0.0  # a zero address: every score ties
+        k1 = rng.standard_normal((3, n_sub, d_a // 2)).astype(np.float32)
+        k2 = rng.standard_normal((3, n_sub, d_a // 2)).astype(np.float32)
+        k1[:, 1] = k1[:, 0]
+        big = S.pk_address(t(z), t(k1), t(k2), k)          # 12,000 addresses: thread kernel
+        small = S.pk_address(t(z[:50]), t(k1), t(k2), k)   # 150 addresses: warp kernel
+        for b_, s_ in zip(big, small):
+            assert torch.equal(b_[:50], s_), (n_sub, k)
+
+
 def test_pk_address_exact_ties_follow_index_order(cuda_ok):
     """Duplicated sub-keys give exactly equal scores (in the kernel and in the oracle alike); the selection then
     breaks ties by sub-key index and the combine by flat index, as the oracle does.  Equal scores also make the
