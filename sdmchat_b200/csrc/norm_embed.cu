@@ -26,6 +26,43 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
   }
 }
 
+// The same RMSNorm with the row held in registers: each lane loads NCH 16-byte chunks (chunk q of lane l covers
+// columns (l + 32 q) * E .. +E-1, E = 16 / sizeof(T)), so x is read once with coalesced 16-byte accesses.
+template <typename T, int NCH>
+__global__ void rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t rows, float eps,
+                                   T* __restrict__ y) {
+  constexpr int E = 16 / sizeof(T), D = NCH * 32 * E;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * D);
+  uint4 raw[NCH];
+#pragma unroll
+  for (int q = 0; q < NCH; ++q) raw[q] = xr[lane + 32 * q];
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < NCH; ++q) {
+    const T* v = reinterpret_cast<const T*>(&raw[q]);
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss = fmaf(to_f32(v[e]), to_f32(v[e]), ss);
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrt_rn(__fdiv_rn(ss, (float)D) + eps);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + row * D);
+#pragma unroll
+  for (int q = 0; q < NCH; ++q) {
+    const uint4 wv = wr[lane + 32 * q];
+    const T* v = reinterpret_cast<const T*>(&raw[q]);
+    const T* wt = reinterpret_cast<const T*>(&wv);
+    uint4 out;
+    T* o = reinterpret_cast<T*>(&out);
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[e] = from_f32<T>(round_to<T>(to_f32(v[e]) * r) * to_f32(wt[e]));
+    yr[lane + 32 * q] = out;
+  }
+}
+
 template <typename T>
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restrict__ emb, int64_t N, int d, int V,
                              T* __restrict__ out, int* bad) {
@@ -246,11 +283,79 @@ __global__ void ts_gather_vec_kernel(const int32_t* __restrict__ si, const float
   }
 }
 
+// Decode-sized gathers: a block of 8 warps takes 2 (token, head) items, each item's k rows split over 4 warps (k/4
+// loads in flight per warp), the 4 partial rows summed in shared memory in warp order.
+__global__ void __launch_bounds__(256) ts_gather_split_kernel(const int32_t* __restrict__ si,
+                                                              const float* __restrict__ w,
+                                                              const bf16_t* __restrict__ values, int64_t N, int h,
+                                                              int M, int dh, int k, bf16_t* __restrict__ r, int split) {
+  __shared__ float part[8][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * 2 + (warp >> 2);
+  const int sp = warp & 3;
+  const bool live = item < N * h;
+  const int hh = live ? (int)(item % h) : 0;
+  const int jn = (k + 3) / 4, j0 = sp * jn, j1 = min(k, j0 + jn);
+  const int my_s = live && j0 + lane < j1 ? si[item * k + j0 + lane] : 0;
+  const float my_w = live && j0 + lane < j1 ? w[item * k + j0 + lane] : 0.f;
+  const bool active = live && 8 * lane < dh;
+  const bf16_t* base = values + (int64_t)hh * M * dh + 8 * lane;
+  float acc[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+#pragma unroll 8
+  for (int j = 0; j < j1 - j0; ++j) {
+    const int slot = __shfl_sync(0xffffffffu, my_s, j);
+    const float wj = __shfl_sync(0xffffffffu, my_w, j);
+    if (active) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)slot * dh));
+      const float4 a = unpack_bf16x4(make_uint2(u.x, u.y)), b = unpack_bf16x4(make_uint2(u.z, u.w));
+      acc[0] = fmaf(wj, a.x, acc[0]);
+      acc[1] = fmaf(wj, a.y, acc[1]);
+      acc[2] = fmaf(wj, a.z, acc[2]);
+      acc[3] = fmaf(wj, a.w, acc[3]);
+      acc[4] = fmaf(wj, b.x, acc[4]);
+      acc[5] = fmaf(wj, b.y, acc[5]);
+      acc[6] = fmaf(wj, b.z, acc[6]);
+      acc[7] = fmaf(wj, b.w, acc[7]);
+    }
+  }
+  if (active) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) part[warp][8 * lane + q] = acc[q];
+  }
+  __syncthreads();
+  if (sp == 0 && active) {
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = part[warp][8 * lane + q] + part[warp + 1][8 * lane + q] +
+                                      part[warp + 2][8 * lane + q] + part[warp + 3][8 * lane + q];
+    const int64_t n = item / h, c = (int64_t)hh * dh + 8 * lane;
+    store_split4<bf16_t>(r, n, (int64_t)h * dh, c, make_float4(v[0], v[1], v[2], v[3]), split);
+    store_split4<bf16_t>(r, n, (int64_t)h * dh, c + 4, make_float4(v[4], v[5], v[6], v[7]), split);
+  }
+}
+
 // ------------------------------------------------------------------------------------------------- launchers
 template <typename T>
 cudaError_t launch_rmsnorm(const T* x, const T* w, int64_t rows, int d, float eps, T* y, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   LaunchScope scope_("rmsnorm", st);
+  constexpr int E = 16 / sizeof(T);
+  const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) &
+                   15) == 0;
+  const int nch = d % (32 * E) == 0 ? d / (32 * E) : 0;
+  if (al && nch >= 1 && nch <= 4) {
+    const int wpb = rows < 148 * 8 ? 2 : 8;  // small launches: fewer warps per block, more SMs
+    const unsigned grid = (unsigned)ceil_div(rows, wpb);
+    switch (nch) {
+      case 1: rmsnorm_vec_kernel<T, 1><<<grid, wpb * 32, 0, st>>>(x, w, rows, eps, y); break;
+      case 2: rmsnorm_vec_kernel<T, 2><<<grid, wpb * 32, 0, st>>>(x, w, rows, eps, y); break;
+      case 3: rmsnorm_vec_kernel<T, 3><<<grid, wpb * 32, 0, st>>>(x, w, rows, eps, y); break;
+      default: rmsnorm_vec_kernel<T, 4><<<grid, wpb * 32, 0, st>>>(x, w, rows, eps, y); break;
+    }
+    return cudaGetLastError();
+  }
   rmsnorm_kernel<T><<<(unsigned)ceil_div(rows, 8), 256, 0, st>>>(x, w, rows, d, eps, y);
   return cudaGetLastError();
 }
@@ -308,6 +413,10 @@ cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values,
   LaunchScope scope_("ts_gather", st);
   if constexpr (sizeof(T) == 2) {
     if (dh % 8 == 0 && dh <= 256 && k <= 32 && (reinterpret_cast<uintptr_t>(values) & 15) == 0) {
+      if (N * h < 148 * 8) {  // decode-sized: spread each item's rows over four warps
+        ts_gather_split_kernel<<<(unsigned)ceil_div(N * h, 2), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r, split);
+        return cudaGetLastError();
+      }
       ts_gather_vec_kernel<<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r, split);
       return cudaGetLastError();
     }
