@@ -517,18 +517,21 @@ sdm_status sdm_rt_decode_step(const sdm_rt_params* p, const void* x, int S_, con
   da.cnt = cnt;
   da.scale = scale;
   da.last_w = last_w;
-  da.num = w.num;
-  da.den = w.den;
-  SDM_TRY(launch_rt_decode(da, st));
+  da.read_sum = p->read_sum;
+  da.read_eps = p->read_eps;
+  da.out_norm = p->out_norm;
+  da.out_norm_eps = p->out_norm_eps;
+  da.onorm_w = p->onorm_w;
+  da.r = w.rbuf;
   if (p->dtype == SDM_BF16) {
-    SDM_TRY(launch_rt_finish<bf16_t>(w.num, w.den, S_, h, dh, p->read_sum, p->read_eps, p->out_norm, p->out_norm_eps,
-                                     p->onorm_w, (bf16_t*)w.rbuf, 1, st));
+    da.split = 1;
+    SDM_TRY(launch_rt_decode<bf16_t>(da, st));
     EpiResid<bf16_t> er{add_residual ? (const bf16_t*)x : nullptr, (bf16_t*)out, d};
     SDM_TRY(launch_gemm<bf16_t, EpiResid<bf16_t>>((bf16_t*)w.rbuf, 2 * d, (const bf16_t*)p->wo, d, S_, 2 * d, d, er, st,
                                                   d));
   } else {
-    SDM_TRY(launch_rt_finish<float>(w.num, w.den, S_, h, dh, p->read_sum, p->read_eps, p->out_norm, p->out_norm_eps,
-                                    p->onorm_w, (float*)w.rbuf, 0, st));
+    da.split = 0;
+    SDM_TRY(launch_rt_decode<float>(da, st));
     EpiResid<float> er{add_residual ? (const float*)x : nullptr, (float*)out, d};
     SDM_TRY(launch_gemm<float, EpiResid<float>>((float*)w.rbuf, d, (const float*)p->wo, d, S_, d, d, er, st));
   }

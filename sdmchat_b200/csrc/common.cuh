@@ -38,6 +38,37 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Programmatic dependent launch.  Every kernel of the library is launched with launch_k and begins with
+// pdl_enter(): wait until the kernel before it in the stream has completed with its writes visible (so every
+// kernel has waited for its predecessor before it can complete, and the chain stays ordered), then allow the next
+// kernel to start.  Small launches (decode: tens of rows, a fraction of one wave) get the programmatic attribute,
+// so the next kernel's launch and block scheduling overlap this one's run; its blocks can be resident only once
+// all of this kernel's blocks have started.  Large launches (prefill) keep plain stream order: their launch gaps
+// are hidden by the second row stream, whose kernels early-resident waiting blocks would crowd out.  Both
+// instructions are no-ops for a launch without the attribute.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+constexpr int64_t PDL_MAX_THREADS = 148 * 512;   // a quarter of the B200's resident threads
+constexpr size_t PDL_MAX_SMEM = 48 * 1024;
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const int64_t threads = (int64_t)grid.x * grid.y * grid.z * block.x * block.y * block.z;
+  cfg.attrs = attr;
+  cfg.numAttrs = (threads <= PDL_MAX_THREADS && smem <= PDL_MAX_SMEM) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 // Every kernel launch sits inside a LaunchScope: it counts the launch (sdm_kernel_launch_count) and, while
 // sdm_profile_begin/end is recording, brackets it with CUDA events on the launch stream, grouped by kernel name
 // and the call-site tag of the innermost OpTag.

@@ -11,6 +11,7 @@ template <typename TA, typename Epi>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const TA* __restrict__ x, int64_t ldx,
                                                         const TA* __restrict__ w, int64_t ldw, int64_t rows, int K,
                                                         int n, Epi epi, int kwrap) {
+  pdl_enter();
   __shared__ float As[SG_BK][SG_BM + 4];
   __shared__ float Bs[SG_BK][SG_BN + 4];
   const int tid = threadIdx.x;
@@ -72,7 +73,7 @@ cudaError_t launch_gemm_simt(const TA* x, int64_t ldx, const TA* w, int64_t ldw,
   if (rows == 0 || n == 0) return cudaSuccess;
   dim3 grid((unsigned)ceil_div(n, SG_BN), (unsigned)ceil_div(rows, SG_BM));
   LaunchScope scope_("gemm_simt", st);
-  gemm_simt_kernel<TA, Epi><<<grid, 256, 0, st>>>(x, ldx, w, ldw, rows, K, n, epi, kwrap);
+  launch_k(gemm_simt_kernel<TA, Epi>, dim3(grid), dim3(256), 0, st, x, ldx, w, ldw, rows, K, n, epi, kwrap);
   return cudaGetLastError();
 }
 
@@ -112,6 +113,7 @@ template <typename TA, typename Epi>
 __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_kernel(const TA* __restrict__ x, int64_t ldx,
                                                                    const TA* __restrict__ w, int64_t ldw, int rows,
                                                                    int K, int n, Epi epi, int kwrap) {
+  pdl_enter();
   extern __shared__ __align__(16) unsigned char sk_smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int col = blockIdx.x * SK_WARPS + warp;
@@ -190,7 +192,7 @@ static cudaError_t launch_gemm_skinny(const TA* x, int64_t ldx, const TA* w, int
   if (e != cudaSuccess) return e;
   const int64_t grid = ceil_div(n, SK_WARPS);
   LaunchScope scope_("gemm_skinny", st);
-  kern<<<(unsigned)grid, SK_WARPS * 32, smem, st>>>(x, ldx, w, ldw, (int)rows, K, n, epi, kwrap);
+  launch_k(kern, dim3((unsigned)grid), dim3(SK_WARPS * 32), smem, st, x, ldx, w, ldw, (int)rows, K, n, epi, kwrap);
   return cudaGetLastError();
 }
 
@@ -220,6 +222,7 @@ template <typename Epi>
 __global__ void __launch_bounds__(SMT_WARPS * 32) gemm_small_tc_kernel(const bf16_t* __restrict__ x, int64_t ldx,
                                                                       const bf16_t* __restrict__ w, int64_t ldw,
                                                                       int rows, int K, int n, Epi epi, int kwrap) {
+  pdl_enter();
   __shared__ float part[SMT_WARPS][32][9];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -282,7 +285,7 @@ cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int6
   if constexpr (sizeof(TA) == 2) {
     if (small_tc_ok(x, ldx, w, ldw, rows, K, kwrap)) {
       LaunchScope scope_("gemm_small_tc", st);
-      gemm_small_tc_kernel<Epi><<<(unsigned)ceil_div(n, 8), SMT_WARPS * 32, 0, st>>>(x, ldx, w, ldw, (int)rows, K, n,
+      launch_k(gemm_small_tc_kernel<Epi>, dim3((unsigned)ceil_div(n, 8)), dim3(SMT_WARPS * 32), 0, st, x, ldx, w, ldw, (int)rows, K, n,
                                                                                      epi, kwrap);
       return cudaGetLastError();
     }

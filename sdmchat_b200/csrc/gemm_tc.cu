@@ -83,6 +83,7 @@ template <typename Epi, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t rows,
                    int K, int n, Epi epi, int kwrap) {
+  pdl_enter();
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) unsigned char dsmem[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
@@ -307,7 +308,7 @@ static cudaError_t launch_tc_bn(const bf16_t* x, int64_t ldx, const bf16_t* w, i
   const int64_t tiles = ceil_div(n, BN) * ceil_div(rows, tc::BM);
   const int grid = (int)(tiles < tc::num_sms() ? tiles : tc::num_sms());
   LaunchScope scope_("gemm_tc", st);
-  kern<<<grid, tc::THREADS, C::SMEM_BYTES, st>>>(ma, mb, rows, K, n, epi, kwrap);
+  launch_k(kern, dim3(grid), dim3(tc::THREADS), C::SMEM_BYTES, st, ma, mb, rows, K, n, epi, kwrap);
   return cudaGetLastError();
 }
 

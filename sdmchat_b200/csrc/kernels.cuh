@@ -355,8 +355,11 @@ struct DecodeArgs {
   const float* decay; const uint8_t* reset;
   int S, h, M, dh, k;
   float* mem; float* cnt; float* scale; int32_t* last_w;
-  float* num; float* den;  // (S, h, dh), (S, h)
+  // RunTimeSdm.finish up to wo, fused: r (S, h * dh) in T (hi/lo bfloat16 rows (S, 2, h * dh) when split)
+  int read_sum; float read_eps; int out_norm; float out_norm_eps; const float* onorm_w;
+  void* r; int split;
 };
+template <typename T>
 cudaError_t launch_rt_decode(const DecodeArgs& a, cudaStream_t st);
 
 // Tied-head loss / argmax reductions over a materialised logits block (rows, V) float32.

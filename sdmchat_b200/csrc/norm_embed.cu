@@ -8,6 +8,7 @@ namespace sdm {
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t rows, int d, float eps,
                                T* __restrict__ y) {
+  pdl_enter();
   int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -31,6 +32,7 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
 template <typename T, int NCH>
 __global__ void rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t rows, float eps,
                                    T* __restrict__ y) {
+  pdl_enter();
   constexpr int E = 16 / sizeof(T), D = NCH * 32 * E;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -66,6 +68,7 @@ __global__ void rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict_
 template <typename T>
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restrict__ emb, int64_t N, int d, int V,
                              T* __restrict__ out, int* bad) {
+  pdl_enter();
   int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (row >= N) return;
@@ -78,6 +81,7 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restric
 // SwiGLU activation (track4_sdmllm_models.py:96-97): p = silu(g) * u with the bf16 roundings of a bf16 module.
 template <typename T>
 __global__ void swiglu_act_kernel(const T* __restrict__ g, const T* __restrict__ u, int64_t n, T* __restrict__ p) {
+  pdl_enter();
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (; i < n; i += stride) {
@@ -118,6 +122,7 @@ template <typename T>
 __global__ void rt_finish_kernel(const float* __restrict__ num, const float* __restrict__ den, int64_t N, int h,
                                  int dh, int read_sum, float read_eps, int out_norm, float out_norm_eps,
                                  const float* __restrict__ onorm_w, T* __restrict__ r, int split) {
+  pdl_enter();
   int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (item >= N * h) return;
@@ -159,6 +164,7 @@ __global__ void __launch_bounds__(256) rt_finish_vec_kernel(const float* __restr
                                                             int out_norm, float out_norm_eps,
                                                             const float* __restrict__ onorm_w, T* __restrict__ r,
                                                             int split) {
+  pdl_enter();
   constexpr int dh = 32 * STEPS;
   const int64_t item0 = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3) * FIN_ROWS;
   const int g = threadIdx.x & 7;
@@ -215,6 +221,7 @@ template <typename T>
 __global__ void ts_gather_kernel(const int32_t* __restrict__ si, const float* __restrict__ w,
                                  const T* __restrict__ values, int64_t N, int h, int M, int dh, int k,
                                  T* __restrict__ r, int split) {
+  pdl_enter();
   int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (item >= N * h) return;
@@ -248,6 +255,7 @@ __global__ void ts_gather_kernel(const int32_t* __restrict__ si, const float* __
 __global__ void ts_gather_vec_kernel(const int32_t* __restrict__ si, const float* __restrict__ w,
                                      const bf16_t* __restrict__ values, int64_t N, int h, int M, int dh, int k,
                                      bf16_t* __restrict__ r, int split) {
+  pdl_enter();
   const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (item >= N * h) return;
@@ -289,6 +297,7 @@ __global__ void __launch_bounds__(256) ts_gather_split_kernel(const int32_t* __r
                                                               const float* __restrict__ w,
                                                               const bf16_t* __restrict__ values, int64_t N, int h,
                                                               int M, int dh, int k, bf16_t* __restrict__ r, int split) {
+  pdl_enter();
   __shared__ float part[8][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t item = (int64_t)blockIdx.x * 2 + (warp >> 2);
@@ -349,14 +358,14 @@ cudaError_t launch_rmsnorm(const T* x, const T* w, int64_t rows, int d, float ep
     const int wpb = rows < 148 * 8 ? 2 : 8;  // small launches: fewer warps per block, more SMs
     const unsigned grid = (unsigned)ceil_div(rows, wpb);
     switch (nch) {
-      case 1: rmsnorm_vec_kernel<T, 1><<<grid, wpb * 32, 0, st>>>(x, w, rows, eps, y); break;
-      case 2: rmsnorm_vec_kernel<T, 2><<<grid, wpb * 32, 0, st>>>(x, w, rows, eps, y); break;
-      case 3: rmsnorm_vec_kernel<T, 3><<<grid, wpb * 32, 0, st>>>(x, w, rows, eps, y); break;
-      default: rmsnorm_vec_kernel<T, 4><<<grid, wpb * 32, 0, st>>>(x, w, rows, eps, y); break;
+      case 1: launch_k(rmsnorm_vec_kernel<T, 1>, dim3(grid), dim3(wpb * 32), 0, st, x, w, rows, eps, y); break;
+      case 2: launch_k(rmsnorm_vec_kernel<T, 2>, dim3(grid), dim3(wpb * 32), 0, st, x, w, rows, eps, y); break;
+      case 3: launch_k(rmsnorm_vec_kernel<T, 3>, dim3(grid), dim3(wpb * 32), 0, st, x, w, rows, eps, y); break;
+      default: launch_k(rmsnorm_vec_kernel<T, 4>, dim3(grid), dim3(wpb * 32), 0, st, x, w, rows, eps, y); break;
     }
     return cudaGetLastError();
   }
-  rmsnorm_kernel<T><<<(unsigned)ceil_div(rows, 8), 256, 0, st>>>(x, w, rows, d, eps, y);
+  launch_k(rmsnorm_kernel<T>, dim3((unsigned)ceil_div(rows, 8)), dim3(256), 0, st, x, w, rows, d, eps, y);
   return cudaGetLastError();
 }
 template <typename T>
@@ -364,7 +373,7 @@ cudaError_t launch_embed(const int32_t* ids, const T* emb, int64_t N, int d, int
                          cudaStream_t st) {
   if (N == 0) return cudaSuccess;
   LaunchScope scope_("embed", st);
-  embed_kernel<T><<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(ids, emb, N, d, V, out, bad);
+  launch_k(embed_kernel<T>, dim3((unsigned)ceil_div(N, 8)), dim3(256), 0, st, ids, emb, N, d, V, out, bad);
   return cudaGetLastError();
 }
 template <typename T>
@@ -373,7 +382,7 @@ cudaError_t launch_swiglu_act(const T* g, const T* u, int64_t n, T* p, cudaStrea
   int64_t blocks = ceil_div(n, 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
   LaunchScope scope_("swiglu_act", st);
-  swiglu_act_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(g, u, n, p);
+  launch_k(swiglu_act_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, st, g, u, n, p);
   return cudaGetLastError();
 }
 template <typename T>
@@ -389,10 +398,10 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
     const int rows_per = big ? 4 : 1;
     const unsigned grid = (unsigned)ceil_div(ceil_div(N * h, rows_per) * 8, 256);
 #define SDM_FIN(STEPS)                                                                                          \
-  (big ? rt_finish_vec_kernel<T, STEPS, 4><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm,   \
-                                                                 out_norm_eps, onorm_w, r, split)                \
-       : rt_finish_vec_kernel<T, STEPS, 1><<<grid, 256, 0, st>>>(num, den, N, h, read_sum, read_eps, out_norm,   \
-                                                                 out_norm_eps, onorm_w, r, split))
+  (big ? launch_k(rt_finish_vec_kernel<T, STEPS, 4>, dim3(grid), dim3(256), 0, st, num, den, N, h, read_sum,      \
+                  read_eps, out_norm, out_norm_eps, onorm_w, r, split)                                          \
+       : launch_k(rt_finish_vec_kernel<T, STEPS, 1>, dim3(grid), dim3(256), 0, st, num, den, N, h, read_sum,      \
+                  read_eps, out_norm, out_norm_eps, onorm_w, r, split))
     if (dh == 64)
       SDM_FIN(2);
     else if (dh == 32)
@@ -402,7 +411,7 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
 #undef SDM_FIN
     return cudaGetLastError();
   }
-  rt_finish_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(num, den, N, h, dh, read_sum, read_eps,
+  launch_k(rt_finish_kernel<T>, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, num, den, N, h, dh, read_sum, read_eps,
                                                                     out_norm, out_norm_eps, onorm_w, r, split);
   return cudaGetLastError();
 }
@@ -414,14 +423,14 @@ cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values,
   if constexpr (sizeof(T) == 2) {
     if (dh % 8 == 0 && dh <= 256 && k <= 32 && (reinterpret_cast<uintptr_t>(values) & 15) == 0) {
       if (N * h < 148 * 8) {  // decode-sized: spread each item's rows over four warps
-        ts_gather_split_kernel<<<(unsigned)ceil_div(N * h, 2), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r, split);
+        launch_k(ts_gather_split_kernel, dim3((unsigned)ceil_div(N * h, 2)), dim3(256), 0, st, si, w, values, N, h, M, dh, k, r, split);
         return cudaGetLastError();
       }
-      ts_gather_vec_kernel<<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r, split);
+      launch_k(ts_gather_vec_kernel, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, si, w, values, N, h, M, dh, k, r, split);
       return cudaGetLastError();
     }
   }
-  ts_gather_kernel<T><<<(unsigned)ceil_div(N * h, 8), 256, 0, st>>>(si, w, values, N, h, M, dh, k, r, split);
+  launch_k(ts_gather_kernel<T>, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, si, w, values, N, h, M, dh, k, r, split);
   return cudaGetLastError();
 }
 

@@ -31,6 +31,27 @@ __device__ __forceinline__ float pk_key_score(KT k) {
 }
 __device__ __forceinline__ uint32_t pk_key_tie(KT k) { return 0xFFFFFFFFu - (uint32_t)k; }
 
+// Cosine score of a normalised half against one sub-key row kr (shared memory, 16-byte aligned when HALF is a
+// multiple of 4): fmaf in dd order, the row read four floats at a time.
+template <int HALF>
+__device__ __forceinline__ float half_dot(const float (&zn)[HALF], const float* kr) {
+  float s = 0.f;
+  if constexpr (HALF % 4 == 0) {
+#pragma unroll
+    for (int d4 = 0; d4 < HALF / 4; ++d4) {
+      const float4 kv = reinterpret_cast<const float4*>(kr)[d4];
+      s = fmaf(zn[4 * d4], kv.x, s);
+      s = fmaf(zn[4 * d4 + 1], kv.y, s);
+      s = fmaf(zn[4 * d4 + 2], kv.z, s);
+      s = fmaf(zn[4 * d4 + 3], kv.w, s);
+    }
+  } else {
+#pragma unroll
+    for (int dd = 0; dd < HALF; ++dd) s = fmaf(zn[dd], kr[dd], s);
+  }
+  return s;
+}
+
 // Sort C (power of two) keys descending: a bitonic network of max/min pairs (directions fixed at compile time).
 template <int C>
 __device__ __forceinline__ void bitonic_sort_desc(KT (&k)[C]) {
@@ -82,10 +103,7 @@ __device__ __forceinline__ void half_topc(const float (&zn)[HALF], const float* 
       const int j = g0 + q;
       float s = -INFINITY;
       if (j < n_sub) {
-        const float* kr = kn + j * HALF;
-        s = 0.f;
-#pragma unroll
-        for (int dd = 0; dd < HALF; ++dd) s = fmaf(zn[dd], kr[dd], s);
+        s = half_dot<HALF>(zn, kn + j * HALF);
         if (s != s) s = -INFINITY;
       }
       gk[q] = pk_key(s, j < n_sub ? (uint32_t)j : 0xFFFFFFFFu);
@@ -165,10 +183,7 @@ __device__ __forceinline__ bool half_topc_fast(const float (&zn)[HALF], const fl
       const int j = g0 + q;
       uint32_t key = 0u;  // padding: below every real key
       if (j < n_sub) {
-        const float* kr = kn + j * HALF;
-        float s = 0.f;
-#pragma unroll
-        for (int dd = 0; dd < HALF; ++dd) s = fmaf(zn[dd], kr[dd], s);
+        float s = half_dot<HALF>(zn, kn + j * HALF);
         if (s != s) s = -INFINITY;
         sc[j * PK_STRIDE] = s;
         key = fast_key(s, (uint32_t)j);
@@ -208,20 +223,146 @@ __device__ __noinline__ void half_topc_stored(const float* sc, int n_sub, KT (&t
   }
 }
 
+// F.normalize of one half: src[0..HALF) / max(||src||, 1e-12).  vec: src is 16-byte aligned (HALF a multiple
+// of 4) and is read four floats at a time.
 template <int HALF>
-__device__ __forceinline__ void normalize_half(const float* src, float (&zn)[HALF]) {
+__device__ __forceinline__ void normalize_half(const float* src, float (&zn)[HALF], bool vec = false) {
+  if constexpr (HALF % 4 == 0) {
+    if (vec) {
+#pragma unroll
+      for (int d4 = 0; d4 < HALF / 4; ++d4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(src) + d4);
+        zn[4 * d4] = v.x;
+        zn[4 * d4 + 1] = v.y;
+        zn[4 * d4 + 2] = v.z;
+        zn[4 * d4 + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int dd = 0; dd < HALF; ++dd) zn[dd] = src[dd];
+    }
+  } else {
+#pragma unroll
+    for (int dd = 0; dd < HALF; ++dd) zn[dd] = src[dd];
+  }
   float ss = 0.f;
 #pragma unroll
-  for (int dd = 0; dd < HALF; ++dd) {
-    zn[dd] = src[dd];
-    ss = fmaf(zn[dd], zn[dd], ss);
-  }
+  for (int dd = 0; dd < HALF; ++dd) ss = fmaf(zn[dd], zn[dd], ss);
   const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
 #pragma unroll
   for (int dd = 0; dd < HALF; ++dd) zn[dd] = __fdiv_rn(zn[dd], nrm);
 }
 
 constexpr int PK_THREADS = 128;
+
+// First output element of address (token n, head hh): the (B, h, T_bh, kk) layout when T_bh > 0 (token
+// n = b * T_bh + t), else (N, h, kk).  32-bit division whenever n fits.
+__device__ __forceinline__ int64_t pk_dst(int64_t n, int hh, int h, int T_bh, int kk) {
+  if (T_bh <= 0) return (n * h + hh) * kk;
+  int64_t bb, t;
+  if (n <= 0x7fffffff) {
+    const uint32_t q = (uint32_t)n / (uint32_t)T_bh;
+    bb = q;
+    t = (uint32_t)n - q * (uint32_t)T_bh;
+  } else {
+    bb = n / T_bh;
+    t = n % T_bh;
+  }
+  return ((bb * h + hh) * T_bh + t) * kk;
+}
+
+// The top-kk of the c1 x c1 grid of combined scores (v1[a] + v2[b]) / 2 over two lists sorted descending, in
+// (score descending, flat index a * c1 + b ascending) order: a frontier walk, row a's next candidate being
+// (a, b_a).  The lists (value, sub-key id) live at v1s/i1s, v2s/i2s with stride PK_THREADS; the picks go to
+// ov (combined score) and oi (slot id a' * n_sub + b') rows.
+//
+// walk_rows, for kk <= c1 (no row runs out of candidates before the walk ends): row q's first candidate ranks
+// after row q-1's (the lists are sorted and rounding is monotone; equal scores go to the lower flat index), so at
+// step s the largest candidate is in rows 0..s and the step's max tree spans s + 1 rows.  Between rows, flat
+// index order is row order, so float compares with ties kept by the lower row give the exact order.
+// One step (S, a compile-time constant, so every register index below is one too).
+template <int C, int S>
+__device__ __forceinline__ void walk_rows_step(float (&kv)[C], int (&kp)[C], const float* v1s, const int* i1s,
+                                               const float* v2s, const int* i2s, float* ov, int* oi, int kk,
+                                               int n_sub, int tid) {
+  if constexpr (S < C) {
+    if (S >= kk) return;
+    float tv[S + 1];
+    int tp[S + 1];
+#pragma unroll
+    for (int q = 0; q <= S; ++q) {
+      tv[q] = kv[q];
+      tp[q] = kp[q];
+    }
+#pragma unroll
+    for (int w = 1; w <= S; w <<= 1) {
+#pragma unroll
+      for (int q = 0; q + w <= S; q += 2 * w) {
+        const bool hi = tv[q + w] > tv[q];  // the higher rows' candidate only when strictly larger
+        tv[q] = hi ? tv[q + w] : tv[q];
+        tp[q] = hi ? tp[q + w] : tp[q];
+      }
+    }
+    const int r = tp[0] >> 8, b = tp[0] & 255;
+    ov[S * PK_THREADS + tid] = tv[0] + 0.f;  // -0 -> +0
+    oi[S * PK_THREADS + tid] = i1s[r * PK_THREADS + tid] * n_sub + i2s[b * PK_THREADS + tid];
+    const int nb = min(b + 1, C - 1);  // b + 1 = c1 only after the last pick
+    const float nk = (v1s[r * PK_THREADS + tid] + v2s[nb * PK_THREADS + tid]) * 0.5f;
+#pragma unroll
+    for (int q = 0; q <= S; ++q) {
+      const bool mine = q == r;
+      kv[q] = mine ? nk : kv[q];
+      kp[q] = mine ? kp[q] + 1 : kp[q];
+    }
+    walk_rows_step<C, S + 1>(kv, kp, v1s, i1s, v2s, i2s, ov, oi, kk, n_sub, tid);
+  }
+}
+template <int C>
+__device__ __forceinline__ void walk_rows(const float* v1s, const int* i1s, const float* v2s, const int* i2s,
+                                          float* ov, int* oi, int kk, int n_sub, int tid) {
+  float kv[C];
+  int kp[C];  // row q's current candidate: q << 8 | b
+  const float v2_0 = v2s[tid];
+#pragma unroll
+  for (int q = 0; q < C; ++q) {
+    kv[q] = (v1s[q * PK_THREADS + tid] + v2_0) * 0.5f;
+    kp[q] = q << 8;
+  }
+  walk_rows_step<C, 0>(kv, kp, v1s, i1s, v2s, i2s, ov, oi, kk, n_sub, tid);
+}
+
+// walk_keys, any kk <= c1 * c1: the candidates as 64-bit keys (tie r << 6 | b_r, which orders like the flat
+// index); a row that runs out holds the key below every real one; each step takes the largest key of all C rows.
+template <int C>
+__device__ __forceinline__ void walk_keys(const float* v1s, const int* i1s, const float* v2s, const int* i2s,
+                                          float* ov, int* oi, int c1, int kk, int n_sub, int tid) {
+  KT kq[C];
+  const float v2_0 = v2s[tid];
+  const KT kminv = pk_key(-INFINITY, 0xFFFFFFFFu);
+#pragma unroll
+  for (int q = 0; q < C; ++q)
+    kq[q] = q < c1 ? pk_key((v1s[q * PK_THREADS + tid] + v2_0) * 0.5f, (uint32_t)(q << 6)) : kminv;
+  for (int step = 0; step < kk; ++step) {
+    KT t[C];
+#pragma unroll
+    for (int q = 0; q < C; ++q) t[q] = kq[q];
+#pragma unroll
+    for (int w = C / 2; w >= 1; w >>= 1) {
+#pragma unroll
+      for (int q = 0; q < w; ++q) t[q] = kmax(t[q], t[q + w]);
+    }
+    const uint32_t tie = pk_key_tie(t[0]);
+    const int r = (int)(tie >> 6), b = (int)(tie & 63u);
+    ov[step * PK_THREADS + tid] = pk_key_score(t[0]);
+    oi[step * PK_THREADS + tid] = i1s[r * PK_THREADS + tid] * n_sub + i2s[b * PK_THREADS + tid];
+    const int nb = b + 1;
+    const KT nk = nb < c1 ? pk_key((v1s[r * PK_THREADS + tid] + v2s[min(nb, C - 1) * PK_THREADS + tid]) * 0.5f,
+                                   (uint32_t)((r << 6) | nb))
+                          : kminv;
+#pragma unroll
+    for (int q = 0; q < C; ++q) kq[q] = q == r ? nk : kq[q];
+  }
+}
 
 // Resident blocks per SM the register budget is sized for: 4 for lists up to 16, 2 for 32.
 template <int C>
@@ -231,6 +372,7 @@ struct PkOcc {
 
 template <int HALF, int C>
 __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs a, int c1, int kk) {
+  pdl_enter();
   extern __shared__ float pk_smem[];
   const int hh = blockIdx.y % a.h, pr = blockIdx.y / a.h;  // pr: which address set of a paired launch
   const float* const zb = pr ? a.z2 : a.z;
@@ -264,11 +406,12 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
   const int64_t n = (int64_t)blockIdx.x * PK_THREADS + tid;
   if (n >= a.N) return;
   const float* zr = zb + n * a.ldz + (int64_t)hh * a.d_a;
+  const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(zb) & 15) | (a.ldz & 3) | (a.d_a & 3)) == 0;
   // the two halves one after the other through one register list (fewer live registers, more resident warps)
 #pragma unroll 1
   for (int hf = 0; hf < 2; ++hf) {
     float zn[HALF];
-    normalize_half<HALF>(zr + hf * HALF, zn);
+    normalize_half<HALF>(zr + hf * HALF, zn, zvec);
     float* vs = hf ? v2s : v1s;
     int* is = hf ? i2s : i1s;
     bool done = false;
@@ -305,42 +448,12 @@ __global__ void __launch_bounds__(PK_THREADS, PkOcc<C>::value) pk_kernel(PkArgs 
       }
     }
   }
-  // frontier walk over the c1 x c1 grid: row r's next candidate is (r, b_r), held as the key of its combined
-  // score with tie r << 6 | b_r (which orders like the flat index r * c1 + b_r); each step takes the largest key
-  // by a max tree and advances the winning row.
-  KT kq[C];
-  const float v2_0 = v2s[tid];
-  const KT kminv = pk_key(-INFINITY, 0xFFFFFFFFu);
-#pragma unroll
-  for (int q = 0; q < C; ++q) kq[q] = q < c1 ? pk_key((v1s[q * PK_THREADS + tid] + v2_0) * 0.5f, (uint32_t)(q << 6)) : kminv;
-  for (int step = 0; step < kk; ++step) {
-    KT t[C];
-#pragma unroll
-    for (int q = 0; q < C; ++q) t[q] = kq[q];
-#pragma unroll
-    for (int w = C / 2; w >= 1; w >>= 1) {
-#pragma unroll
-      for (int q = 0; q < w; ++q) t[q] = kmax(t[q], t[q + w]);
-    }
-    const uint32_t tie = pk_key_tie(t[0]);
-    const int r = (int)(tie >> 6), b = (int)(tie & 63u);
-    ov[step * PK_THREADS + tid] = pk_key_score(t[0]);
-    oi[step * PK_THREADS + tid] = i1s[r * PK_THREADS + tid] * n_sub + i2s[b * PK_THREADS + tid];
-    const int nb = b + 1;
-    const KT nk = nb < c1 ? pk_key((v1s[r * PK_THREADS + tid] + v2s[min(nb, C - 1) * PK_THREADS + tid]) * 0.5f,
-                                       (uint32_t)((r << 6) | nb))
-                              : kminv;
-#pragma unroll
-    for (int q = 0; q < C; ++q) kq[q] = q == r ? nk : kq[q];
-  }
+  if (kk <= c1)
+    walk_rows<C>(v1s, i1s, v2s, i2s, ov, oi, kk, n_sub, tid);
+  else
+    walk_keys<C>(v1s, i1s, v2s, i2s, ov, oi, c1, kk, n_sub, tid);
   // outputs and softmax(scale * score) (* gate); exp(scale * s - max) is kept in place of the score
-  int64_t dst;
-  if (a.T_bh > 0) {
-    const int64_t bb = n / a.T_bh, t = n % a.T_bh;
-    dst = ((bb * a.h + hh) * a.T_bh + t) * kk;
-  } else {
-    dst = (n * a.h + hh) * kk;
-  }
+  const int64_t dst = pk_dst(n, hh, a.h, a.T_bh, kk);
   const bool vec = (kk & 3) == 0 && ((reinterpret_cast<uintptr_t>(sib + dst) | (wb ? reinterpret_cast<uintptr_t>(wb + dst) : 0) |
                                       (svb ? reinterpret_cast<uintptr_t>(svb + dst) : 0)) & 15) == 0;
   if (svb) {
@@ -386,7 +499,7 @@ static cudaError_t launch_pk_tc(const PkArgs& a, int c1, int kk, cudaStream_t st
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)ceil_div(a.N, PK_THREADS), (unsigned)(a.h * (a.pairs > 1 ? 2 : 1)));
   LaunchScope scope_("pk_address", st);
-  kern<<<grid, PK_THREADS, smem, st>>>(a, c1, kk);
+  launch_k(kern, dim3(grid), dim3(PK_THREADS), smem, st, a, c1, kk);
   return cudaGetLastError();
 }
 
@@ -396,6 +509,271 @@ static cudaError_t launch_pk_half(const PkArgs& a, int c1, int kk, cudaStream_t 
   if (c1 <= 8) return launch_pk_tc<HALF, 8>(a, c1, kk, st);
   if (c1 <= 16) return launch_pk_tc<HALF, 16>(a, c1, kk, st);
   return launch_pk_tc<HALF, 32>(a, c1, kk, st);
+}
+
+// ------------------------------------------------------------------------------------ 32-bit-key variant
+// The selection of pk_kernel with 32-bit keys for any n_sub <= 256, fewer registers and about half the shared
+// memory, so more warps are resident.  A key is the score's order-preserving image with its low ib bits (ib: the
+// bits of n_sub - 1) replaced by (2^ib - 1 - index); the replaced bits are kept, one byte per score, so the exact
+// image of every selected score is restored.  Key order is the exact (score desc, index asc) order except between
+// keys with equal high bits: an isolated such pair among the top C is put in exact order from the restored
+// images; a run of three, or equal high bits between the C-th key and the best key left out (where the selected
+// set itself may differ), sends the half through the exact 64-bit path -- rare: scores within ~2^-(23-ib) relative
+// of each other.  Sub-key ids, the walk's per-row positions and the picks are bytes.
+constexpr int PKF_THREADS = 128;
+
+__device__ __forceinline__ uint32_t mono_image(float s) {
+  const uint32_t b = __float_as_uint(s + 0.f);  // -0 -> +0
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float mono_score(uint32_t m) {
+  return __uint_as_float((m & 0x80000000u) ? (m & 0x7FFFFFFFu) : ~m);
+}
+
+// The exact top-C of one half (64-bit keys) as (score, sub-key id) lists.  Out of line: the rare path.
+template <int HALF, int C>
+__device__ __noinline__ void half_lists_exact(const float* src, bool vec, const float* kn, int n_sub, float* vs,
+                                              uint8_t* is, int tid) {
+  float zn[HALF];
+  normalize_half<HALF>(src, zn, vec);
+  KT tk[C];
+  half_topc<HALF, C>(zn, kn, n_sub, tk);
+#pragma unroll
+  for (int q = 0; q < C; ++q) {
+    vs[q * PKF_THREADS + tid] = pk_key_score(tk[q]);
+    is[q * PKF_THREADS + tid] = (uint8_t)pk_key_tie(tk[q]);
+  }
+}
+
+// The top-C of one half with 32-bit keys as (score, sub-key id) lists; false when the exact path must redo it.
+template <int HALF, int C>
+__device__ __forceinline__ bool half_lists_fast(const float (&zn)[HALF], const float* kn, int n_sub, int ib,
+                                               uint8_t* lowb, float* vs, uint8_t* is, int tid) {
+  const uint32_t mask = (1u << ib) - 1u;
+  uint32_t tk[C];
+  uint32_t disc = 0u;
+  for (int g0 = 0; g0 < n_sub; g0 += C) {
+    uint32_t gk[C];
+#pragma unroll
+    for (int q = 0; q < C; ++q) {
+      const int j = g0 + q;
+      uint32_t key = 0u;  // padding: below every real key (a real key is at least the image of -inf)
+      if (j < n_sub) {
+        float sc = half_dot<HALF>(zn, kn + j * HALF);
+        if (sc != sc) sc = -INFINITY;
+        const uint32_t m = mono_image(sc);
+        lowb[j * PKF_THREADS + tid] = (uint8_t)(m & mask);
+        key = (m & ~mask) | (mask - (uint32_t)j);
+      }
+      gk[q] = key;
+    }
+    bitonic_sort_desc32<C>(gk);
+    if (g0 == 0) {
+#pragma unroll
+      for (int q = 0; q < C; ++q) tk[q] = gk[q];
+    } else {
+      merge_top32<C>(tk, gk, disc);
+    }
+  }
+  if (disc != 0u && tk[C - 1] != 0u && (disc >> ib) == (tk[C - 1] >> ib)) return false;
+  uint32_t eqm = 0u;  // bit q: keys q and q + 1 share their high bits
+#pragma unroll
+  for (int q = 0; q + 1 < C; ++q) eqm |= (tk[q + 1] != 0u && (tk[q] >> ib) == (tk[q + 1] >> ib)) ? (1u << q) : 0u;
+  if (eqm & (eqm >> 1)) return false;
+  if (eqm) {
+#pragma unroll
+    for (int q = 0; q + 1 < C; ++q) {
+      if ((eqm >> q) & 1u) {  // exact images; equal images keep the key order (index ascending)
+        const uint32_t ja = mask - (tk[q] & mask), jb = mask - (tk[q + 1] & mask);
+        const uint32_t ma = (tk[q] & ~mask) | lowb[ja * PKF_THREADS + tid];
+        const uint32_t mb = (tk[q + 1] & ~mask) | lowb[jb * PKF_THREADS + tid];
+        if (mb > ma) {
+          const uint32_t t = tk[q];
+          tk[q] = tk[q + 1];
+          tk[q + 1] = t;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < C; ++q) {
+    const uint32_t key = tk[q];
+    const uint32_t j = mask - (key & mask);
+    vs[q * PKF_THREADS + tid] = key ? mono_score((key & ~mask) | lowb[j * PKF_THREADS + tid]) : -INFINITY;
+    is[q * PKF_THREADS + tid] = (uint8_t)j;
+  }
+  return true;
+}
+
+// walk_rows with the rows' positions b_r and the picks (r, b) in shared memory as bytes.  Every byte array here
+// is (rows, PKF_THREADS) with thread tid owning column tid, so regions that alias across phases are still private
+// to their thread (a warp in its walk never touches a byte another warp's halves use).
+template <int C, int S>
+__device__ __forceinline__ void walkf_step(float (&kv)[C], const float* v1s, const float* v2s, uint8_t* brow,
+                                          uint8_t* pick_r, uint8_t* pick_b, int kk, int tid) {
+  if constexpr (S < C) {
+    if (S >= kk) return;
+    brow[S * PKF_THREADS + tid] = 0;  // row S can first win at this step
+    float tv[S + 1];
+    int tp[S + 1];
+#pragma unroll
+    for (int q = 0; q <= S; ++q) {
+      tv[q] = kv[q];
+      tp[q] = q;
+    }
+#pragma unroll
+    for (int w = 1; w <= S; w <<= 1) {
+#pragma unroll
+      for (int q = 0; q + w <= S; q += 2 * w) {
+        const bool hi = tv[q + w] > tv[q];  // the higher rows' candidate only when strictly larger
+        tv[q] = hi ? tv[q + w] : tv[q];
+        tp[q] = hi ? tp[q + w] : tp[q];
+      }
+    }
+    const int r = tp[0];
+    const int b = brow[r * PKF_THREADS + tid];
+    pick_r[S * PKF_THREADS + tid] = (uint8_t)r;
+    pick_b[S * PKF_THREADS + tid] = (uint8_t)b;
+    const int nb = b + 1;  // b + 1 = c1 only after the last pick
+    brow[r * PKF_THREADS + tid] = (uint8_t)nb;
+    const float nk = (v1s[r * PKF_THREADS + tid] + v2s[min(nb, C - 1) * PKF_THREADS + tid]) * 0.5f;
+#pragma unroll
+    for (int q = 0; q <= S; ++q) kv[q] = q == r ? nk : kv[q];
+    walkf_step<C, S + 1>(kv, v1s, v2s, brow, pick_r, pick_b, kk, tid);
+  }
+}
+
+// Resident blocks per SM the register budget is sized for.
+template <int C>
+struct PkfOcc {
+  static constexpr int value = C <= 8 ? 8 : (C <= 16 ? 6 : 3);
+};
+
+template <int HALF, int C>
+__global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_fast_kernel(PkArgs a, int c1, int kk, int ib) {
+  pdl_enter();
+  extern __shared__ __align__(16) float pkf_smem[];
+  const int hh = blockIdx.y % a.h, pr = blockIdx.y / a.h;  // pr: which address set of a paired launch
+  const float* const zb = pr ? a.z2 : a.z;
+  float* const svb = pr ? a.sv2 : a.sv;
+  float* const wb = pr ? a.w2 : a.w;
+  int32_t* const sib = pr ? a.si2 : a.si;
+  const float* const gb = pr ? a.gate2 : a.gate;
+  const int tid = threadIdx.x;
+  const int n_sub = a.n_sub;
+  constexpr int P = PKF_THREADS;
+  float* kn1 = pkf_smem;             // (n_sub, HALF)
+  float* kn2 = kn1 + n_sub * HALF;   // (n_sub, HALF)
+  float* v1s = kn2 + n_sub * HALF;   // (C, P) per-thread sorted half lists: scores
+  float* v2s = v1s + C * P;
+  uint8_t* i1s = reinterpret_cast<uint8_t*>(v2s + C * P);  // (C, P) sub-key ids
+  uint8_t* i2s = i1s + C * P;
+  uint8_t* lowb = i2s + C * P;  // (n_sub, P) a half's low image bits; after the halves: brow (C, P), the picks'
+  uint8_t* brow = lowb;         // rows (kk, P) and columns (kk, P)
+  uint8_t* pick_r = lowb + C * P;
+  uint8_t* pick_b = pick_r + kk * P;
+
+  // F.normalize(keys, dim=-1) for this head
+  for (int j = tid; j < 2 * n_sub; j += P) {
+    const float* src = (j < n_sub ? a.keys1 + ((int64_t)hh * n_sub + j) * HALF
+                                  : a.keys2 + ((int64_t)hh * n_sub + (j - n_sub)) * HALF);
+    float kv[HALF];
+    normalize_half<HALF>(src, kv);
+    float* dst = (j < n_sub ? kn1 + j * HALF : kn2 + (j - n_sub) * HALF);
+#pragma unroll
+    for (int dd = 0; dd < HALF; ++dd) dst[dd] = kv[dd];
+  }
+  __syncthreads();
+
+  const int64_t n = (int64_t)blockIdx.x * P + tid;
+  if (n >= a.N) return;
+  const float* zr = zb + n * a.ldz + (int64_t)hh * a.d_a;
+  const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(zb) & 15) | (a.ldz & 3) | (a.d_a & 3)) == 0;
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    const float* src = zr + hf * HALF;
+    float zn[HALF];
+    normalize_half<HALF>(src, zn, zvec);
+    float* vs = hf ? v2s : v1s;
+    uint8_t* is = hf ? i2s : i1s;
+    const float* kn = hf ? kn2 : kn1;
+    if (!half_lists_fast<HALF, C>(zn, kn, n_sub, ib, lowb, vs, is, tid))
+      half_lists_exact<HALF, C>(src, zvec, kn, n_sub, vs, is, tid);
+  }
+  {
+    float kv[C];
+    const float v2_0 = v2s[tid];
+#pragma unroll
+    for (int q = 0; q < C; ++q) kv[q] = (v1s[q * P + tid] + v2_0) * 0.5f;
+    walkf_step<C, 0>(kv, v1s, v2s, brow, pick_r, pick_b, kk, tid);
+  }
+  // outputs and softmax(scale * score) (* gate), in pick order; a pick's score and slot come back from the lists
+  const int64_t dst = pk_dst(n, hh, a.h, a.T_bh, kk);
+  auto pick_score = [&](int j) {
+    const int r = pick_r[j * P + tid], b = pick_b[j * P + tid];
+    return (v1s[r * P + tid] + v2s[b * P + tid]) * 0.5f + 0.f;
+  };
+  auto pick_slot = [&](int j) {
+    const int r = pick_r[j * P + tid], b = pick_b[j * P + tid];
+    return (int)i1s[r * P + tid] * n_sub + (int)i2s[b * P + tid];
+  };
+  const bool vec = (kk & 3) == 0 && ((reinterpret_cast<uintptr_t>(sib + dst) | (wb ? reinterpret_cast<uintptr_t>(wb + dst) : 0) |
+                                      (svb ? reinterpret_cast<uintptr_t>(svb + dst) : 0)) & 15) == 0;
+  if (svb) {
+    if (vec) {
+      for (int j = 0; j < kk; j += 4)
+        *reinterpret_cast<float4*>(svb + dst + j) =
+            make_float4(pick_score(j), pick_score(j + 1), pick_score(j + 2), pick_score(j + 3));
+    } else {
+      for (int j = 0; j < kk; ++j) svb[dst + j] = pick_score(j);
+    }
+  }
+  if (vec) {
+    for (int j = 0; j < kk; j += 4)
+      *reinterpret_cast<int4*>(sib + dst + j) = make_int4(pick_slot(j), pick_slot(j + 1), pick_slot(j + 2), pick_slot(j + 3));
+  } else {
+    for (int j = 0; j < kk; ++j) sib[dst + j] = pick_slot(j);
+  }
+  if (wb) {
+    const float scale = expf(a.log_scale[hh]);
+    float mx = -INFINITY, sum = 0.f;
+    for (int j = 0; j < kk; ++j) mx = fmaxf(mx, pick_score(j) * scale);
+    for (int j = 0; j < kk; ++j) sum += expf(pick_score(j) * scale - mx);
+    const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
+    auto wt = [&](int j) {
+      const float wj = __fdiv_rn(expf(pick_score(j) * scale - mx), sum);
+      return gb ? wj * g : wj;
+    };
+    if (vec) {
+      for (int j = 0; j < kk; j += 4)
+        *reinterpret_cast<float4*>(wb + dst + j) = make_float4(wt(j), wt(j + 1), wt(j + 2), wt(j + 3));
+    } else {
+      for (int j = 0; j < kk; ++j) wb[dst + j] = wt(j);
+    }
+  }
+}
+
+template <int HALF, int C>
+static cudaError_t launch_pkf(const PkArgs& a, int c1, int kk, cudaStream_t st) {
+  int ib = 1;
+  while ((1 << ib) < a.n_sub) ++ib;
+  const size_t low_rows = (size_t)(a.n_sub > C + 2 * kk ? a.n_sub : C + 2 * kk);
+  const size_t smem = (size_t)2 * a.n_sub * HALF * 4 + (size_t)2 * C * PKF_THREADS * 4 + (size_t)2 * C * PKF_THREADS +
+                      low_rows * PKF_THREADS;
+  auto kern = pk_fast_kernel<HALF, C>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)ceil_div(a.N, PKF_THREADS), (unsigned)(a.h * (a.pairs > 1 ? 2 : 1)));
+  LaunchScope scope_("pk_address", st);
+  return launch_k(kern, grid, dim3(PKF_THREADS), smem, st, a, c1, kk, ib);
+}
+
+template <int HALF>
+static cudaError_t launch_pkf_half(const PkArgs& a, int c1, int kk, cudaStream_t st) {
+  if (c1 <= 4) return launch_pkf<HALF, 4>(a, c1, kk, st);
+  if (c1 <= 8) return launch_pkf<HALF, 8>(a, c1, kk, st);
+  if (c1 <= 16) return launch_pkf<HALF, 16>(a, c1, kk, st);
+  return launch_pkf<HALF, 32>(a, c1, kk, st);
 }
 
 // ------------------------------------------------------------------------------------ warp-per-address variant
@@ -442,6 +820,7 @@ __device__ __forceinline__ void warp_sort_desc(KT (&v)[S]) {
 
 template <int HALF, int S>
 __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c1, int kk) {
+  pdl_enter();
   extern __shared__ float pkw_smem[];
   const int hh = blockIdx.y % a.h, pr = blockIdx.y / a.h;  // pr: which address set of a paired launch
   const float* const zb = pr ? a.z2 : a.z;
@@ -479,10 +858,11 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
   const int64_t n = (int64_t)blockIdx.x * PKW_WARPS + warp;
   if (n >= a.N) return;
   const float* zr = zb + n * a.ldz + (int64_t)hh * a.d_a;
+  const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(zb) & 15) | (a.ldz & 3) | (a.d_a & 3)) == 0;
 #pragma unroll 1
   for (int hf = 0; hf < 2; ++hf) {
     float zn[HALF];
-    normalize_half<HALF>(zr + hf * HALF, zn);
+    normalize_half<HALF>(zr + hf * HALF, zn, zvec);
     const float* kn = hf ? kn2 : kn1;
     KT key[S];
 #pragma unroll
@@ -490,9 +870,7 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
       const int j = lane * S + q;
       key[q] = 0ull;  // padding: below every real key
       if (j < n_sub) {
-        float sc = 0.f;
-#pragma unroll
-        for (int dd = 0; dd < HALF; ++dd) sc = fmaf(zn[dd], kn[j * HALF + dd], sc);
+        float sc = half_dot<HALF>(zn, kn + j * HALF);
         if (sc != sc) sc = -INFINITY;
         key[q] = pk_key(sc, (uint32_t)j);
       }
@@ -523,13 +901,7 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
     }
   }
   warp_sort_desc<S>(ck);
-  int64_t dst;
-  if (a.T_bh > 0) {
-    const int64_t bb = n / a.T_bh, t = n % a.T_bh;
-    dst = ((bb * a.h + hh) * a.T_bh + t) * kk;
-  } else {
-    dst = (n * a.h + hh) * kk;
-  }
+  const int64_t dst = pk_dst(n, hh, a.h, a.T_bh, kk);
   float sv[S], ex[S];
   const float scale = wb ? expf(a.log_scale[hh]) : 0.f;
   const float mx = pk_key_score(__shfl_sync(0xffffffffu, ck[0], 0)) * scale;  // the first pick is the largest
@@ -575,7 +947,7 @@ static cudaError_t launch_pk_warp_s(const PkArgs& a, int c1, int kk, cudaStream_
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)ceil_div(a.N, PKW_WARPS), (unsigned)(a.h * (a.pairs > 1 ? 2 : 1)));
   LaunchScope scope_("pk_address", st);
-  kern<<<grid, PKW_WARPS * 32, smem, st>>>(a, c1, kk);
+  launch_k(kern, dim3(grid), dim3(PKW_WARPS * 32), smem, st, a, c1, kk);
   return cudaGetLastError();
 }
 
@@ -613,6 +985,17 @@ cudaError_t launch_pk_address(const PkArgs& a, cudaStream_t st) {
       case 8: return launch_pk_warp<8>(a, c1, kk, st);
       case 16: return launch_pk_warp<16>(a, c1, kk, st);
       case 32: return launch_pk_warp<32>(a, c1, kk, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  if (a.n_sub <= 256 && c1 <= 32 && kk <= c1) {  // the 32-bit-key kernel (no row of the walk runs out)
+    switch (a.d_a / 2) {
+      case 2: return launch_pkf_half<2>(a, c1, kk, st);
+      case 4: return launch_pkf_half<4>(a, c1, kk, st);
+      case 6: return launch_pkf_half<6>(a, c1, kk, st);
+      case 8: return launch_pkf_half<8>(a, c1, kk, st);
+      case 16: return launch_pkf_half<16>(a, c1, kk, st);
+      case 32: return launch_pkf_half<32>(a, c1, kk, st);
       default: return cudaErrorInvalidValue;
     }
   }

@@ -1,19 +1,29 @@
 // Single-token decode on the carried run-time memory state (new API: the reference has no carried-state decode;
-// its recurrence RunTimeSdm.forward_sequential, track4_onesdm_models.py:285-299, is the oracle step by step).
+// its recurrence RunTimeSdm.forward_sequential, track4_onesdm_models.py:285-299, is the oracle step by step),
+// fused with RunTimeSdm.finish up to wo (:243-246: mean read, per-head RMS out-norm).
 //
 // The state of each (stream, head) lives in HBM as (mem, cnt, scale): the true state is scale * (mem, cnt).
 // A step reads k rows (before the write, as the reference does), then applies the fade lazily: scale <- scale*lam
 // and the k written rows get ww * v / scale.  So a step touches 2k rows instead of decaying all M rows.  When
 // scale falls below 2^-60 the head's state is renormalised once (one pass, amortised over >= 1/log2(1/lam)*60
 // steps).  Fade 0 is special: the state after a write is exactly that write, so the rows written at the previous
-// step (last_w) are cleared instead.  One CTA per (stream, head); thread c owns value column c (thread 0 also the
-// slot counts and the per-head words), so after one barrier (everyone has read scale and last_w) no two threads
-// touch the same word.
+// step (last_w) are cleared instead.
+//
+// One CTA per (stream, head); thread c owns value column c (thread 0 also the slot counts and the per-head words).
+// The step's slot ids and weights are staged in shared memory, then every row the step touches (k read rows, k
+// written rows) is loaded in one round trip before any store; the read is finished in the block (one block
+// reduction for the out-norm) and written as the wo GEMM's input.
 #include "kernels.cuh"
 
 namespace sdm {
 
+constexpr int DEC_MAX_K = 32;
+
+template <typename T>
 __global__ void rt_decode_kernel(DecodeArgs a) {
+  pdl_enter();
+  __shared__ int s_ir[DEC_MAX_K], s_iw[DEC_MAX_K], s_prev[DEC_MAX_K];
+  __shared__ float s_fr[DEC_MAX_K], s_fw[DEC_MAX_K], s_red[32];
   const int sh = blockIdx.x;
   const int hh = sh % a.h;
   const int s = sh / a.h;
@@ -21,111 +31,143 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   float* mem = a.mem + (int64_t)sh * M * dh;
   float* cnt = a.cnt + (int64_t)sh * M;
   int32_t* lw = a.last_w + (int64_t)sh * k;
-  const int32_t* sir = a.sir + (int64_t)sh * k;
-  const int32_t* siw = a.siw + (int64_t)sh * k;
-  const float* wr = a.wr + (int64_t)sh * k;
-  const float* ww = a.ww + (int64_t)sh * k;
+  const int t = threadIdx.x;
+  if (t < k) {  // slot ids are clamped into the state (see rt_scan.cu)
+    s_ir[t] = min(max(a.sir[(int64_t)sh * k + t], 0), M - 1);
+    s_fr[t] = a.wr[(int64_t)sh * k + t];
+    s_iw[t] = min(max(a.siw[(int64_t)sh * k + t], 0), M - 1);
+    s_fw[t] = a.ww[(int64_t)sh * k + t];
+    s_prev[t] = lw[t];
+  }
   const float lam = a.decay[hh];
-  // every thread reads the shared per-head words (scale, last written rows) before thread 0 rewrites them
+  // every thread reads the per-head words (scale, last written rows) before thread 0 rewrites them
   const float sc = a.scale[sh];
-  int prev[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) prev[j] = j < k ? lw[j] : -1;
   const bool reset = a.reset && a.reset[s];
   __syncthreads();
-  const int c = threadIdx.x;
-  if (c >= dh) return;
+  const int c = t;
+  const bool act = c < dh;
   const bool own_cnt = (c == 0);
-  if (reset) {
+  const bool keep_old = lam != 0.f && !reset;
+  // every row this step touches, loaded before the first store: the k read rows (each thread also loads the read
+  // rows' counts, a warp-uniform broadcast, for the denominator) and the k written rows
+  float rv[DEC_MAX_K], rc[DEC_MAX_K], wv[DEC_MAX_K], wc[DEC_MAX_K];
+#pragma unroll
+  for (int i = 0; i < DEC_MAX_K; ++i) {
+    if (i < k) {
+      const int r = s_ir[i], q = s_iw[i];
+      rv[i] = (act && !reset) ? mem[(int64_t)r * dh + c] : 0.f;
+      rc[i] = reset ? 0.f : cnt[r];
+      wv[i] = (act && keep_old) ? mem[(int64_t)q * dh + c] : 0.f;
+      wc[i] = (own_cnt && keep_old) ? cnt[q] : 0.f;
+    }
+  }
+  const float scr = reset ? 1.f : sc;
+  float acc = 0.f, accd = 0.f;
+#pragma unroll
+  for (int i = 0; i < DEC_MAX_K; ++i) {
+    if (i < k) {
+      acc = fmaf(s_fr[i], rv[i], acc);
+      accd = fmaf(s_fr[i], rc[i], accd);
+    }
+  }
+  // finish: mean (or sum) read, RMS over the head's dh columns, onorm_w
+  float v = acc * scr;
+  if (!a.read_sum) v = __fdiv_rn(v, accd * scr + a.read_eps);
+  float ss = act ? v * v : 0.f;
+  ss = warp_sum(ss);
+  if ((t & 31) == 0) s_red[t >> 5] = ss;
+  __syncthreads();  // also: every thread's loads of the state are done before the first store below
+  if (act) {
+    float tot = 0.f;
+    for (int w = 0; w < (int)((blockDim.x + 31) >> 5); ++w) tot += s_red[w];
+    const float rs = a.out_norm ? rsqrt_rn(__fdiv_rn(tot, (float)dh) + a.out_norm_eps) : 1.f;
+    float o = v;
+    if (a.out_norm) o = (o * rs) * a.onorm_w[hh * dh + c];
+    const int64_t d = (int64_t)a.h * dh, col = (int64_t)hh * dh + c;
+    T* r = static_cast<T*>(a.r);
+    if (a.split) {
+      const float hi = round_to<T>(o);
+      r[s * 2 * d + col] = from_f32<T>(hi);
+      r[s * 2 * d + d + col] = from_f32<T>(o - hi);
+    } else {
+      r[s * d + col] = from_f32<T>(o);
+    }
+  }
+  if (reset && act) {
     for (int r = 0; r < M; ++r) mem[(int64_t)r * dh + c] = 0.f;
     if (own_cnt)
       for (int r = 0; r < M; ++r) cnt[r] = 0.f;
   }
-  const float scr = reset ? 1.f : sc;
-  // read k rows before the write: all k loads issued before the first use
-  float rv[32], rc[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    if (i < k) {
-      const int r = min(max(sir[i], 0), M - 1);  // slot ids are clamped into the state (see rt_scan.cu)
-      rv[i] = mem[(int64_t)r * dh + c];
-      rc[i] = own_cnt ? cnt[r] : 0.f;
-    }
-  }
-  float acc = 0.f, accd = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    if (i < k) {
-      acc = fmaf(wr[i], rv[i], acc);
-      accd = fmaf(wr[i], rc[i], accd);
-    }
-  }
-  a.num[(int64_t)sh * dh + c] = acc * scr;
-  if (own_cnt) a.den[sh] = accd * scr;
-  // write: state <- lam * state + sum_j ww_j (e_{siw_j} v^T, e_{siw_j})
-  const float* v = a.V + (int64_t)s * a.ldv + (int64_t)hh * dh;
   float ns;
   if (lam == 0.f) {
-    if (!reset) {
+    if (!reset && act) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int r = prev[j];
-        if (r >= 0 && r < M) {
-          mem[(int64_t)r * dh + c] = 0.f;
-          if (own_cnt) cnt[r] = 0.f;
+      for (int j = 0; j < DEC_MAX_K; ++j) {
+        if (j < k) {
+          const int r = s_prev[j];
+          if (r >= 0 && r < M) {
+            mem[(int64_t)r * dh + c] = 0.f;
+            if (own_cnt) cnt[r] = 0.f;
+          }
         }
       }
     }
     ns = 1.f;
   } else {
     ns = scr * lam;
-    if (ns < 8.673617e-19f) {  // 2^-60: fold the scale into the state
-      for (int r = 0; r < M; ++r) mem[(int64_t)r * dh + c] *= ns;
-      if (own_cnt)
-        for (int r = 0; r < M; ++r) cnt[r] *= ns;
+    if (ns < 8.673617e-19f) {  // 2^-60: fold the scale into the state (the written rows' loaded values too)
+      if (act) {
+        for (int r = 0; r < M; ++r) mem[(int64_t)r * dh + c] *= ns;
+        if (own_cnt)
+          for (int r = 0; r < M; ++r) cnt[r] *= ns;
+      }
+#pragma unroll
+      for (int j = 0; j < DEC_MAX_K; ++j) {
+        if (j < k) {
+          wv[j] *= ns;
+          wc[j] *= ns;
+        }
+      }
       ns = 1.f;
     }
   }
-  const float vc = v[c];
-  // the k written rows are distinct (a top-k): load them all, then store them all.  With fade 0 every row that
-  // is not cleared above is already zero, so the written value is the write alone.
-  const bool keep_old = lam != 0.f;
+  // write: state <- lam * state + sum_j ww_j (e_{siw_j} v^T, e_{siw_j}); the k written rows are distinct (a
+  // top-k).  With fade 0 (or after a reset) every row not cleared above is zero, so the written value is the write.
+  if (act) {
+    const float vc = a.V[(int64_t)s * a.ldv + (int64_t)hh * dh + c];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (j < k) {
-      const int r = min(max(siw[j], 0), M - 1);
-      rv[j] = keep_old ? mem[(int64_t)r * dh + c] : 0.f;
-      rc[j] = (keep_old && own_cnt) ? cnt[r] : 0.f;
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (j < k) {
-      const int r = min(max(siw[j], 0), M - 1);
-      const float f = __fdiv_rn(ww[j], ns);
-      mem[(int64_t)r * dh + c] = fmaf(f, vc, rv[j]);
-      if (own_cnt) cnt[r] = rc[j] + f;
+    for (int j = 0; j < DEC_MAX_K; ++j) {
+      if (j < k) {
+        const int r = s_iw[j];
+        const float f = __fdiv_rn(s_fw[j], ns);
+        mem[(int64_t)r * dh + c] = fmaf(f, vc, wv[j]);
+        if (own_cnt) cnt[r] = wc[j] + f;
+      }
     }
   }
   if (own_cnt) {
     a.scale[sh] = ns;
-    for (int j = 0; j < k; ++j) lw[j] = min(max(siw[j], 0), M - 1);
+    for (int j = 0; j < k; ++j) lw[j] = s_iw[j];
   }
 }
 
+template <typename T>
 cudaError_t launch_rt_decode(const DecodeArgs& a, cudaStream_t st) {
   if (a.S == 0) return cudaSuccess;
-  const int threads = ((a.dh + 31) / 32) * 32;  // one thread per value column (dh <= 1024)
+  if (a.k > DEC_MAX_K || a.dh > 1024) return cudaErrorInvalidValue;
+  const int threads = ((a.dh + 31) / 32) * 32;  // one thread per value column
   LaunchScope scope_("rt_decode", st);
-  rt_decode_kernel<<<(unsigned)((int64_t)a.S * a.h), threads, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_k(rt_decode_kernel<T>, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), 0, st, a);
 }
+template cudaError_t launch_rt_decode<float>(const DecodeArgs&, cudaStream_t);
+template cudaError_t launch_rt_decode<bf16_t>(const DecodeArgs&, cudaStream_t);
 
 // ----------------------------------------------------------------------------------------------- tied head
 // Cross-entropy of one logits row (logsumexp - target logit), summed into a float64 total (ce_chunked's
 // F.cross_entropy(..., reduction="sum"), track4_sdmllm24_fused_ce.py:76-77).  One block per row.
 __global__ void ce_rows_kernel(const float* __restrict__ lg, int64_t rows, int V, const int32_t* __restrict__ tgt,
                                double* loss_sum) {
+  pdl_enter();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int t = tgt[row];
@@ -159,6 +201,7 @@ __global__ void ce_rows_kernel(const float* __restrict__ lg, int64_t rows, int V
 
 // argmax of one row, lowest index on ties.  One block per row.
 __global__ void argmax_rows_kernel(const float* __restrict__ lg, int64_t rows, int V, int32_t* __restrict__ ids) {
+  pdl_enter();
   __shared__ float rv[32];
   __shared__ int ri[32];
   const int64_t row = blockIdx.x;
@@ -203,6 +246,7 @@ __global__ void argmax_rows_kernel(const float* __restrict__ lg, int64_t rows, i
 // the column tiles, minus the target's logit; rows with target < 0 are skipped.  One warp per row, float64 total.
 __global__ void ce_combine_kernel(const float2* __restrict__ part, const float* __restrict__ tgt_logit,
                                   const int32_t* __restrict__ targets, int64_t rows, int tiles_n, double* loss_sum) {
+  pdl_enter();
   __shared__ double red[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + warp;
@@ -232,6 +276,7 @@ __global__ void ce_combine_kernel(const float2* __restrict__ part, const float* 
 // Greedy id from the fused head's per-tile (best, column) partials; lowest column on ties.  One warp per row.
 __global__ void argmax_combine_kernel(const float2* __restrict__ part, int64_t rows, int tiles_n,
                                       int32_t* __restrict__ ids) {
+  pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + warp;
   if (row >= rows) return;
@@ -261,14 +306,14 @@ cudaError_t launch_ce_combine(const float2* part, const float* tgt_logit, const 
                               int tiles_n, double* loss_sum, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   LaunchScope scope_("ce_combine", st);
-  ce_combine_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, st>>>(part, tgt_logit, targets, rows, tiles_n, loss_sum);
+  launch_k(ce_combine_kernel, dim3((unsigned)ceil_div(rows, 8)), dim3(256), 0, st, part, tgt_logit, targets, rows, tiles_n, loss_sum);
   return cudaGetLastError();
 }
 
 cudaError_t launch_argmax_combine(const float2* part, int64_t rows, int tiles_n, int32_t* ids, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   LaunchScope scope_("argmax_combine", st);
-  argmax_combine_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, st>>>(part, rows, tiles_n, ids);
+  launch_k(argmax_combine_kernel, dim3((unsigned)ceil_div(rows, 8)), dim3(256), 0, st, part, rows, tiles_n, ids);
   return cudaGetLastError();
 }
 
@@ -276,13 +321,13 @@ cudaError_t launch_ce_rows(const float* logits, int64_t rows, int V, const int32
                            cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   LaunchScope scope_("ce_rows", st);
-  ce_rows_kernel<<<(unsigned)rows, 256, 0, st>>>(logits, rows, V, targets, loss_sum);
+  launch_k(ce_rows_kernel, dim3((unsigned)rows), dim3(256), 0, st, logits, rows, V, targets, loss_sum);
   return cudaGetLastError();
 }
 cudaError_t launch_argmax_rows(const float* logits, int64_t rows, int V, int32_t* ids, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   LaunchScope scope_("argmax_rows", st);
-  argmax_rows_kernel<<<(unsigned)rows, 256, 0, st>>>(logits, rows, V, ids);
+  launch_k(argmax_rows_kernel, dim3((unsigned)rows), dim3(256), 0, st, logits, rows, V, ids);
   return cudaGetLastError();
 }
 

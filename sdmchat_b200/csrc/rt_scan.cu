@@ -216,6 +216,7 @@ __host__ __device__ inline ListSmem list_layout(int M, int k, int dh) {
 // K: compile-time k (0: runtime).  DH: compile-time head width, a multiple of 32 (0: runtime, any width).
 template <int K, int DH>
 __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int nch) {
+  pdl_enter();
   extern __shared__ __align__(16) unsigned char smem[];
   const int k = K > 0 ? K : a.k;
   const int dh = DH > 0 ? DH : a.dh;
@@ -697,6 +698,7 @@ template <int K>
 __global__ void __launch_bounds__(SCAN_THREADS, 1)
     rt_scan_kernel(ScanArgs a, int nch, int n_slices, const __grid_constant__ CUtensorMap mapV,
                    const __grid_constant__ CUtensorMap mapN, const __grid_constant__ CUtensorMap mapD, int use_tma) {
+  pdl_enter();
   __shared__ __align__(8) uint64_t full_bar[2];
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
@@ -1017,13 +1019,13 @@ static cudaError_t launch_scan_k(const ScanArgs& a, int nch, int n_slices, cudaS
   if (e != cudaSuccess) return e;
   {
     LaunchScope scope_("rt_lists", st);
-    rt_lists_kernel<K, DH><<<(unsigned)((int64_t)a.B * a.h * nch), LIST_THREADS, lsm, st>>>(a, nch);
+    launch_k(rt_lists_kernel<K, DH>, dim3((unsigned)((int64_t)a.B * a.h * nch)), dim3(LIST_THREADS), lsm, st, a, nch);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   const ScanMaps m = scan_maps(a);
   LaunchScope scope_("rt_scan", st);
-  rt_scan_kernel<K><<<(unsigned)((int64_t)a.B * a.h * n_slices), SCAN_THREADS, ssm, st>>>(a, nch, n_slices, m.v,
+  launch_k(rt_scan_kernel<K>, dim3((unsigned)((int64_t)a.B * a.h * n_slices)), dim3(SCAN_THREADS), ssm, st, a, nch, n_slices, m.v,
                                                                                          m.num, m.den, m.use_tma);
   return cudaGetLastError();
 }
