@@ -230,17 +230,23 @@ def gemm_flops(tag, rows, layers):
 
 
 # DRAM bytes (read + write) per token of one launch, from the ncu capture summarised in
-# profiles/{pk_kernel,rt_lists_rt_scan,ts_gather_rt_finish}_lm_d768_L12_B4_T2048.md (8,192 tokens, layer 6),
+# profiles/{pk_fast_kernel,rt_lists_rt_scan,ts_gather_rt_finish}_lm_d768_L12_B4_T2048.md (8,192 tokens, layer 6),
 # scaled by tokens: the bench's 65,536-token launches are too large to capture with every metric.
 NCU_DRAM_PER_TOKEN = {
-    ("pk_address", "rt_address"): (26591744 + 33536) / 8192,
-    ("pk_address", "ts"): 4334080 / 8192,
+    ("pk_address", "rt_address"): (26652160 + 49920) / 8192,
+    ("pk_address", "ts"): 4578816 / 8192,
     ("rt_lists", ""): (51309056 + 4100608) / 8192,
     ("rt_scan", ""): (64075264 + 2735616) / 8192,
     ("ts_gather", "ts"): 15511808 / 8192,
     ("rt_finish", "rt_out"): (25603840 + 92160) / 8192,
 }
 
+
+# Algorithmic HBM bytes of the SDM scan per (token, head), the per-unit figure of the reference's chunked form
+# (chunk L = 128, M = 1024 slots, dh = 64, k = 16): the state in and out once per chunk 2*M*(dh+1)*4/L = 4,160,
+# slot ids + weights of the writes and reads 2k*(4+4) = 256, the bf16 value row 2*dh = 128, num/den
+# 4*(dh+1) = 260.  This design keeps the state on chip, so its own traffic is far below this figure.
+SCAN_BYTES_PER_TOKEN_HEAD = 2 * 1024 * 65 * 4 // 128 + 2 * 16 * 8 + 2 * 64 + 4 * 65
 
 ROW_STREAMS = 2  # rows split over two CUDA streams in the timed steps (OneSdmLM.loss_sum row_streams)
 
@@ -396,6 +402,37 @@ def run_ours(a):
                 "traffic_source": "ncu dram bytes per token of a 8,192-token capture, scaled to the launch",
                 "algorithmic_bytes_per_launch": round(byts / nl), "peak_source": f"{how} hbm_gbs",
                 "avg_launch_ms": round(per_kernel[dom]["ms"] / nl, 4)}
+    # every kernel against its own roofline (tensor for the GEMM, HBM for the rest)
+    by_kernel = {}
+    for k, v in per_kernel.items():
+        if k == "gemm_tc":
+            fl = sum(gemm_flops(tag, rows_tokens, a.layers) * n for kk, tag, n, ms in groups if kk == k)
+            ach = fl / (v["ms"] / 1e3) / 1e12
+            by_kernel[k] = {"bound": "tensor", "achieved": round(ach, 1), "unit": "TFLOP/s",
+                            "frac": round(ach / pk["bf16_tflops_sustained"], 4)}
+        else:
+            byts = sum(kernel_bytes(k, tag, rows_tokens) * n for kk, tag, n, ms in groups if kk == k)
+            if byts:
+                ach = byts / (v["ms"] / 1e3) / 1e9
+                by_kernel[k] = {"bound": "hbm", "achieved": round(ach, 1), "unit": "GB/s",
+                                "frac": round(ach / pk["hbm_gbs"], 4)}
+    # the SDM scan (rt_lists + rt_scan) at SURVEY's algorithmic bytes of the reference's chunked form
+    scan_ms = sum(per_kernel[k]["ms"] for k in ("rt_lists", "rt_scan") if k in per_kernel)
+    roof_scan = None
+    if scan_ms > 0:
+        th = rows_tokens * HEADS * a.layers * a.steps  # (token, head) units of the profiled pass
+        alg = th * SCAN_BYTES_PER_TOKEN_HEAD
+        ach = alg / (scan_ms / 1e3) / 1e9
+        own = th * (kernel_bytes("rt_lists", "", 1) + kernel_bytes("rt_scan", "", 1)) / HEADS
+        dram = th * (NCU_DRAM_PER_TOKEN[("rt_lists", "")] + NCU_DRAM_PER_TOKEN[("rt_scan", "")]) / HEADS
+        roof_scan = {"kernels": "rt_lists + rt_scan", "bound": "hbm", "achieved": round(ach, 1), "unit": "GB/s",
+                     "peak": pk["hbm_gbs"], "frac": round(ach / pk["hbm_gbs"], 4),
+                     "algorithmic_bytes_per_token_head": SCAN_BYTES_PER_TOKEN_HEAD,
+                     "algorithmic_basis": "the reference's chunked scan (L=128): state in + out per chunk "
+                                          "2*M*(dh+1)*4/L + ids/weights 2k*8 + V 2*dh + num/den 4*(dh+1)",
+                     "own_bytes_per_token_head": round(own / th, 1),
+                     "own_frac": round(own / (scan_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+                     "traffic_per_token_head": round(dram / th, 1), "ms_per_step": round(scan_ms / a.steps, 3)}
     breakdown = {k: {"ms_per_step": round(v["ms"] / a.steps, 3), "launches_per_step": v["launches"] / a.steps,
                      "by_call_site_ms": {t: round(ms / a.steps, 3) for t, ms in v["tags"].items()}}
                  for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1]["ms"])}
@@ -444,7 +481,8 @@ def run_ours(a):
                                       f"k32, V32768, {B} rows x {T} tokens per GPU",
                           "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world} (batch shards)",
                           "row_streams": ROW_STREAMS, "l2": "per-step working set > 126 MB L2 (no flush)"},
-               "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu,
+               "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "roofline_scan": roof_scan,
+               "roofline_by_kernel": by_kernel, "cpu_baseline": cpu,
                "profiled_pass": f"{a.steps} steps, one row stream, CUDA events around every launch (roofline, kernels)",
                "clocks": clk, "decode": decode, "loss_mean": round(loss_mean, 5), "kernels": breakdown}
         print(json.dumps(out), flush=True)

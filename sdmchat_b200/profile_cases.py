@@ -5,6 +5,7 @@
     python -m sdmchat_b200.profile_cases pk       # product-key addressing of 16384 tokens x 12 heads
     python -m sdmchat_b200.profile_cases decode   # 32 streams x 12 layers FULL decode steps
     python -m sdmchat_b200.profile_cases lm       # FULL d768 L12 forward + CE sum, 4 x 2048 Zipf(1.1) tokens
+    python -m sdmchat_b200.profile_cases scaled   # scaled FULL d1536 L24 forward + CE sum at T = 2K / 8K / 16K
 
 Each case runs its workload once untimed and then `--reps` times (default 2), and prints one line of CUDA-event
 timings; nothing else runs on the GPU, so `ncu -k regex:<kernel> -c N` captures exactly the launches of interest.
@@ -41,6 +42,21 @@ def _full_model(dev):
     return model.to_bf16_stream().to(dev)
 
 
+def _scaled_model(dev):
+    """Scaled FULL (d1536, 24 layers, 24 heads x 64, 1,024 slots, k16; TrainedSdm 4 heads, n_sub 103, dh 384, k32;
+    tied 32,768-row table): seed-0 init with the zero-initialised output maps perturbed."""
+    torch.manual_seed(0)
+    model = S.build_onesdm("onesdm_allsdm", 32768, dict(d=1536, layers=24, mlp_f=4096, heads=24,
+                                                         decays=S.readme_fades(24)))
+    with torch.no_grad():
+        for m in model.mems:
+            torch.nn.init.normal_(m.wo.weight, std=0.02)
+            torch.nn.init.normal_(m.wg.weight, std=0.5 / 1536 ** 0.5)
+        for s in model.sdms:
+            torch.nn.init.normal_(s.values, std=0.02)
+    return model.to_bf16_stream().to(dev)
+
+
 def _timed(fn, reps):
     fn()  # first call: module load and attribute setup stay out of the timing
     torch.cuda.synchronize()
@@ -56,8 +72,9 @@ def _timed(fn, reps):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["scan", "gemm", "pk", "decode", "lm"])
+    ap.add_argument("case", choices=["scan", "gemm", "pk", "decode", "lm", "scaled"])
     ap.add_argument("--reps", type=int, default=2)
+    ap.add_argument("--rows", type=int, default=4, help="scaled: batch rows per window length")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
@@ -94,6 +111,19 @@ def main():
             tgt = torch.from_numpy(ids_np[:, 1:].astype(np.int32)).to(dev)
             ms = _timed(lambda: model.loss_sum(ids, tgt), a.reps)
             out = {"case": "lm", "tokens": 4 * 2048, "ms_per_forward": ms, "tok_per_s": 8192 / (ms / 1e3)}
+        elif a.case == "scaled":
+            import numpy as np
+            model = _scaled_model(dev)
+            rng = np.random.default_rng(1001)
+            per_t = {}
+            for T in (2048, 8192, 16384):
+                ids_np = np.minimum(rng.zipf(1.1, size=(a.rows, T + 1)) - 1, 32767)
+                ids = torch.from_numpy(ids_np[:, :-1].astype(np.int32)).to(dev)
+                tgt = torch.from_numpy(ids_np[:, 1:].astype(np.int32)).to(dev)
+                ms = _timed(lambda: model.loss_sum(ids, tgt), a.reps)
+                per_t[T] = {"ms_per_forward": round(ms, 3), "tok_per_s": round(a.rows * T / (ms / 1e3), 1)}
+            out = {"case": "scaled", "model": "FULL d1536 L24 h24x64 M1024 k16, TrainedSdm n_sub 103", "rows": a.rows,
+                   "by_window": per_t}
         else:
             model = _full_model(dev)
             state = model.init_decode(32, dev)

@@ -6,7 +6,7 @@ import pytest
 import torch
 
 import sdmchat_b200 as S
-from goldens import rel, rel_bf16
+from goldens import rel, rel_bf16, same_selection
 from oracle import sdm_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -156,3 +156,57 @@ def test_loss_sum_row_streams_equal(cuda_ok):
         b = float(model.loss_sum(idx, tgt, row_streams=2).item())
         c = float(model.loss_sum(idx, tgt, row_streams=2).item())
     assert abs(a - b) <= 1e-12 * abs(a) and abs(b - c) <= 1e-12 * abs(a)
+
+
+def test_scaled_full_d1536_window16k_state_carry(cuda_ok):
+    """Scaled FULL shapes (d1536, 24 heads x 64, 1,024 slots, k16, window 16,384): the chunked scan carries the
+    state through 256 chunks; the prefix's chunked forward followed by 64 carried-state decode steps (the token
+    recurrence) gives the chunked forward's last 64 outputs and its final memory."""
+    torch.manual_seed(7)
+    m = S.RunTimeSdm(1536, heads=24, n_sub=32, d_a=32, k=16, decays=S.readme_fades(24))
+    with torch.no_grad():
+        for lin in (m.wk, m.wq, m.wv):
+            torch.nn.init.normal_(lin.weight, std=0.02)
+        torch.nn.init.normal_(m.wo.weight, std=0.02)
+        torch.nn.init.normal_(m.wg.weight, std=0.5 / 1536 ** 0.5)
+    m = m.to(DEV)
+    T, tail = 16384, 64
+    g = torch.Generator(device=DEV).manual_seed(8)
+    x = torch.randn(1, T, 1536, device=DEV, generator=g)
+    with torch.no_grad():
+        full = m(x)
+        mem_full, cnt_full = (t.clone() for t in m.last_state)
+        _, o = m.forward_with(x[:, :T - tail], want=("sel",))
+        st = m.init_state(1, DEV)
+        st["mem"].copy_(m.last_state[0])
+        st["cnt"].copy_(m.last_state[1])
+        st["last_w"].copy_(o["siw"][:, :, -1, :])
+        steps = torch.stack([m.decode_step(x[:, t], st) for t in range(T - tail, T)], 1)
+    assert torch.isfinite(full).all()
+    torch.testing.assert_close(steps, full[:, T - tail:], atol=1e-5, rtol=1e-4)
+    mem_dec = st["mem"] * st["scale"][..., None, None]
+    cnt_dec = st["cnt"] * st["scale"][..., None]
+    assert float((mem_dec - mem_full).abs().max() / mem_full.abs().max()) < 1e-4
+    assert float((cnt_dec - cnt_full).abs().max() / cnt_full.abs().max()) < 1e-4
+
+
+def test_scaled_trained_sdm_d1536_against_oracle(cuda_ok):
+    """Scaled FULL's TrainedSdm body (d1536: 4 heads, d_a 32, n_sub 103 -> 10,609 slots, dh 384, k 32) against the
+    CPU oracle: selections exact wherever the margin exceeds 1e-6, outputs within 2e-3."""
+    rng = np.random.default_rng(9)
+    torch.manual_seed(9)
+    n_sub = O.matched_sdm_n_sub(1536, 4096, 4, 32)
+    ts = S.TrainedSdm(1536, n_sub=n_sub, heads=4, d_a=32, k=32)
+    with torch.no_grad():
+        torch.nn.init.normal_(ts.values, std=0.02)
+        torch.nn.init.normal_(ts.wo.weight, std=0.02)
+    sd = {k: v.detach().float().numpy() for k, v in ts.state_dict().items()}
+    ts = ts.to(DEV)
+    x = rng.standard_normal((2, 300, 1536)).astype(np.float32)
+    p = O.TrainedSdmParams(sd, 4, n_sub, 32, 32)
+    want, si_o, margin = O.trained_sdm(p, x)
+    with torch.no_grad():
+        out = ts(torch.from_numpy(x).to(DEV)).cpu().numpy()
+    ok, n, bad = same_selection(ts.last_si.cpu().numpy().reshape(si_o.shape), si_o, margin, 1e-6)
+    assert ok, f"{bad} of {n}"
+    assert rel(out, want) < 2e-3
