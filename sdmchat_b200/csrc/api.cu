@@ -89,7 +89,7 @@ RtWs carve_rt(Bump& bp, const sdm_rt_params* p, int64_t N, bool own_sel, bool ow
 // rmsnorm -> projection GEMM -> write and read addresses (+ soft weights, gate) for N tokens (token n = b*T + t).
 template <typename T>
 cudaError_t rt_prepare(const sdm_rt_params* p, const T* x, int64_t N, int T_bh, T* hx, float* proj, int32_t* siw,
-                       float* ww, int32_t* sir, float* wr, cudaStream_t st) {
+                       float* ww, int32_t* sir, float* wr, cudaStream_t st, bool address = true) {
   const int h = p->heads, d = p->d;
   const int64_t C = 2LL * h * p->d_a + d + h;
   cudaError_t e = launch_rmsnorm<T>(x, static_cast<const T*>(p->norm_w), N, d, p->norm_eps, hx, st);
@@ -97,7 +97,7 @@ cudaError_t rt_prepare(const sdm_rt_params* p, const T* x, int64_t N, int T_bh, 
   EpiProj ep{proj, C, p->addr_b, p->wg_bias, h * p->d_a, 2 * h * p->d_a + d};
   OpTag tag_("rt_proj");
   e = launch_gemm<T, EpiProj>(hx, d, static_cast<const T*>(p->w_proj), d, N, d, (int)C, ep, st);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || !address) return e;
   OpTag tag2_("rt_address");
   PkArgs pa{};
   pa.ldz = C;
@@ -228,6 +228,17 @@ sdm_status ts_forward_t(const sdm_ts_params* p, const void* xv, int64_t N, int a
   OpTag tag_("ts");
   EpiF32 eq{q, (int64_t)h * p->d_a};
   SDM_TRY(launch_gemm<T, EpiF32>(static_cast<T*>(hs), d, static_cast<const T*>(p->wq), d, N, d, h * p->d_a, eq, st));
+  constexpr int split = sizeof(T) == 2;
+  if (sizeof(T) == 2 && ts_addr_gather_ok(N, h, p->d_a, p->n_sub, p->k, dh) &&
+      (reinterpret_cast<uintptr_t>(p->values) & 15) == 0) {  // decode-sized: selection and read in one launch
+    SDM_TRY(launch_ts_addr_gather(q, (int64_t)h * p->d_a, p->keys1, p->keys2, p->log_scale, p->n_sub, p->k,
+                                  static_cast<const bf16_t*>(p->values), N, h, dh, si, w,
+                                  reinterpret_cast<bf16_t*>(rb), split, st));
+    EpiResid<T> er{add_res ? x : nullptr, static_cast<T*>(outv), d};
+    SDM_TRY(launch_gemm<T, EpiResid<T>>(static_cast<T*>(rb), (1 + split) * d, static_cast<const T*>(p->wo), d, N,
+                                        (1 + split) * d, d, er, st, d));
+    return SDM_OK;
+  }
   PkArgs pa{};
   pa.z = q;
   pa.ldz = (int64_t)h * p->d_a;
@@ -243,7 +254,6 @@ sdm_status ts_forward_t(const sdm_ts_params* p, const void* xv, int64_t N, int a
   pa.si = si;
   pa.log_scale = p->log_scale;
   SDM_TRY(launch_pk_address(pa, st));
-  constexpr int split = sizeof(T) == 2;
   SDM_TRY(launch_ts_gather<T>(si, w, static_cast<const T*>(p->values), N, h, p->n_sub * p->n_sub, dh, kk,
                               static_cast<T*>(rb), split, st));
   EpiResid<T> er{add_res ? x : nullptr, static_cast<T*>(outv), d};
@@ -493,10 +503,13 @@ sdm_status sdm_rt_decode_step(const sdm_rt_params* p, const void* x, int S_, con
   const int h = p->heads, d = p->d, dh = d / h, kk = sel_k(p->k, p->n_sub);
   const int64_t C = 2LL * h * p->d_a + d + h;
   cudaStream_t st = S(stream);
+  const bool fused = rt_decode_fused_ok(p->d_a, p->n_sub, kk);  // the step selects its slots itself
   if (p->dtype == SDM_BF16) {
-    SDM_TRY(rt_prepare<bf16_t>(p, (const bf16_t*)x, S_, 1, (bf16_t*)w.hx, w.proj, w.siw, w.ww, w.sir, w.wr, st));
+    SDM_TRY(rt_prepare<bf16_t>(p, (const bf16_t*)x, S_, 1, (bf16_t*)w.hx, w.proj, w.siw, w.ww, w.sir, w.wr, st,
+                               !fused));
   } else {
-    SDM_TRY(rt_prepare<float>(p, (const float*)x, S_, 1, (float*)w.hx, w.proj, w.siw, w.ww, w.sir, w.wr, st));
+    SDM_TRY(rt_prepare<float>(p, (const float*)x, S_, 1, (float*)w.hx, w.proj, w.siw, w.ww, w.sir, w.wr, st,
+                              !fused));
   }
   OpTag tag_("rt_decode");
   DecodeArgs da{};
@@ -523,6 +536,16 @@ sdm_status sdm_rt_decode_step(const sdm_rt_params* p, const void* x, int S_, con
   da.out_norm_eps = p->out_norm_eps;
   da.onorm_w = p->onorm_w;
   da.r = w.rbuf;
+  if (fused) {
+    da.proj = w.proj;
+    da.ldp = C;
+    da.keys1 = p->keys1;
+    da.keys2 = p->keys2;
+    da.log_scale = p->log_scale;
+    da.n_sub = p->n_sub;
+    da.d_a = p->d_a;
+    da.gate_col = p->write_gate ? (int)(2LL * h * p->d_a + d) : -1;
+  }
   if (p->dtype == SDM_BF16) {
     da.split = 1;
     SDM_TRY(launch_rt_decode<bf16_t>(da, st));

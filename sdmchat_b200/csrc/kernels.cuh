@@ -330,6 +330,12 @@ struct PkArgs {
   const float* gate2;
 };
 cudaError_t launch_pk_address(const PkArgs& a, cudaStream_t st);
+// TrainedSdm selection + value read in one launch for decode-sized calls (N * h below 1,184, d_a 32, bf16 values):
+// q (N, ldq) float32 queries -> si, w (N, h, kk) and the read r (hi/lo split rows when split).
+bool ts_addr_gather_ok(int64_t N, int h, int d_a, int n_sub, int k, int dh);
+cudaError_t launch_ts_addr_gather(const float* q, int64_t ldq, const float* keys1, const float* keys2,
+                                  const float* log_scale, int n_sub, int k, const bf16_t* values, int64_t N, int h,
+                                  int dh, int32_t* si, float* w, bf16_t* r, int split, cudaStream_t st);
 
 // The chunked write-then-read scan of RunTimeSdm (track4_onesdm_models.py:215-241, 255-272): a parallel pass per
 // (row, head, chunk) that builds the chunk's slot lists and its intra-chunk reads, then the state scan.
@@ -358,7 +364,14 @@ struct DecodeArgs {
   // RunTimeSdm.finish up to wo, fused: r (S, h * dh) in T (hi/lo bfloat16 rows (S, 2, h * dh) when split)
   int read_sum; float read_eps; int out_norm; float out_norm_eps; const float* onorm_w;
   void* r; int split;
+  // addressing inside the step (keys1 != nullptr; then siw/ww/sir/wr are unused): the projection row of stream s
+  // holds the write keys at proj[s * ldp + hh * d_a], the read queries h * d_a further, the gate at column
+  // gate_col + hh (gate_col < 0: no write gate)
+  const float* proj; int64_t ldp; const float* keys1; const float* keys2; const float* log_scale;
+  int n_sub, d_a, gate_col;
 };
+// True when the decode step can select its slots itself (d_a 32 and a warp-sized selection).
+bool rt_decode_fused_ok(int d_a, int n_sub, int k);
 template <typename T>
 cudaError_t launch_rt_decode(const DecodeArgs& a, cudaStream_t st);
 

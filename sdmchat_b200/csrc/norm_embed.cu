@@ -1,5 +1,5 @@
 // RMSNorm, token-table lookup, SwiGLU activation, RunTimeSdm finish and TrainedSdm value gather.
-#include "kernels.cuh"
+#include "pk_common.cuh"
 
 namespace sdm {
 
@@ -415,6 +415,130 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
                                                                     out_norm, out_norm_eps, onorm_w, r, split);
   return cudaGetLastError();
 }
+// TrainedSdm address + read for decode-sized launches (track4_onesdm_models.py:438-456), one block of four warps
+// per (token, head): warp 0 selects the slots (the warp-per-address selection of the addressing kernels, so the
+// picks are identical) into shared memory and global memory (si, w), then the four warps gather the picked
+// value rows as ts_gather_split_kernel does.  Saves the separate addressing launch of every decode step.
+template <int HALF, int S>
+__global__ void __launch_bounds__(128) ts_addr_gather_kernel(const float* __restrict__ q, int64_t ldq,
+                                                             const float* __restrict__ keys1,
+                                                             const float* __restrict__ keys2,
+                                                             const float* __restrict__ log_scale, int n_sub, int d_a,
+                                                             int kk, const bf16_t* __restrict__ values, int64_t N,
+                                                             int h, int dh, int32_t* __restrict__ si,
+                                                             float* __restrict__ w, bf16_t* __restrict__ r, int split) {
+  pdl_enter();
+  extern __shared__ float tsd_smem[];  // sub-keys (2 x n_sub x HALF), warp scratch (128), candidates (32 S)
+  __shared__ float part[4][256];
+  __shared__ int s_si[32];
+  __shared__ float s_w[32];
+  __shared__ int s_nc;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t item = blockIdx.x;
+  const int hh = (int)(item % h);
+  const int64_t n = item / h;
+  float* kn = tsd_smem;
+  int* cand = reinterpret_cast<int*>(kn + 2 * n_sub * HALF + 128);
+  for (int j = threadIdx.x; j < 2 * n_sub; j += blockDim.x) {  // F.normalize(keys, dim=-1) for this head
+    const float* src = (j < n_sub ? keys1 + ((int64_t)hh * n_sub + j) * HALF
+                                  : keys2 + ((int64_t)hh * n_sub + (j - n_sub)) * HALF);
+    float kv[HALF];
+    normalize_half<HALF>(src, kv);
+#pragma unroll
+    for (int dd = 0; dd < HALF; ++dd) kn[j * HALF + dd] = kv[dd];
+  }
+  const int c1 = kk < n_sub ? kk : n_sub;
+  if (warp == 0) {
+    const int nc = warp_candidates(cand, c1, kk);
+    if (lane == 0) s_nc = nc;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(q) & 15) | (ldq & 3) | (d_a & 3)) == 0;
+    warp_address<HALF, S>(q + n * ldq + (int64_t)hh * d_a, zvec, kn, kn + n_sub * HALF, n_sub, c1, kk, cand, s_nc,
+                          kn + 2 * n_sub * HALF, expf(log_scale[hh]), nullptr, s_si, s_w, nullptr);
+    __syncwarp();
+    if (lane < kk) {
+      si[item * kk + lane] = s_si[lane];
+      w[item * kk + lane] = s_w[lane];
+    }
+  }
+  __syncthreads();
+  const int jn = (kk + 3) / 4, j0 = warp * jn, j1 = min(kk, j0 + jn);
+  const bool active = 8 * lane < dh;
+  const bf16_t* base = values + (int64_t)hh * n_sub * n_sub * dh + 8 * lane;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  for (int j = j0; j < j1; ++j) {
+    const int slot = s_si[j];
+    const float wj = s_w[j];
+    if (active) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)slot * dh));
+      const float4 a = unpack_bf16x4(make_uint2(u.x, u.y)), b = unpack_bf16x4(make_uint2(u.z, u.w));
+      acc[0] = fmaf(wj, a.x, acc[0]);
+      acc[1] = fmaf(wj, a.y, acc[1]);
+      acc[2] = fmaf(wj, a.z, acc[2]);
+      acc[3] = fmaf(wj, a.w, acc[3]);
+      acc[4] = fmaf(wj, b.x, acc[4]);
+      acc[5] = fmaf(wj, b.y, acc[5]);
+      acc[6] = fmaf(wj, b.z, acc[6]);
+      acc[7] = fmaf(wj, b.w, acc[7]);
+    }
+  }
+  if (active) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[warp][8 * lane + e] = acc[e];
+  }
+  __syncthreads();
+  if (warp == 0 && active) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = part[0][8 * lane + e] + part[1][8 * lane + e] + part[2][8 * lane + e] +
+                                      part[3][8 * lane + e];
+    const int64_t c = (int64_t)hh * dh + 8 * lane;
+    store_split4<bf16_t>(r, n, (int64_t)h * dh, c, make_float4(v[0], v[1], v[2], v[3]), split);
+    store_split4<bf16_t>(r, n, (int64_t)h * dh, c + 4, make_float4(v[4], v[5], v[6], v[7]), split);
+  }
+}
+
+bool ts_addr_gather_ok(int64_t N, int h, int d_a, int n_sub, int k, int dh) {
+  const int c1 = k < n_sub ? k : n_sub, kk = k < c1 * c1 ? k : c1 * c1;
+  return N * h < 148 * 8 && d_a == 32 && kk <= 32 && c1 <= 32 && dh % 8 == 0 && dh <= 256 &&
+         pk_warp_slots(n_sub, c1, kk) > 0;
+}
+
+template <int S>
+static cudaError_t launch_ts_addr_gather_s(const float* q, int64_t ldq, const float* keys1, const float* keys2,
+                                           const float* log_scale, int n_sub, int kk, const bf16_t* values,
+                                           int64_t N, int h, int dh, int32_t* si, float* w, bf16_t* r, int split,
+                                           cudaStream_t st) {
+  const size_t smem = ((size_t)2 * n_sub * 16 + 128 + 32 * S) * 4;
+  auto kern = ts_addr_gather_kernel<16, S>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_k(kern, dim3((unsigned)(N * h)), dim3(128), smem, st, q, ldq, keys1, keys2, log_scale, n_sub, 32, kk,
+                  values, N, h, dh, si, w, r, split);
+}
+
+cudaError_t launch_ts_addr_gather(const float* q, int64_t ldq, const float* keys1, const float* keys2,
+                                  const float* log_scale, int n_sub, int k, const bf16_t* values, int64_t N, int h,
+                                  int dh, int32_t* si, float* w, bf16_t* r, int split, cudaStream_t st) {
+  if (N == 0) return cudaSuccess;
+  if (!ts_addr_gather_ok(N, h, 32, n_sub, k, dh) || (reinterpret_cast<uintptr_t>(values) & 15) != 0)
+    return cudaErrorInvalidValue;
+  const int c1 = k < n_sub ? k : n_sub, kk = k < c1 * c1 ? k : c1 * c1;
+  LaunchScope scope_("ts_addr_gather", st);
+  switch (pk_warp_slots(n_sub, c1, kk)) {
+    case 1: return launch_ts_addr_gather_s<1>(q, ldq, keys1, keys2, log_scale, n_sub, kk, values, N, h, dh, si, w, r,
+                                              split, st);
+    case 2: return launch_ts_addr_gather_s<2>(q, ldq, keys1, keys2, log_scale, n_sub, kk, values, N, h, dh, si, w, r,
+                                              split, st);
+    default: return launch_ts_addr_gather_s<4>(q, ldq, keys1, keys2, log_scale, n_sub, kk, values, N, h, dh, si, w,
+                                               r, split, st);
+  }
+}
+
 template <typename T>
 cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values, int64_t N, int h, int M, int dh,
                              int k, T* r, int split, cudaStream_t st) {

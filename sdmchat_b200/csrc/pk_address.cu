@@ -6,50 +6,12 @@
 // built: a frontier walk over the two sorted lists emits the top-kk combined scores in (score descending,
 // flat index a*c1+b ascending) order, which is the order a stable top-k of the reference's flattened `comb`
 // gives.  Only exactly equal scores can order differently from aten::topk, whose tie order is unspecified.
-#include "kernels.cuh"
+#include "pk_common.cuh"
 
 namespace sdm {
 
 __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
   return va > vb || (va == vb && ia < ib);
-}
-
-// (score, tie) as one 64-bit key whose unsigned order is the selection order: score descending, tie ascending.
-// High word: the order-preserving bit image of the float score; low word: 0xFFFFFFFF - tie.  One 64-bit compare
-// then orders both at once, exactly, and a compare-exchange is that compare plus four selects.
-typedef unsigned long long KT;
-__device__ __forceinline__ KT kmax(KT a, KT b) { return a > b ? a : b; }
-__device__ __forceinline__ KT kmin(KT a, KT b) { return a > b ? b : a; }
-__device__ __forceinline__ KT pk_key(float s, uint32_t tie) {
-  const uint32_t b = __float_as_uint(s + 0.f);  // -0 -> +0: equal scores share one image
-  const uint32_t m = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  return ((KT)m << 32) | (KT)(0xFFFFFFFFu - tie);
-}
-__device__ __forceinline__ float pk_key_score(KT k) {
-  const uint32_t m = (uint32_t)(k >> 32);
-  return __uint_as_float((m & 0x80000000u) ? (m & 0x7FFFFFFFu) : ~m);
-}
-__device__ __forceinline__ uint32_t pk_key_tie(KT k) { return 0xFFFFFFFFu - (uint32_t)k; }
-
-// Cosine score of a normalised half against one sub-key row kr (shared memory, 16-byte aligned when HALF is a
-// multiple of 4): fmaf in dd order, the row read four floats at a time.
-template <int HALF>
-__device__ __forceinline__ float half_dot(const float (&zn)[HALF], const float* kr) {
-  float s = 0.f;
-  if constexpr (HALF % 4 == 0) {
-#pragma unroll
-    for (int d4 = 0; d4 < HALF / 4; ++d4) {
-      const float4 kv = reinterpret_cast<const float4*>(kr)[d4];
-      s = fmaf(zn[4 * d4], kv.x, s);
-      s = fmaf(zn[4 * d4 + 1], kv.y, s);
-      s = fmaf(zn[4 * d4 + 2], kv.z, s);
-      s = fmaf(zn[4 * d4 + 3], kv.w, s);
-    }
-  } else {
-#pragma unroll
-    for (int dd = 0; dd < HALF; ++dd) s = fmaf(zn[dd], kr[dd], s);
-  }
-  return s;
 }
 
 // Sort C (power of two) keys descending: a bitonic network of max/min pairs (directions fixed at compile time).
@@ -223,53 +185,7 @@ __device__ __noinline__ void half_topc_stored(const float* sc, int n_sub, KT (&t
   }
 }
 
-// F.normalize of one half: src[0..HALF) / max(||src||, 1e-12).  vec: src is 16-byte aligned (HALF a multiple
-// of 4) and is read four floats at a time.
-template <int HALF>
-__device__ __forceinline__ void normalize_half(const float* src, float (&zn)[HALF], bool vec = false) {
-  if constexpr (HALF % 4 == 0) {
-    if (vec) {
-#pragma unroll
-      for (int d4 = 0; d4 < HALF / 4; ++d4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(src) + d4);
-        zn[4 * d4] = v.x;
-        zn[4 * d4 + 1] = v.y;
-        zn[4 * d4 + 2] = v.z;
-        zn[4 * d4 + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int dd = 0; dd < HALF; ++dd) zn[dd] = src[dd];
-    }
-  } else {
-#pragma unroll
-    for (int dd = 0; dd < HALF; ++dd) zn[dd] = src[dd];
-  }
-  float ss = 0.f;
-#pragma unroll
-  for (int dd = 0; dd < HALF; ++dd) ss = fmaf(zn[dd], zn[dd], ss);
-  const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
-#pragma unroll
-  for (int dd = 0; dd < HALF; ++dd) zn[dd] = __fdiv_rn(zn[dd], nrm);
-}
-
 constexpr int PK_THREADS = 128;
-
-// First output element of address (token n, head hh): the (B, h, T_bh, kk) layout when T_bh > 0 (token
-// n = b * T_bh + t), else (N, h, kk).  32-bit division whenever n fits.
-__device__ __forceinline__ int64_t pk_dst(int64_t n, int hh, int h, int T_bh, int kk) {
-  if (T_bh <= 0) return (n * h + hh) * kk;
-  int64_t bb, t;
-  if (n <= 0x7fffffff) {
-    const uint32_t q = (uint32_t)n / (uint32_t)T_bh;
-    bb = q;
-    t = (uint32_t)n - q * (uint32_t)T_bh;
-  } else {
-    bb = n / T_bh;
-    t = n % T_bh;
-  }
-  return ((bb * h + hh) * T_bh + t) * kk;
-}
 
 // The top-kk of the c1 x c1 grid of combined scores (v1[a] + v2[b]) / 2 over two lists sorted descending, in
 // (score descending, flat index a * c1 + b ascending) order: a frontier walk, row a's next candidate being
@@ -785,39 +701,6 @@ static cudaError_t launch_pkf_half(const PkArgs& a, int c1, int kk, cudaStream_t
 // (a, b) -- are sorted by (combined score desc, flat index a*c1+b asc) and the first kk are the selection.
 constexpr int PKW_WARPS = 4;
 
-// Descending bitonic sort of the warp's 32*S keys, element e = lane*S + s in v[s].
-template <int S>
-__device__ __forceinline__ void warp_sort_desc(KT (&v)[S]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int size = 2; size <= 32 * S; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      if (stride >= S) {  // partner in another lane, same slot
-        const int lm = stride / S;
-#pragma unroll
-        for (int q = 0; q < S; ++q) {
-          const int e = lane * S + q;
-          const KT o = __shfl_xor_sync(0xffffffffu, v[q], lm);
-          const bool keep_max = ((lane & lm) == 0) == ((e & size) == 0);
-          v[q] = keep_max ? (v[q] > o ? v[q] : o) : (v[q] > o ? o : v[q]);
-        }
-      } else {  // partner in this lane
-#pragma unroll
-        for (int q = 0; q < S; ++q) {
-          const int q2 = q ^ stride;
-          if (q2 > q) {
-            const bool desc = ((lane * S + q) & size) == 0;
-            const KT hi = v[q] > v[q2] ? v[q] : v[q2], lo = v[q] > v[q2] ? v[q2] : v[q];
-            v[q] = desc ? hi : lo;
-            v[q2] = desc ? lo : hi;
-          }
-        }
-      }
-    }
-  }
-}
-
 template <int HALF, int S>
 __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c1, int kk) {
   pdl_enter();
@@ -828,15 +711,11 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
   float* const wb = pr ? a.w2 : a.w;
   int32_t* const sib = pr ? a.si2 : a.si;
   const float* const gb = pr ? a.gate2 : a.gate;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int n_sub = a.n_sub;
   float* kn1 = pkw_smem;                 // (n_sub, HALF)
   float* kn2 = kn1 + n_sub * HALF;
   float* wsm = kn2 + n_sub * HALF + warp * 4 * 32;  // per warp: v1[32], i1[32], v2[32], i2[32]
-  float* v1 = wsm;
-  int* i1 = reinterpret_cast<int*>(wsm + 32);
-  float* v2 = wsm + 64;
-  int* i2 = reinterpret_cast<int*>(wsm + 96);
   int* cand = reinterpret_cast<int*>(pkw_smem + 2 * n_sub * HALF + PKW_WARPS * 4 * 32);  // (a << 8 | b) pairs
   int* ncand = cand + 32 * S;
   for (int j = tid; j < 2 * n_sub; j += PKW_WARPS * 32) {
@@ -848,95 +727,19 @@ __global__ void __launch_bounds__(PKW_WARPS * 32) pk_warp_kernel(PkArgs a, int c
 #pragma unroll
     for (int dd = 0; dd < HALF; ++dd) dst[dd] = kv[dd];
   }
-  if (tid == 0) {  // the candidate pairs, in (a, b) order
-    int nc = 0;
-    for (int ra = 0; ra < c1; ++ra)
-      for (int rb = 0; rb < c1 && (ra + 1) * (rb + 1) <= kk; ++rb) cand[nc++] = (ra << 8) | rb;
-    *ncand = nc;
+  if (warp == 0) {
+    const int nc = warp_candidates(cand, c1, kk);
+    if (tid == 0) *ncand = nc;
   }
   __syncthreads();
   const int64_t n = (int64_t)blockIdx.x * PKW_WARPS + warp;
   if (n >= a.N) return;
   const float* zr = zb + n * a.ldz + (int64_t)hh * a.d_a;
   const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(zb) & 15) | (a.ldz & 3) | (a.d_a & 3)) == 0;
-#pragma unroll 1
-  for (int hf = 0; hf < 2; ++hf) {
-    float zn[HALF];
-    normalize_half<HALF>(zr + hf * HALF, zn, zvec);
-    const float* kn = hf ? kn2 : kn1;
-    KT key[S];
-#pragma unroll
-    for (int q = 0; q < S; ++q) {
-      const int j = lane * S + q;
-      key[q] = 0ull;  // padding: below every real key
-      if (j < n_sub) {
-        float sc = half_dot<HALF>(zn, kn + j * HALF);
-        if (sc != sc) sc = -INFINITY;
-        key[q] = pk_key(sc, (uint32_t)j);
-      }
-    }
-    warp_sort_desc<S>(key);
-    float* vo = hf ? v2 : v1;
-    int* io = hf ? i2 : i1;
-#pragma unroll
-    for (int q = 0; q < S; ++q) {
-      const int e = lane * S + q;
-      if (e < c1) {
-        vo[e] = pk_key_score(key[q]);
-        io[e] = (int)pk_key_tie(key[q]);
-      }
-    }
-    __syncwarp();
-  }
-  // the combined candidates, sorted: the first kk elements are the selection in order
-  const int nc = *ncand;
-  KT ck[S];
-#pragma unroll
-  for (int q = 0; q < S; ++q) {
-    const int e = lane * S + q;
-    ck[q] = 0ull;
-    if (e < nc) {
-      const int ab = cand[e], ra = ab >> 8, rb = ab & 255;
-      ck[q] = pk_key((v1[ra] + v2[rb]) * 0.5f, (uint32_t)(ra * c1 + rb));
-    }
-  }
-  warp_sort_desc<S>(ck);
   const int64_t dst = pk_dst(n, hh, a.h, a.T_bh, kk);
-  float sv[S], ex[S];
-  const float scale = wb ? expf(a.log_scale[hh]) : 0.f;
-  const float mx = pk_key_score(__shfl_sync(0xffffffffu, ck[0], 0)) * scale;  // the first pick is the largest
-#pragma unroll
-  for (int q = 0; q < S; ++q) {
-    const int e = lane * S + q;
-    sv[q] = pk_key_score(ck[q]);
-    ex[q] = e < kk ? expf(sv[q] * scale - mx) : 0.f;
-    if (e < kk) {
-      const int flat = (int)pk_key_tie(ck[q]), ra = flat / c1, rb = flat - ra * c1;
-      sib[dst + e] = i1[ra] * n_sub + i2[rb];
-      if (svb) svb[dst + e] = sv[q];
-    }
-  }
-  if (wb) {
-    // the sum in pick order, as the thread-per-address kernel adds it
-    float sum = 0.f;
-    for (int j = 0; j < kk; ++j) {
-      float ej = ex[0];
-#pragma unroll
-      for (int q = 1; q < S; ++q)
-        if ((j % S) == q) ej = ex[q];
-      sum += __shfl_sync(0xffffffffu, ej, j / S);
-    }
-    const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
-#pragma unroll
-    for (int q = 0; q < S; ++q) {
-      const int e = lane * S + q;
-      if (e < kk) {
-        float wj = __fdiv_rn(ex[q], sum);
-        if (gb) wj = wj * g;
-        wb[dst + e] = wj;
-      }
-    }
-  }
+  warp_address<HALF, S>(zr, zvec, kn1, kn2, n_sub, c1, kk, cand, *ncand, wsm, wb ? expf(a.log_scale[hh]) : 0.f,
+                        gb ? gb + n * a.ldgate + hh : nullptr, sib + dst, wb ? wb + dst : nullptr,
+                        svb ? svb + dst : nullptr);
 }
 
 template <int HALF, int S>
@@ -949,15 +752,6 @@ static cudaError_t launch_pk_warp_s(const PkArgs& a, int c1, int kk, cudaStream_
   LaunchScope scope_("pk_address", st);
   launch_k(kern, dim3(grid), dim3(PKW_WARPS * 32), smem, st, a, c1, kk);
   return cudaGetLastError();
-}
-
-// Slots per lane: enough for the n_sub scores of a half and for the candidate pairs.
-static int pk_warp_slots(int n_sub, int c1, int kk) {
-  int nc = 0;
-  for (int ra = 0; ra < c1; ++ra)
-    for (int rb = 0; rb < c1 && (ra + 1) * (rb + 1) <= kk; ++rb) ++nc;
-  const int need = n_sub > nc ? n_sub : nc;
-  return need <= 32 ? 1 : (need <= 64 ? 2 : (need <= 128 ? 4 : 0));
 }
 
 template <int HALF>

@@ -13,17 +13,21 @@
 // The step's slot ids and weights are staged in shared memory, then every row the step touches (k read rows, k
 // written rows) is loaded in one round trip before any store; the read is finished in the block (one block
 // reduction for the out-norm) and written as the wo GEMM's input.
-#include "kernels.cuh"
+#include "pk_common.cuh"
 
 namespace sdm {
 
 constexpr int DEC_MAX_K = 32;
 
-template <typename T>
+// HALF > 0: the step selects its slots itself (warp 0 the write address, warp 1 the read address, S slots per
+// lane; shared-memory normalised sub-keys); HALF == 0: the selections come in siw/ww/sir/wr.
+template <typename T, int HALF, int S>
 __global__ void rt_decode_kernel(DecodeArgs a) {
   pdl_enter();
   __shared__ int s_ir[DEC_MAX_K], s_iw[DEC_MAX_K], s_prev[DEC_MAX_K];
   __shared__ float s_fr[DEC_MAX_K], s_fw[DEC_MAX_K], s_red[32];
+  __shared__ int s_nc;
+  extern __shared__ float dec_smem[];  // HALF > 0: sub-keys (2 x n_sub x HALF), two warps' scratch, candidates
   const int sh = blockIdx.x;
   const int hh = sh % a.h;
   const int s = sh / a.h;
@@ -31,19 +35,50 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   float* mem = a.mem + (int64_t)sh * M * dh;
   float* cnt = a.cnt + (int64_t)sh * M;
   int32_t* lw = a.last_w + (int64_t)sh * k;
-  const int t = threadIdx.x;
-  if (t < k) {  // slot ids are clamped into the state (see rt_scan.cu)
+  const int t = threadIdx.x, warp = t >> 5;
+  if constexpr (HALF > 0) {
+    const int n_sub = a.n_sub;
+    float* kn = dec_smem;
+    for (int j = t; j < 2 * n_sub; j += blockDim.x) {  // F.normalize(keys, dim=-1) for this head
+      const float* src = (j < n_sub ? a.keys1 + ((int64_t)hh * n_sub + j) * HALF
+                                    : a.keys2 + ((int64_t)hh * n_sub + (j - n_sub)) * HALF);
+      float kv[HALF];
+      normalize_half<HALF>(src, kv);
+#pragma unroll
+      for (int dd = 0; dd < HALF; ++dd) kn[j * HALF + dd] = kv[dd];
+    }
+    if (warp == 0) {
+      const int c1 = min(a.k, n_sub);
+      const int nc = warp_candidates(reinterpret_cast<int*>(kn + 2 * n_sub * HALF + 2 * 128), c1, k);
+      if (t == 0) s_nc = nc;
+    }
+  } else if (t < k) {  // slot ids are clamped into the state (see rt_scan.cu)
     s_ir[t] = min(max(a.sir[(int64_t)sh * k + t], 0), M - 1);
     s_fr[t] = a.wr[(int64_t)sh * k + t];
     s_iw[t] = min(max(a.siw[(int64_t)sh * k + t], 0), M - 1);
     s_fw[t] = a.ww[(int64_t)sh * k + t];
-    s_prev[t] = lw[t];
   }
+  if (t < k) s_prev[t] = lw[t];
   const float lam = a.decay[hh];
   // every thread reads the per-head words (scale, last written rows) before thread 0 rewrites them
   const float sc = a.scale[sh];
   const bool reset = a.reset && a.reset[s];
   __syncthreads();
+  if constexpr (HALF > 0) {
+    if (warp < 2) {  // warp 0: the write address (gated keys), warp 1: the read address (queries)
+      const int n_sub = a.n_sub;
+      const float* kn = dec_smem;
+      const float* zb = a.proj + (int64_t)s * a.ldp + (warp ? a.h * a.d_a : 0);
+      const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(a.proj) & 15) | (a.ldp & 3) | (a.d_a & 3) |
+                                          (a.h * a.d_a & 3)) == 0;
+      const float* gate = (warp == 0 && a.gate_col >= 0) ? a.proj + (int64_t)s * a.ldp + a.gate_col + hh : nullptr;
+      warp_address<HALF, S>(zb + hh * a.d_a, zvec, kn, kn + n_sub * HALF, n_sub, min(a.k, n_sub), k,
+                            reinterpret_cast<const int*>(kn + 2 * n_sub * HALF + 2 * 128), s_nc,
+                            const_cast<float*>(kn) + 2 * n_sub * HALF + warp * 128, expf(a.log_scale[hh]), gate,
+                            warp ? s_ir : s_iw, warp ? s_fr : s_fw, nullptr);
+    }
+    __syncthreads();
+  }
   const int c = t;
   const bool act = c < dh;
   const bool own_cnt = (c == 0);
@@ -151,13 +186,36 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   }
 }
 
+bool rt_decode_fused_ok(int d_a, int n_sub, int k) {
+  const int c1 = k < n_sub ? k : n_sub, kk = k < c1 * c1 ? k : c1 * c1;
+  return d_a == 32 && k <= DEC_MAX_K && c1 <= 32 && kk <= 32 && pk_warp_slots(n_sub, c1, kk) > 0;
+}
+
+template <typename T, int S>
+static cudaError_t launch_rt_decode_fused(const DecodeArgs& a, int threads, cudaStream_t st) {
+  const size_t smem = ((size_t)2 * a.n_sub * 16 + 2 * 128 + 32 * S) * 4;
+  auto kern = rt_decode_kernel<T, 16, S>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_k(kern, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), smem, st, a);
+}
+
 template <typename T>
 cudaError_t launch_rt_decode(const DecodeArgs& a, cudaStream_t st) {
   if (a.S == 0) return cudaSuccess;
   if (a.k > DEC_MAX_K || a.dh > 1024) return cudaErrorInvalidValue;
-  const int threads = ((a.dh + 31) / 32) * 32;  // one thread per value column
   LaunchScope scope_("rt_decode", st);
-  return launch_k(rt_decode_kernel<T>, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), 0, st, a);
+  if (a.keys1) {  // one thread per value column, and at least the two address warps
+    if (!rt_decode_fused_ok(a.d_a, a.n_sub, a.k)) return cudaErrorInvalidValue;
+    const int threads = a.dh > 64 ? ((a.dh + 31) / 32) * 32 : 64;
+    switch (pk_warp_slots(a.n_sub, a.k < a.n_sub ? a.k : a.n_sub, a.k)) {
+      case 1: return launch_rt_decode_fused<T, 1>(a, threads, st);
+      case 2: return launch_rt_decode_fused<T, 2>(a, threads, st);
+      default: return launch_rt_decode_fused<T, 4>(a, threads, st);
+    }
+  }
+  const int threads = ((a.dh + 31) / 32) * 32;  // one thread per value column
+  return launch_k(rt_decode_kernel<T, 0, 1>, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), 0, st, a);
 }
 template cudaError_t launch_rt_decode<float>(const DecodeArgs&, cudaStream_t);
 template cudaError_t launch_rt_decode<bf16_t>(const DecodeArgs&, cudaStream_t);

@@ -303,3 +303,24 @@ def test_scan_abi_against_token_recurrence(cuda_ok, dup):
         assert rel(den.cpu().numpy().transpose(0, 2, 1), want_den.reshape(B, h, T)) < 1e-5
         assert rel(mem.cpu().numpy(), want_mem) < 1e-5
         assert rel(cnt.cpu().numpy(), want_cnt) < 1e-5
+
+
+def test_trained_sdm_decode_sized_equals_batched(cuda_ok):
+    """Decode-sized TrainedSdm calls select and read in one launch (ts_addr_gather_kernel); large calls use the
+    addressing kernel and the batched gather.  The selections are identical and the reads agree to float32
+    rounding (the two gathers add the 32 picked rows in different groupings)."""
+    rng = np.random.default_rng(21)
+    torch.manual_seed(21)
+    ts = S.TrainedSdm(768, n_sub=72, heads=4, d_a=32, k=32)
+    with torch.no_grad():
+        torch.nn.init.normal_(ts.values, std=0.02)
+        torch.nn.init.normal_(ts.wo.weight, std=0.02)
+    ts = ts.to(DEV).to(torch.bfloat16)
+    x = torch.from_numpy(rng.standard_normal((1, 2000, 768)).astype(np.float32)).to(DEV).bfloat16()
+    with torch.no_grad():
+        big = ts(x)
+        si_big = ts.last_si.clone()
+        small = ts(x[:, :40])
+        si_small = ts.last_si.clone()
+    assert torch.equal(si_big.reshape(2000, 4, 32)[:40], si_small.reshape(40, 4, 32))
+    assert rel_bf16(small.float().cpu().numpy(), big[:, :40].float().cpu().numpy()) < 1e-4
