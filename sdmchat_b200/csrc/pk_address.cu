@@ -559,10 +559,48 @@ __device__ __forceinline__ void walkf_step(float (&kv)[C], const float* v1s, con
   }
 }
 
+// walkf_step with every pick kept in registers (lists up to 16): pick S's combined score in sc[S] and its slot
+// id in sl[S] (S is a compile-time constant, so these are registers), so the outputs need no shared memory.
+template <int C, int S>
+__device__ __forceinline__ void walkr_step(float (&kv)[C], float (&sc)[C], int (&sl)[C], const float* v1s,
+                                          const float* v2s, const uint8_t* i1s, const uint8_t* i2s, uint8_t* brow,
+                                          int n_sub, int kk, int tid) {
+  if constexpr (S < C) {
+    if (S >= kk) return;
+    brow[S * PKF_THREADS + tid] = 0;  // row S can first win at this step
+    float tv[S + 1];
+    int tp[S + 1];
+#pragma unroll
+    for (int q = 0; q <= S; ++q) {
+      tv[q] = kv[q];
+      tp[q] = q;
+    }
+#pragma unroll
+    for (int w = 1; w <= S; w <<= 1) {
+#pragma unroll
+      for (int q = 0; q + w <= S; q += 2 * w) {
+        const bool hi = tv[q + w] > tv[q];  // the higher rows' candidate only when strictly larger
+        tv[q] = hi ? tv[q + w] : tv[q];
+        tp[q] = hi ? tp[q + w] : tp[q];
+      }
+    }
+    const int r = tp[0];
+    const int b = brow[r * PKF_THREADS + tid];
+    sc[S] = tv[0] + 0.f;  // -0 -> +0
+    sl[S] = (int)i1s[r * PKF_THREADS + tid] * n_sub + (int)i2s[b * PKF_THREADS + tid];
+    const int nb = b + 1;  // b + 1 = c1 only after the last pick
+    brow[r * PKF_THREADS + tid] = (uint8_t)nb;
+    const float nk = (v1s[r * PKF_THREADS + tid] + v2s[min(nb, C - 1) * PKF_THREADS + tid]) * 0.5f;
+#pragma unroll
+    for (int q = 0; q <= S; ++q) kv[q] = q == r ? nk : kv[q];
+    walkr_step<C, S + 1>(kv, sc, sl, v1s, v2s, i1s, i2s, brow, n_sub, kk, tid);
+  }
+}
+
 // Resident blocks per SM the register budget is sized for.
 template <int C>
 struct PkfOcc {
-  static constexpr int value = C <= 8 ? 8 : (C <= 16 ? 6 : 3);
+  static constexpr int value = C <= 8 ? 8 : (C <= 16 ? 5 : 3);
 };
 
 template <int HALF, int C>
@@ -616,55 +654,113 @@ __global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_fast_kernel(
     if (!half_lists_fast<HALF, C>(zn, kn, n_sub, ib, lowb, vs, is, tid))
       half_lists_exact<HALF, C>(src, zvec, kn, n_sub, vs, is, tid);
   }
-  {
-    float kv[C];
+  const int64_t dst = pk_dst(n, hh, a.h, a.T_bh, kk);
+  const bool vec = (kk & 3) == 0 && ((reinterpret_cast<uintptr_t>(sib + dst) | (wb ? reinterpret_cast<uintptr_t>(wb + dst) : 0) |
+                                      (svb ? reinterpret_cast<uintptr_t>(svb + dst) : 0)) & 15) == 0;
+  if constexpr (C <= 16) {
+    // picks in registers; outputs and softmax(scale * score) (* gate) in pick order
+    float kv[C], sc[C];
+    int sl[C];
     const float v2_0 = v2s[tid];
 #pragma unroll
     for (int q = 0; q < C; ++q) kv[q] = (v1s[q * P + tid] + v2_0) * 0.5f;
-    walkf_step<C, 0>(kv, v1s, v2s, brow, pick_r, pick_b, kk, tid);
-  }
-  // outputs and softmax(scale * score) (* gate), in pick order; a pick's score and slot come back from the lists
-  const int64_t dst = pk_dst(n, hh, a.h, a.T_bh, kk);
-  auto pick_score = [&](int j) {
-    const int r = pick_r[j * P + tid], b = pick_b[j * P + tid];
-    return (v1s[r * P + tid] + v2s[b * P + tid]) * 0.5f + 0.f;
-  };
-  auto pick_slot = [&](int j) {
-    const int r = pick_r[j * P + tid], b = pick_b[j * P + tid];
-    return (int)i1s[r * P + tid] * n_sub + (int)i2s[b * P + tid];
-  };
-  const bool vec = (kk & 3) == 0 && ((reinterpret_cast<uintptr_t>(sib + dst) | (wb ? reinterpret_cast<uintptr_t>(wb + dst) : 0) |
-                                      (svb ? reinterpret_cast<uintptr_t>(svb + dst) : 0)) & 15) == 0;
-  if (svb) {
+    walkr_step<C, 0>(kv, sc, sl, v1s, v2s, i1s, i2s, brow, n_sub, kk, tid);
     if (vec) {
-      for (int j = 0; j < kk; j += 4)
-        *reinterpret_cast<float4*>(svb + dst + j) =
-            make_float4(pick_score(j), pick_score(j + 1), pick_score(j + 2), pick_score(j + 3));
+#pragma unroll
+      for (int j = 0; j < C; j += 4) {
+        if (j < kk) {
+          *reinterpret_cast<int4*>(sib + dst + j) = make_int4(sl[j], sl[j + 1], sl[j + 2], sl[j + 3]);
+          if (svb) *reinterpret_cast<float4*>(svb + dst + j) = make_float4(sc[j], sc[j + 1], sc[j + 2], sc[j + 3]);
+        }
+      }
     } else {
-      for (int j = 0; j < kk; ++j) svb[dst + j] = pick_score(j);
+#pragma unroll
+      for (int j = 0; j < C; ++j) {
+        if (j < kk) {
+          sib[dst + j] = sl[j];
+          if (svb) svb[dst + j] = sc[j];
+        }
+      }
     }
-  }
-  if (vec) {
-    for (int j = 0; j < kk; j += 4)
-      *reinterpret_cast<int4*>(sib + dst + j) = make_int4(pick_slot(j), pick_slot(j + 1), pick_slot(j + 2), pick_slot(j + 3));
-  } else {
-    for (int j = 0; j < kk; ++j) sib[dst + j] = pick_slot(j);
-  }
-  if (wb) {
-    const float scale = expf(a.log_scale[hh]);
-    float mx = -INFINITY, sum = 0.f;
-    for (int j = 0; j < kk; ++j) mx = fmaxf(mx, pick_score(j) * scale);
-    for (int j = 0; j < kk; ++j) sum += expf(pick_score(j) * scale - mx);
-    const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
-    auto wt = [&](int j) {
-      const float wj = __fdiv_rn(expf(pick_score(j) * scale - mx), sum);
-      return gb ? wj * g : wj;
+    if (wb) {
+      const float scale = expf(a.log_scale[hh]);
+      float mx = -INFINITY, sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < C; ++j)
+        if (j < kk) mx = fmaxf(mx, sc[j] * scale);
+#pragma unroll
+      for (int j = 0; j < C; ++j) {
+        if (j < kk) {
+          sc[j] = expf(sc[j] * scale - mx);
+          sum += sc[j];
+        }
+      }
+      const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
+#pragma unroll
+      for (int j = 0; j < C; ++j) {
+        if (j < kk) {
+          const float wj = __fdiv_rn(sc[j], sum);
+          sc[j] = gb ? wj * g : wj;
+        }
+      }
+      if (vec) {
+#pragma unroll
+        for (int j = 0; j < C; j += 4)
+          if (j < kk) *reinterpret_cast<float4*>(wb + dst + j) = make_float4(sc[j], sc[j + 1], sc[j + 2], sc[j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < C; ++j)
+          if (j < kk) wb[dst + j] = sc[j];
+      }
+    }
+    return;
+  } else {  // picks in shared memory (bytes); a pick's score and slot come back from the lists
+    {
+      float kv[C];
+      const float v2_0 = v2s[tid];
+#pragma unroll
+      for (int q = 0; q < C; ++q) kv[q] = (v1s[q * P + tid] + v2_0) * 0.5f;
+      walkf_step<C, 0>(kv, v1s, v2s, brow, pick_r, pick_b, kk, tid);
+    }
+    auto pick_score = [&](int j) {
+      const int r = pick_r[j * P + tid], b = pick_b[j * P + tid];
+      return (v1s[r * P + tid] + v2s[b * P + tid]) * 0.5f + 0.f;
     };
+    auto pick_slot = [&](int j) {
+      const int r = pick_r[j * P + tid], b = pick_b[j * P + tid];
+      return (int)i1s[r * P + tid] * n_sub + (int)i2s[b * P + tid];
+    };
+    if (svb) {
+      if (vec) {
+        for (int j = 0; j < kk; j += 4)
+          *reinterpret_cast<float4*>(svb + dst + j) =
+              make_float4(pick_score(j), pick_score(j + 1), pick_score(j + 2), pick_score(j + 3));
+      } else {
+        for (int j = 0; j < kk; ++j) svb[dst + j] = pick_score(j);
+      }
+    }
     if (vec) {
       for (int j = 0; j < kk; j += 4)
-        *reinterpret_cast<float4*>(wb + dst + j) = make_float4(wt(j), wt(j + 1), wt(j + 2), wt(j + 3));
+        *reinterpret_cast<int4*>(sib + dst + j) = make_int4(pick_slot(j), pick_slot(j + 1), pick_slot(j + 2), pick_slot(j + 3));
     } else {
-      for (int j = 0; j < kk; ++j) wb[dst + j] = wt(j);
+      for (int j = 0; j < kk; ++j) sib[dst + j] = pick_slot(j);
+    }
+    if (wb) {
+      const float scale = expf(a.log_scale[hh]);
+      float mx = -INFINITY, sum = 0.f;
+      for (int j = 0; j < kk; ++j) mx = fmaxf(mx, pick_score(j) * scale);
+      for (int j = 0; j < kk; ++j) sum += expf(pick_score(j) * scale - mx);
+      const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
+      auto wt = [&](int j) {
+        const float wj = __fdiv_rn(expf(pick_score(j) * scale - mx), sum);
+        return gb ? wj * g : wj;
+      };
+      if (vec) {
+        for (int j = 0; j < kk; j += 4)
+          *reinterpret_cast<float4*>(wb + dst + j) = make_float4(wt(j), wt(j + 1), wt(j + 2), wt(j + 3));
+      } else {
+        for (int j = 0; j < kk; ++j) wb[dst + j] = wt(j);
+      }
     }
   }
 }
