@@ -521,79 +521,121 @@ __device__ __forceinline__ bool half_lists_fast(const float (&zn)[HALF], const f
   return true;
 }
 
-// walk_rows with the rows' positions b_r and the picks (r, b) in shared memory as bytes.  Every byte array here
-// is (rows, PKF_THREADS) with thread tid owning column tid, so regions that alias across phases are still private
-// to their thread (a warp in its walk never touches a byte another warp's halves use).
-template <int C, int S>
-__device__ __forceinline__ void walkf_step(float (&kv)[C], const float* v1s, const float* v2s, uint8_t* brow,
-                                          uint8_t* pick_r, uint8_t* pick_b, int kk, int tid) {
-  if constexpr (S < C) {
-    if (S >= kk) return;
-    brow[S * PKF_THREADS + tid] = 0;  // row S can first win at this step
-    float tv[S + 1];
-    int tp[S + 1];
+// The walk of pk_fast_kernel.  Rows r >= C/2 (>= kk/2) can only ever contribute their first candidate ((r+1)(b+1)
+// <= kk forces b = 0) and those candidates are sorted already (v1 descending, all with v2[0]), so the walk keeps a
+// max tree over the head rows 0..C/2-1 only, plus the next unused tail row, which takes a step only when strictly
+// larger (tail rows come later in flat-index order).  At step s the tree spans rows 0..min(s, C/2-1); the tail's
+// first row cannot win before step C/2.  The rows' positions b_r are bytes in shared memory, each byte array laid
+// out (rows, PKF_THREADS) with thread tid owning column tid, so regions that alias across phases stay private to
+// their thread (a warp in its walk never touches a byte another warp's halves use).
+template <int C>
+struct WalkHT {
+  static constexpr int H = C / 2;
+  float kv[H];  // head row q's current candidate (q, b_q)
+  int tail;     // tail rows taken; the next one is row H + tail
+};
+
+// Take step S's pick over NT head rows (and the tail when TAIL): (r, b) and its score; advance the state.
+template <int C, int NT, bool TAIL>
+__device__ __forceinline__ void walk_take(WalkHT<C>& w, const float* v1s, const float* v2s, uint8_t* brow,
+                                          float v2_0, int c1, int tid, int& r, int& b, float& score) {
+  constexpr int H = C / 2;
+  float tv[NT];
+  int tp[NT];
 #pragma unroll
-    for (int q = 0; q <= S; ++q) {
-      tv[q] = kv[q];
-      tp[q] = q;
+  for (int q = 0; q < NT; ++q) {
+    tv[q] = w.kv[q];
+    tp[q] = q;
+  }
+#pragma unroll
+  for (int st = 1; st < NT; st <<= 1) {
+#pragma unroll
+    for (int q = 0; q + st < NT; q += 2 * st) {
+      const bool hi = tv[q + st] > tv[q];  // the higher rows' candidate only when strictly larger
+      tv[q] = hi ? tv[q + st] : tv[q];
+      tp[q] = hi ? tp[q + st] : tp[q];
     }
-#pragma unroll
-    for (int w = 1; w <= S; w <<= 1) {
-#pragma unroll
-      for (int q = 0; q + w <= S; q += 2 * w) {
-        const bool hi = tv[q + w] > tv[q];  // the higher rows' candidate only when strictly larger
-        tv[q] = hi ? tv[q + w] : tv[q];
-        tp[q] = hi ? tp[q + w] : tp[q];
-      }
+  }
+  if constexpr (TAIL) {  // the next tail row's first candidate, read afresh each step
+    const int rr = H + w.tail;
+    const float vt = rr < c1 ? (v1s[rr * PKF_THREADS + tid] + v2_0) * 0.5f : -INFINITY;
+    if (vt > tv[0]) {
+      r = rr;
+      b = 0;
+      score = vt + 0.f;  // -0 -> +0
+      ++w.tail;
+      return;
     }
-    const int r = tp[0];
-    const int b = brow[r * PKF_THREADS + tid];
-    pick_r[S * PKF_THREADS + tid] = (uint8_t)r;
-    pick_b[S * PKF_THREADS + tid] = (uint8_t)b;
+  }
+  {
+    r = tp[0];
+    b = brow[r * PKF_THREADS + tid];
+    score = tv[0] + 0.f;
     const int nb = b + 1;  // b + 1 = c1 only after the last pick
     brow[r * PKF_THREADS + tid] = (uint8_t)nb;
     const float nk = (v1s[r * PKF_THREADS + tid] + v2s[min(nb, C - 1) * PKF_THREADS + tid]) * 0.5f;
 #pragma unroll
-    for (int q = 0; q <= S; ++q) kv[q] = q == r ? nk : kv[q];
-    walkf_step<C, S + 1>(kv, v1s, v2s, brow, pick_r, pick_b, kk, tid);
+    for (int q = 0; q < NT; ++q) w.kv[q] = q == r ? nk : w.kv[q];
   }
 }
 
-// walkf_step with every pick kept in registers (lists up to 16): pick S's combined score in sc[S] and its slot
-// id in sl[S] (S is a compile-time constant, so these are registers), so the outputs need no shared memory.
+__device__ __forceinline__ int pick_slot_of(const uint8_t* i1s, const uint8_t* i2s, int r, int b, int n_sub,
+                                            int tid) {
+  return (int)i1s[r * PKF_THREADS + tid] * n_sub + (int)i2s[b * PKF_THREADS + tid];
+}
+
+template <int C>
+__device__ __forceinline__ void walk_init(WalkHT<C>& w, const float* v1s, uint8_t* brow, float v2_0, int c1,
+                                          int tid) {
+  constexpr int H = C / 2;
+#pragma unroll
+  for (int q = 0; q < H; ++q) w.kv[q] = (v1s[q * PKF_THREADS + tid] + v2_0) * 0.5f;
+  w.tail = 0;
+}
+
+// Every step unrolled, every pick in registers (lists up to 16): pick S's score in sc[S], its slot id in sl[S].
 template <int C, int S>
-__device__ __forceinline__ void walkr_step(float (&kv)[C], float (&sc)[C], int (&sl)[C], const float* v1s,
+__device__ __forceinline__ void walkr_step(WalkHT<C>& w, float (&sc)[C], int (&sl)[C], const float* v1s,
                                           const float* v2s, const uint8_t* i1s, const uint8_t* i2s, uint8_t* brow,
-                                          int n_sub, int kk, int tid) {
+                                          float v2_0, int c1, int n_sub, int kk, int tid) {
   if constexpr (S < C) {
     if (S >= kk) return;
-    brow[S * PKF_THREADS + tid] = 0;  // row S can first win at this step
-    float tv[S + 1];
-    int tp[S + 1];
-#pragma unroll
-    for (int q = 0; q <= S; ++q) {
-      tv[q] = kv[q];
-      tp[q] = q;
-    }
-#pragma unroll
-    for (int w = 1; w <= S; w <<= 1) {
-#pragma unroll
-      for (int q = 0; q + w <= S; q += 2 * w) {
-        const bool hi = tv[q + w] > tv[q];  // the higher rows' candidate only when strictly larger
-        tv[q] = hi ? tv[q + w] : tv[q];
-        tp[q] = hi ? tp[q + w] : tp[q];
-      }
-    }
-    const int r = tp[0];
-    const int b = brow[r * PKF_THREADS + tid];
-    sc[S] = tv[0] + 0.f;  // -0 -> +0
-    sl[S] = (int)i1s[r * PKF_THREADS + tid] * n_sub + (int)i2s[b * PKF_THREADS + tid];
-    const int nb = b + 1;  // b + 1 = c1 only after the last pick
-    brow[r * PKF_THREADS + tid] = (uint8_t)nb;
-    const float nk = (v1s[r * PKF_THREADS + tid] + v2s[min(nb, C - 1) * PKF_THREADS + tid]) * 0.5f;
-#pragma unroll
-    for (int q = 0; q <= S; ++q) kv[q] = q == r ? nk : kv[q];
-    walkr_step<C, S + 1>(kv, sc, sl, v1s, v2s, i1s, i2s, brow, n_sub, kk, tid);
+    constexpr int H = C / 2;
+    constexpr int NT = S + 1 < H ? S + 1 : H;
+    if constexpr (S < H) brow[S * PKF_THREADS + tid] = 0;  // head row S can first win at this step
+    int r, b;
+    walk_take<C, NT, (S >= H)>(w, v1s, v2s, brow, v2_0, c1, tid, r, b, sc[S]);
+    sl[S] = pick_slot_of(i1s, i2s, r, b, n_sub, tid);
+    walkr_step<C, S + 1>(w, sc, sl, v1s, v2s, i1s, i2s, brow, v2_0, c1, n_sub, kk, tid);
+  }
+}
+
+// The head steps unrolled, the rest one rolled loop over the full head tree; picks (r, b) to shared memory.
+template <int C, int S>
+__device__ __forceinline__ void walkf_head(WalkHT<C>& w, const float* v1s, const float* v2s, uint8_t* brow,
+                                          uint8_t* pick_r, uint8_t* pick_b, float v2_0, int c1, int kk, int tid) {
+  if constexpr (S < C / 2) {
+    if (S >= kk) return;
+    brow[S * PKF_THREADS + tid] = 0;
+    int r, b;
+    float sc;
+    walk_take<C, S + 1, false>(w, v1s, v2s, brow, v2_0, c1, tid, r, b, sc);
+    pick_r[S * PKF_THREADS + tid] = (uint8_t)r;
+    pick_b[S * PKF_THREADS + tid] = (uint8_t)b;
+    walkf_head<C, S + 1>(w, v1s, v2s, brow, pick_r, pick_b, v2_0, c1, kk, tid);
+  }
+}
+template <int C>
+__device__ __forceinline__ void walkf(WalkHT<C>& w, const float* v1s, const float* v2s, uint8_t* brow,
+                                     uint8_t* pick_r, uint8_t* pick_b, float v2_0, int c1, int kk, int tid) {
+  walkf_head<C, 0>(w, v1s, v2s, brow, pick_r, pick_b, v2_0, c1, kk, tid);
+#pragma unroll 1
+  for (int s = C / 2; s < kk; ++s) {
+    int r, b;
+    float sc;
+    walk_take<C, C / 2, true>(w, v1s, v2s, brow, v2_0, c1, tid, r, b, sc);
+    pick_r[s * PKF_THREADS + tid] = (uint8_t)r;
+    pick_b[s * PKF_THREADS + tid] = (uint8_t)b;
   }
 }
 
@@ -659,12 +701,12 @@ __global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_fast_kernel(
                                       (svb ? reinterpret_cast<uintptr_t>(svb + dst) : 0)) & 15) == 0;
   if constexpr (C <= 16) {
     // picks in registers; outputs and softmax(scale * score) (* gate) in pick order
-    float kv[C], sc[C];
+    float sc[C];
     int sl[C];
     const float v2_0 = v2s[tid];
-#pragma unroll
-    for (int q = 0; q < C; ++q) kv[q] = (v1s[q * P + tid] + v2_0) * 0.5f;
-    walkr_step<C, 0>(kv, sc, sl, v1s, v2s, i1s, i2s, brow, n_sub, kk, tid);
+    WalkHT<C> w;
+    walk_init<C>(w, v1s, brow, v2_0, c1, tid);
+    walkr_step<C, 0>(w, sc, sl, v1s, v2s, i1s, i2s, brow, v2_0, c1, n_sub, kk, tid);
     if (vec) {
 #pragma unroll
       for (int j = 0; j < C; j += 4) {
@@ -716,11 +758,10 @@ __global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_fast_kernel(
     return;
   } else {  // picks in shared memory (bytes); a pick's score and slot come back from the lists
     {
-      float kv[C];
       const float v2_0 = v2s[tid];
-#pragma unroll
-      for (int q = 0; q < C; ++q) kv[q] = (v1s[q * P + tid] + v2_0) * 0.5f;
-      walkf_step<C, 0>(kv, v1s, v2s, brow, pick_r, pick_b, kk, tid);
+      WalkHT<C> w;
+      walk_init<C>(w, v1s, brow, v2_0, c1, tid);
+      walkf<C>(w, v1s, v2s, brow, pick_r, pick_b, v2_0, c1, kk, tid);
     }
     auto pick_score = [&](int j) {
       const int r = pick_r[j * P + tid], b = pick_b[j * P + tid];
