@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--decode-steps", type=int, default=64)
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--row-streams", type=int, default=ROW_STREAMS, help="CUDA streams the rows are split over")
     return ap.parse_args()
 
 
@@ -300,7 +301,7 @@ def run_ours(a):
     tgt = tgt_host.to(dev)
     loss_buf = torch.zeros(2, dtype=torch.float64, device=dev)  # (loss sum, token count)
 
-    def step(idx, tg, row_streams=ROW_STREAMS):
+    def step(idx, tg, row_streams=a.row_streams):
         loss_buf.zero_()
         with torch.no_grad():
             model.loss_sum(idx, tg, out=loss_buf[:1], row_streams=row_streams)
@@ -480,7 +481,7 @@ def run_ours(a):
                "config": {"workload": f"FULL onesdm_allsdm d768 L{a.layers} h12x64 M1024 k16, TrainedSdm n_sub72 "
                                       f"k32, V32768, {B} rows x {T} tokens per GPU",
                           "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world} (batch shards)",
-                          "row_streams": ROW_STREAMS, "l2": "per-step working set > 126 MB L2 (no flush)"},
+                          "row_streams": a.row_streams, "l2": "per-step working set > 126 MB L2 (no flush)"},
                "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "roofline_scan": roof_scan,
                "roofline_by_kernel": by_kernel, "cpu_baseline": cpu,
                "profiled_pass": f"{a.steps} steps, one row stream, CUDA events around every launch (roofline, kernels)",

@@ -97,16 +97,21 @@ class OneSdmLM(nn.Module):
         x, _ = self.enfold(idx)
         reset = (idx == self.bos_id) if self.reset_at_bos else None
         for i in range(self.n_layers):
-            m = self.mems[i]
-            if m.enabled:
-                if sequential:
-                    x = x + m.forward_sequential(x, reset)
-                else:
-                    x = m._run(x, reset, add_residual=True)[0]
-            if self.ffn == "mlp":
-                x = self.mlps[i].block(x, self.mnorms[i].w, self.mnorms[i].eps)
-            elif self.ffn == "sdm":
-                x = self.sdms[i]._run(x, add_residual=True)[0]
+            x = self._layer(i, x, reset, sequential)
+        return x
+
+    def _layer(self, i, x, reset, sequential=False):
+        """Layer i of residual(): the memory, then the body, each with its residual add."""
+        m = self.mems[i]
+        if m.enabled:
+            if sequential:
+                x = x + m.forward_sequential(x, reset)
+            else:
+                x = m._run(x, reset, add_residual=True)[0]
+        if self.ffn == "mlp":
+            x = self.mlps[i].block(x, self.mnorms[i].w, self.mnorms[i].eps)
+        elif self.ffn == "sdm":
+            x = self.sdms[i]._run(x, add_residual=True)[0]
         return x
 
     def hidden(self, idx, sequential=False):
@@ -151,7 +156,8 @@ class OneSdmLM(nn.Module):
         float64 device scalar accumulated into `out` if given; the logits are never materialised whole.
 
         row_streams > 1 splits the rows (independent sequences) into that many groups, each run on its own CUDA
-        stream after the current one, so one group's kernels fill the other's partial waves; the current stream
+        stream after the current one, so one group's kernels fill the other's partial waves; the work is submitted
+        layer by layer across the groups (so every stream has queued work from the start) and the current stream
         waits for all of them.  The sum is the same up to the order of its float64 additions."""
         B = idx.shape[0]
         if row_streams <= 1 or B < row_streams:
@@ -167,9 +173,19 @@ class OneSdmLM(nn.Module):
         bounds = [B * i // row_streams for i in range(row_streams + 1)]
         for s in side:
             s.wait_stream(main)
+        _forward_only(self.emb.weight)
+        xs, resets = [], []
         for s, r0, r1 in zip(side, bounds[:-1], bounds[1:]):
             with torch.cuda.stream(s):
-                self._head(self.residual(idx[r0:r1]), "ce", targets[r0:r1], out)
+                xs.append(self.enfold(idx[r0:r1])[0])
+                resets.append((idx[r0:r1] == self.bos_id) if self.reset_at_bos else None)
+        for i in range(self.n_layers):
+            for g, s in enumerate(side):
+                with torch.cuda.stream(s):
+                    xs[g] = self._layer(i, xs[g], resets[g])
+        for g, (s, r0, r1) in enumerate(zip(side, bounds[:-1], bounds[1:])):
+            with torch.cuda.stream(s):
+                self._head(xs[g], "ce", targets[r0:r1], out)
         for s in side:
             main.wait_stream(s)
         return out
