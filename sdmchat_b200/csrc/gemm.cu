@@ -73,8 +73,7 @@ cudaError_t launch_gemm_simt(const TA* x, int64_t ldx, const TA* w, int64_t ldw,
   if (rows == 0 || n == 0) return cudaSuccess;
   dim3 grid((unsigned)ceil_div(n, SG_BN), (unsigned)ceil_div(rows, SG_BM));
   LaunchScope scope_("gemm_simt", st);
-  launch_k(gemm_simt_kernel<TA, Epi>, dim3(grid), dim3(256), 0, st, x, ldx, w, ldw, rows, K, n, epi, kwrap);
-  return cudaGetLastError();
+  return launch_k(gemm_simt_kernel<TA, Epi>, dim3(grid), dim3(256), 0, st, x, ldx, w, ldw, rows, K, n, epi, kwrap);
 }
 
 // ---------------------------------------------------------------------------------------------- skinny GEMM
@@ -192,8 +191,8 @@ static cudaError_t launch_gemm_skinny(const TA* x, int64_t ldx, const TA* w, int
   if (e != cudaSuccess) return e;
   const int64_t grid = ceil_div(n, SK_WARPS);
   LaunchScope scope_("gemm_skinny", st);
-  launch_k(kern, dim3((unsigned)grid), dim3(SK_WARPS * 32), smem, st, x, ldx, w, ldw, (int)rows, K, n, epi, kwrap);
-  return cudaGetLastError();
+  return launch_k(kern, dim3((unsigned)grid), dim3(SK_WARPS * 32), smem, st, x, ldx, w, ldw, (int)rows, K, n, epi,
+                  kwrap);
 }
 
 // ------------------------------------------------------------------------------------- small-M tensor-core GEMM
@@ -285,12 +284,12 @@ cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int6
   if constexpr (sizeof(TA) == 2) {
     if (small_tc_ok(x, ldx, w, ldw, rows, K, kwrap)) {
       LaunchScope scope_("gemm_small_tc", st);
-      launch_k(gemm_small_tc_kernel<Epi>, dim3((unsigned)ceil_div(n, 8)), dim3(SMT_WARPS * 32), 0, st, x, ldx, w, ldw, (int)rows, K, n,
-                                                                                     epi, kwrap);
-      return cudaGetLastError();
+      return launch_k(gemm_small_tc_kernel<Epi>, dim3((unsigned)ceil_div(n, 8)), dim3(SMT_WARPS * 32), 0, st, x,
+                      ldx, w, ldw, (int)rows, K, n, epi, kwrap);
     }
   }
-  if (skinny_ok(x, ldx, w, ldw, rows, K, kwrap)) return launch_gemm_skinny<TA, Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
+  if (skinny_ok(x, ldx, w, ldw, rows, K, kwrap))
+    return launch_gemm_skinny<TA, Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
   if constexpr (sizeof(TA) == 2) {
     if (tc_gemm_supported(x, ldx, w, ldw, K, kwrap))
       return launch_gemm_tc<Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);

@@ -27,12 +27,13 @@ namespace sdm {
 namespace tc {
 
 constexpr int BM = 128, BK = 64, EPI_WARPS = 8, THREADS = 64 + 32 * EPI_WARPS;
-constexpr int STG_LD = 36;  // padded row (floats) of an epilogue warp's 32 x 32 transpose
+constexpr int STG_LD = 32;  // row (floats) of an epilogue warp's 32 x 32 transpose; float4 chunk j of row r sits
+                            // at chunk j ^ (r & 7), so row writes and column reads are both conflict-free
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
 template <int BN>
 struct Cfg {
-  static constexpr int STAGES = BN >= 256 ? 3 : 5;
+  static constexpr int STAGES = BN >= 256 ? 4 : 6;
   static constexpr uint32_t B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr size_t RING_BYTES = (size_t)STAGES * STAGE_BYTES;
   static constexpr size_t SMEM_BYTES = RING_BYTES + (size_t)EPI_WARPS * 32 * STG_LD * 4 + 1024;
@@ -211,14 +212,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           float4* srow = reinterpret_cast<float4*>(stg + lane * STG_LD);  // this thread's row
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            srow[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                  __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            srow[j ^ (lane & 7)] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
           __syncwarp();
           const int col = cb + ch * 32 + 4 * c4;
 #pragma unroll
           for (int it = 0; it < 8; ++it) {
             const int rr = 4 * it + rsub;
-            const float4 v = *reinterpret_cast<const float4*>(stg + rr * STG_LD + 4 * c4);
+            const float4 v = *reinterpret_cast<const float4*>(stg + rr * STG_LD + 4 * (c4 ^ (rr & 7)));
             if (row0 + rr < rows && col < n) epi.store4(pre[ch], it, row0 + rr, col, v, n);
           }
           __syncwarp();
@@ -308,8 +309,7 @@ static cudaError_t launch_tc_bn(const bf16_t* x, int64_t ldx, const bf16_t* w, i
   const int64_t tiles = ceil_div(n, BN) * ceil_div(rows, tc::BM);
   const int grid = (int)(tiles < tc::num_sms() ? tiles : tc::num_sms());
   LaunchScope scope_("gemm_tc", st);
-  launch_k(kern, dim3(grid), dim3(tc::THREADS), C::SMEM_BYTES, st, ma, mb, rows, K, n, epi, kwrap);
-  return cudaGetLastError();
+  return launch_k(kern, dim3(grid), dim3(tc::THREADS), C::SMEM_BYTES, st, ma, mb, rows, K, n, epi, kwrap);
 }
 
 // Column tile: 256 wide moves a third fewer operand bytes per flop; 128 wide when it finishes in fewer rounds of

@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(256) rt_finish_vec_kernel(const float* __restr
     const int64_t it = item0 + i < items ? item0 + i : items - 1;
     const float4* nr = reinterpret_cast<const float4*>(num + it * dh);
 #pragma unroll
-    for (int q = 0; q < STEPS; ++q) vals[i][q] = nr[q * 8 + g];
+    for (int q = 0; q < STEPS; ++q) vals[i][q] = nr[g * STEPS + q];  // lane g: columns g*dh/8 .. +dh/8-1
     dv[i] = read_sum ? 0.f : den[it] + read_eps;
   }
 #pragma unroll
@@ -202,16 +202,37 @@ __global__ void __launch_bounds__(256) rt_finish_vec_kernel(const float* __restr
     const int hh = (int)(item % h);
     const float rs = out_norm ? rsqrt_rn(__fdiv_rn(ss, (float)dh) + out_norm_eps) : 1.f;
     const int64_t n = item / h;
+    float4 o[STEPS];
 #pragma unroll
     for (int q = 0; q < STEPS; ++q) {
-      const int c = q * 32 + g * 4;
-      float4 o = vals[i][q];
+      const int c = (g * STEPS + q) * 4;
+      o[q] = vals[i][q];
       if (out_norm) {
         const float4 wv = *reinterpret_cast<const float4*>(onorm_w + hh * dh + c);
-        o = make_float4((o.x * rs) * wv.x, (o.y * rs) * wv.y, (o.z * rs) * wv.z, (o.w * rs) * wv.w);
+        o[q] = make_float4((o[q].x * rs) * wv.x, (o[q].y * rs) * wv.y, (o[q].z * rs) * wv.z, (o[q].w * rs) * wv.w);
       }
-      store_split4<T>(r, n, (int64_t)h * dh, (int64_t)hh * dh + c, o, split);
     }
+    if constexpr (sizeof(T) == 2 && STEPS % 2 == 0) {
+      if (split) {  // eight consecutive columns per 16-byte store, hi and lo rows (the launcher checks alignment)
+        const int64_t d = (int64_t)h * dh;
+#pragma unroll
+        for (int q = 0; q < STEPS; q += 2) {
+          const float4 h0 = make_float4(round_to<T>(o[q].x), round_to<T>(o[q].y), round_to<T>(o[q].z), round_to<T>(o[q].w));
+          const float4 h1 = make_float4(round_to<T>(o[q + 1].x), round_to<T>(o[q + 1].y), round_to<T>(o[q + 1].z),
+                                        round_to<T>(o[q + 1].w));
+          const float4 l0 = make_float4(o[q].x - h0.x, o[q].y - h0.y, o[q].z - h0.z, o[q].w - h0.w);
+          const float4 l1 = make_float4(o[q + 1].x - h1.x, o[q + 1].y - h1.y, o[q + 1].z - h1.z, o[q + 1].w - h1.w);
+          const uint2 ph0 = pack_bf16x4(h0), ph1 = pack_bf16x4(h1), pl0 = pack_bf16x4(l0), pl1 = pack_bf16x4(l1);
+          T* dst = r + n * 2 * d + (int64_t)hh * dh + (g * STEPS + q) * 4;
+          *reinterpret_cast<uint4*>(dst) = make_uint4(ph0.x, ph0.y, ph1.x, ph1.y);
+          *reinterpret_cast<uint4*>(dst + d) = make_uint4(pl0.x, pl0.y, pl1.x, pl1.y);
+        }
+        continue;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < STEPS; ++q)
+      store_split4<T>(r, n, (int64_t)h * dh, (int64_t)hh * dh + (g * STEPS + q) * 4, o[q], split);
   }
 }
 
@@ -365,16 +386,14 @@ cudaError_t launch_rmsnorm(const T* x, const T* w, int64_t rows, int d, float ep
     }
     return cudaGetLastError();
   }
-  launch_k(rmsnorm_kernel<T>, dim3((unsigned)ceil_div(rows, 8)), dim3(256), 0, st, x, w, rows, d, eps, y);
-  return cudaGetLastError();
+  return launch_k(rmsnorm_kernel<T>, dim3((unsigned)ceil_div(rows, 8)), dim3(256), 0, st, x, w, rows, d, eps, y);
 }
 template <typename T>
 cudaError_t launch_embed(const int32_t* ids, const T* emb, int64_t N, int d, int V, T* out, int* bad,
                          cudaStream_t st) {
   if (N == 0) return cudaSuccess;
   LaunchScope scope_("embed", st);
-  launch_k(embed_kernel<T>, dim3((unsigned)ceil_div(N, 8)), dim3(256), 0, st, ids, emb, N, d, V, out, bad);
-  return cudaGetLastError();
+  return launch_k(embed_kernel<T>, dim3((unsigned)ceil_div(N, 8)), dim3(256), 0, st, ids, emb, N, d, V, out, bad);
 }
 template <typename T>
 cudaError_t launch_swiglu_act(const T* g, const T* u, int64_t n, T* p, cudaStream_t st) {
@@ -382,8 +401,7 @@ cudaError_t launch_swiglu_act(const T* g, const T* u, int64_t n, T* p, cudaStrea
   int64_t blocks = ceil_div(n, 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
   LaunchScope scope_("swiglu_act", st);
-  launch_k(swiglu_act_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, st, g, u, n, p);
-  return cudaGetLastError();
+  return launch_k(swiglu_act_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, st, g, u, n, p);
 }
 template <typename T>
 cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int h, int dh, int read_sum,
@@ -391,7 +409,8 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
                              cudaStream_t st) {
   if (N == 0) return cudaSuccess;
   LaunchScope scope_("rt_finish", st);
-  const bool al = ((reinterpret_cast<uintptr_t>(num) | reinterpret_cast<uintptr_t>(onorm_w)) & 15) == 0;
+  const bool al = ((reinterpret_cast<uintptr_t>(num) | reinterpret_cast<uintptr_t>(onorm_w) |
+                    reinterpret_cast<uintptr_t>(r)) & 15) == 0;
   if (al && (dh == 64 || dh == 32 || dh == 128)) {
     // rows per lane group: 4 while that still leaves at least two waves of 148 SMs x 8 blocks, else 1
     const bool big = N * h >= (int64_t)148 * 8 * 32 * 4 * 2;
@@ -411,9 +430,8 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
 #undef SDM_FIN
     return cudaGetLastError();
   }
-  launch_k(rt_finish_kernel<T>, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, num, den, N, h, dh, read_sum, read_eps,
-                                                                    out_norm, out_norm_eps, onorm_w, r, split);
-  return cudaGetLastError();
+  return launch_k(rt_finish_kernel<T>, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, num, den, N, h, dh,
+                  read_sum, read_eps, out_norm, out_norm_eps, onorm_w, r, split);
 }
 // TrainedSdm address + read for decode-sized launches (track4_onesdm_models.py:438-456), one block of four warps
 // per (token, head): warp 0 selects the slots (the warp-per-address selection of the addressing kernels, so the
@@ -547,15 +565,15 @@ cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values,
   if constexpr (sizeof(T) == 2) {
     if (dh % 8 == 0 && dh <= 256 && k <= 32 && (reinterpret_cast<uintptr_t>(values) & 15) == 0) {
       if (N * h < 148 * 8) {  // decode-sized: spread each item's rows over four warps
-        launch_k(ts_gather_split_kernel, dim3((unsigned)ceil_div(N * h, 2)), dim3(256), 0, st, si, w, values, N, h, M, dh, k, r, split);
-        return cudaGetLastError();
+        return launch_k(ts_gather_split_kernel, dim3((unsigned)ceil_div(N * h, 2)), dim3(256), 0, st, si, w, values,
+                        N, h, M, dh, k, r, split);
       }
-      launch_k(ts_gather_vec_kernel, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, si, w, values, N, h, M, dh, k, r, split);
-      return cudaGetLastError();
+      return launch_k(ts_gather_vec_kernel, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, si, w, values, N,
+                      h, M, dh, k, r, split);
     }
   }
-  launch_k(ts_gather_kernel<T>, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, si, w, values, N, h, M, dh, k, r, split);
-  return cudaGetLastError();
+  return launch_k(ts_gather_kernel<T>, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, si, w, values, N, h, M,
+                  dh, k, r, split);
 }
 
 #define SDM_INST(T)                                                                                              \

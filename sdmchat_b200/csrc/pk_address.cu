@@ -415,8 +415,7 @@ static cudaError_t launch_pk_tc(const PkArgs& a, int c1, int kk, cudaStream_t st
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)ceil_div(a.N, PK_THREADS), (unsigned)(a.h * (a.pairs > 1 ? 2 : 1)));
   LaunchScope scope_("pk_address", st);
-  launch_k(kern, dim3(grid), dim3(PK_THREADS), smem, st, a, c1, kk);
-  return cudaGetLastError();
+  return launch_k(kern, dim3(grid), dim3(PK_THREADS), smem, st, a, c1, kk);
 }
 
 template <int HALF>
@@ -887,8 +886,7 @@ static cudaError_t launch_pk_warp_s(const PkArgs& a, int c1, int kk, cudaStream_
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)ceil_div(a.N, PKW_WARPS), (unsigned)(a.h * (a.pairs > 1 ? 2 : 1)));
   LaunchScope scope_("pk_address", st);
-  launch_k(kern, dim3(grid), dim3(PKW_WARPS * 32), smem, st, a, c1, kk);
-  return cudaGetLastError();
+  return launch_k(kern, dim3(grid), dim3(PKW_WARPS * 32), smem, st, a, c1, kk);
 }
 
 template <int HALF>

@@ -364,29 +364,26 @@ cudaError_t launch_ce_combine(const float2* part, const float* tgt_logit, const 
                               int tiles_n, double* loss_sum, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   LaunchScope scope_("ce_combine", st);
-  launch_k(ce_combine_kernel, dim3((unsigned)ceil_div(rows, 8)), dim3(256), 0, st, part, tgt_logit, targets, rows, tiles_n, loss_sum);
-  return cudaGetLastError();
+  return launch_k(ce_combine_kernel, dim3((unsigned)ceil_div(rows, 8)), dim3(256), 0, st, part, tgt_logit, targets,
+                  rows, tiles_n, loss_sum);
 }
 
 cudaError_t launch_argmax_combine(const float2* part, int64_t rows, int tiles_n, int32_t* ids, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   LaunchScope scope_("argmax_combine", st);
-  launch_k(argmax_combine_kernel, dim3((unsigned)ceil_div(rows, 8)), dim3(256), 0, st, part, rows, tiles_n, ids);
-  return cudaGetLastError();
+  return launch_k(argmax_combine_kernel, dim3((unsigned)ceil_div(rows, 8)), dim3(256), 0, st, part, rows, tiles_n, ids);
 }
 
 cudaError_t launch_ce_rows(const float* logits, int64_t rows, int V, const int32_t* targets, double* loss_sum,
                            cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   LaunchScope scope_("ce_rows", st);
-  launch_k(ce_rows_kernel, dim3((unsigned)rows), dim3(256), 0, st, logits, rows, V, targets, loss_sum);
-  return cudaGetLastError();
+  return launch_k(ce_rows_kernel, dim3((unsigned)rows), dim3(256), 0, st, logits, rows, V, targets, loss_sum);
 }
 cudaError_t launch_argmax_rows(const float* logits, int64_t rows, int V, int32_t* ids, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   LaunchScope scope_("argmax_rows", st);
-  launch_k(argmax_rows_kernel, dim3((unsigned)rows), dim3(256), 0, st, logits, rows, V, ids);
-  return cudaGetLastError();
+  return launch_k(argmax_rows_kernel, dim3((unsigned)rows), dim3(256), 0, st, logits, rows, V, ids);
 }
 
 }  // namespace sdm

@@ -1025,9 +1025,8 @@ static cudaError_t launch_scan_k(const ScanArgs& a, int nch, int n_slices, cudaS
   }
   const ScanMaps m = scan_maps(a);
   LaunchScope scope_("rt_scan", st);
-  launch_k(rt_scan_kernel<K>, dim3((unsigned)((int64_t)a.B * a.h * n_slices)), dim3(SCAN_THREADS), ssm, st, a, nch, n_slices, m.v,
-                                                                                         m.num, m.den, m.use_tma);
-  return cudaGetLastError();
+  return launch_k(rt_scan_kernel<K>, dim3((unsigned)((int64_t)a.B * a.h * n_slices)), dim3(SCAN_THREADS), ssm, st, a,
+                  nch, n_slices, m.v, m.num, m.den, m.use_tma);
 }
 
 cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st) {
