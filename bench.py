@@ -240,6 +240,12 @@ NCU_DRAM_PER_TOKEN = {
     ("rt_scan", ""): (64075264 + 2735616) / 8192,
     ("ts_gather", "ts"): 15511808 / 8192,
     ("rt_finish", "rt_out"): (25603840 + 92160) / 8192,
+    # tensor-core GEMMs, from a one-pass capture of one full bench step (65,536 rows per launch), averaged over the
+    # 12 layers of each call site (profiles/gemm_tc_dram_full_prefill_d768_L12_B32_T2048.md)
+    ("gemm_tc", "rt_proj"): 6893.9,
+    ("gemm_tc", "rt_out"): 5772.4,
+    ("gemm_tc", "ts"): 3687.0,
+    ("gemm_tc", "head_ce"): 4475.6,
 }
 
 
@@ -385,9 +391,15 @@ def run_ours(a):
         flops = sum(gemm_flops(tag, rows_tokens, a.layers) * n for k, tag, n, ms in groups if k == "gemm_tc")
         launches_dom = per_kernel[dom]["launches"]
         ach = flops / (per_kernel[dom]["ms"] / 1e3) / 1e12
+        traffic = None
+        if all((k, tag) in NCU_DRAM_PER_TOKEN for k, tag, n, ms in groups if k == dom):
+            traffic = round(sum(NCU_DRAM_PER_TOKEN[(k, tag)] * rows_tokens * n
+                                for k, tag, n, ms in groups if k == dom) / launches_dom)
         roof = {"kernel": "gemm_tc (tcgen05 bf16 GEMM, all call sites)", "bound": "tensor",
                 "achieved": round(ach, 1), "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                "frac": round(ach / pk["bf16_tflops_sustained"], 4), "traffic": None,
+                "frac": round(ach / pk["bf16_tflops_sustained"], 4), "traffic": traffic,
+                "traffic_unit": "bytes per launch (DRAM read + write)",
+                "traffic_source": "ncu dram bytes of one full-size bench step (65,536 rows per launch)",
                 "peak_source": f"{how} bf16_tflops_sustained",
                 "avg_launch_ms": round(per_kernel[dom]["ms"] / launches_dom, 4)}
     else:
