@@ -471,10 +471,15 @@ __global__ void __launch_bounds__(128) ts_addr_gather_kernel(const float* __rest
     if (lane == 0) s_nc = nc;
   }
   __syncthreads();
-  if (warp == 0) {
+  float* wsm = kn + 2 * n_sub * HALF;  // v1, i1, v2, i2
+  if (warp < 2) {  // the two halves' lists in parallel
     const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(q) & 15) | (ldq & 3) | (d_a & 3)) == 0;
-    warp_address<HALF, S>(q + n * ldq + (int64_t)hh * d_a, zvec, kn, kn + n_sub * HALF, n_sub, c1, kk, cand, s_nc,
-                          kn + 2 * n_sub * HALF, expf(log_scale[hh]), nullptr, s_si, s_w, nullptr);
+    warp_half_list<HALF, S>(q + n * ldq + (int64_t)hh * d_a + warp * HALF, zvec, kn + warp * n_sub * HALF, n_sub,
+                            c1, wsm + warp * 64, reinterpret_cast<int*>(wsm + warp * 64 + 32));
+  }
+  __syncthreads();
+  if (warp == 0) {
+    warp_combine<S>(wsm, n_sub, c1, kk, cand, s_nc, expf(log_scale[hh]), nullptr, s_si, s_w, nullptr);
     __syncwarp();
     if (lane < kk) {
       si[item * kk + lane] = s_si[lane];

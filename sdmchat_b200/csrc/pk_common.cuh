@@ -147,45 +147,70 @@ __device__ __forceinline__ int warp_candidates(int* cand, int c1, int kk) {
 // flat index a*c1+b asc); the first kk are the selection in order.  Writes element e < kk of the slot ids
 // (si_out), the soft weights softmax(scale * score) [* gate] (w_out, when not null; scale = exp(log_scale)) and
 // the scores (sv_out, when not null); wsm is 128 words of this warp's scratch (shared memory).
+// One warp's sorted top-c1 of one address half (HALF floats at zh) against sub-keys kn (n_sub x HALF): lane l
+// holds sub-keys l*S .. l*S+S-1, a warp-wide bitonic sort of 64-bit (score, index) keys orders them; element e < c1
+// goes to vo[e] (score) and io[e] (sub-key id).
+template <int HALF, int S>
+__device__ __forceinline__ void warp_half_list(const float* zh, bool zvec, const float* kn, int n_sub, int c1,
+                                               float* vo, int* io) {
+  const int lane = threadIdx.x & 31;
+  float zn[HALF];
+  normalize_half<HALF>(zh, zn, zvec);
+  KT key[S];
+#pragma unroll
+  for (int q = 0; q < S; ++q) {
+    const int j = lane * S + q;
+    key[q] = 0ull;  // padding: below every real key
+    if (j < n_sub) {
+      float sc = half_dot<HALF>(zn, kn + j * HALF);
+      if (sc != sc) sc = -INFINITY;
+      key[q] = pk_key(sc, (uint32_t)j);
+    }
+  }
+  warp_sort_desc<S>(key);
+#pragma unroll
+  for (int q = 0; q < S; ++q) {
+    const int e = lane * S + q;
+    if (e < c1) {
+      vo[e] = pk_key_score(key[q]);
+      io[e] = (int)pk_key_tie(key[q]);
+    }
+  }
+}
+
+template <int S>
+__device__ __forceinline__ void warp_combine(const float* wsm, int n_sub, int c1, int kk, const int* cand, int nc,
+                                             float scale, const float* gate, int32_t* si_out, float* w_out,
+                                             float* sv_out);
+
+// One warp selects one address (z at zr, its two halves of HALF floats) against the head's normalised sub-keys
+// kn1/kn2 (n_sub x HALF each): (1) each half's n_sub scores, sorted by 64-bit (score, index) keys, give its top-c1
+// (warp_half_list); (2) the nc candidate pairs `cand`, sorted by (combined score desc, flat index a*c1+b asc); the
+// first kk are the selection in order (warp_combine).  Writes element e < kk of the slot ids (si_out), the soft
+// weights softmax(scale * score) [* gate] (w_out, when not null; scale = exp(log_scale)) and the scores (sv_out,
+// when not null); wsm is 128 words of scratch (shared memory): v1[32], i1[32], v2[32], i2[32].  The two halves and
+// the combine may also run on three warps (halves in parallel) with a barrier before the combine: the result is
+// the same.
 template <int HALF, int S>
 __device__ __forceinline__ void warp_address(const float* zr, bool zvec, const float* kn1, const float* kn2,
                                              int n_sub, int c1, int kk, const int* cand, int nc, float* wsm,
                                              float scale, const float* gate, int32_t* si_out, float* w_out,
                                              float* sv_out) {
+  warp_half_list<HALF, S>(zr, zvec, kn1, n_sub, c1, wsm, reinterpret_cast<int*>(wsm + 32));
+  warp_half_list<HALF, S>(zr + HALF, zvec, kn2, n_sub, c1, wsm + 64, reinterpret_cast<int*>(wsm + 96));
+  __syncwarp();
+  warp_combine<S>(wsm, n_sub, c1, kk, cand, nc, scale, gate, si_out, w_out, sv_out);
+}
+
+template <int S>
+__device__ __forceinline__ void warp_combine(const float* wsm, int n_sub, int c1, int kk, const int* cand, int nc,
+                                             float scale, const float* gate, int32_t* si_out, float* w_out,
+                                             float* sv_out) {
   const int lane = threadIdx.x & 31;
-  float* v1 = wsm;
-  int* i1 = reinterpret_cast<int*>(wsm + 32);
-  float* v2 = wsm + 64;
-  int* i2 = reinterpret_cast<int*>(wsm + 96);
-#pragma unroll 1
-  for (int hf = 0; hf < 2; ++hf) {
-    float zn[HALF];
-    normalize_half<HALF>(zr + hf * HALF, zn, zvec);
-    const float* kn = hf ? kn2 : kn1;
-    KT key[S];
-#pragma unroll
-    for (int q = 0; q < S; ++q) {
-      const int j = lane * S + q;
-      key[q] = 0ull;  // padding: below every real key
-      if (j < n_sub) {
-        float sc = half_dot<HALF>(zn, kn + j * HALF);
-        if (sc != sc) sc = -INFINITY;
-        key[q] = pk_key(sc, (uint32_t)j);
-      }
-    }
-    warp_sort_desc<S>(key);
-    float* vo = hf ? v2 : v1;
-    int* io = hf ? i2 : i1;
-#pragma unroll
-    for (int q = 0; q < S; ++q) {
-      const int e = lane * S + q;
-      if (e < c1) {
-        vo[e] = pk_key_score(key[q]);
-        io[e] = (int)pk_key_tie(key[q]);
-      }
-    }
-    __syncwarp();
-  }
+  const float* v1 = wsm;
+  const int* i1 = reinterpret_cast<const int*>(wsm + 32);
+  const float* v2 = wsm + 64;
+  const int* i2 = reinterpret_cast<const int*>(wsm + 96);
   KT ck[S];
 #pragma unroll
   for (int q = 0; q < S; ++q) {

@@ -65,17 +65,23 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   const bool reset = a.reset && a.reset[s];
   __syncthreads();
   if constexpr (HALF > 0) {
-    if (warp < 2) {  // warp 0: the write address (gated keys), warp 1: the read address (queries)
-      const int n_sub = a.n_sub;
-      const float* kn = dec_smem;
-      const float* zb = a.proj + (int64_t)s * a.ldp + (warp ? a.h * a.d_a : 0);
-      const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(a.proj) & 15) | (a.ldp & 3) | (a.d_a & 3) |
-                                          (a.h * a.d_a & 3)) == 0;
+    // warps 0-3: (write keys, read queries) x (first, second half) lists in parallel, then warps 0 and 2 combine
+    const int n_sub = a.n_sub, c1 = min(a.k, n_sub);
+    const float* kn = dec_smem;
+    float* wsm = dec_smem + 2 * n_sub * HALF + (warp >> 1) * 128;  // per address: v1, i1, v2, i2
+    const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(a.proj) & 15) | (a.ldp & 3) | (a.d_a & 3) |
+                                        (a.h * a.d_a & 3)) == 0;
+    if (warp < 4) {
+      const int ad = warp >> 1, hf = warp & 1;
+      const float* zh = a.proj + (int64_t)s * a.ldp + (ad ? a.h * a.d_a : 0) + hh * a.d_a + hf * HALF;
+      warp_half_list<HALF, S>(zh, zvec, kn + hf * n_sub * HALF, n_sub, c1, wsm + hf * 64,
+                              reinterpret_cast<int*>(wsm + hf * 64 + 32));
+    }
+    __syncthreads();
+    if (warp == 0 || warp == 2) {
       const float* gate = (warp == 0 && a.gate_col >= 0) ? a.proj + (int64_t)s * a.ldp + a.gate_col + hh : nullptr;
-      warp_address<HALF, S>(zb + hh * a.d_a, zvec, kn, kn + n_sub * HALF, n_sub, min(a.k, n_sub), k,
-                            reinterpret_cast<const int*>(kn + 2 * n_sub * HALF + 2 * 128), s_nc,
-                            const_cast<float*>(kn) + 2 * n_sub * HALF + warp * 128, expf(a.log_scale[hh]), gate,
-                            warp ? s_ir : s_iw, warp ? s_fr : s_fw, nullptr);
+      warp_combine<S>(wsm, n_sub, c1, k, reinterpret_cast<const int*>(dec_smem + 2 * n_sub * HALF + 2 * 128), s_nc,
+                      expf(a.log_scale[hh]), gate, warp ? s_ir : s_iw, warp ? s_fr : s_fw, nullptr);
     }
     __syncthreads();
   }
@@ -205,9 +211,9 @@ cudaError_t launch_rt_decode(const DecodeArgs& a, cudaStream_t st) {
   if (a.S == 0) return cudaSuccess;
   if (a.k > DEC_MAX_K || a.dh > 1024) return cudaErrorInvalidValue;
   LaunchScope scope_("rt_decode", st);
-  if (a.keys1) {  // one thread per value column, and at least the two address warps
+  if (a.keys1) {  // one thread per value column, and at least the four address warps
     if (!rt_decode_fused_ok(a.d_a, a.n_sub, a.k)) return cudaErrorInvalidValue;
-    const int threads = a.dh > 64 ? ((a.dh + 31) / 32) * 32 : 64;
+    const int threads = a.dh > 128 ? ((a.dh + 31) / 32) * 32 : 128;
     switch (pk_warp_slots(a.n_sub, a.k < a.n_sub ? a.k : a.n_sub, a.k)) {
       case 1: return launch_rt_decode_fused<T, 1>(a, threads, st);
       case 2: return launch_rt_decode_fused<T, 2>(a, threads, st);
