@@ -31,9 +31,19 @@ constexpr int STG_LD = 32;  // row (floats) of an epilogue warp's 32 x 32 transp
                             // at chunk j ^ (r & 7), so row writes and column reads are both conflict-free
 constexpr uint32_t A_BYTES = BM * BK * 2;
 
-template <int BN>
+// Ring depth: 4 stages (BN 256) / 6 (BN 128) -- the K = 1,536 residual GEMMs gain from the deeper ring -- except for
+// the float32-output projection, measured faster with 3 / 5 (its epilogue, not operand latency, sets its pace).
+template <typename Epi>
+struct RingStages {
+  static constexpr int deep = 1;
+};
+template <>
+struct RingStages<EpiProj> {
+  static constexpr int deep = 0;
+};
+template <int BN, int DEEP = 1>
 struct Cfg {
-  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr int STAGES = (BN >= 256 ? 3 : 5) + DEEP;
   static constexpr uint32_t B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr size_t RING_BYTES = (size_t)STAGES * STAGE_BYTES;
   static constexpr size_t SMEM_BYTES = RING_BYTES + (size_t)EPI_WARPS * 32 * STG_LD * 4 + 1024;
@@ -85,7 +95,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t rows,
                    int K, int n, Epi epi, int kwrap) {
   pdl_enter();
-  using C = Cfg<BN>;
+  using C = Cfg<BN, RingStages<Epi>::deep>;
   extern __shared__ __align__(1024) unsigned char dsmem[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -298,7 +308,7 @@ bool tc_gemm_supported(const void* x, int64_t ldx, const void* w, int64_t ldw, i
 template <typename Epi, int BN>
 static cudaError_t launch_tc_bn(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K,
                                 int n, Epi epi, cudaStream_t st, int kwrap) {
-  using C = tc::Cfg<BN>;
+  using C = tc::Cfg<BN, tc::RingStages<Epi>::deep>;
   CUtensorMap ma, mb;
   if (!tc::make_map(&ma, x, (uint64_t)K, (uint64_t)rows, (uint64_t)ldx, tc::BM) ||
       !tc::make_map(&mb, w, (uint64_t)kwrap, (uint64_t)n, (uint64_t)ldw, BN))
