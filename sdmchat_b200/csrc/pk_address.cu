@@ -110,6 +110,26 @@ __device__ __forceinline__ void bitonic_sort_desc32(uint32_t (&k)[C]) {
     }
   }
 }
+// Sort only k[0..NS) descending (NS a power of two dividing C); entries past NS are left as they are.
+template <int C, int NS>
+__device__ __forceinline__ void bitonic_sort_desc32_head(uint32_t (&k)[C]) {
+#pragma unroll
+  for (int size = 2; size <= NS; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < NS; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint32_t hi = max(k[i], k[j]), lo = min(k[i], k[j]);
+          const bool desc = (i & size) == 0;
+          k[i] = desc ? hi : lo;
+          k[j] = desc ? lo : hi;
+        }
+      }
+    }
+  }
+}
 // t <- top-C of (t U g); disc <- max(disc, the best key left out).
 template <int C>
 __device__ __forceinline__ void merge_top32(uint32_t (&t)[C], const uint32_t (&g)[C], uint32_t& disc) {
@@ -482,7 +502,11 @@ __device__ __forceinline__ bool half_lists_fast(const float (&zn)[HALF], const f
       }
       gk[q] = key;
     }
-    bitonic_sort_desc32<C>(gk);
+    // a group with at most C/4 real keys: those sorted, then the zero padding, is already sorted descending
+    if (C >= 16 && n_sub - g0 <= C / 4)
+      bitonic_sort_desc32_head<C, (C >= 16 ? C / 4 : 1)>(gk);
+    else
+      bitonic_sort_desc32<C>(gk);
     if (g0 == 0) {
 #pragma unroll
       for (int q = 0; q < C; ++q) tk[q] = gk[q];
