@@ -164,6 +164,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t dt = tmem + buf * BN;
+        // a last column tile narrower than BN multiplies only its columns (rounded up to 16; the box's rows past n
+        // are zero-filled): N is field 17-22 of the instruction descriptor
+        const int nrem = n - (int)(t % tiles_n) * BN;
+        const int nt = nrem >= BN ? BN : ((nrem + 15) & ~15);
+        const uint32_t idesc = (C::IDESC & ~(0x3Fu << 17)) | ((uint32_t)(nt >> 3) << 17);
         for (int kt = 0; kt < kt_count; ++kt, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1u;
@@ -176,7 +181,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b_base = a_base + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma_bf16(dt, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), C::IDESC, (kt | kk) != 0);
+            umma_bf16(dt, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), idesc, (kt | kk) != 0);
           umma_commit(&empty_bar[s]);
         }
         if (ok) umma_commit(&acc_full[buf]);
