@@ -275,6 +275,13 @@ def kernel_bytes(kernel, tag, tokens):
         ("ts_gather", "ts"): ts_h * (ts_k * 8 + ts_dh * 4),
         # finish: num, den in; bf16 hi/lo read out
         ("rt_finish", "rt_out"): HEADS * (dh * 4 + 4) + D * 4,
+        # RMSNorm of the bf16 stream (per layer, and the final norm before the tied head): the row in, the row out
+        ("rmsnorm", ""): D * 2 * 2,
+        ("rmsnorm", "head_ce"): D * 2 * 2,
+        # embedding: the id in, the table row in, the stream row out
+        ("embed", ""): 4 + D * 2 * 2,
+        # CE combine: the head's (max, sum) partial per 128 columns, the target logit and the target in
+        ("ce_combine", "head_ce"): (V // 128) * 8 + 4 + 4,
     }
     return per.get((kernel, tag), 0) * tokens
 
