@@ -223,10 +223,9 @@ class Clocks:
 def gemm_flops(tag, rows, layers):
     """Algorithmic FLOPs of the tensor-core GEMM launches of one step, by call site (2 * rows * K * N of the
     reference's matmul; the float32-accurate hi/lo split of the wo inputs is not counted)."""
-    hda, C = HEADS * 32, 2 * HEADS * 32 + D + HEADS
+    C = 2 * HEADS * 32 + D + HEADS  # [wk; wq; wv; wg] columns: 1,548
     per_row = {"rt_proj": 2 * D * C, "rt_out": 2 * D * D, "ts": 2 * D * (4 * 32) + 2 * D * D,
                "head_ce": 2 * D * V, "head_logits": 2 * D * V, "head_argmax": 2 * D * V}
-    del hda
     return per_row.get(tag, 0) * rows
 
 
