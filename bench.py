@@ -435,7 +435,8 @@ def run_ours(a):
                 ach = byts / (v["ms"] / 1e3) / 1e9
                 by_kernel[k] = {"bound": "hbm", "achieved": round(ach, 1), "unit": "GB/s",
                                 "frac": round(ach / pk["hbm_gbs"], 4)}
-    # the SDM scan (rt_lists + rt_scan) at SURVEY's algorithmic bytes of the reference's chunked form
+    # the SDM scan (rt_lists + rt_scan) at the algorithmic bytes of the reference's chunked form
+    # (SCAN_BYTES_PER_TOKEN_HEAD per (token, head))
     scan_ms = sum(per_kernel[k]["ms"] for k in ("rt_lists", "rt_scan") if k in per_kernel)
     roof_scan = None
     if scan_ms > 0:
