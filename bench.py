@@ -5,7 +5,7 @@
     python bench.py --impl reference [...]                        the reference algorithm on the host CPU cores
     torchrun --nproc-per-node N bench.py --gpus N ...             one process per GPU (NCCL)
 
-Workload: OneSdmLM FULL arm, d 768, 12 layers, 12 run-time memory heads x 64, 1,024 slots per
+Workload (the reference's headline case): OneSdmLM FULL arm, d 768, 12 layers, 12 run-time memory heads x 64, 1,024 slots per
 head (32 x 32 product keys), k 16, fades (0, .8, .99, 1) x 3, TrainedSdm body at the reference defaults (4 heads,
 n_sub 72, k 32, value width 192), tied 32,768-row token table; bf16 weights and activations, float32 memory state.
 Weights: random init of that architecture (seed 0) with the zero-initialised output maps / value tables perturbed
@@ -15,7 +15,7 @@ tied-head cross-entropy sum against the next token, then an NCCL all-reduce of (
 Every step's working set (activations, 0.4 GB per layer) is larger than the 126 MB L2, so no L2 flush is added.
 
 The JSON line adds: e2e (the same step through the public API from pinned host ids, H2D + D2H inside the timed
-region), decode (config 4: 32 streams per GPU carried-state greedy decode after a 2,048-token prefill), roofline of
+region), decode (32 streams per GPU carried-state greedy decode after a 2,048-token prefill), roofline of
 the dominant kernel (measured live with CUDA events around every launch of a profiled pass of the same K steps on
 one row stream, right after the timed region), cpu_baseline (the CPU
 oracle port of the reference algorithm, bounded sample, rank 0 at N = 1), clocks sampled during the timed region.
@@ -457,7 +457,7 @@ def run_ours(a):
                      "by_call_site_ms": {t: round(ms / a.steps, 3) for t, ms in v["tags"].items()}}
                  for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1]["ms"])}
 
-    # decode (config 4): S streams per GPU, 2,048-token prompt prefilled, then carried-state greedy steps
+    # decode: S streams per GPU, 2,048-token prompt prefilled, then carried-state greedy steps
     decode = None
     if not a.no_decode:
         Sd = a.decode_streams

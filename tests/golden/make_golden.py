@@ -12,7 +12,7 @@ Cases (reference lines are in track4_onesdm_models.py unless noted):
   pk_selftest     the self-test's brute-force product-key case (:694-702): z (30,2,12), keys (2,9,6), k 5
   pk_k4 / pk_k16  z (256, 4, 32), keys (4, 32, 16): the run-time memory's addressing at k 4 and k 16
   pk_ns72_k32     z (128, 4, 32), keys (4, 72, 16), k 32: the FULL arm's trained-table addressing (n_sub 72)
-  rt_config1      BASELINE config 1: RunTimeSdm(256, heads 4, n_sub 32, d_a 32, k 4) with Uniform[0.90, 0.999]
+  rt_config1      the reference's CPU-runnable benchmark case: RunTimeSdm(256, heads 4, n_sub 32, d_a 32, k 4) with Uniform[0.90, 0.999]
                   fades, x (2, 256, 256) N(0,1); prepare outputs, forward, num/den, last_state, forward_sequential
   rt_small_*      the self-test's tiny memory (d 32, 4 heads, n_sub 6, d_a 8, k 5, fades 0/0.7/0.95/1, chunk 7)
                   with perturbed wo/wg (:713-718): plain, reset at BOS, learned fades, sum read without out-norm,

@@ -107,6 +107,6 @@ int main() {
   r |= run<16, 32>(103, 32, 32, 200, 2, 5);  // scaled TrainedSdm, n_sub 103
   r |= run<16, 8>(16, 8, 32, 300, 3, 3);
   r |= run<6, 8>(9, 5, 12, 300, 3, 4);
-  r |= run<16, 4>(32, 4, 32, 300, 3, 6);     // BASELINE config 1 (k 4)
+  r |= run<16, 4>(32, 4, 32, 300, 3, 6);     // the 4-head, k 4 RunTimeSdm case
   return r;
 }

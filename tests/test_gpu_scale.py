@@ -1,4 +1,4 @@
-"""GPU parity at BASELINE's shapes: the d768 / 12 heads x 64 / k16 / 1,024-slot layer against the CPU oracle on
+"""GPU parity at the benchmark's shapes: the d768 / 12 heads x 64 / k16 / 1,024-slot layer against the CPU oracle on
 identical inputs, and size-independent properties of the full FULL d768 L12 T2048 stack (determinism, causality,
 loss = CE of its own logits, decode = recurrence across a state renormalisation)."""
 import numpy as np

@@ -7,8 +7,8 @@ from goldens import load, params
 
 
 def test_runtime_sdm_constructor_reproduces_reference_weights():
-    """BASELINE config 1 built the reference's way (torch.manual_seed(0), Uniform[0.90, 0.999] fades drawn first)
-    gives the reference module's exact weights (tests/golden/rt_config1.npz holds its state_dict)."""
+    """The CPU-runnable benchmark case (RunTimeSdm 256, 4 heads, k 4) built the reference's way
+    (torch.manual_seed(0), Uniform[0.90, 0.999] fades drawn first) gives the reference module's exact weights (tests/golden/rt_config1.npz holds its state_dict)."""
     g = load("rt_config1")
     torch.manual_seed(0)
     decays = torch.empty(4).uniform_(0.90, 0.999)

@@ -65,5 +65,5 @@ def test_noalloc_rejects_requests_beyond_its_scratch(cuda_ok):
     rc = lib.sdm_rt_decode_step_noalloc(p, _lib.ptr(fake), n, None, 0, _lib.ptr(fake), _lib.ptr(fake),
                                         _lib.ptr(fake), _lib.ptr(fake), _lib.ptr(fake), _lib.stream_ptr())
     assert rc == 6  # SDM_ERR_WORKSPACE
-    assert lib.sdm_rt_decode_workspace_size(p, 256) <= cap  # BASELINE decode: 32 streams per GPU fit easily
+    assert lib.sdm_rt_decode_workspace_size(p, 256) <= cap  # the benchmark's decode: 32 streams per GPU fit easily
     np.testing.assert_equal(int(lib.sdm_rt_decode_workspace_size(p, 32)) > 0, True)
