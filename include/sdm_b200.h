@@ -9,7 +9,10 @@
  *    Host pointers are never accepted.  Nothing on these paths allocates device memory: the staged entry points
  *    that need intermediate buffers take a caller-provided workspace and have a *_workspace_size() query.
  *  - `stream` is a cudaStream_t passed as void*; all work is enqueued on it and the call returns without a
- *    device synchronisation.  Calls on different streams are independent; nothing here keeps global mutable state.
+ *    device synchronisation.  Calls on different streams are independent.  Global mutable state is limited to:
+ *    the per-module device flags that a bounded wait sets when it gives up (sdm_device_status reads and clears
+ *    them) and the wait limit beside them (sdm_set_wait_limit_ns); the host launch counter and launch profiler;
+ *    and the fixed scratch array of sdm_rt_decode_step_noalloc.
  *  - Every function returns an sdm_status.  Argument, shape and range errors are detected on the host before
  *    anything is launched and leave the outputs untouched.  SDM_ERR_CUDA reports a launch error.
  *  - Dtype codes: SDM_F32 (float32) or SDM_BF16 (bfloat16).  In SDM_BF16 mode activations (x, normalised
@@ -58,6 +61,15 @@ sdm_status sdm_profile_group(int i, char* kernel, char* tag, int name_len, int* 
  * mbarrier waits and the scan's chunk-copy waits give up after about 4 s) gave up since the previous call, and
  * clears the flags. */
 sdm_status sdm_device_status(void* stream);
+/* Failure-handling checks (no counterpart in the reference, which has no device-side waits).
+ * sdm_set_wait_limit_ns sets, on the current device, how long every bounded device-side wait polls before it gives
+ * up (0 restores the default of about 4 s); it is synchronous, and a caller changes it only while no kernel of this
+ * library is running.  sdm_wait_probe launches one thread that waits, through the same bounded wait the GEMM and
+ * the scan use, on an mbarrier nothing arrives on and no copy completes: the wait gives up after the limit, the
+ * kernel writes 2 to *done (device int; 1 would mean the wait completed) and returns, and the next
+ * sdm_device_status reports SDM_ERR_TIMEOUT. */
+sdm_status sdm_set_wait_limit_ns(uint64_t ns);
+sdm_status sdm_wait_probe(int* done, void* stream);
 
 /* ---------------------------------------------------------------------------------------- product-key address
  * pk_address (M:134-148).  z (N, h, d_a) float32, keys1/keys2 (h, n_sub, d_a/2) float32 ->
@@ -136,8 +148,10 @@ sdm_status sdm_rt_decode_step(const sdm_rt_params* p, const void* x, int S, cons
  * no decode API at all).  It allocates nothing and takes no workspace: its scratch is a fixed 8 MiB array inside
  * the library (sdm_rt_decode_noalloc_scratch_bytes()), held on every GPU that loads the library until exit.
  * Returns SDM_ERR_WORKSPACE when sdm_rt_decode_workspace_size(p, S) exceeds it (about 490 streams at d 768,
- * 12 heads, k 16).  The first call on a device looks up the scratch's device address with that device current:
- * make it before any stream capture.  Calls share the scratch; calls that overlap on the GPU race on it. */
+ * 12 heads, k 16).  A call made outside stream capture looks up the scratch's device address with the device
+ * current and remembers it; a call inside a capture uses the remembered address, so the first call on a device (and
+ * the first after a cudaDeviceReset) must come before any capture (else SDM_ERR_ARG).  Calls share the scratch;
+ * calls that overlap on the GPU race on it. */
 size_t sdm_rt_decode_noalloc_scratch_bytes(void);
 sdm_status sdm_rt_decode_step_noalloc(const sdm_rt_params* p, const void* x, int S, const uint8_t* reset,
                                       int add_residual, void* out, float* mem, float* cnt, float* scale,

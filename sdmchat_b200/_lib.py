@@ -47,6 +47,8 @@ _SIGS = {
     "sdm_profile_group": (c_int, [c_int, ctypes.c_char_p, ctypes.c_char_p, c_int, ctypes.POINTER(c_int),
                                   ctypes.POINTER(c_double)]),
     "sdm_device_status": (c_int, [P]),
+    "sdm_set_wait_limit_ns": (c_int, [ctypes.c_uint64]),
+    "sdm_wait_probe": (c_int, [P, P]),
     "sdm_pk_address": (c_int, [P, P, P, c_int64, c_int, c_int, c_int, c_int, P, P, P]),
     "sdm_rmsnorm": (c_int, [P, P, c_int64, c_int, c_float, c_int, P, P]),
     "sdm_rt_forward_workspace_size": (c_size_t, [ctypes.POINTER(RtParams), c_int, c_int]),

@@ -373,6 +373,17 @@ sdm_status sdm_device_status(void* stream) {
   return (gemm || scan) ? SDM_ERR_TIMEOUT : SDM_OK;
 }
 
+sdm_status sdm_set_wait_limit_ns(uint64_t ns) {
+  if (set_gemm_wait_limit(ns) != cudaSuccess) return SDM_ERR_CUDA;
+  if (set_scan_wait_limit(ns) != cudaSuccess) return SDM_ERR_CUDA;
+  return SDM_OK;
+}
+
+sdm_status sdm_wait_probe(int* done, void* stream) {
+  if (!done) return SDM_ERR_ARG;
+  return to_status(launch_wait_probe(done, S(stream)));
+}
+
 const char* sdm_status_string(sdm_status s) {
   switch (s) {
     case SDM_OK: return "ok";

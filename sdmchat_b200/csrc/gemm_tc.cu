@@ -357,5 +357,21 @@ SDM_TC_INST(EpiArgmax)
 
 // Read and clear the bounded-wait timeout flag of the GEMM module.
 cudaError_t read_and_clear_timeout(int* flag, cudaStream_t st) { return tma::read_and_clear_wait_timeout(flag, st); }
+cudaError_t set_gemm_wait_limit(unsigned long long ns) { return tma::set_wait_limit(ns); }
+
+// One thread waits, through the GEMM's bounded mbarrier wait, on a barrier that nothing arrives on and that no
+// copy completes: the wait gives up after the module's limit, sets the timeout flag and the kernel returns.
+__global__ void wait_probe_kernel(int* done) {
+  pdl_enter();
+  __shared__ __align__(8) uint64_t bar;
+  tma::mbar_init(&bar, 1);
+  tma::mbar_init_fence();
+  const bool ok = tma::mbar_wait(&bar, 0u);
+  *done = ok ? 1 : 2;
+}
+cudaError_t launch_wait_probe(int* done, cudaStream_t st) {
+  LaunchScope scope_("wait_probe", st);
+  return launch_k(wait_probe_kernel, dim3(1), dim3(1), 0, st, done);
+}
 
 }  // namespace sdm

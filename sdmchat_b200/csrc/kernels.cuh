@@ -353,6 +353,10 @@ cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st);
 bool rt_scan_supported(int M, int dh, int k);
 size_t rt_scan_workspace_bytes(int B, int T, int h, int k);
 cudaError_t read_and_clear_scan_timeout(int* flag, cudaStream_t st);
+// Bounded-wait limits of the scan and GEMM modules (0 = the default, about 4 s), and the wait probe.
+cudaError_t set_scan_wait_limit(unsigned long long ns);
+cudaError_t set_gemm_wait_limit(unsigned long long ns);
+cudaError_t launch_wait_probe(int* done, cudaStream_t st);
 
 // Single-token decode on the lazily-decayed state.
 struct DecodeArgs {

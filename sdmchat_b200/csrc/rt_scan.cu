@@ -1046,5 +1046,6 @@ cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st) {
 cudaError_t read_and_clear_scan_timeout(int* flag, cudaStream_t st) {
   return tma::read_and_clear_wait_timeout(flag, st);
 }
+cudaError_t set_scan_wait_limit(unsigned long long ns) { return tma::set_wait_limit(ns); }
 
 }  // namespace sdm

@@ -9,6 +9,10 @@ namespace tma {
 
 // Set by a bounded wait that gave up (one copy per .cu module; read back through that module's host function).
 static __device__ int g_wait_timeout;
+// How long a bounded wait keeps polling before it gives up, in ns of %globaltimer (one copy per .cu module; set
+// through set_wait_limit, e.g. shortened by a test that makes a wait run out).
+constexpr unsigned long long kDefaultWaitLimitNs = 4000000000ull;
+static __device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -39,14 +43,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Wait for the phase with the given parity to complete; false (and the timeout flag set) after ~4 s.
+// Wait for the phase with the given parity to complete; false (and the timeout flag set) once g_wait_limit_ns
+// (about 4 s unless changed) has passed.
 static __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
+  const uint64_t limit = *(volatile unsigned long long*)&g_wait_limit_ns;
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > 4000000000ull) {
+    if (global_ns() - t0 > limit) {
       atomicExch(&g_wait_timeout, 1);
       return false;
     }
@@ -85,6 +91,12 @@ static inline cudaError_t read_and_clear_wait_timeout(int* flag, cudaStream_t st
   e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return e;
   return cudaMemcpyToSymbol(g_wait_timeout, &zero, sizeof(int));
+}
+
+// Sets this module's bounded-wait limit on the current device (0 restores the default); synchronous.
+static inline cudaError_t set_wait_limit(unsigned long long ns) {
+  const unsigned long long v = ns ? ns : kDefaultWaitLimitNs;
+  return cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v));
 }
 
 }  // namespace tma

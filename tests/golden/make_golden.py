@@ -1,7 +1,7 @@
 """Write the golden fixtures of this directory from the UNMODIFIED SDMCHAT reference module.
 
 Run from the repository root, where the reference checkout is readable:
-    python tests/golden/make_golden.py [--ref PATH_TO_SDMCHAT_CHECKOUT]
+    python tests/golden/make_golden.py --ref PATH_TO_SDMCHAT_CHECKOUT   (or SDMCHAT_REF=PATH in the environment)
 
 It imports experiments/track4/sdmllm/track4_onesdm_models.py (the reference's own RunTimeSdm, TrainedSdm,
 pk_address and OneSdmLM) on the CPU in float32, builds seeded modules exactly as the reference's constructors and
@@ -237,8 +237,11 @@ def lm_case(OM, name, arm, reset_at_bos=False):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("SDMCHAT_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("SDMCHAT_REF"),
+                    help="path of an SDMCHAT checkout (required; or set SDMCHAT_REF)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("--ref (or SDMCHAT_REF) must name an SDMCHAT checkout")
     OM = load_reference(a.ref)
     torch.set_num_threads(1)  # bit-reproducible CPU reductions, as the reference's trainer self-test does
     pk_cases(OM)

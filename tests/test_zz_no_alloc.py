@@ -3,8 +3,9 @@
 Some callers cannot allocate device memory on their decode path: a serving loop that owns every byte of the GPU in
 a fixed pool, or a host runtime behind an FFI with no device allocator to provide a workspace.  For them the library
 runs the decode step on a fixed scratch array of its own.  This test calls that entry point through the C ABI and
-checks that two consecutive calls reproduce sdm_rt_decode_step (outputs within the bf16-output tolerance the other
-tests use, carried state equal), and that a request larger than the fixed scratch is refused before any launch.
+checks that two consecutive calls, and a third that empties some streams through its reset mask, reproduce
+sdm_rt_decode_step bit for bit (the same kernels on the same inputs: output and carried state identical), and that a
+request larger than the fixed scratch is refused before any launch.
 It is collected last and passes alone in a fresh process as well as after the other tests.
 """
 import numpy as np
@@ -12,7 +13,6 @@ import pytest
 import torch
 
 import sdmchat_b200 as S
-from goldens import rel, rel_bf16
 from sdmchat_b200 import _lib
 
 pytestmark = pytest.mark.gpu
@@ -35,21 +35,27 @@ def test_noalloc_decode_matches_workspace_decode(cuda_ok):
     p, _ = m._params(torch.bfloat16)
     lib = _lib.lib()
     g = torch.Generator(device="cuda").manual_seed(1)
+    # two calls in a row (the second reads the state the first wrote), then a third that empties streams 1 and 5
+    resets = [None, None, torch.tensor([0, 1, 0, 0, 0, 1, 0, 0], dtype=torch.uint8, device="cuda")]
     with torch.no_grad():
-        for call in range(2):  # two calls in a row: the second reads the state the first wrote
+        for call, rs in enumerate(resets):
             x = (torch.randn(n, 768, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
-            want = m.decode_step(x, ref_state, add_residual=True)
+            want = m.decode_step(x, ref_state, reset=rs, add_residual=True)
             out = torch.empty_like(x)
-            rc = lib.sdm_rt_decode_step_noalloc(p, _lib.ptr(x), n, None, 1, _lib.ptr(out), _lib.ptr(state["mem"]),
-                                                _lib.ptr(state["cnt"]), _lib.ptr(state["scale"]),
-                                                _lib.ptr(state["last_w"]), _lib.stream_ptr())
+            rc = lib.sdm_rt_decode_step_noalloc(p, _lib.ptr(x), n, _lib.ptr(rs), 1, _lib.ptr(out),
+                                                _lib.ptr(state["mem"]), _lib.ptr(state["cnt"]),
+                                                _lib.ptr(state["scale"]), _lib.ptr(state["last_w"]),
+                                                _lib.stream_ptr())
             assert rc == 0, lib.sdm_status_string(rc)
             torch.cuda.synchronize()
-            assert rel_bf16(out.float().cpu().numpy(), want.float().cpu().numpy()) < 2e-3, call
-            for key in ("mem", "cnt", "scale"):
-                assert rel(state[key].cpu().numpy(), ref_state[key].cpu().numpy()) < 2e-3, (call, key)
-            assert torch.equal(state["last_w"], ref_state["last_w"]), call
+            # the same kernels on the same inputs: bit-identical output and carried state
+            assert torch.equal(out, want), call
+            for key in ("mem", "cnt", "scale", "last_w"):
+                assert torch.equal(state[key], ref_state[key]), (call, key)
             assert float(state["cnt"].abs().sum()) > 0
+        # the reset streams hold only the third token's writes: one write per selected slot
+        cnt = state["cnt"] * state["scale"][..., None]
+        assert torch.count_nonzero(cnt[1]) <= 12 * 16 and torch.count_nonzero(cnt[0]) > 12 * 16
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch(cuda_ok):
