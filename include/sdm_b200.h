@@ -122,16 +122,27 @@ sdm_status sdm_rt_forward(const sdm_rt_params* p, const void* x, int B, int T, c
                           int32_t* siw, float* ww, int32_t* sir, float* wr, float* gate, float* values, float* num,
                           float* den, void* workspace, size_t workspace_bytes, void* stream);
 
-/* The chunk loop alone (RunTimeSdm._chunk over all chunks, M:215-241, 255-272) from prepared selections:
- * siw, sir (B, h, T, k) int32; ww, wr (B, h, T, k) float32; V (B*T rows, row stride ldv floats, head hh's dh
- * values at column hh*dh); decay (h).  num (B, T, h, dh), den (B, T, h) float32; mem_out/cnt_out optional.
- * The state stays resident in shared memory for the whole window; the workspace (16-byte aligned,
+/* The chunk loop (RunTimeSdm._chunk over all chunks of a window, M:215-241, 255-272; one call with T = L is one
+ * _chunk) from prepared selections: siw, sir (B, h, T, k) int32; ww, wr (B, h, T, k) float32; V (B*T rows, row
+ * stride ldv floats, head hh's dh values at column hh*dh); decay (h).  mem_in (B, h, M, dh) / cnt_in (B, h, M): the
+ * state carried in (_chunk's mem, cnt), or both NULL for an empty memory.  reset (B, T) uint8 or NULL empties the
+ * memory before that position reads (_chunk's seg / seg_prev: reset[t] = seg[t] != seg[t-1], seg[-1] = seg_prev).
+ * num (B, T, h, dh), den (B, T, h) float32; mem_out / cnt_out (the state after the window) optional.  The state
+ * stays resident in shared memory for the whole window; the workspace (16-byte aligned,
  * sdm_rt_scan_workspace_size bytes) holds the per-chunk slot lists. */
 size_t sdm_rt_scan_workspace_size(int B, int T, int heads, int k);
 sdm_status sdm_rt_scan(const int32_t* siw, const float* ww, const int32_t* sir, const float* wr, const float* V,
                        int64_t ldv, const float* decay, const uint8_t* reset, int B, int T, int heads, int n_sub,
-                       int dh, int k, float* num, float* den, float* mem_out, float* cnt_out, void* workspace,
-                       size_t workspace_bytes, void* stream);
+                       int dh, int k, const float* mem_in, const float* cnt_in, float* num, float* den,
+                       float* mem_out, float* cnt_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* RunTimeSdm.finish (M:243-247): r = num / (den + read_eps) (read_mode "mean") or num; the per-head RMS out-norm
+ * with onorm_w; out (N, d) in p->dtype = wo(r), plus x (N, d) when x is not NULL (the residual add of
+ * OneSdmLM.residual, M:540).  num (N, h, dh) and den (N, h) float32, token-major as sdm_rt_scan writes them.  In
+ * bf16 mode wo's float32 input is fed to the tensor cores as an exact bf16 hi + lo pair. */
+size_t sdm_rt_finish_workspace_size(const sdm_rt_params* p, int64_t N);
+sdm_status sdm_rt_finish(const sdm_rt_params* p, const float* num, const float* den, int64_t N, const void* x,
+                         void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Carried-state decode (new API; the reference has none, M:249-258): one token per stream through one
  * RunTimeSdm, the state read and then written in place.  x, out (S, d) in p->dtype (one token per stream).
@@ -180,7 +191,19 @@ sdm_status sdm_ts_forward(const sdm_ts_params* p, const void* x, int64_t N, int 
                           int32_t* si, float* w, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------------------ SwiGLU
- * x + SwiGLU(RMSNorm(x)) (M:544-545, L:96-97): w_gate, w_up (f, d), w_down (d, f), norm_w (d). */
+ * SwiGLU.forward (L:96-97): down(silu(gate x) * up x); w_gate, w_up (f, d), w_down (d, f); f a multiple of 16.
+ * In bf16 mode gate and up are one tensor-core GEMM against a packed (2f, d) weight whose epilogue applies
+ * silu(g) * u (each factor rounded as the bf16 reference rounds), so only the product reaches memory.
+ * sdm_swiglu_pack writes that packed weight (rows 32j .. 32j+15 = gate rows 16j .. 16j+15, the next 16 the same
+ * up rows); pack once per weight update.
+ * sdm_swiglu_forward: x, out (N, d); norm_w (d) or NULL: with it the input is RMSNorm(x) (OneSdmLM's mnorms[i],
+ * M:544-545); add_residual: out = x + SwiGLU(...) rounded as the reference's residual add.
+ * sdm_swiglu_block: x + SwiGLU(RMSNorm(x)) from the unpacked weights (packs into its workspace on every call). */
+sdm_status sdm_swiglu_pack(const void* w_gate, const void* w_up, int d, int f, int dtype, void* w_gu, void* stream);
+size_t sdm_swiglu_forward_workspace_size(int64_t N, int d, int f, int dtype);
+sdm_status sdm_swiglu_forward(const void* x, const void* norm_w, const void* w_gu, const void* w_down, int64_t N,
+                              int d, int f, float eps, int dtype, int add_residual, void* out, void* workspace,
+                              size_t workspace_bytes, void* stream);
 size_t sdm_swiglu_workspace_size(int64_t N, int d, int f, int dtype);
 sdm_status sdm_swiglu_block(const void* x, const void* norm_w, const void* w_gate, const void* w_up,
                             const void* w_down, int64_t N, int d, int f, float eps, int dtype, void* out,
@@ -200,6 +223,10 @@ sdm_status sdm_tied_ce_sum(const void* x, const void* nf_w, const void* emb, con
                            size_t workspace_bytes, void* stream);
 sdm_status sdm_tied_argmax(const void* x, const void* nf_w, const void* emb, int64_t N, int d, int V, float eps,
                            int dtype, int32_t* ids, void* workspace, size_t workspace_bytes, void* stream);
+
+/* OneSdmLM.project (M:528-529) of the tied head: logits (N, V) = h (N, d) @ emb (V, d)^T in dtype (no norm). */
+sdm_status sdm_tied_project(const void* h, const void* emb, int64_t N, int d, int V, int dtype, void* logits,
+                            void* stream);
 
 /* Token table lookup (OneSdmLM.enfold, M:525-526): out (N, d) = emb[ids]; ids outside [0, V) -> SDM_ERR_RANGE
  * is reported through *bad (device int, set to 1) since ids live on the device; the row is then zero. */

@@ -225,15 +225,19 @@ sdm_status ts_forward_t(const sdm_ts_params* p, const void* xv, int64_t N, int a
   const T* x = static_cast<const T*>(xv);
   const int h = p->heads, d = p->d, dh = d / h, kk = sel_k(p->k, p->n_sub);
   SDM_TRY(launch_rmsnorm<T>(x, static_cast<const T*>(p->norm_w), N, d, p->norm_eps, static_cast<T*>(hs), st));
+  {
+    OpTag tq_("ts_q");
+    EpiF32 eq{q, (int64_t)h * p->d_a};
+    SDM_TRY(launch_gemm<T, EpiF32>(static_cast<T*>(hs), d, static_cast<const T*>(p->wq), d, N, d, h * p->d_a, eq, st));
+  }
   OpTag tag_("ts");
-  EpiF32 eq{q, (int64_t)h * p->d_a};
-  SDM_TRY(launch_gemm<T, EpiF32>(static_cast<T*>(hs), d, static_cast<const T*>(p->wq), d, N, d, h * p->d_a, eq, st));
   constexpr int split = sizeof(T) == 2;
   if (sizeof(T) == 2 && ts_addr_gather_ok(N, h, p->d_a, p->n_sub, p->k, dh) &&
       (reinterpret_cast<uintptr_t>(p->values) & 15) == 0) {  // decode-sized: selection and read in one launch
     SDM_TRY(launch_ts_addr_gather(q, (int64_t)h * p->d_a, p->keys1, p->keys2, p->log_scale, p->n_sub, p->k,
                                   static_cast<const bf16_t*>(p->values), N, h, dh, si, w,
                                   reinterpret_cast<bf16_t*>(rb), split, st));
+    OpTag two_("ts_wo");
     EpiResid<T> er{add_res ? x : nullptr, static_cast<T*>(outv), d};
     SDM_TRY(launch_gemm<T, EpiResid<T>>(static_cast<T*>(rb), (1 + split) * d, static_cast<const T*>(p->wo), d, N,
                                         (1 + split) * d, d, er, st, d));
@@ -256,40 +260,71 @@ sdm_status ts_forward_t(const sdm_ts_params* p, const void* xv, int64_t N, int a
   SDM_TRY(launch_pk_address(pa, st));
   SDM_TRY(launch_ts_gather<T>(si, w, static_cast<const T*>(p->values), N, h, p->n_sub * p->n_sub, dh, kk,
                               static_cast<T*>(rb), split, st));
+  OpTag two_("ts_wo");
   EpiResid<T> er{add_res ? x : nullptr, static_cast<T*>(outv), d};
   SDM_TRY(launch_gemm<T, EpiResid<T>>(static_cast<T*>(rb), (1 + split) * d, static_cast<const T*>(p->wo), d, N,
                                       (1 + split) * d, d, er, st, d));
   return SDM_OK;
 }
 
-size_t swiglu_ws(int64_t N, int d, int f, int dtype, void* base, void** hm, void** g, void** u, void** pp) {
+// Rows of the packed gate|up weight (2f, d): block j of 32 rows = gate rows [16j, 16j + 16) then up rows
+// [16j, 16j + 16) (two strided 2-D copies).
+cudaError_t swiglu_pack_rows(const void* wg, const void* wu, int d, int f, size_t es, void* wgu, cudaStream_t st) {
+  const size_t blk = (size_t)16 * d * es;
+  cudaError_t e = cudaMemcpy2DAsync(wgu, 2 * blk, wg, blk, blk, f / 16, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return e;
+  return cudaMemcpy2DAsync(static_cast<char*>(wgu) + blk, 2 * blk, wu, blk, blk, f / 16, cudaMemcpyDeviceToDevice, st);
+}
+
+// The fused path: bf16 on the tensor cores (d >= 16 and a multiple of 8; f a multiple of 16, which every entry
+// point requires).  Its operands are 16-byte aligned: the normalised rows live in the workspace, an input without a
+// norm is first copied there when it is not aligned, and a misaligned packed weight is refused.
+bool swiglu_fused_shape(int dtype, int d) { return dtype == SDM_BF16 && d >= 16 && (d % 8) == 0; }
+
+// Workspace of the SwiGLU entry points: the normalised (or aligned) rows and p = silu(gate) * up; the unfused path
+// adds the (N, 2f) gate|up output.  `packed`: room for the packed weight too (sdm_swiglu_block).
+size_t swiglu_ws(int64_t N, int d, int f, int dtype, bool packed, void* base, void** hm, void** pp, void** gu,
+                 void** wgu) {
   Bump bp(base);
   const size_t es = dtype == SDM_BF16 ? 2 : 4;
   *hm = bp.take<char>(N * d * es);
-  *g = bp.take<char>(N * f * es);
-  *u = bp.take<char>(N * f * es);
   *pp = bp.take<char>(N * f * es);
+  *gu = swiglu_fused_shape(dtype, d) ? nullptr : bp.take<char>(N * 2 * f * es);
+  *wgu = packed ? bp.take<char>((size_t)2 * f * d * es) : nullptr;
   return bp.off;
 }
 
 template <typename T>
-sdm_status swiglu_t(const void* xv, const void* nw, const void* wg, const void* wu, const void* wd, int64_t N, int d,
-                    int f, float eps, void* outv, void* ws, size_t ws_bytes, cudaStream_t st) {
-  void *hm, *g, *u, *pp;
-  const int dtype = sizeof(T) == 2 ? SDM_BF16 : SDM_F32;
-  const size_t need = swiglu_ws(N, d, f, dtype, nullptr, &hm, &g, &u, &pp);
-  if (ws_bytes < need || (need && !ws)) return SDM_ERR_WORKSPACE;
-  swiglu_ws(N, d, f, dtype, ws, &hm, &g, &u, &pp);
+sdm_status swiglu_t(const void* xv, const void* nw, const void* wgu, const void* wd, int64_t N, int d, int f,
+                    float eps, int add_res, void* outv, void* hm, void* pp, void* gu, cudaStream_t st) {
   if (N == 0) return SDM_OK;
   const T* x = static_cast<const T*>(xv);
+  const int dtype = sizeof(T) == 2 ? SDM_BF16 : SDM_F32;
   OpTag tag_("swiglu");
-  SDM_TRY(launch_rmsnorm<T>(x, static_cast<const T*>(nw), N, d, eps, static_cast<T*>(hm), st));
-  SDM_TRY(launch_gemm<T, EpiStore<T>>(static_cast<T*>(hm), d, static_cast<const T*>(wg), d, N, d, f,
-                                      EpiStore<T>{static_cast<T*>(g), f}, st));
-  SDM_TRY(launch_gemm<T, EpiStore<T>>(static_cast<T*>(hm), d, static_cast<const T*>(wu), d, N, d, f,
-                                      EpiStore<T>{static_cast<T*>(u), f}, st));
-  SDM_TRY(launch_swiglu_act<T>(static_cast<T*>(g), static_cast<T*>(u), N * f, static_cast<T*>(pp), st));
-  EpiResid<T> er{x, static_cast<T*>(outv), d};
+  const T* h = x;
+  if (nw) {
+    SDM_TRY(launch_rmsnorm<T>(x, static_cast<const T*>(nw), N, d, eps, static_cast<T*>(hm), st));
+    h = static_cast<const T*>(hm);
+  }
+  if (swiglu_fused_shape(dtype, d)) {
+    if ((reinterpret_cast<uintptr_t>(wgu) & 15) != 0) return SDM_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(h) & 15) != 0) {
+      SDM_TRY(cudaMemcpyAsync(hm, h, (size_t)N * d * sizeof(T), cudaMemcpyDeviceToDevice, st));
+      h = static_cast<const T*>(hm);
+    }
+    if constexpr (sizeof(T) == 2) {
+      OpTag tag2_("swiglu_gu");
+      SDM_TRY(launch_gemm_tc<EpiSwiGLU>(h, d, static_cast<const bf16_t*>(wgu), d, N, d, 2 * f,
+                                        EpiSwiGLU{static_cast<bf16_t*>(pp), f}, st, d));
+    }
+  } else {
+    OpTag tag2_("swiglu_gu");
+    SDM_TRY(launch_gemm<T, EpiStore<T>>(h, d, static_cast<const T*>(wgu), d, N, d, 2 * f,
+                                        EpiStore<T>{static_cast<T*>(gu), 2 * f}, st));
+    SDM_TRY(launch_swiglu_act<T>(static_cast<T*>(gu), N, f, static_cast<T*>(pp), st));
+  }
+  OpTag tag3_("swiglu_down");
+  EpiResid<T> er{add_res ? x : nullptr, static_cast<T*>(outv), d};
   SDM_TRY(launch_gemm<T, EpiResid<T>>(static_cast<T*>(pp), f, static_cast<const T*>(wd), f, N, f, d, er, st));
   return SDM_OK;
 }
@@ -364,7 +399,7 @@ sdm_status head_t(int mode, const void* xv, const void* nf_w, const void* emb, c
 
 extern "C" {
 
-int sdm_abi_version(void) { return 1; }
+int sdm_abi_version(void) { return 2; }
 
 sdm_status sdm_device_status(void* stream) {
   int gemm = 0, scan = 0;
@@ -460,9 +495,10 @@ size_t sdm_rt_scan_workspace_size(int B, int T, int heads, int k) {
 
 sdm_status sdm_rt_scan(const int32_t* siw, const float* ww, const int32_t* sir, const float* wr, const float* V,
                        int64_t ldv, const float* decay, const uint8_t* reset, int B, int T, int heads, int n_sub,
-                       int dh, int k, float* num, float* den, float* mem_out, float* cnt_out, void* workspace,
-                       size_t workspace_bytes, void* stream) {
+                       int dh, int k, const float* mem_in, const float* cnt_in, float* num, float* den,
+                       float* mem_out, float* cnt_out, void* workspace, size_t workspace_bytes, void* stream) {
   if (!siw || !ww || !sir || !wr || !V || !decay || !num || !den) return SDM_ERR_ARG;
+  if ((mem_in == nullptr) != (cnt_in == nullptr)) return SDM_ERR_ARG;
   if (B < 0 || T < 0 || heads < 1 || n_sub < 1 || dh < 1 || k < 1 || ldv < (int64_t)heads * dh) return SDM_ERR_SHAPE;
   if (!rt_scan_supported(n_sub * n_sub, dh, k)) return SDM_ERR_SHAPE;
   const size_t need = rt_scan_workspace_bytes(B, T, heads, k);
@@ -488,7 +524,45 @@ sdm_status sdm_rt_scan(const int32_t* siw, const float* ww, const int32_t* sir, 
   sa.mem_out = mem_out;
   sa.cnt_out = cnt_out;
   sa.rec = static_cast<unsigned char*>(workspace);
+  sa.mem_in = mem_in;
+  sa.cnt_in = cnt_in;
   return to_status(launch_rt_scan(sa, S(stream)));
+}
+
+size_t sdm_rt_finish_workspace_size(const sdm_rt_params* p, int64_t N) {
+  if (check_rt(p) != SDM_OK || N < 0) return 0;
+  Bump meas(nullptr);
+  meas.take<char>(N * p->d * 4);  // bf16: the read's hi | lo halves; float32: the read
+  return meas.off;
+}
+
+sdm_status sdm_rt_finish(const sdm_rt_params* p, const float* num, const float* den, int64_t N, const void* x,
+                         void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  sdm_status s = check_rt(p);
+  if (s != SDM_OK) return s;
+  if (!num || !den || !out) return SDM_ERR_ARG;
+  if (N < 0) return SDM_ERR_SHAPE;
+  const size_t need = sdm_rt_finish_workspace_size(p, N);
+  if (workspace_bytes < need || (need && !workspace)) return SDM_ERR_WORKSPACE;
+  if (N == 0) return SDM_OK;
+  const int h = p->heads, d = p->d, dh = d / h;
+  cudaStream_t st = S(stream);
+  OpTag tag_("rt_out");
+  if (p->dtype == SDM_BF16) {
+    bf16_t* r = static_cast<bf16_t*>(workspace);
+    SDM_TRY(launch_rt_finish<bf16_t>(num, den, N, h, dh, p->read_sum, p->read_eps, p->out_norm, p->out_norm_eps,
+                                     p->onorm_w, r, 1, st));
+    EpiResid<bf16_t> er{static_cast<const bf16_t*>(x), static_cast<bf16_t*>(out), d};
+    SDM_TRY(launch_gemm<bf16_t, EpiResid<bf16_t>>(r, 2 * d, static_cast<const bf16_t*>(p->wo), d, N, 2 * d, d, er, st,
+                                                  d));
+  } else {
+    float* r = static_cast<float*>(workspace);
+    SDM_TRY(launch_rt_finish<float>(num, den, N, h, dh, p->read_sum, p->read_eps, p->out_norm, p->out_norm_eps,
+                                    p->onorm_w, r, 0, st));
+    EpiResid<float> er{static_cast<const float*>(x), static_cast<float*>(out), d};
+    SDM_TRY(launch_gemm<float, EpiResid<float>>(r, d, static_cast<const float*>(p->wo), d, N, d, d, er, st));
+  }
+  return SDM_OK;
 }
 
 size_t sdm_rt_decode_workspace_size(const sdm_rt_params* p, int S_) {
@@ -591,21 +665,60 @@ sdm_status sdm_ts_forward(const sdm_ts_params* p, const void* x, int64_t N, int 
   return ts_forward_t<float>(p, x, N, add_residual, out, si, w, workspace, workspace_bytes, S(stream));
 }
 
+sdm_status sdm_swiglu_pack(const void* w_gate, const void* w_up, int d, int f, int dtype, void* w_gu, void* stream) {
+  if (!w_gate || !w_up || !w_gu) return SDM_ERR_ARG;
+  if (dtype != SDM_F32 && dtype != SDM_BF16) return SDM_ERR_ARG;
+  if (d < 1 || f < 16 || f % 16) return SDM_ERR_SHAPE;
+  return to_status(swiglu_pack_rows(w_gate, w_up, d, f, dtype == SDM_BF16 ? 2 : 4, w_gu, S(stream)));
+}
+
+size_t sdm_swiglu_forward_workspace_size(int64_t N, int d, int f, int dtype) {
+  void *a, *b, *c, *e;
+  if (N < 0 || d < 1 || f < 1) return 0;
+  return swiglu_ws(N, d, f, dtype, false, nullptr, &a, &b, &c, &e);
+}
+
+static sdm_status swiglu_run(const void* x, const void* norm_w, const void* w_gu, const void* w_down, int64_t N, int d,
+                             int f, float eps, int dtype, int add_res, void* out, bool pack_from, const void* wg,
+                             const void* wu, void* ws, size_t wsb, cudaStream_t st) {
+  void *hm, *pp, *gu, *wgu;
+  const size_t need = swiglu_ws(N, d, f, dtype, pack_from, nullptr, &hm, &pp, &gu, &wgu);
+  if (wsb < need || (need && !ws)) return SDM_ERR_WORKSPACE;
+  swiglu_ws(N, d, f, dtype, pack_from, ws, &hm, &pp, &gu, &wgu);
+  if (pack_from) {
+    if (N == 0) return SDM_OK;
+    SDM_TRY(swiglu_pack_rows(wg, wu, d, f, dtype == SDM_BF16 ? 2 : 4, wgu, st));
+    w_gu = wgu;
+  }
+  if (dtype == SDM_BF16)
+    return swiglu_t<bf16_t>(x, norm_w, w_gu, w_down, N, d, f, eps, add_res, out, hm, pp, gu, st);
+  return swiglu_t<float>(x, norm_w, w_gu, w_down, N, d, f, eps, add_res, out, hm, pp, gu, st);
+}
+
+sdm_status sdm_swiglu_forward(const void* x, const void* norm_w, const void* w_gu, const void* w_down, int64_t N,
+                              int d, int f, float eps, int dtype, int add_residual, void* out, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (!x || !w_gu || !w_down || !out) return SDM_ERR_ARG;
+  if (dtype != SDM_F32 && dtype != SDM_BF16) return SDM_ERR_ARG;
+  if (N < 0 || d < 1 || f < 16 || f % 16) return SDM_ERR_SHAPE;
+  return swiglu_run(x, norm_w, w_gu, w_down, N, d, f, eps, dtype, add_residual, out, false, nullptr, nullptr,
+                    workspace, workspace_bytes, S(stream));
+}
+
 size_t sdm_swiglu_workspace_size(int64_t N, int d, int f, int dtype) {
   void *a, *b, *c, *e;
-  return swiglu_ws(N < 0 ? 0 : N, d, f, dtype, nullptr, &a, &b, &c, &e);
+  if (N < 0 || d < 1 || f < 1) return 0;
+  return swiglu_ws(N, d, f, dtype, true, nullptr, &a, &b, &c, &e);
 }
 
 sdm_status sdm_swiglu_block(const void* x, const void* norm_w, const void* w_gate, const void* w_up,
                             const void* w_down, int64_t N, int d, int f, float eps, int dtype, void* out,
                             void* workspace, size_t workspace_bytes, void* stream) {
   if (!x || !norm_w || !w_gate || !w_up || !w_down || !out) return SDM_ERR_ARG;
-  if (N < 0 || d < 1 || f < 1) return SDM_ERR_SHAPE;
-  if (dtype == SDM_BF16)
-    return swiglu_t<bf16_t>(x, norm_w, w_gate, w_up, w_down, N, d, f, eps, out, workspace, workspace_bytes, S(stream));
-  if (dtype == SDM_F32)
-    return swiglu_t<float>(x, norm_w, w_gate, w_up, w_down, N, d, f, eps, out, workspace, workspace_bytes, S(stream));
-  return SDM_ERR_ARG;
+  if (dtype != SDM_F32 && dtype != SDM_BF16) return SDM_ERR_ARG;
+  if (N < 0 || d < 1 || f < 16 || f % 16) return SDM_ERR_SHAPE;
+  return swiglu_run(x, norm_w, nullptr, w_down, N, d, f, eps, dtype, 1, out, true, w_gate, w_up, workspace,
+                    workspace_bytes, S(stream));
 }
 
 size_t sdm_tied_head_workspace_size(int64_t N, int d, int V, int dtype) {
@@ -647,6 +760,20 @@ sdm_status sdm_tied_argmax(const void* x, const void* nf_w, const void* emb, int
   if (!ids) return SDM_ERR_ARG;
   return head_dispatch(2, x, nf_w, emb, nullptr, N, d, V, eps, dtype, nullptr, nullptr, ids, workspace,
                        workspace_bytes, stream);
+}
+
+sdm_status sdm_tied_project(const void* h, const void* emb, int64_t N, int d, int V, int dtype, void* logits,
+                            void* stream) {
+  if (!h || !emb || !logits) return SDM_ERR_ARG;
+  if (N < 0 || d < 1 || V < 1) return SDM_ERR_SHAPE;
+  OpTag tag_("head_project");
+  if (dtype == SDM_BF16)
+    return to_status(launch_gemm<bf16_t, EpiStore<bf16_t>>((const bf16_t*)h, d, (const bf16_t*)emb, d, N, d, V,
+                                                           EpiStore<bf16_t>{(bf16_t*)logits, V}, S(stream)));
+  if (dtype == SDM_F32)
+    return to_status(launch_gemm<float, EpiStore<float>>((const float*)h, d, (const float*)emb, d, N, d, V,
+                                                         EpiStore<float>{(float*)logits, V}, S(stream)));
+  return SDM_ERR_ARG;
 }
 
 sdm_status sdm_embed(const int32_t* ids, const void* emb, int64_t N, int d, int V, int dtype, void* out, int* bad,

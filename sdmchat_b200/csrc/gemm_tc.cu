@@ -354,6 +354,7 @@ SDM_TC_INST(EpiF32R<bf16_t>)
 SDM_TC_INST(EpiResid<bf16_t>)
 SDM_TC_INST(EpiCE)
 SDM_TC_INST(EpiArgmax)
+SDM_TC_INST(EpiSwiGLU)
 
 // Read and clear the bounded-wait timeout flag of the GEMM module.
 cudaError_t read_and_clear_timeout(int* flag, cudaStream_t st) { return tma::read_and_clear_wait_timeout(flag, st); }

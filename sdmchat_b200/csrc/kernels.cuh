@@ -267,6 +267,44 @@ struct EpiArgmax {
     if (row < rows) part[row * tiles_n + tn] = make_float2(rs.best, __int_as_float(rs.idx));
   }
 };
+// EpiSwiGLU: SwiGLU's gate and up maps (L:96-97) as one GEMM against the packed weight of swiglu_pack_rows: packed
+// columns [32j, 32j + 16) are gate rows [16j, 16j + 16) and [32j + 16, 32j + 32) the up rows of the same f-indices,
+// so one thread's 32-column chunk holds both factors of 16 outputs.  Each is rounded as the bfloat16 reference
+// rounds: g and u (the Linear outputs), silu(g), then the product; only p = silu(g) * u reaches memory (bfloat16,
+// (rows, f) with row stride ldp, 32-byte row segments).
+struct EpiSwiGLU {
+  static constexpr bool kRowMode = true;
+  bf16_t* p;
+  int64_t ldp;
+  struct RowState {
+    int64_t row;
+    bool live;
+  };
+  __device__ __forceinline__ void row_begin(RowState& rs, int64_t row, int64_t rows, int) const {
+    rs.row = row;
+    rs.live = row < rows;
+  }
+  __device__ __forceinline__ void row_chunk(RowState& rs, int col0, int n, const uint32_t (&r)[32]) const {
+    if (!rs.live || col0 >= n) return;
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float v[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float g = bf16_round(__uint_as_float(r[2 * i + j]));
+        const float u = bf16_round(__uint_as_float(r[16 + 2 * i + j]));
+        v[j] = bf16_round(g / (1.f + expf(-g))) * u;
+      }
+      const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[0], v[1]);
+      o[i] = *reinterpret_cast<const uint32_t*>(&b2);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(p + rs.row * ldp + (col0 >> 1));
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+  __device__ __forceinline__ void row_end(const RowState&, int64_t, int64_t, int, int) const {}
+};
 // The tensor-core GEMM directly (row-owned epilogues have no CUDA-core path).
 template <typename Epi>
 cudaError_t launch_gemm_tc(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K, int n,
@@ -292,8 +330,9 @@ cudaError_t launch_rmsnorm(const T* x, const T* w, int64_t rows, int d, float ep
 template <typename T>
 cudaError_t launch_embed(const int32_t* ids, const T* emb, int64_t N, int d, int V, T* out, int* bad,
                          cudaStream_t st);
+// p (rows, f) = silu(gate) * up from the packed gate|up GEMM output gu (rows, 2f) (layout of EpiSwiGLU).
 template <typename T>
-cudaError_t launch_swiglu_act(const T* g, const T* u, int64_t n, T* p, cudaStream_t st);
+cudaError_t launch_swiglu_act(const T* gu, int64_t rows, int f, T* p, cudaStream_t st);
 // The module outputs below feed a wo GEMM whose reference input is float32: with split, row n of r holds the
 // bfloat16 high part in columns [0, d) and the bfloat16 remainder in [d, 2d) (r is (N, 2d)); else r is (N, d).
 template <typename T>
@@ -348,6 +387,8 @@ struct ScanArgs {
   float* den;   // (B*T, h)
   float* mem_out; float* cnt_out;
   unsigned char* rec;  // chunk records, rt_scan_workspace_bytes(B, T, h, k) bytes
+  // the state carried in (RunTimeSdm._chunk's mem, cnt: (B, h, M, dh), (B, h, M)), or both nullptr for an empty one
+  const float* mem_in; const float* cnt_in;
 };
 cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st);
 bool rt_scan_supported(int M, int dh, int k);

@@ -80,14 +80,20 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restric
 
 // SwiGLU activation (track4_sdmllm_models.py:96-97): p = silu(g) * u with the bf16 roundings of a bf16 module.
 template <typename T>
-__global__ void swiglu_act_kernel(const T* __restrict__ g, const T* __restrict__ u, int64_t n, T* __restrict__ p) {
+__global__ void swiglu_act_kernel(const T* __restrict__ gu, int64_t rows, int f, T* __restrict__ p) {
+  // gu (rows, 2f) in the packed layout of swiglu_pack_rows: output column j reads gate column 32*(j/16) + j%16 and
+  // up column 16 further
   pdl_enter();
+  const int64_t n = rows * f;
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (; i < n; i += stride) {
-    float gv = to_f32(g[i]);
-    float s = round_to<T>(gv / (1.f + expf(-gv)));
-    p[i] = from_f32<T>(s * to_f32(u[i]));
+    const int64_t r = i / f;
+    const int j = (int)(i - r * f);
+    const T* row = gu + r * 2 * f + 32 * (j >> 4) + (j & 15);
+    const float gv = to_f32(row[0]);
+    const float s = round_to<T>(gv / (1.f + expf(-gv)));
+    p[i] = from_f32<T>(s * to_f32(row[16]));
   }
 }
 
@@ -396,12 +402,13 @@ cudaError_t launch_embed(const int32_t* ids, const T* emb, int64_t N, int d, int
   return launch_k(embed_kernel<T>, dim3((unsigned)ceil_div(N, 8)), dim3(256), 0, st, ids, emb, N, d, V, out, bad);
 }
 template <typename T>
-cudaError_t launch_swiglu_act(const T* g, const T* u, int64_t n, T* p, cudaStream_t st) {
+cudaError_t launch_swiglu_act(const T* gu, int64_t rows, int f, T* p, cudaStream_t st) {
+  const int64_t n = rows * f;
   if (n == 0) return cudaSuccess;
   int64_t blocks = ceil_div(n, 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
   LaunchScope scope_("swiglu_act", st);
-  return launch_k(swiglu_act_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, st, g, u, n, p);
+  return launch_k(swiglu_act_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, st, gu, rows, f, p);
 }
 template <typename T>
 cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int h, int dh, int read_sum,
@@ -584,7 +591,7 @@ cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values,
 #define SDM_INST(T)                                                                                              \
   template cudaError_t launch_rmsnorm<T>(const T*, const T*, int64_t, int, float, T*, cudaStream_t);            \
   template cudaError_t launch_embed<T>(const int32_t*, const T*, int64_t, int, int, T*, int*, cudaStream_t);    \
-  template cudaError_t launch_swiglu_act<T>(const T*, const T*, int64_t, T*, cudaStream_t);                     \
+  template cudaError_t launch_swiglu_act<T>(const T*, int64_t, int, T*, cudaStream_t);                          \
   template cudaError_t launch_rt_finish<T>(const float*, const float*, int64_t, int, int, int, float, int, float, \
                                            const float*, T*, int, cudaStream_t);                                 \
   template cudaError_t launch_ts_gather<T>(const int32_t*, const float*, const T*, int64_t, int, int, int, int, T*, \

@@ -393,6 +393,20 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
     for (int t = warp; t < Lc; t += LIST_WARPS) {
       const int ri = lane < k ? sir_s[t * k + lane] : -1;
       const float wi = lane < k ? wr_s[t * k + lane] : 0.f;
+      if (t == 0 && c0 == 0 && a.mem_in) {
+        // the window's first token reads the carried state unfaded (lam^0); nothing of it reaches later tokens
+        const bool live = !rst_s[0];
+        const float* mi = a.mem_in + (int64_t)bh * M * dh;
+        const float dsum = live ? warp_sum(lane < k ? wi * a.cnt_in[(int64_t)bh * M + ri] : 0.f) : 0.f;
+        float* dst = a.num + (tok0 * h + hh) * dh;
+        for (int col = lane; col < dh; col += 32) {
+          float acc = 0.f;
+          for (int j = 0; j < k; ++j) acc = fmaf(wr_s[j], mi[(int64_t)sir_s[j] * dh + col], acc);
+          dst[col] = live ? acc : 0.f;
+        }
+        if (lane == 0) a.den[tok0 * h + hh] = dsum;
+        continue;
+      }
       const bool has_src = !rst_s[t] && (t > 0 || c0 > 0);
       const float* sv = t > 0 ? V_s + (t - 1) * dh : prev_v;
       float dsum = 0.f;
@@ -730,8 +744,19 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
   const bool reads = mode != 0;
   const int4* hdrs = reinterpret_cast<const int4*>(a.rec + rec_region_bytes(a.B, T, h, k)) + (int64_t)bh * nch;
 
-  for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_THREADS) P4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] = 0.f;
+  if (a.mem_in && mode != 0) {
+    // the carried state (fade 0 keeps none of it past the first token, whose read the list kernel makes)
+    const float* mi = a.mem_in + ((int64_t)b * h + hh) * (int64_t)M * dh + cs * SCAN_CW;
+    for (int i = tid; i < M * SCAN_CW; i += SCAN_THREADS) {
+      const int r = i / SCAN_CW, cc = i % SCAN_CW;
+      P[i] = cc < ncols ? mi[(int64_t)r * dh + cc] : 0.f;
+    }
+    const float* ci = a.cnt_in + ((int64_t)b * h + hh) * (int64_t)M;
+    for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] = ci[i];
+  } else {
+    for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_THREADS) P4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] = 0.f;
+  }
   if (ncols < SCAN_CW) {  // columns past dh stay zero in both buffers (never copied, never stored)
     for (int i = tid; i < 2 * L * SCAN_CW; i += SCAN_THREADS) {
       const int bb = i / (L * SCAN_CW), j = i - bb * L * SCAN_CW;

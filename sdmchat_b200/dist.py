@@ -40,3 +40,36 @@ def reduce_loss(loss_sum, count, device=None):
 
 def env_world():
     return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+
+
+def world_size():
+    return dist.get_world_size() if dist.is_initialized() else 1
+
+
+def all_reduce_(buf):
+    """In-place sum of a tensor over all ranks (the per-step (loss sum, token count) exchange); no-op alone."""
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(buf)
+    return buf
+
+
+def barrier():
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x, device=None):
+    """The largest of a per-rank float (a timed duration: the job takes as long as its slowest rank)."""
+    if not (dist.is_initialized() and dist.get_world_size() > 1):
+        return float(x)
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def finalize():
+    """Last barrier, then destroy the process group (after every CUDA graph holding collectives is released)."""
+    if dist.is_initialized():
+        if dist.get_world_size() > 1:
+            dist.barrier()
+        dist.destroy_process_group()

@@ -91,34 +91,53 @@ class OneSdmLM(nn.Module):
                               stream_ptr(E.device)), "sdm_embed")
         return out, bad
 
-    def residual(self, idx, sequential=False):
-        """OneSdmLM.residual (M:534-548) with each residual add fused into the module's last GEMM."""
+    def residual(self, idx, sequential=False, trace=None):
+        """OneSdmLM.residual (M:534-548) with each residual add fused into the module's last GEMM.  trace: a list
+        that receives, per layer, the layer input, the stream after the memory, and the slot selections (write and
+        read ids (B, h, T, k) of the memory; TrainedSdm ids (B*T, h, k))."""
         _forward_only(self.emb.weight)
         x, _ = self.enfold(idx)
         reset = (idx == self.bos_id) if self.reset_at_bos else None
         for i in range(self.n_layers):
-            x = self._layer(i, x, reset, sequential)
+            x = self._layer(i, x, reset, sequential, trace)
         return x
 
-    def _layer(self, i, x, reset, sequential=False):
+    def _layer(self, i, x, reset, sequential=False, trace=None):
         """Layer i of residual(): the memory, then the body, each with its residual add."""
         m = self.mems[i]
+        rec = None if trace is None else {"x_in": x}
         if m.enabled:
             if sequential:
                 x = x + m.forward_sequential(x, reset)
+            elif rec is not None:
+                x, o = m._run(x, reset, add_residual=True, want=("sel",))
+                rec["siw"], rec["sir"] = o["siw"], o["sir"]
             else:
                 x = m._run(x, reset, add_residual=True)[0]
+        if rec is not None:
+            rec["x_mid"] = x
         if self.ffn == "mlp":
             x = self.mlps[i].block(x, self.mnorms[i].w, self.mnorms[i].eps)
         elif self.ffn == "sdm":
-            x = self.sdms[i]._run(x, add_residual=True)[0]
+            x, si, _ = self.sdms[i]._run(x, add_residual=True, want_sel=rec is not None)
+            if rec is not None:
+                rec["sdm_si"] = si
+        if rec is not None:
+            trace.append(rec)
         return x
 
     def hidden(self, idx, sequential=False):
         return self.nf(self.residual(idx, sequential))
 
     def project(self, h):
-        return h @ self.emb.weight.t()
+        """OneSdmLM.project (M:528-529): the tied head h @ E^T (no norm), in h's dtype, on the library's GEMM."""
+        _forward_only(h, self.emb.weight)
+        h = h.contiguous()
+        E = self.emb.weight.detach().to(h.dtype).contiguous()
+        out = torch.empty(*h.shape[:-1], self.V, dtype=h.dtype, device=h.device)
+        check(lib().sdm_tied_project(ptr(h), ptr(E), h.numel() // self.d, self.d, self.V, dtype_code(h.dtype), ptr(out),
+                                     stream_ptr(h.device)), "sdm_tied_project")
+        return out
 
     def unfold(self, x):
         return self.project(self.nf(x))
@@ -190,8 +209,45 @@ class OneSdmLM(nn.Module):
             main.wait_stream(s)
         return out
 
+    def loss_graph(self, B, T, row_streams=1, device=None):
+        """Capture loss_sum over a (B, T) batch as one CUDA graph; returns step(idx, targets) -> the (1,) float64
+        device loss sum (the graph's static output, overwritten by the next call).
+
+        The step launches about a dozen kernels per layer; replaying them as a graph removes the host's per-launch
+        work, which at a few rows per GPU is as long as the kernels themselves.  idx and targets (B, T) may be host
+        tensors (pinned memory copies asynchronously) or device tensors; they are copied into static buffers.  Warm-up
+        runs on a side stream before capture, so every weight cache and workspace exists when the graph is built."""
+        dev = device or self.emb.weight.device
+        ids_in = torch.zeros(B, T, dtype=torch.int32, device=dev)
+        tgt_in = torch.full((B, T), -1, dtype=torch.int32, device=dev)
+        out = torch.zeros(1, dtype=torch.float64, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.no_grad():
+            for _ in range(2):
+                self.loss_sum(ids_in, tgt_in, out=out, row_streams=row_streams)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph), torch.no_grad():
+            out.zero_()
+            self.loss_sum(ids_in, tgt_in, out=out, row_streams=row_streams)
+
+        def step(idx, targets):
+            ids_in.copy_(idx, non_blocking=True)
+            tgt_in.copy_(targets, non_blocking=True)
+            graph.replay()
+            return out
+        step.graph = graph
+        return step
+
     def memory_parameters(self):
         return {n for n, _ in self.named_parameters() if n.startswith("mems.")}
+
+    def set_leak(self, on):
+        """OneSdmLM.set_leak (M:560-564): the reference's test-only causality-leak switch of every memory.  The
+        kernels have no leaking variant, so a forward with the switch on raises NotImplementedError."""
+        for m in self.mems:
+            m._leak = on
 
     # ------------------------------------------------------------------------------------------ decode
     def init_decode(self, S, device=None):

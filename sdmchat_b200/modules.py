@@ -71,27 +71,54 @@ class RMSNorm(nn.Module):
 
 
 class SwiGLU(nn.Module):
-    """SwiGLU (L:89-97); `block(x, norm_w)` computes x + SwiGLU(RMSNorm(x)) in one call (M:544-545)."""
+    """SwiGLU (L:89-97): forward(x) = down(silu(gate x) * up x); `block(x, norm_w)` computes x + SwiGLU(RMSNorm(x))
+    in one call (M:544-545).  In bf16 the gate and up maps are one tensor-core GEMM against a packed weight (cached
+    until a weight changes) whose epilogue forms silu(g) * u, so only the product reaches memory."""
 
     def __init__(self, d, f):
         super().__init__()
         self.gate = nn.Linear(d, f, bias=False)
         self.up = nn.Linear(d, f, bias=False)
         self.down = nn.Linear(f, d, bias=False)
+        self._pcache = None
 
-    def block(self, x, norm_w, eps=1e-6, out=None):
+    def _packed(self, dt, device):
+        """(packed gate|up weight (2f, d), down weight) in dtype dt, rebuilt only when a weight changes."""
+        mats = (self.gate.weight, self.up.weight, self.down.weight)
+        key = (dt, device) + tuple((t.data_ptr(), t._version) for t in mats)
+        if self._pcache is not None and self._pcache[0] == key:
+            return self._pcache[1]
+        d, f = self.gate.in_features, self.gate.out_features
+        wg, wu = _cdt(self.gate.weight, dt), _cdt(self.up.weight, dt)
+        wgu = torch.empty(2 * f, d, dtype=dt, device=device)
+        check(lib().sdm_swiglu_pack(ptr(wg), ptr(wu), d, f, dtype_code(dt), ptr(wgu), stream_ptr(device)),
+              "sdm_swiglu_pack")
+        keep = (wgu, _cdt(self.down.weight, dt))
+        self._pcache = (key, keep)
+        return keep
+
+    def _run(self, x, norm_w, eps, add_residual, out=None):
         _forward_only(x, self.gate.weight)
         x = x.contiguous()
         d, f = self.gate.in_features, self.gate.out_features
         N = x.numel() // d
         dt = x.dtype
+        wgu, wd = self._packed(dt, x.device)
         out = torch.empty_like(x) if out is None else out
-        ws = workspace(lib().sdm_swiglu_workspace_size(N, d, f, dtype_code(dt)), x.device)
-        check(lib().sdm_swiglu_block(ptr(x), ptr(_cdt(norm_w, dt)), ptr(_cdt(self.gate.weight, dt)),
-                                     ptr(_cdt(self.up.weight, dt)), ptr(_cdt(self.down.weight, dt)), N, d, f, eps,
-                                     dtype_code(dt), ptr(out), ptr(ws), ws.numel(), stream_ptr(x.device)),
-              "sdm_swiglu_block")
+        nw = None if norm_w is None else _cdt(norm_w, dt)
+        ws = workspace(lib().sdm_swiglu_forward_workspace_size(N, d, f, dtype_code(dt)), x.device)
+        check(lib().sdm_swiglu_forward(ptr(x), ptr(nw), ptr(wgu), ptr(wd), N, d, f, eps, dtype_code(dt),
+                                       int(add_residual), ptr(out), ptr(ws), ws.numel(), stream_ptr(x.device)),
+              "sdm_swiglu_forward")
         return out
+
+    def forward(self, x):
+        """SwiGLU.forward (L:96-97), in x's dtype."""
+        return self._run(x, None, 0.0, False)
+
+    def block(self, x, norm_w, eps=1e-6, out=None):
+        """x + SwiGLU(RMSNorm(x)) with RMSNorm weight norm_w (OneSdmLM.residual, M:544-545)."""
+        return self._run(x, norm_w, eps, True, out)
 
 
 class RunTimeSdm(nn.Module):
@@ -215,6 +242,50 @@ class RunTimeSdm(nn.Module):
         _, o = self._run(x, want=("sel", "values"))
         V = o["V"].view(B, T, self.h, self.dh).transpose(1, 2)
         return o["siw"].long(), o["ww"], o["sir"].long(), o["wr"], V
+
+    def _chunk(self, siw, ww, sir, wr, Vc, mem, cnt, lam, seg=None, seg_prev=None):
+        """RunTimeSdm._chunk (M:215-241): one chunk of the write-then-read from the carried state (mem (B,h,M,dh),
+        cnt (B,h,M)).  siw, sir (B,h,L,k); ww, wr (B,h,L,k); Vc (B,h,L,dh); lam (h,); seg (B,L) / seg_prev (B,):
+        segment numbers (a change empties the memory before that position reads).  Returns num (B,h,L,dh),
+        den (B,h,L,1) and the state after the chunk, all float32."""
+        _forward_only(Vc, ww, wr, mem)
+        if self._leak:
+            raise NotImplementedError("the reference's causality-leak control (_leak) is a test-only switch of the "
+                                      "PyTorch module and is not built into the kernels")
+        B, h, L, k = siw.shape
+        dev = Vc.device
+        f32 = dict(dtype=torch.float32, device=dev)
+        i32 = lambda t: t.detach().to(device=dev, dtype=torch.int32).contiguous()  # noqa: E731
+        sel = [i32(siw), _f32(ww), i32(sir), _f32(wr)]
+        V = Vc.detach().float().transpose(1, 2).reshape(B * L, h * self.dh).contiguous()  # token-major rows
+        rs = None
+        if seg is not None:
+            prev = torch.cat([seg_prev.reshape(B, 1).to(seg.dtype), seg[:, :-1]], 1)
+            rs = (seg != prev).to(torch.uint8).contiguous()
+        mem_in, cnt_in = _f32(mem), _f32(cnt)
+        lam_d = _f32(lam).to(dev)
+        num = torch.empty(B, L, h, self.dh, **f32)
+        den = torch.empty(B, L, h, **f32)
+        mem_o = torch.empty(B, h, self.M, self.dh, **f32)
+        cnt_o = torch.empty(B, h, self.M, **f32)
+        ws = workspace(lib().sdm_rt_scan_workspace_size(B, L, h, k), dev)
+        check(lib().sdm_rt_scan(*(ptr(t) for t in sel), ptr(V), h * self.dh, ptr(lam_d), ptr(rs), B, L, h, self.n_sub,
+                                self.dh, k, ptr(mem_in), ptr(cnt_in), ptr(num), ptr(den), ptr(mem_o), ptr(cnt_o),
+                                ptr(ws), ws.numel(), stream_ptr(dev)), "sdm_rt_scan")
+        return num.transpose(1, 2), den.transpose(1, 2)[..., None], mem_o, cnt_o
+
+    def finish(self, num, den, B, T, dtype):
+        """RunTimeSdm.finish (M:243-247): num (B,h,T,dh), den (B,h,T,1) -> wo(out-normed read) (B,T,d) in dtype."""
+        _forward_only(num, den, self.wo.weight)
+        dev = num.device
+        p, _ = self._params(dtype)
+        n = num.detach().float().transpose(1, 2).contiguous()          # (B, T, h, dh)
+        dn = den.detach().float().reshape(B, self.h, T).transpose(1, 2).contiguous()  # (B, T, h)
+        out = torch.empty(B, T, self.d, dtype=dtype, device=dev)
+        ws = workspace(lib().sdm_rt_finish_workspace_size(p, B * T), dev)
+        check(lib().sdm_rt_finish(p, ptr(n), ptr(dn), B * T, None, ptr(out), ptr(ws), ws.numel(), stream_ptr(dev)),
+              "sdm_rt_finish")
+        return out
 
     def forward(self, x, reset=None):
         """RunTimeSdm.forward (M:249-274): every call starts from an empty memory; reset (B, T) bool empties it

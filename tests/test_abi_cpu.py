@@ -49,13 +49,16 @@ def test_host_side_argument_errors():
     assert lib.sdm_rmsnorm(fake, fake, 4, 16, 1e-6, 7, fake, None) == 1
     assert lib.sdm_gemm(fake, fake, 4, 0, 8, 1, fake, None) == 2
     # the scan: too many slots for the shared-memory state
-    assert lib.sdm_rt_scan(fake, fake, fake, fake, fake, 64, fake, None, 1, 8, 1, 128, 64, 16, fake, fake, None,
-                           None, fake, 1 << 20, None) == 2
+    assert lib.sdm_rt_scan(fake, fake, fake, fake, fake, 64, fake, None, 1, 8, 1, 128, 64, 16, None, None, fake, fake,
+                           None, None, fake, 1 << 20, None) == 2
+    # a carried state needs both mem and cnt
+    assert lib.sdm_rt_scan(fake, fake, fake, fake, fake, 64, fake, None, 1, 8, 1, 32, 64, 16, fake, None, fake, fake,
+                           None, None, fake, 1 << 20, None) == 1
     # the scan's chunk lists need their workspace
     need = lib.sdm_rt_scan_workspace_size(2, 2048, 12, 16)
     assert need == 2 * 12 * 32 * lib.sdm_rt_scan_workspace_size(1, 64, 1, 16)
-    assert lib.sdm_rt_scan(fake, fake, fake, fake, fake, 768, fake, None, 2, 2048, 12, 32, 64, 16, fake, fake, None,
-                           None, fake, need - 1, None) == 6
+    assert lib.sdm_rt_scan(fake, fake, fake, fake, fake, 768, fake, None, 2, 2048, 12, 32, 64, 16, None, None, fake,
+                           fake, None, None, fake, need - 1, None) == 6
 
 
 def rt_params(d=768, heads=12, n_sub=32, d_a=32, k=16, dtype=_lib.SDM_BF16):

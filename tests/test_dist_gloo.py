@@ -44,9 +44,14 @@ def _loss_worker(rank, world, port, q):
     lg = O.lm_forward(P, idx[lo:hi], bf16_stream=True, chunk=16, margins=False)
     part = O.ce_sum(lg[:, :-1], idx[lo:hi, 1:])
     tot, cnt = D.reduce_loss(part, (hi - lo) * (idx.shape[1] - 1))
-    q.put((rank, tot, cnt))
-    import torch.distributed as dist
-    dist.destroy_process_group()
+    # bench.py's per-step exchange: the in-place all-reduce of (loss sum, token count), then the slowest rank's time
+    import torch
+    buf = torch.tensor([part, float((hi - lo) * (idx.shape[1] - 1))], dtype=torch.float64)
+    D.all_reduce_(buf)
+    slowest = D.max_over_ranks(1.0 + rank)
+    D.barrier()
+    q.put((rank, tot, cnt, float(buf[0]), float(buf[1]), slowest, D.world_size()))
+    D.finalize()
 
 
 def test_sharded_loss_sum_equals_unsharded():
@@ -65,9 +70,10 @@ def test_sharded_loss_sum_equals_unsharded():
     for p in procs:
         p.join(timeout=60)
     assert all(p.exitcode == 0 for p in procs)
-    for _, tot, cnt in res:
-        assert cnt == g["idx"].shape[0] * (g["idx"].shape[1] - 1)
-        assert abs(tot - want) / abs(want) < 1e-6
+    for _, tot, cnt, tot2, cnt2, slowest, world in res:
+        assert cnt == cnt2 == g["idx"].shape[0] * (g["idx"].shape[1] - 1)
+        assert abs(tot - want) / abs(want) < 1e-6 and abs(tot2 - want) / abs(want) < 1e-6
+        assert slowest == 2.0 and world == 2
 
 
 def _early_exit_worker(rank, world, port, q):

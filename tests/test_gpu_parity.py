@@ -295,7 +295,8 @@ def test_scan_abi_against_token_recurrence(cuda_ok, dup):
         args = [t(siw), t(ww), t(sir), t(wr), Vt]  # kept alive until the call has run
         lam_d, reset_d = t(lam), t(reset.astype(np.uint8))
         st = lib.sdm_rt_scan(*map(_lib.ptr, args), h * dh, _lib.ptr(lam_d), _lib.ptr(reset_d),
-                             B, T, h, n_sub, dh, k, _lib.ptr(num), _lib.ptr(den), _lib.ptr(mem), _lib.ptr(cnt),
+                             B, T, h, n_sub, dh, k, None, None, _lib.ptr(num), _lib.ptr(den), _lib.ptr(mem),
+                             _lib.ptr(cnt),
                              _lib.ptr(ws), ws.numel(), _lib.stream_ptr(torch.device(DEV)))
         _lib.check(st, "sdm_rt_scan")
         torch.cuda.synchronize()

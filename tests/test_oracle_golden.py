@@ -133,3 +133,22 @@ def test_bf16_rounding_matches_torch():
     x = (rng.standard_normal(10000) * 10.0 ** rng.integers(-8, 8, 10000)).astype(np.float32)
     want = torch.from_numpy(x).bfloat16().float().numpy()
     np.testing.assert_array_equal(O.bf16(x), want)
+
+
+def test_teacher_forcing_with_own_selection_is_identity():
+    """Forcing the oracle's own slot ids (as the full-depth GPU parity test forces the GPU's) changes nothing."""
+    g = load("rt_config1")
+    p = rt_params(g)
+    x = g["x"]
+    out, prep = O.rt_forward(p, x)
+    out2, prep2 = O.rt_forward(p, x, force={"siw": prep["siw"], "sir": prep["sir"]})
+    np.testing.assert_array_equal(prep2["siw"], prep["siw"])
+    np.testing.assert_array_equal(prep2["ww"], prep["ww"])
+    np.testing.assert_array_equal(out2, out)
+    gt = load("ts_selftest")
+    sd = params(gt)
+    pt = O.TrainedSdmParams(sd, int(gt["heads"]), int(gt["n_sub"]), int(gt["d_a"]), int(gt["k"]))
+    o1, si, _ = O.trained_sdm(pt, gt["x"])
+    o2, si2, _ = O.trained_sdm(pt, gt["x"], force_si=si)
+    np.testing.assert_array_equal(si2, si)
+    np.testing.assert_array_equal(o2, o1)
