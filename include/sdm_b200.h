@@ -115,12 +115,13 @@ size_t sdm_rt_forward_workspace_size(const sdm_rt_params* p, int B, int T);
  * position reads (M:229-233).  add_residual: out = x + forward(x) rounded as the reference's residual add
  * (OneSdmLM.residual, M:540).  mem_out (B, h, M, dh) / cnt_out (B, h, M): the final state (last_state), or NULL.
  * Optional outputs (NULL to skip): siw, sir (B, h, T, k) int32, ww, wr (B, h, T, k) float32, gate (B, T, h),
- * values (B, T, d) float32 (the write values V of prepare, token-major), num (B, T, h, dh) and den (B, T, h)
- * float32 (the read before finish). */
+ * values (B, T, d) float32 (the write values V of prepare, token-major), z (B, T, 2, h, d_a) float32 (the
+ * write keys kz and read queries qz of prepare, M:199-200, addr_b added: the addresses pk_address scores),
+ * num (B, T, h, dh) and den (B, T, h) float32 (the read before finish). */
 sdm_status sdm_rt_forward(const sdm_rt_params* p, const void* x, int B, int T, const uint8_t* reset,
                           int add_residual, void* out, float* mem_out, float* cnt_out,
-                          int32_t* siw, float* ww, int32_t* sir, float* wr, float* gate, float* values, float* num,
-                          float* den, void* workspace, size_t workspace_bytes, void* stream);
+                          int32_t* siw, float* ww, int32_t* sir, float* wr, float* gate, float* values, float* z,
+                          float* num, float* den, void* workspace, size_t workspace_bytes, void* stream);
 
 /* The chunk loop (RunTimeSdm._chunk over all chunks of a window, M:215-241, 255-272; one call with T = L is one
  * _chunk) from prepared selections: siw, sir (B, h, T, k) int32; ww, wr (B, h, T, k) float32; V (B*T rows, row
@@ -185,10 +186,10 @@ typedef struct {
 } sdm_ts_params;
 
 size_t sdm_ts_forward_workspace_size(const sdm_ts_params* p, int64_t N);
-/* x, out (N, d); si (N, h, k) int32 and w (N, h, k) float32 (TrainedSdm.address, M:438-446) optional.
- * add_residual as for sdm_rt_forward (M:547). */
+/* x, out (N, d); si (N, h, k) int32 and w (N, h, k) float32 (TrainedSdm.address, M:438-446) and the queries
+ * q (N, h, d_a) float32 (M:439) optional.  add_residual as for sdm_rt_forward (M:547). */
 sdm_status sdm_ts_forward(const sdm_ts_params* p, const void* x, int64_t N, int add_residual, void* out,
-                          int32_t* si, float* w, void* workspace, size_t workspace_bytes, void* stream);
+                          int32_t* si, float* w, float* q, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------------------ SwiGLU
  * SwiGLU.forward (L:96-97): down(silu(gate x) * up x); w_gate, w_up (f, d), w_down (d, f); f a multiple of 16.

@@ -13,7 +13,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libsdm_b200.so")
 
 SDM_F32, SDM_BF16 = 0, 1
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 c_int, c_int64, c_float, c_size_t, c_void_p, c_double = (ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t,
                                                           ctypes.c_void_p, ctypes.c_double)
@@ -52,7 +52,7 @@ _SIGS = {
     "sdm_pk_address": (c_int, [P, P, P, c_int64, c_int, c_int, c_int, c_int, P, P, P]),
     "sdm_rmsnorm": (c_int, [P, P, c_int64, c_int, c_float, c_int, P, P]),
     "sdm_rt_forward_workspace_size": (c_size_t, [ctypes.POINTER(RtParams), c_int, c_int]),
-    "sdm_rt_forward": (c_int, [ctypes.POINTER(RtParams), P, c_int, c_int, P, c_int, P, P, P, P, P, P, P, P, P, P, P,
+    "sdm_rt_forward": (c_int, [ctypes.POINTER(RtParams), P, c_int, c_int, P, c_int, P, P, P, P, P, P, P, P, P, P, P, P,
                                P, c_size_t, P]),
     "sdm_rt_scan_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
     "sdm_rt_scan": (c_int, [P, P, P, P, P, c_int64, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P,
@@ -64,7 +64,7 @@ _SIGS = {
     "sdm_rt_decode_noalloc_scratch_bytes": (c_size_t, []),
     "sdm_rt_decode_step_noalloc": (c_int, [ctypes.POINTER(RtParams), P, c_int, P, c_int, P, P, P, P, P, P]),
     "sdm_ts_forward_workspace_size": (c_size_t, [ctypes.POINTER(TsParams), c_int64]),
-    "sdm_ts_forward": (c_int, [ctypes.POINTER(TsParams), P, c_int64, c_int, P, P, P, P, c_size_t, P]),
+    "sdm_ts_forward": (c_int, [ctypes.POINTER(TsParams), P, c_int64, c_int, P, P, P, P, P, c_size_t, P]),
     "sdm_swiglu_pack": (c_int, [P, P, c_int, c_int, c_int, P, P]),
     "sdm_swiglu_forward_workspace_size": (c_size_t, [c_int64, c_int, c_int, c_int]),
     "sdm_swiglu_forward": (c_int, [P, P, P, P, c_int64, c_int, c_int, c_float, c_int, c_int, P, P, c_size_t, P]),

@@ -127,7 +127,7 @@ cudaError_t rt_prepare(const sdm_rt_params* p, const T* x, int64_t N, int T_bh, 
 template <typename T>
 sdm_status rt_forward_t(const sdm_rt_params* p, const void* xv, int B, int T_, const uint8_t* reset, int add_res,
                         void* outv, float* mem_out, float* cnt_out, int32_t* siw_o, float* ww_o, int32_t* sir_o,
-                        float* wr_o, float* gate_o, float* v_o, float* num_o, float* den_o, void* ws,
+                        float* wr_o, float* gate_o, float* v_o, float* z_o, float* num_o, float* den_o, void* ws,
                         size_t ws_bytes, cudaStream_t st) {
   const int64_t N = (int64_t)B * T_;
   const int h = p->heads, d = p->d, dh = d / h, kk = sel_k(p->k, p->n_sub);
@@ -154,6 +154,9 @@ sdm_status rt_forward_t(const sdm_rt_params* p, const void* xv, int B, int T_, c
   if (v_o)
     SDM_TRY(cudaMemcpy2DAsync(v_o, d * sizeof(float), w.proj + 2LL * h * p->d_a, C * sizeof(float), d * sizeof(float),
                               N, cudaMemcpyDeviceToDevice, st));
+  if (z_o)
+    SDM_TRY(cudaMemcpy2DAsync(z_o, 2 * h * p->d_a * sizeof(float), w.proj, C * sizeof(float),
+                              2 * h * p->d_a * sizeof(float), N, cudaMemcpyDeviceToDevice, st));
   ScanArgs sa{};
   sa.siw = siw;
   sa.ww = ww;
@@ -212,7 +215,7 @@ size_t ts_ws(const sdm_ts_params* p, int64_t N, bool own_si, void* base, void** 
 
 template <typename T>
 sdm_status ts_forward_t(const sdm_ts_params* p, const void* xv, int64_t N, int add_res, void* outv, int32_t* si_o,
-                        float* w_o, void* ws, size_t ws_bytes, cudaStream_t st) {
+                        float* w_o, float* q_o, void* ws, size_t ws_bytes, cudaStream_t st) {
   void *hs, *rb;
   float *q, *w;
   int32_t* si;
@@ -230,6 +233,8 @@ sdm_status ts_forward_t(const sdm_ts_params* p, const void* xv, int64_t N, int a
     EpiF32 eq{q, (int64_t)h * p->d_a};
     SDM_TRY(launch_gemm<T, EpiF32>(static_cast<T*>(hs), d, static_cast<const T*>(p->wq), d, N, d, h * p->d_a, eq, st));
   }
+  if (q_o)
+    SDM_TRY(cudaMemcpyAsync(q_o, q, (size_t)N * h * p->d_a * sizeof(float), cudaMemcpyDeviceToDevice, st));
   OpTag tag_("ts");
   constexpr int split = sizeof(T) == 2;
   if (sizeof(T) == 2 && ts_addr_gather_ok(N, h, p->d_a, p->n_sub, p->k, dh) &&
@@ -399,7 +404,7 @@ sdm_status head_t(int mode, const void* xv, const void* nf_w, const void* emb, c
 
 extern "C" {
 
-int sdm_abi_version(void) { return 2; }
+int sdm_abi_version(void) { return 3; }
 
 sdm_status sdm_device_status(void* stream) {
   int gemm = 0, scan = 0;
@@ -475,7 +480,7 @@ size_t sdm_rt_forward_workspace_size(const sdm_rt_params* p, int B, int T) {
 
 sdm_status sdm_rt_forward(const sdm_rt_params* p, const void* x, int B, int T, const uint8_t* reset,
                           int add_residual, void* out, float* mem_out, float* cnt_out, int32_t* siw, float* ww,
-                          int32_t* sir, float* wr, float* gate, float* values, float* num, float* den,
+                          int32_t* sir, float* wr, float* gate, float* values, float* z, float* num, float* den,
                           void* workspace, size_t workspace_bytes, void* stream) {
   sdm_status s = check_rt(p);
   if (s != SDM_OK) return s;
@@ -483,9 +488,9 @@ sdm_status sdm_rt_forward(const sdm_rt_params* p, const void* x, int B, int T, c
   if (B < 0 || T < 0) return SDM_ERR_SHAPE;
   if (p->dtype == SDM_BF16)
     return rt_forward_t<bf16_t>(p, x, B, T, reset, add_residual, out, mem_out, cnt_out, siw, ww, sir, wr, gate,
-                                values, num, den, workspace, workspace_bytes, S(stream));
+                                values, z, num, den, workspace, workspace_bytes, S(stream));
   return rt_forward_t<float>(p, x, B, T, reset, add_residual, out, mem_out, cnt_out, siw, ww, sir, wr, gate, values,
-                             num, den, workspace, workspace_bytes, S(stream));
+                             z, num, den, workspace, workspace_bytes, S(stream));
 }
 
 size_t sdm_rt_scan_workspace_size(int B, int T, int heads, int k) {
@@ -655,14 +660,14 @@ size_t sdm_ts_forward_workspace_size(const sdm_ts_params* p, int64_t N) {
 }
 
 sdm_status sdm_ts_forward(const sdm_ts_params* p, const void* x, int64_t N, int add_residual, void* out, int32_t* si,
-                          float* w, void* workspace, size_t workspace_bytes, void* stream) {
+                          float* w, float* q, void* workspace, size_t workspace_bytes, void* stream) {
   sdm_status s = check_ts(p);
   if (s != SDM_OK) return s;
   if (!x || !out) return SDM_ERR_ARG;
   if (N < 0) return SDM_ERR_SHAPE;
   if (p->dtype == SDM_BF16)
-    return ts_forward_t<bf16_t>(p, x, N, add_residual, out, si, w, workspace, workspace_bytes, S(stream));
-  return ts_forward_t<float>(p, x, N, add_residual, out, si, w, workspace, workspace_bytes, S(stream));
+    return ts_forward_t<bf16_t>(p, x, N, add_residual, out, si, w, q, workspace, workspace_bytes, S(stream));
+  return ts_forward_t<float>(p, x, N, add_residual, out, si, w, q, workspace, workspace_bytes, S(stream));
 }
 
 sdm_status sdm_swiglu_pack(const void* w_gate, const void* w_up, int d, int f, int dtype, void* w_gu, void* stream) {

@@ -93,8 +93,9 @@ class OneSdmLM(nn.Module):
 
     def residual(self, idx, sequential=False, trace=None):
         """OneSdmLM.residual (M:534-548) with each residual add fused into the module's last GEMM.  trace: a list
-        that receives, per layer, the layer input, the stream after the memory, and the slot selections (write and
-        read ids (B, h, T, k) of the memory; TrainedSdm ids (B*T, h, k))."""
+        that receives, per layer, the layer input, the stream after the memory, the memory's addresses z
+        (B, T, 2, h, d_a) and slot ids (write and read, (B, h, T, k)), and the TrainedSdm queries (B*T, h, d_a) and
+        slot ids (B*T, h, k)."""
         _forward_only(self.emb.weight)
         x, _ = self.enfold(idx)
         reset = (idx == self.bos_id) if self.reset_at_bos else None
@@ -110,8 +111,8 @@ class OneSdmLM(nn.Module):
             if sequential:
                 x = x + m.forward_sequential(x, reset)
             elif rec is not None:
-                x, o = m._run(x, reset, add_residual=True, want=("sel",))
-                rec["siw"], rec["sir"] = o["siw"], o["sir"]
+                x, o = m._run(x, reset, add_residual=True, want=("sel", "z"))
+                rec["siw"], rec["sir"], rec["z"] = o["siw"], o["sir"], o["z"]
             else:
                 x = m._run(x, reset, add_residual=True)[0]
         if rec is not None:
@@ -119,9 +120,10 @@ class OneSdmLM(nn.Module):
         if self.ffn == "mlp":
             x = self.mlps[i].block(x, self.mnorms[i].w, self.mnorms[i].eps)
         elif self.ffn == "sdm":
-            x, si, _ = self.sdms[i]._run(x, add_residual=True, want_sel=rec is not None)
             if rec is not None:
-                rec["sdm_si"] = si
+                x, rec["sdm_si"], _, rec["sdm_q"] = self.sdms[i]._run(x, add_residual=True, want_sel=True, want_q=True)
+            else:
+                x = self.sdms[i]._run(x, add_residual=True)[0]
         if rec is not None:
             trace.append(rec)
         return x

@@ -221,6 +221,8 @@ class RunTimeSdm(nn.Module):
             o["wr"] = torch.empty(B, h, T, kk, **f32)
         if "values" in want:
             o["V"] = torch.empty(B, T, self.d, **f32)
+        if "z" in want:
+            o["z"] = torch.empty(B, T, 2, h, self.d_a, **f32)
         if "read" in want:
             o["num"] = torch.empty(B, T, h, self.dh, **f32)
             o["den"] = torch.empty(B, T, h, **f32)
@@ -230,8 +232,8 @@ class RunTimeSdm(nn.Module):
         ws = workspace(lib().sdm_rt_forward_workspace_size(p, B, T), dev)
         check(lib().sdm_rt_forward(p, ptr(x), B, T, ptr(rs), int(add_residual), ptr(out), ptr(mem), ptr(cnt),
                                    ptr(o.get("siw")), ptr(o.get("ww")), ptr(o.get("sir")), ptr(o.get("wr")),
-                                   ptr(gate), ptr(o.get("V")), ptr(o.get("num")), ptr(o.get("den")), ptr(ws),
-                                   ws.numel(), stream_ptr(dev)), "sdm_rt_forward")
+                                   ptr(gate), ptr(o.get("V")), ptr(o.get("z")), ptr(o.get("num")), ptr(o.get("den")),
+                                   ptr(ws), ws.numel(), stream_ptr(dev)), "sdm_rt_forward")
         self.last_state = (mem, cnt)
         self.last_gate = gate
         return out, o
@@ -369,7 +371,8 @@ class TrainedSdm(nn.Module):
         self._pcache = (key, (p, keep))
         return p, keep
 
-    def _run(self, x, add_residual=False, want_sel=False, out=None):
+    def _run(self, x, add_residual=False, want_sel=False, out=None, want_q=False):
+        """One sdm_ts_forward call: (out, slot ids, weights[, queries (N, h, d_a) when want_q])."""
         _forward_only(x, self.wq.weight)
         x = x.contiguous()
         N = x.numel() // self.d
@@ -377,14 +380,16 @@ class TrainedSdm(nn.Module):
         c1 = min(self.k, self.n_sub)
         kk = min(self.k, c1 * c1)
         out = torch.empty_like(x) if out is None else out
-        si = w = None
+        si = w = q = None
         if want_sel:
             si = torch.empty(N, self.h, kk, dtype=torch.int32, device=x.device)
             w = torch.empty(N, self.h, kk, dtype=torch.float32, device=x.device)
+        if want_q:
+            q = torch.empty(N, self.h, self.d_a, dtype=torch.float32, device=x.device)
         ws = workspace(lib().sdm_ts_forward_workspace_size(p, N), x.device)
-        check(lib().sdm_ts_forward(p, ptr(x), N, int(add_residual), ptr(out), ptr(si), ptr(w), ptr(ws), ws.numel(),
-                                   stream_ptr(x.device)), "sdm_ts_forward")
-        return out, si, w
+        check(lib().sdm_ts_forward(p, ptr(x), N, int(add_residual), ptr(out), ptr(si), ptr(w), ptr(q), ptr(ws),
+                                   ws.numel(), stream_ptr(x.device)), "sdm_ts_forward")
+        return (out, si, w, q) if want_q else (out, si, w)
 
     def address(self, x):
         """TrainedSdm.address (M:438-446): soft weights (N, h, k) and slot ids (N, h, k)."""

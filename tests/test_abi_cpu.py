@@ -77,12 +77,12 @@ def test_workspace_queries_and_too_small_workspace():
     assert need >= N * 768 * 2 + N * 1548 * 4 + 4 * N * 12 * 16 * 4 + N * 768 * 4 + N * 768 * 2
     fake = ctypes.c_void_p(0x10000)
     st = lib.sdm_rt_forward(p, fake, 2, 256, None, 0, fake, None, None, None, None, None, None, None, None, None,
-                            None, fake, need - 1, None)
+                            None, None, fake, need - 1, None)
     assert st == 6
     bad = rt_params(heads=7)
     assert lib.sdm_rt_forward_workspace_size(bad, 2, 256) == 0
     assert lib.sdm_rt_forward(bad, fake, 2, 256, None, 0, fake, None, None, None, None, None, None, None, None, None,
-                              None, fake, 1 << 30, None) == 2
+                              None, None, fake, 1 << 30, None) == 2
     assert lib.sdm_rt_decode_workspace_size(p, 32) > 0
     assert lib.sdm_tied_head_workspace_size(65536, 768, 32768, 1) > 4096 * 32768 * 4
 

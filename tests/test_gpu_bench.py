@@ -15,9 +15,10 @@ ROWS, SEQ, LAYERS = 2, 512, 2
 
 @pytest.mark.gpu
 def test_bench_json_line_and_loss(cuda_ok):
-    p = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--rows", str(ROWS), "--seq", str(SEQ),
+    p = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--global-rows", str(ROWS), "--seq", str(SEQ),
                         "--layers", str(LAYERS), "--steps", "3", "--warmup", "3", "--decode-streams", "4",
-                        "--decode-steps", "4"], cwd=ROOT, capture_output=True, text=True, timeout=900)
+                        "--decode-steps", "4", "--decode-prompt", "64", "--no-scaled"], cwd=ROOT, capture_output=True,
+                       text=True, timeout=900)
     assert p.returncode == 0, p.stderr[-3000:]
     d = json.loads(p.stdout.strip().splitlines()[-1])
 
@@ -47,6 +48,14 @@ def test_bench_json_line_and_loss(cuda_ok):
     clk = d["clocks"]
     assert "sm_mhz" in clk and "sm_max_mhz" in clk and isinstance(clk["reasons"], list)
     assert d["decode"]["value"] > 0 and d["decode"]["cuda_graph"] is True
+    assert d["decode"]["roofline"]["achieved"] > 0 and d["decode"]["steps"] == 4
+    assert d["scaling"] == "strong" and d["config"]["global_batch"] == ROWS
+    for tag, site in d["roofline_by_call_site"].items():  # every GEMM call site has its own FLOP figure
+        assert site["achieved"] > 0, tag
+    assert {"rt_proj", "rt_out", "ts_q", "ts_wo", "head_ce"} <= set(d["roofline_by_call_site"])
+    part = d["partial"]
+    assert part["value"] > 0 and part["roofline_gemm"]["achieved"] > 0
+    assert {"swiglu_gu", "swiglu_down", "head_logits"} <= set(part["roofline_by_call_site"])
 
     # the timed steps' loss against the oracle on the bench's own ids (rank 0 seed) and weights
     sys.path.insert(0, ROOT)
