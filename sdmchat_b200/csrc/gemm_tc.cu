@@ -253,6 +253,240 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------------ CTA pairs
+// The same GEMM on pairs of CTAs (a cluster of two, tcgen05 cta_group::2): the pair owns a 256 x 256 tile, each CTA
+// stages its 128 rows of A and its 128 rows of B (one half of the tile's columns) per K step, and one thread of the
+// even CTA issues 256 x N x 16 MMAs that read both CTAs' shared memory and leave each CTA's 128 rows of the
+// accumulator in its own TMEM.  Per CTA and K step 32 KB of operands feed 128 x 256 outputs (48 KB in the
+// single-CTA tile), so the L2 -> SM operand traffic per flop falls by a third.  Loads are plain TMA tile loads
+// (no multicast); each CTA's copies complete on the even CTA's `full` barrier, whose expected bytes cover both
+// halves.  The MMA commits arrive on the `empty` / `acc_full` barriers of both CTAs; every epilogue warp of both
+// CTAs arrives on the even CTA's `acc_empty`.  All waits are the bounded mbarrier waits; the two cluster barriers
+// (after set-up, before TMEM release) are reached on every path.
+constexpr int PAIR_N = 256;
+template <int DEEP>
+struct Cfg2 {
+  static constexpr int STAGES = 5 + DEEP;
+  static constexpr uint32_t B_BYTES = (PAIR_N / 2) * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr size_t RING_BYTES = (size_t)STAGES * STAGE_BYTES;
+  static constexpr size_t SMEM_BYTES = RING_BYTES + (size_t)EPI_WARPS * 32 * STG_LD * 4 + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * PAIR_N;
+  static constexpr int NCH = PAIR_N / 64;
+  // kind::f16: D float32, A and B bfloat16, both K-major, M = 256 (the pair), N = 256
+  static constexpr uint32_t IDESC =
+      (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(PAIR_N >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 2-D tile load into this CTA's shared memory, completing on an mbarrier of either CTA of the pair (no multicast).
+__device__ __forceinline__ void load_2d_pair(const CUtensorMap* map, uint32_t mbar_cluster, void* dst, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+// Arrives once on `bar` (the same offset) in both CTAs of the pair when the issued MMAs have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+template <typename Epi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t rows,
+                    int K, int n, Epi epi, int kwrap) {
+  pdl_enter();
+  using C = Cfg2<RingStages<Epi>::deep>;
+  extern __shared__ __align__(1024) unsigned char dsmem[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ uint32_t tmem_slot;
+
+  unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
+  float* stage_all = reinterpret_cast<float*>(ring + C::RING_BYTES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int kt_count = (K + BK - 1) / BK;
+  const int tiles_n = (n + PAIR_N - 1) / PAIR_N;
+  const int64_t tiles = (int64_t)tiles_n * ((rows + 2 * BM - 1) / (2 * BM));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);   // the even CTA's producer (expect_tx of both halves)
+      mbar_init(&empty_bar[s], 1);  // the pair's MMA commit
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 2 * EPI_WARPS);  // every epilogue warp of both CTAs
+    }
+    mbar_init_fence();
+    prefetch_map(&tmA);
+    prefetch_map(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                 "r"(C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated before any copy or MMA
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t t = pair; t < tiles && ok; t += npairs) {
+        const int tn = (int)(t % tiles_n);
+        const int m0 = (int)(t / tiles_n) * 2 * BM + (int)rank * BM;
+        const int nrem = n - tn * PAIR_N;
+        const int nt = nrem >= PAIR_N ? PAIR_N : ((nrem + 31) & ~31);
+        const int nb = tn * PAIR_N + (int)rank * (nt >> 1);
+        for (int kt = 0; kt < kt_count; ++kt, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1u;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u)) {
+            ok = false;
+            break;
+          }
+          unsigned char* a_dst = ring + s * C::STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * C::STAGE_BYTES);
+          const uint32_t fb = peer_addr(&full_bar[s], 0);
+          load_2d_pair(&tmA, fb, a_dst, kt * BK, m0);
+          load_2d_pair(&tmB, fb, a_dst + A_BYTES, (kt * BK) % kwrap, nb);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      uint32_t it = 0, tl = 0;
+      bool ok = true;
+      for (int64_t t = pair; t < tiles && ok; t += npairs, ++tl) {
+        const uint32_t buf = tl & 1u, use = tl >> 1;
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t dt = tmem + buf * PAIR_N;
+        const int nrem = n - (int)(t % tiles_n) * PAIR_N;
+        const int nt = nrem >= PAIR_N ? PAIR_N : ((nrem + 31) & ~31);
+        const uint32_t idesc = (C::IDESC & ~(0x3Fu << 17)) | ((uint32_t)(nt >> 3) << 17);
+        for (int kt = 0; kt < kt_count; ++kt, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1u;
+          if (!mbar_wait(&full_bar[s], ph)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_base = smem_u32(ring + s * C::STAGE_BYTES);
+          const uint32_t b_base = a_base + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16_pair(dt, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), idesc, (kt | kk) != 0);
+          umma_commit_pair(&empty_bar[s]);
+        }
+        if (ok) umma_commit_pair(&acc_full[buf]);
+      }
+    }
+  } else {
+    const int ew = warp - 2, q = warp & 3, half = ew >> 2;
+    float* stg = stage_all + ew * 32 * STG_LD;
+    const int rsub = lane >> 3, c4 = lane & 7;
+    const uint32_t release = peer_addr(&acc_empty[0], 0);  // acc_empty[buf] of the even CTA: + 8 * buf
+    uint32_t tl = 0;
+    for (int64_t t = pair; t < tiles; t += npairs, ++tl) {
+      const uint32_t buf = tl & 1u, use = tl >> 1;
+      const int tn = (int)(t % tiles_n);
+      const int64_t m0 = (t / tiles_n) * 2 * BM + (int64_t)rank * BM;
+      const int64_t row0 = m0 + q * 32;
+      const int cb = tn * PAIR_N + half * (PAIR_N / 2);
+      const uint32_t taddr = tmem + buf * PAIR_N + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * (PAIR_N / 2));
+      if constexpr (Epi::kRowMode) {
+        if (!mbar_wait(&acc_full[buf], use & 1u)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        typename Epi::RowState rs;
+        epi.row_begin(rs, row0 + lane, rows, cb);
+#pragma unroll 1
+        for (int ch = 0; ch < C::NCH; ++ch) {
+          uint32_t r[32];
+          tmem_ld32(taddr + (uint32_t)(ch * 32), r);
+          epi.row_chunk(rs, cb + ch * 32, n, r);
+        }
+        if (cb < n) epi.row_end(rs, row0 + lane, rows, cb / (PAIR_N / 2), (n + PAIR_N / 2 - 1) / (PAIR_N / 2));
+      } else {
+        typename Epi::Pre pre[C::NCH];
+        const int64_t rl0 = row0 + rsub;
+#pragma unroll
+        for (int ch = 0; ch < C::NCH; ++ch) epi.prefetch(pre[ch], rl0, rows, cb + ch * 32 + 4 * c4, n);
+        if (!mbar_wait(&acc_full[buf], use & 1u)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+        for (int ch = 0; ch < C::NCH; ++ch) {
+          uint32_t r[32];
+          tmem_ld32(taddr + (uint32_t)(ch * 32), r);
+          float4* srow = reinterpret_cast<float4*>(stg + lane * STG_LD);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            srow[j ^ (lane & 7)] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          __syncwarp();
+          const int col = cb + ch * 32 + 4 * c4;
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = 4 * it + rsub;
+            const float4 v = *reinterpret_cast<const float4*>(stg + rr * STG_LD + 4 * (c4 ^ (rr & 7)));
+            if (row0 + rr < rows && col < n) epi.store4(pre[ch], it, row0 + rr, col, v, n);
+          }
+          __syncwarp();
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(release + 8u * buf);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // no MMA of the pair still reads this CTA's shared memory or writes its TMEM
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
+  }
+}
+
 // 2-D bf16 tensor map over a row-major (outer, inner) matrix with row stride ld elements; box (64, box_outer),
 // 128-byte swizzle (the UMMA K-major operand layout).
 static bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_outer) {
@@ -327,19 +561,57 @@ static cudaError_t launch_tc_bn(const bf16_t* x, int64_t ldx, const bf16_t* w, i
   return launch_k(kern, dim3(grid), dim3(tc::THREADS), C::SMEM_BYTES, st, ma, mb, rows, K, n, epi, kwrap);
 }
 
+// CTA-pair launch: clusters of two, as many pairs as fit at once (the persistent loop covers the rest).
+template <typename Epi>
+static cudaError_t launch_tc_pair(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K,
+                                  int n, Epi epi, cudaStream_t st, int kwrap) {
+  using C = tc::Cfg2<tc::RingStages<Epi>::deep>;
+  CUtensorMap ma, mb;
+  if (!tc::make_map(&ma, x, (uint64_t)K, (uint64_t)rows, (uint64_t)ldx, tc::BM) ||
+      !tc::make_map(&mb, w, (uint64_t)kwrap, (uint64_t)n, (uint64_t)ldw, tc::PAIR_N / 2))
+    return cudaErrorInvalidValue;
+  auto kern = tc::gemm_tc2_kernel<Epi>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int pairs_cap = tc::num_sms() / 2;
+  if (dev >= 0 && dev < 64) {
+    if (!max_pairs[dev]) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * pairs_cap);
+      cfg.blockDim = dim3(tc::THREADS);
+      cfg.dynamicSmemBytes = C::SMEM_BYTES;
+      int nc = 0;
+      max_pairs[dev] = (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) == cudaSuccess && nc > 0) ? nc : pairs_cap;
+      cudaGetLastError();
+    }
+    pairs_cap = max_pairs[dev] < pairs_cap ? max_pairs[dev] : pairs_cap;
+  }
+  const int64_t tiles = ceil_div(n, tc::PAIR_N) * ceil_div(rows, 2 * tc::BM);
+  const int pairs = (int)(tiles < pairs_cap ? tiles : pairs_cap);
+  LaunchScope scope_("gemm_tc", st);
+  return launch_k(kern, dim3(2 * pairs), dim3(tc::THREADS), C::SMEM_BYTES, st, ma, mb, rows, K, n, epi, kwrap);
+}
+
 // Column tile: 256 wide moves a third fewer operand bytes per flop; 128 wide when it finishes in fewer rounds of
-// persistent tiles (small problems).  Row-owned epilogues always take 256 (two 128-column partials per tile).
+// persistent tiles (small problems).  Row-owned epilogues always take 256 (two 128-column partials per tile).  A
+// 256-wide tile over at least 256 rows runs on CTA pairs (256 x 256 per pair).
 template <typename Epi>
 cudaError_t launch_gemm_tc(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K, int n,
                            Epi epi, cudaStream_t st, int kwrap) {
   if (rows == 0 || n == 0) return cudaSuccess;
   if constexpr (Epi::kRowMode) {
+    if (rows >= 2 * tc::BM) return launch_tc_pair<Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
     return launch_tc_bn<Epi, 256>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
   } else {
     const int64_t sms = tc::num_sms(), mt = ceil_div(rows, tc::BM);
     const int64_t rounds256 = ceil_div(mt * ceil_div(n, 256), sms), rounds128 = ceil_div(mt * ceil_div(n, 128), sms);
-    if (rounds256 * 256 * 3 <= rounds128 * 128 * 4)  // a 256-wide round costs about 1.5x a 128-wide one
+    if (rounds256 * 256 * 3 <= rounds128 * 128 * 4) {  // a 256-wide round costs about 1.5x a 128-wide one
+      if (rows >= 2 * tc::BM) return launch_tc_pair<Epi>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
       return launch_tc_bn<Epi, 256>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
+    }
     return launch_tc_bn<Epi, 128>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
   }
 }

@@ -248,9 +248,11 @@ def test_bf16_lm_decode_equals_prefix_forward(cuda_ok):
 
 def test_gemm_bf16_against_fp32_reference(cuda_ok):
     torch.manual_seed(0)
-    # (7 | 1 | 32 rows: the decode-sized tensor-core kernel; 5 x 72: the CUDA-core skinny kernel; rest: tcgen05)
+    # (7 | 1 | 32 rows: the decode-sized tensor-core kernel; 5 x 72: the CUDA-core skinny kernel; rest: tcgen05 --
+    # 4096 x 2048 x 768, 2300 x 768 x 1548 and 4224 x 768 x 520 on CTA pairs, with row and column tails)
     for rows, K, n in ((128, 64, 128), (1000, 768, 1548), (333, 256, 96), (4096, 2048, 768), (7, 768, 32768),
-                       (1, 768, 1548), (32, 1536, 768), (17, 2048, 100), (5, 72, 40)):
+                       (1, 768, 1548), (32, 1536, 768), (17, 2048, 100), (5, 72, 40), (2300, 768, 1548),
+                       (4224, 768, 520)):
         x = torch.randn(rows, K, device=DEV).bfloat16()
         w = torch.randn(n, K, device=DEV).bfloat16()
         y = torch.empty(rows, n, device=DEV)
