@@ -258,9 +258,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 // stages its 128 rows of A and its 128 rows of B (one half of the tile's columns) per K step, and one thread of the
 // even CTA issues 256 x N x 16 MMAs that read both CTAs' shared memory and leave each CTA's 128 rows of the
 // accumulator in its own TMEM.  Per CTA and K step 32 KB of operands feed 128 x 256 outputs (48 KB in the
-// single-CTA tile), so the L2 -> SM operand traffic per flop falls by a third.  Loads are plain TMA tile loads
-// (no multicast); each CTA's copies complete on the even CTA's `full` barrier, whose expected bytes cover both
-// halves.  The MMA commits arrive on the `empty` / `acc_full` barriers of both CTAs; every epilogue warp of both
+// single-CTA tile), so the L2 -> SM operand traffic per flop falls by a third.  Loads are plain TMA tile loads,
+// each into its own CTA; they complete on the even CTA's `full` barrier, whose expected bytes cover both halves.
+// The MMA thread commits each consumed stage to the even CTA's `empty` barrier, whose producer passes the release on
+// to the odd CTA's, and each finished accumulator to both CTAs' `acc_full`; every epilogue warp of both
 // CTAs arrives on the even CTA's `acc_empty`.  All waits are the bounded mbarrier waits; the two cluster barriers
 // (after set-up, before TMEM release) are reached on every path.
 constexpr int PAIR_N = 256;
@@ -291,7 +292,7 @@ __device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// 2-D tile load into this CTA's shared memory, completing on an mbarrier of either CTA of the pair (no multicast).
+// 2-D tile load into this CTA's shared memory only, completing on an mbarrier of either CTA of the pair.
 __device__ __forceinline__ void load_2d_pair(const CUtensorMap* map, uint32_t mbar_cluster, void* dst, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
@@ -307,13 +308,18 @@ __device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t da, uin
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
 }
-// Arrives once on `bar` (the same offset) in both CTAs of the pair when the issued MMAs have completed.
+// Arrives on `bar` in this (the even) CTA when the issued MMAs have completed.
+__device__ __forceinline__ void umma_commit_own(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer_addr(bar, 0))
+               : "memory");
+}
+// Arrives once on `bar` (the same offset) in both CTAs of the pair when the issued MMAs have completed: one
+// commit per CTA's barrier (each tracks every MMA this thread issued before it).
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"((uint16_t)3)
-      : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer_addr(bar, 0))
+               : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer_addr(bar, 1))
+               : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
@@ -383,6 +389,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             ok = false;
             break;
           }
+          // the MMA thread commits a consumed stage to the even CTA's `empty` only; its producer passes each
+          // release on to the odd CTA's `empty`, one arrival per reuse of the stage
+          if (leader && it >= (uint32_t)C::STAGES) mbar_arrive_remote(peer_addr(&empty_bar[s], 1));
           unsigned char* a_dst = ring + s * C::STAGE_BYTES;
           if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * C::STAGE_BYTES);
           const uint32_t fb = peer_addr(&full_bar[s], 0);
@@ -416,7 +425,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             umma_bf16_pair(dt, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), idesc, (kt | kk) != 0);
-          umma_commit_pair(&empty_bar[s]);
+          umma_commit_own(&empty_bar[s]);
         }
         if (ok) umma_commit_pair(&acc_full[buf]);
       }

@@ -7,6 +7,7 @@
 // flat index a*c1+b ascending) order, which is the order a stable top-k of the reference's flattened `comb`
 // gives.  Only exactly equal scores can order differently from aten::topk, whose tie order is unspecified.
 #include "pk_common.cuh"
+#include "tma.cuh"
 
 namespace sdm {
 
@@ -481,20 +482,22 @@ __device__ __noinline__ void half_lists_exact(const float* src, bool vec, const 
 }
 
 // The top-C of one half with 32-bit keys as (score, sub-key id) lists; false when the exact path must redo it.
-template <int HALF, int C>
-__device__ __forceinline__ bool half_lists_fast(const float (&zn)[HALF], const float* kn, int n_sub, int ib,
-                                               uint8_t* lowb, float* vs, uint8_t* is, int tid) {
+// score(j) gives sub-key j's cosine score; NSU > 0 bounds n_sub at compile time (the groups are then unrolled, so a
+// score held in a register array is indexed statically).
+template <int C, int NSU, typename ScoreFn>
+__device__ __forceinline__ bool half_lists_fast_core(ScoreFn score, int n_sub, int ib, uint8_t* lowb, float* vs,
+                                                    uint8_t* is, int tid) {
   const uint32_t mask = (1u << ib) - 1u;
   uint32_t tk[C];
   uint32_t disc = 0u;
-  for (int g0 = 0; g0 < n_sub; g0 += C) {
+  auto group = [&](int g0) {
     uint32_t gk[C];
 #pragma unroll
     for (int q = 0; q < C; ++q) {
       const int j = g0 + q;
       uint32_t key = 0u;  // padding: below every real key (a real key is at least the image of -inf)
       if (j < n_sub) {
-        float sc = half_dot<HALF>(zn, kn + j * HALF);
+        float sc = score(j);
         if (sc != sc) sc = -INFINITY;
         const uint32_t m = mono_image(sc);
         lowb[j * PKF_THREADS + tid] = (uint8_t)(m & mask);
@@ -513,6 +516,13 @@ __device__ __forceinline__ bool half_lists_fast(const float (&zn)[HALF], const f
     } else {
       merge_top32<C>(tk, gk, disc);
     }
+  };
+  if constexpr (NSU > 0) {
+#pragma unroll
+    for (int g0 = 0; g0 < NSU; g0 += C)
+      if (g0 < n_sub) group(g0);
+  } else {
+    for (int g0 = 0; g0 < n_sub; g0 += C) group(g0);
   }
   if (disc != 0u && tk[C - 1] != 0u && (disc >> ib) == (tk[C - 1] >> ib)) return false;
   uint32_t eqm = 0u;  // bit q: keys q and q + 1 share their high bits
@@ -542,6 +552,12 @@ __device__ __forceinline__ bool half_lists_fast(const float (&zn)[HALF], const f
     is[q * PKF_THREADS + tid] = (uint8_t)j;
   }
   return true;
+}
+template <int HALF, int C>
+__device__ __forceinline__ bool half_lists_fast(const float (&zn)[HALF], const float* kn, int n_sub, int ib,
+                                               uint8_t* lowb, float* vs, uint8_t* is, int tid) {
+  return half_lists_fast_core<C, 0>([&](int j) { return half_dot<HALF>(zn, kn + j * HALF); }, n_sub, ib, lowb, vs,
+                                    is, tid);
 }
 
 // The walk of pk_fast_kernel.  Rows r >= C/2 (>= kk/2) can only ever contribute their first candidate ((r+1)(b+1)
@@ -829,6 +845,355 @@ __global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_fast_kernel(
   }
 }
 
+// ------------------------------------------------------------------------------ scores on the tensor cores
+// pk_tc_kernel: the RunTimeSdm addressing (address width 32, n_sub <= 32, c1 <= 16) with the cosine scores of the
+// block's 128 addresses against the head's 2 x n_sub sub-keys computed as one tcgen05 product: A (128 x 32: the two
+// normalised halves of each address) times B^T (64 x 32: sub-key j of half 1 in row j over the first 16 columns,
+// sub-key j of half 2 in row 32 + j over the last 16, zeros elsewhere), so D[t][j] is half 1's score of sub-key j
+// and D[t][32 + j] half 2's.  Every operand value v is split into three bfloat16 parts v = p0 + p1 + p2 (each the
+// rounded remainder of the previous; |v - p0 - p1 - p2| <= 2^-27 |v|) and the six products p_a q_b with a + b <= 2
+// are accumulated in float32, smallest first: a score's error is a few units of 2^-25, below the float32 rounding
+// of the CUDA-core dot product it replaces.  The accumulator (128 lanes x 64 columns) lands in TMEM; each thread
+// reads its own row (its address's 64 scores) and the selection proceeds as in pk_fast_kernel.  A half whose
+// 32-bit keys cannot settle the order (rare near-ties) is re-sorted exactly (64-bit keys) from the same scores.
+namespace pktc {
+constexpr int NSUB = 32, NB = 2 * NSUB;
+constexpr uint32_t A_PART = PKF_THREADS * 64, B_PART = NB * 64;  // rows of 32 bf16 (64 bytes), 64-byte swizzle
+constexpr uint32_t OPS_BYTES = 3 * A_PART + 3 * B_PART;
+constexpr uint32_t TMEM_COLS = 64;
+// kind::f16: D float32, A and B bfloat16, both K-major, M = 128, N = 64
+constexpr uint32_t IDESC =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(PKF_THREADS >> 4) << 24);
+
+// Shared-memory matrix descriptor, K-major, 64-byte swizzle: rows of 64 B, 8-row groups 512 B apart.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused by swizzled K-major layouts)
+  d |= (uint64_t)(512 >> 4) << 32;   // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;            // descriptor version of sm_100
+  d |= (uint64_t)4 << 61;            // SWIZZLE_64B
+  return d;
+}
+__device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(IDESC), "r"(accumulate));
+}
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(tma::smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t pack2(bf16_t lo, bf16_t hi) {
+  return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+// Chunk c (values 8c .. 8c+7) of row `row` of the three parts: v (8 values) split v = p0 + p1 + p2, stored with the
+// 64-byte swizzle (16-byte chunk c of row r at chunk c ^ ((r >> 1) & 3)).
+__device__ __forceinline__ void put_chunk(unsigned char* base, uint32_t part_bytes, int row, int c, const float (&v)[8]) {
+  uint32_t w[3][4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    bf16_t p[2][3];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const float x = v[2 * e + u];
+      p[u][0] = __float2bfloat16_rn(x);
+      const float r1 = x - __bfloat162float(p[u][0]);
+      p[u][1] = __float2bfloat16_rn(r1);
+      const float r2 = r1 - __bfloat162float(p[u][1]);
+      p[u][2] = __float2bfloat16_rn(r2);
+    }
+#pragma unroll
+    for (int q = 0; q < 3; ++q) w[q][e] = pack2(p[0][q], p[1][q]);
+  }
+  const uint32_t off = (uint32_t)row * 64 + ((uint32_t)(c ^ ((row >> 1) & 3)) << 4);
+#pragma unroll
+  for (int q = 0; q < 3; ++q)
+    *reinterpret_cast<uint4*>(base + q * part_bytes + off) = make_uint4(w[q][0], w[q][1], w[q][2], w[q][3]);
+}
+// Row `row` of the three parts of an operand: v (32 values) split v = p0 + p1 + p2, each part's row of 64 bytes
+// stored with the 64-byte swizzle (16-byte chunk c of row r at chunk c ^ ((r >> 1) & 3)).
+__device__ __forceinline__ void put_row(unsigned char* base, uint32_t part_bytes, int row, const float (&v)[32]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t w[3][4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      bf16_t p[2][3];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float x = v[8 * c + 2 * e + u];
+        p[u][0] = __float2bfloat16_rn(x);
+        const float r1 = x - __bfloat162float(p[u][0]);
+        p[u][1] = __float2bfloat16_rn(r1);
+        const float r2 = r1 - __bfloat162float(p[u][1]);
+        p[u][2] = __float2bfloat16_rn(r2);
+      }
+#pragma unroll
+      for (int q = 0; q < 3; ++q) w[q][e] = pack2(p[0][q], p[1][q]);
+    }
+    const uint32_t off = (uint32_t)row * 64 + ((uint32_t)(c ^ ((row >> 1) & 3)) << 4);
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+      *reinterpret_cast<uint4*>(base + q * part_bytes + off) = make_uint4(w[q][0], w[q][1], w[q][2], w[q][3]);
+  }
+}
+}  // namespace pktc
+
+// The exact top-C of one half from scores already computed (64-bit keys); the rare path of pk_tc_kernel.
+template <int C, typename ScoreFn>
+__device__ __forceinline__ void half_lists_exact_scores(ScoreFn score, int n_sub, float* vs, uint8_t* is, int tid) {
+  KT tk[C];
+#pragma unroll
+  for (int g0 = 0; g0 < pktc::NSUB; g0 += C) {
+    if (g0 >= n_sub) break;
+    KT gk[C];
+#pragma unroll
+    for (int q = 0; q < C; ++q) {
+      const int j = g0 + q;
+      float s = -INFINITY;
+      if (j < n_sub) {
+        s = score(j);
+        if (s != s) s = -INFINITY;
+      }
+      gk[q] = pk_key(s, j < n_sub ? (uint32_t)j : 0xFFFFFFFFu);
+    }
+    bitonic_sort_desc<C>(gk);
+    if (g0 == 0) {
+#pragma unroll
+      for (int q = 0; q < C; ++q) tk[q] = gk[q];
+    } else {
+      merge_top<C>(tk, gk);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < C; ++q) {
+    vs[q * PKF_THREADS + tid] = pk_key_score(tk[q]);
+    is[q * PKF_THREADS + tid] = (uint8_t)pk_key_tie(tk[q]);
+  }
+}
+
+template <int C>
+__global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_tc_kernel(PkArgs a, int c1, int kk, int ib) {
+  static_assert(C <= 16, "picks are kept in registers");
+  pdl_enter();
+  extern __shared__ __align__(1024) unsigned char pkt_raw[];
+  __shared__ __align__(8) uint64_t mma_bar;
+  __shared__ uint32_t tmem_slot;
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(pkt_raw) + 1023) & ~(uintptr_t)1023);
+  unsigned char* opA = base;
+  unsigned char* opB = base + 3 * pktc::A_PART;
+  constexpr int P = PKF_THREADS;
+  constexpr int HALF = 16;
+  // once the product has completed, the operands' region holds the selection lists (as in pk_fast_kernel)
+  float* v1s = reinterpret_cast<float*>(base);
+  float* v2s = v1s + C * P;
+  uint8_t* i1s = reinterpret_cast<uint8_t*>(v2s + C * P);
+  uint8_t* i2s = i1s + C * P;
+  uint8_t* lowb = i2s + C * P;
+  uint8_t* brow = lowb;
+  const int hh = blockIdx.y % a.h, pr = blockIdx.y / a.h;  // pr: which address set of a paired launch
+  const float* const zb = pr ? a.z2 : a.z;
+  float* const svb = pr ? a.sv2 : a.sv;
+  float* const wb = pr ? a.w2 : a.w;
+  int32_t* const sib = pr ? a.si2 : a.si;
+  const float* const gb = pr ? a.gate2 : a.gate;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_sub = a.n_sub;
+
+  // this thread's address, loaded first so the loads are in flight while the block sets up its sub-keys
+  const int64_t n = (int64_t)blockIdx.x * P + tid;
+  const bool live = n < a.N;
+  float zraw[32];
+  {
+    const float* zr = zb + (live ? n : 0) * a.ldz + (int64_t)hh * a.d_a;
+    if (((reinterpret_cast<uintptr_t>(zb) & 15) | (a.ldz & 3) | (a.d_a & 3)) == 0) {
+#pragma unroll
+      for (int d4 = 0; d4 < 8; ++d4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(zr) + d4);
+        zraw[4 * d4] = v.x;
+        zraw[4 * d4 + 1] = v.y;
+        zraw[4 * d4 + 2] = v.z;
+        zraw[4 * d4 + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int dd = 0; dd < 32; ++dd) zraw[dd] = zr[dd];
+    }
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tma::smem_u32(&tmem_slot)),
+                 "r"(pktc::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    tma::mbar_init(&mma_bar, 1);
+    tma::mbar_init_fence();
+  }
+  // B row j (j < 32: half 1's sub-key j in columns 0-15; 32 + j: half 2's in columns 16-31), F.normalize(keys):
+  // two threads per row, eight values each (the pair shares its sum of squares by a shuffle)
+  {
+    const int rowb = tid >> 1, part = tid & 1;
+    const int hf = rowb >= pktc::NSUB, j = rowb - hf * pktc::NSUB;
+    float kv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) kv[e] = 0.f;
+    if (j < n_sub) {
+      const float* src = (hf ? a.keys2 : a.keys1) + ((int64_t)hh * n_sub + j) * HALF + 8 * part;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) kv[e] = src[e];
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(kv[e], kv[e], ss);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    // F.normalize: v / max(||v||, 1e-12), the norm as the sum of squares' correctly rounded square root
+    const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) kv[e] = __fdiv_rn(kv[e], nrm);
+    pktc::put_chunk(opB, pktc::B_PART, rowb, hf * 2 + part, kv);
+    const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    pktc::put_chunk(opB, pktc::B_PART, rowb, (1 - hf) * 2 + part, zero);
+  }
+  (void)lane;
+  // A: the address, both halves normalised (F.normalize: v / max(||v||, 1e-12)); a row past N stays zero
+  {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float ss = 0.f;
+#pragma unroll
+      for (int dd = 0; dd < HALF; ++dd) ss = fmaf(zraw[hf * HALF + dd], zraw[hf * HALF + dd], ss);
+      const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
+#pragma unroll
+      for (int dd = 0; dd < HALF; ++dd) zraw[hf * HALF + dd] = live ? __fdiv_rn(zraw[hf * HALF + dd], nrm) : 0.f;
+    }
+    pktc::put_row(opA, pktc::A_PART, tid, zraw);
+  }
+  tma::fence_proxy_async();  // the operands written here are read by the tensor cores (async proxy)
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_slot;
+  if (tid == 0) {
+    const uint32_t aa = tma::smem_u32(opA), bb = tma::smem_u32(opB);
+    constexpr int PA[6] = {2, 1, 0, 1, 0, 0}, PB[6] = {0, 1, 2, 0, 1, 0};  // p_a q_b, smallest products first
+#pragma unroll
+    for (int u = 0; u < 6; ++u)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        pktc::mma(tmem, pktc::sw64_desc(aa + PA[u] * pktc::A_PART + ks * 32),
+                  pktc::sw64_desc(bb + PB[u] * pktc::B_PART + ks * 32), (u | ks) != 0);
+    pktc::commit(&mma_bar);
+  }
+  const bool done = tma::mbar_wait(&mma_bar, 0u);  // bounded; a wait that gave up skips the selection
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  const bool work = live && done;
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    uint32_t r[32];
+    pktc::ld32(lane_base + 32u * hf, r);  // this address's scores of half hf (every lane: the load is collective)
+    float* vs = hf ? v2s : v1s;
+    uint8_t* is = hf ? i2s : i1s;
+    if (work && !half_lists_fast_core<C, pktc::NSUB>([&](int j) { return __uint_as_float(r[j]); }, n_sub, ib, lowb,
+                                                     vs, is, tid))
+      half_lists_exact_scores<C>([&](int j) { return __uint_as_float(r[j]); }, n_sub, vs, is, tid);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(pktc::TMEM_COLS) : "memory");
+  }
+  if (!work) return;
+
+  const int64_t dst = pk_dst(n, hh, a.h, a.T_bh, kk);
+  const bool vec = (kk & 3) == 0 && ((reinterpret_cast<uintptr_t>(sib + dst) | (wb ? reinterpret_cast<uintptr_t>(wb + dst) : 0) |
+                                      (svb ? reinterpret_cast<uintptr_t>(svb + dst) : 0)) & 15) == 0;
+  float sc[C];
+  int sl[C];
+  const float v2_0 = v2s[tid];
+  WalkHT<C> w;
+  walk_init<C>(w, v1s, brow, v2_0, c1, tid);
+  walkr_step<C, 0>(w, sc, sl, v1s, v2s, i1s, i2s, brow, v2_0, c1, n_sub, kk, tid);
+  if (vec) {
+#pragma unroll
+    for (int j = 0; j < C; j += 4) {
+      if (j < kk) {
+        *reinterpret_cast<int4*>(sib + dst + j) = make_int4(sl[j], sl[j + 1], sl[j + 2], sl[j + 3]);
+        if (svb) *reinterpret_cast<float4*>(svb + dst + j) = make_float4(sc[j], sc[j + 1], sc[j + 2], sc[j + 3]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      if (j < kk) {
+        sib[dst + j] = sl[j];
+        if (svb) svb[dst + j] = sc[j];
+      }
+    }
+  }
+  if (wb) {
+    const float scale = expf(a.log_scale[hh]);
+    float mx = -INFINITY, sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < C; ++j)
+      if (j < kk) mx = fmaxf(mx, sc[j] * scale);
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      if (j < kk) {
+        sc[j] = expf(sc[j] * scale - mx);
+        sum += sc[j];
+      }
+    }
+    const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      if (j < kk) {
+        const float wj = __fdiv_rn(sc[j], sum);
+        sc[j] = gb ? wj * g : wj;
+      }
+    }
+    if (vec) {
+#pragma unroll
+      for (int j = 0; j < C; j += 4)
+        if (j < kk) *reinterpret_cast<float4*>(wb + dst + j) = make_float4(sc[j], sc[j + 1], sc[j + 2], sc[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < C; ++j)
+        if (j < kk) wb[dst + j] = sc[j];
+    }
+  }
+}
+
+template <int C>
+static cudaError_t launch_pk_tc(const PkArgs& a, int c1, int kk, cudaStream_t st) {
+  int ib = 1;
+  while ((1 << ib) < a.n_sub) ++ib;
+  const size_t lists = (size_t)2 * C * PKF_THREADS * 4 + (size_t)2 * C * PKF_THREADS +
+                       (size_t)(a.n_sub > C + 2 * kk ? a.n_sub : C + 2 * kk) * PKF_THREADS;
+  const size_t smem = 1024 + (lists > pktc::OPS_BYTES ? lists : (size_t)pktc::OPS_BYTES);
+  auto kern = pk_tc_kernel<C>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)ceil_div(a.N, PKF_THREADS), (unsigned)(a.h * (a.pairs > 1 ? 2 : 1)));
+  LaunchScope scope_("pk_address", st);
+  return launch_k(kern, grid, dim3(PKF_THREADS), smem, st, a, c1, kk, ib);
+}
+
 template <int HALF, int C>
 static cudaError_t launch_pkf(const PkArgs& a, int c1, int kk, cudaStream_t st) {
   int ib = 1;
@@ -940,6 +1305,11 @@ cudaError_t launch_pk_address(const PkArgs& a, cudaStream_t st) {
       case 32: return launch_pk_warp<32>(a, c1, kk, st);
       default: return cudaErrorInvalidValue;
     }
+  }
+  if (a.d_a == 32 && a.n_sub <= pktc::NSUB && c1 <= 16 && kk <= c1) {  // scores on the tensor cores
+    if (c1 <= 4) return launch_pk_tc<4>(a, c1, kk, st);
+    if (c1 <= 8) return launch_pk_tc<8>(a, c1, kk, st);
+    return launch_pk_tc<16>(a, c1, kk, st);
   }
   if (a.n_sub <= 256 && c1 <= 32 && kk <= c1) {  // the 32-bit-key kernel (no row of the walk runs out)
     switch (a.d_a / 2) {

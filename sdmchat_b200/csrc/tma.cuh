@@ -1,5 +1,5 @@
 // mbarrier and TMA helpers shared by the kernels that stage operands with the Tensor Memory Accelerator.
-// None of these copies uses cluster multicast, and every wait is bounded.
+// Every copy here lands in the issuing CTA's own shared memory, and every wait is bounded.
 #pragma once
 #include <cuda.h>
 #include "common.cuh"
@@ -67,7 +67,7 @@ __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled tensor load (no multicast) completing on `bar`.
+// 2-D tiled tensor load into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

@@ -49,9 +49,12 @@ def emit(out_path):
     src = open(os.path.join(CSRC, "pk_address.cu")).read()
     body = src[src.index("namespace sdm {") + len("namespace sdm {"):
                src.index("template <int HALF, int C>\nstatic cudaError_t launch_pkf(")]
-    # keep the helpers and the 32-bit-key kernel; drop the 64-bit-key thread kernel and its launchers
+    # keep the helpers and the 32-bit-key kernel; drop the 64-bit-key thread kernel and its launchers, and the
+    # tensor-core variant (its scores come from tcgen05; its selection is the same half_lists_fast_core and walk)
     body = cut(body, "template <int HALF, int C>\n__global__ void __launch_bounds__(PK_THREADS",
                "// ------------------------------------------------------------------------------------ 32-bit-key variant")
+    body = body[:body.index("// ------------------------------------------------------------------------------ scores on the tensor "
+                            "cores")]
     sig = ("__global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_fast_kernel(PkArgs a, int c1, int kk, "
            "int ib) {\n  pdl_enter();\n  extern __shared__ __align__(16) float pkf_smem[];")
     assert sig in body

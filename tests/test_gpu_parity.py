@@ -69,8 +69,11 @@ def test_pk_address_matches_oracle_bitwise_order(cuda_ok):
 
 
 def test_pk_address_warp_kernel_equals_thread_kernel(cuda_ok):
-    """Small launches (decode) take the warp-per-address kernel, large ones the thread-per-address kernel: both
-    give bit-identical slots, scores and weights on the same addresses (including exact ties)."""
+    """Small launches (decode) take the warp-per-address kernel, large ones a block-per-128-addresses kernel.  Where
+    both score on CUDA cores they give bit-identical slots, scores and weights on the same addresses (exact ties
+    included).  Where the large launch scores on the tensor cores (address width 32, n_sub <= 32, top-c1 <= 16) the
+    scores agree within 1e-6 and the slots wherever the selection is defined (oracle margin and adjacent gaps above
+    1e-6), and exactly on the zero address, whose scores are all exactly zero in both."""
     rng = np.random.default_rng(13)
     for n_sub, k, d_a in ((32, 16, 32), (72, 32, 32), (16, 8, 32), (9, 5, 12)):
         z = rng.standard_normal((4000, 3, d_a)).astype(np.float32)
@@ -80,8 +83,39 @@ def test_pk_address_warp_kernel_equals_thread_kernel(cuda_ok):
         k1[:, 1] = k1[:, 0]
         big = S.pk_address(t(z), t(k1), t(k2), k)          # 12,000 addresses: thread kernel
         small = S.pk_address(t(z[:50]), t(k1), t(k2), k)   # 150 addresses: warp kernel
-        for b_, s_ in zip(big, small):
-            assert torch.equal(b_[:50], s_), (n_sub, k)
+        if not (d_a == 32 and n_sub <= 32 and min(k, n_sub) <= 16):
+            for b_, s_ in zip(big, small):
+                assert torch.equal(b_[:50], s_), (n_sub, k)
+            continue
+        sv_b, si_b = (x[:50].cpu().numpy() for x in big)
+        sv_s, si_s = (x.cpu().numpy() for x in small)
+        np.testing.assert_allclose(sv_b, sv_s, atol=1e-6, rtol=0)
+        sv_o, _, margin = O.pk_address(z[:50], k1, k2, k, return_margin=True)
+        ok = (margin > 1e-6) & (np.abs(np.diff(sv_o, axis=-1)).min(-1) > 1e-6)
+        assert ok.mean() > 0.5
+        assert (si_b == si_s).all(-1)[ok].all(), (n_sub, k)
+        assert (si_b[7] == si_s[7]).all() and (sv_b[7] == 0).all()
+
+
+def test_pk_tensor_core_scores_accuracy(cuda_ok):
+    """The tensor-core scores (three-part bfloat16 split, float32 accumulation) against float64 cosines of the same
+    inputs: the selected scores' error stays far below the 1e-6 margin of the index-exactness rule."""
+    rng = np.random.default_rng(17)
+    z = rng.standard_normal((20000, 4, 32)).astype(np.float32)
+    k1 = rng.standard_normal((4, 32, 16)).astype(np.float32)
+    k2 = rng.standard_normal((4, 32, 16)).astype(np.float32)
+    sv, si = S.pk_address(t(z), t(k1), t(k2), 16)
+    sv, si = sv.cpu().numpy().astype(np.float64), si.cpu().numpy()
+
+    def nrm(v):
+        v = v.astype(np.float64)
+        return v / np.maximum(np.sqrt((v * v).sum(-1, keepdims=True)), 1e-12)
+    s1 = np.einsum("nhd,hsd->nhs", nrm(z[..., :16]), nrm(k1))
+    s2 = np.einsum("nhd,hsd->nhs", nrm(z[..., 16:]), nrm(k2))
+    exact = (np.take_along_axis(s1, si // 32, -1) + np.take_along_axis(s2, si % 32, -1)) * 0.5
+    err = np.abs(sv - exact).max()
+    print(f"tensor-core pk scores: max error {err:.3g} against float64")
+    assert err < 3e-7, err
 
 
 def test_pk_address_exact_ties_follow_index_order(cuda_ok):
