@@ -316,7 +316,8 @@ cudaError_t launch_argmax_combine(const float2* part, int64_t rows, int tiles_n,
 
 // Generic GEMM y = x @ w^T; x (rows, K) row-major (ldx), w (n, K) row-major (ldw) (nn.Linear weight layout).
 // kwrap (0 = K): w's K index is taken modulo kwrap, so x = [hi | lo] (K = 2*kwrap) against one w computes
-// hi @ w^T + lo @ w^T -- the float32-accurate product of a value split into two bfloat16 halves.
+// hi @ w^T + lo @ w^T -- the product of a float32 value split into two bfloat16 parts (16 significant bits,
+// within 2^-17 relative per element) with float32 accumulation.
 // float: CUDA-core FMA; bf16: tcgen05 tensor cores when tc_gemm_supported(), else CUDA cores.
 template <typename TA, typename Epi>
 cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int64_t rows, int K, int n, Epi epi,
