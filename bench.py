@@ -149,6 +149,19 @@ def all_host_threads():
         return None
 
 
+def port_vs_reference():
+    """The port's CPU speed against the unmodified reference module's torch CPU forward, both timed on one host
+    (oracle/time_port_vs_reference.py writes the figures; the reference itself cannot run on the GPU box)."""
+    p = os.path.join(ROOT, "oracle", "port_vs_reference.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        r = json.load(f)
+    return {"reference_torch_cpu_tok_s": r["reference_torch_cpu_tok_s"], "port_tok_s": r["port_numpy_tok_s"],
+            "port_over_reference": r["port_over_reference"], "host_threads": r["host_threads"],
+            "sample": f"1 row x {r['tokens']} tokens, FULL d768 L12, both on the build host", "source": r["script"]}
+
+
 def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -173,7 +186,7 @@ def run_reference(a):
            "config": {"workload": workload(a.layers, a.global_rows, a.seq), "global_batch": a.global_rows,
                       "seq_len": a.seq, "parallelism": "host CPU"},
            "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-                            "sample": sample},
+                            "sample": sample, "port_vs_reference": port_vs_reference()},
            "e2e": {"value": round(val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -555,7 +568,8 @@ def run_ours(a):
         cpu = {"value": round(v, 2), "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
                "sample": f"1 row x {CPU_TOKENS} tokens (sixteen 128-token chunks) of the same FULL d768 "
                          f"L{a.layers} model, forward + tied-head CE sum, numpy float32 port of the reference "
-                         "algorithm (one run after a 16-token warm run)"}
+                         "algorithm (one run after a 16-token warm run)",
+               "port_vs_reference": port_vs_reference()}
 
     if rank == 0:
         out = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,

@@ -18,15 +18,55 @@ outputs, and the residual adds round.  Top-k ties are broken lowest-index-first 
 exactly equal scores is whatever ``aten::topk`` does and is outside the parity contract, so tests compare selections
 only where the k-th / (k+1)-th score margin is non-zero (and report near-ties with their margins).
 """
+import os
+from concurrent.futures import ThreadPoolExecutor
+
 import numpy as np
 
 F32 = np.float32
+
+# Row-independent steps (product-key addressing, bfloat16 rounding of large arrays) run on row blocks in threads;
+# numpy releases the GIL inside these kernels, so the blocks use the host's cores.  Results do not depend on the
+# split.  SDM_ORACLE_THREADS=1 runs everything on the calling thread.
+_THREADS = int(os.environ.get("SDM_ORACLE_THREADS", "0")) or (os.cpu_count() or 1)
+_POOL = None
+
+
+def _pool():
+    global _POOL
+    if _POOL is None:
+        _POOL = ThreadPoolExecutor(max_workers=_THREADS)
+    return _POOL
+
+
+def _row_blocks(n, min_rows):
+    """[(lo, hi)] row ranges for the thread pool (one range when the work is small or threads are off)."""
+    nb = min(_THREADS, max(1, n // min_rows))
+    if nb <= 1:
+        return [(0, n)]
+    step = -(-n // nb)
+    return [(lo, min(n, lo + step)) for lo in range(0, n, step)]
 
 
 # ----------------------------------------------------------------------------------------------- numeric helpers
 def bf16(a):
     """Round float32 values to the nearest bfloat16 (ties to even), returned as float32 (torch's conversion)."""
     a = np.ascontiguousarray(a, dtype=F32)
+    if a.size >= (1 << 22) and a.ndim >= 1:
+        flat = a.reshape(a.shape[0], -1) if a.ndim > 1 else a.reshape(-1, 1)
+        out = np.empty_like(flat)
+        blocks = _row_blocks(flat.shape[0], 1)
+
+        def run(lohi):
+            lo, hi = lohi
+            out[lo:hi] = _bf16_block(flat[lo:hi])
+
+        list(_pool().map(run, blocks))
+        return out.reshape(a.shape)
+    return _bf16_block(a)
+
+
+def _bf16_block(a):
     u = a.view(np.uint32)
     r = (u >> 16) & np.uint32(1)
     r += np.uint32(0x7FFF)
@@ -98,6 +138,17 @@ def linear(x, w, bf16_out=False):
 
 # ------------------------------------------------------------------------------------------- product-key address
 def pk_address(z, keys1, keys2, k, return_margin=False, force_si=None):
+    """pk_address (M:134-148) over row blocks of z in threads; see _pk_address_rows."""
+    blocks = _row_blocks(z.shape[0], 1024)
+    if len(blocks) == 1:
+        return _pk_address_rows(z, keys1, keys2, k, return_margin, force_si)
+    parts = list(_pool().map(lambda lh: _pk_address_rows(
+        z[lh[0]:lh[1]], keys1, keys2, k, return_margin,
+        None if force_si is None else np.asarray(force_si)[lh[0]:lh[1]]), blocks))
+    return tuple(np.concatenate([p[i] for p in parts], 0) for i in range(len(parts[0])))
+
+
+def _pk_address_rows(z, keys1, keys2, k, return_margin=False, force_si=None):
     """pk_address (M:134-148). z (N, h, d_a), keys (h, n_sub, d_a/2) -> scores (N, h, kk) descending and slot ids
     (N, h, kk) in [0, n_sub^2).  With return_margin, also the brute-force gap between the kk-th and (kk+1)-th score
     of the full n_sub x n_sub grid (inf when kk = n_sub^2): a selection is only defined where that gap is > 0.
@@ -380,11 +431,15 @@ def lm_forward(P, idx, bf16_stream=True, chunk=128, reset_at_bos=False, bos_id=0
 
 
 def ce_sum(logits, targets):
-    """Sum over positions of cross-entropy (logsumexp - target logit) in float64 for a stable checker."""
-    lg = logits.astype(np.float64).reshape(-1, logits.shape[-1])
+    """Sum over positions of cross-entropy (logsumexp - target logit).  The max-shifted exponentials are taken in
+    float32 (each within about 1e-7 relative; numpy's float64 exp is scalar and ~50x slower), their sums, logs and
+    the total in float64."""
+    lg = logits.astype(F32, copy=False).reshape(-1, logits.shape[-1])
     m = lg.max(-1, keepdims=True)
-    lse = (m[:, 0] + np.log(np.exp(lg - m).sum(-1)))
-    return float((lse - lg[np.arange(lg.shape[0]), targets.reshape(-1)]).sum())
+    e = np.exp(lg - m).sum(-1, dtype=np.float64)
+    lse = m[:, 0].astype(np.float64) + np.log(e)
+    tl = lg[np.arange(lg.shape[0]), targets.reshape(-1)].astype(np.float64)
+    return float((lse - tl).sum())
 
 
 def matched_sdm_n_sub(d, mlp_f, heads, d_a):
