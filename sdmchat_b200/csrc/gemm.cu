@@ -196,14 +196,17 @@ static cudaError_t launch_gemm_skinny(const TA* x, int64_t ldx, const TA* w, int
 }
 
 // ------------------------------------------------------------------------------------- small-M tensor-core GEMM
-// Decode-sized bf16 products (at most 32 rows) on the tensor cores with mma.sync m16n8k16 (bf16 operands, float32
-// accumulation: the products and accumulation precision of the tcgen05 path).  A CTA owns 8 output columns; its 8
-// warps split the K range in 64-wide blocks (a K wrap, x = [hi | lo] against one w, is just more blocks reading the
+// Decode-sized bf16 products (at most SMT_MAX_ROWS rows) on the tensor cores with mma.sync m16n8k16 (bf16 operands,
+// float32 accumulation: the products and accumulation precision of the tcgen05 path).  A CTA owns 8 output columns of
+// one 32-row block (blockIdx.y; the weight columns stay L2-resident across the row blocks, so a few hundred decode
+// streams keep every SM busy where a 256-wide tensor-core tile would occupy a handful); its 8 warps split the K
+// range in 64-wide blocks (a K wrap, x = [hi | lo] against one w, is just more blocks reading the
 // same weights), each warp covering all rows as two 16-row tiles; the 8 partial 32 x 8 tiles are summed in shared
 // memory in warp order, so results are deterministic.  Inside a 64-block thread t of a quad holds 16 consecutive k
 // of its A rows and B column (two 16-byte loads each) and feeds them to four k-steps: slots (2t, 2t+1, 2t+8, 2t+9)
 // of step s carry its values 4s .. 4s+3 -- the same permutation of k for A and B, so the dot products are unchanged.
 constexpr int SMT_WARPS = 8;
+constexpr int64_t SMT_MAX_ROWS = 512;
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
@@ -224,6 +227,9 @@ __global__ void __launch_bounds__(SMT_WARPS * 32) gemm_small_tc_kernel(const bf1
   pdl_enter();
   __shared__ float part[SMT_WARPS][32][9];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row0 = blockIdx.y * 32;
+  x += (int64_t)row0 * ldx;
+  rows -= row0;
   const int g = lane >> 2, t = lane & 3;
   const int n0 = blockIdx.x * 8;
   const int nb = n0 + g;  // this thread's B column
@@ -266,12 +272,12 @@ __global__ void __launch_bounds__(SMT_WARPS * 32) gemm_small_tc_kernel(const bf1
   float v = 0.f;
 #pragma unroll
   for (int q = 0; q < SMT_WARPS; ++q) v += part[q][row][cc];
-  if (row < rows && col < n) epi.apply(row, col, v);
+  if (row < rows && col < n) epi.apply(row0 + row, col, v);
 }
 
 static bool small_tc_ok(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K, int kwrap) {
   const uintptr_t ax = reinterpret_cast<uintptr_t>(x), aw = reinterpret_cast<uintptr_t>(w);
-  return rows >= 1 && rows <= 32 && K % 64 == 0 && kwrap % 64 == 0 && ldx % 8 == 0 && ldw % 8 == 0 &&
+  return rows >= 1 && rows <= SMT_MAX_ROWS && K % 64 == 0 && kwrap % 64 == 0 && ldx % 8 == 0 && ldw % 8 == 0 &&
          ax % 16 == 0 && aw % 16 == 0;
 }
 
@@ -284,8 +290,8 @@ cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int6
   if constexpr (sizeof(TA) == 2) {
     if (small_tc_ok(x, ldx, w, ldw, rows, K, kwrap)) {
       LaunchScope scope_("gemm_small_tc", st);
-      return launch_k(gemm_small_tc_kernel<Epi>, dim3((unsigned)ceil_div(n, 8)), dim3(SMT_WARPS * 32), 0, st, x,
-                      ldx, w, ldw, (int)rows, K, n, epi, kwrap);
+      return launch_k(gemm_small_tc_kernel<Epi>, dim3((unsigned)ceil_div(n, 8), (unsigned)ceil_div(rows, 32)),
+                      dim3(SMT_WARPS * 32), 0, st, x, ldx, w, ldw, (int)rows, K, n, epi, kwrap);
     }
   }
   if (skinny_ok(x, ldx, w, ldw, rows, K, kwrap))

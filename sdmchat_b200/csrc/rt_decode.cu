@@ -20,8 +20,10 @@ namespace sdm {
 constexpr int DEC_MAX_K = 32;
 
 // HALF > 0: the step selects its slots itself (warp 0 the write address, warp 1 the read address, S slots per
-// lane; shared-memory normalised sub-keys); HALF == 0: the selections come in siw/ww/sir/wr.
-template <typename T, int HALF, int S>
+// lane; shared-memory normalised sub-keys); HALF == 0: the selections come in siw/ww/sir/wr.  KM bounds k at
+// compile time: the touched rows are held in registers (four KM-long arrays), and KM 16 (for k <= 16) keeps the
+// block at about half the registers of KM 32, so twice as many (stream, head) blocks are resident.
+template <typename T, int HALF, int S, int KM>
 __global__ void rt_decode_kernel(DecodeArgs a) {
   pdl_enter();
   __shared__ int s_ir[DEC_MAX_K], s_iw[DEC_MAX_K], s_prev[DEC_MAX_K];
@@ -91,9 +93,9 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   const bool keep_old = lam != 0.f && !reset;
   // every row this step touches, loaded before the first store: the k read rows (each thread also loads the read
   // rows' counts, a warp-uniform broadcast, for the denominator) and the k written rows
-  float rv[DEC_MAX_K], rc[DEC_MAX_K], wv[DEC_MAX_K], wc[DEC_MAX_K];
+  float rv[KM], rc[KM], wv[KM], wc[KM];
 #pragma unroll
-  for (int i = 0; i < DEC_MAX_K; ++i) {
+  for (int i = 0; i < KM; ++i) {
     if (i < k) {
       const int r = s_ir[i], q = s_iw[i];
       rv[i] = (act && !reset) ? mem[(int64_t)r * dh + c] : 0.f;
@@ -105,7 +107,7 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   const float scr = reset ? 1.f : sc;
   float acc = 0.f, accd = 0.f;
 #pragma unroll
-  for (int i = 0; i < DEC_MAX_K; ++i) {
+  for (int i = 0; i < KM; ++i) {
     if (i < k) {
       acc = fmaf(s_fr[i], rv[i], acc);
       accd = fmaf(s_fr[i], rc[i], accd);
@@ -143,7 +145,7 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   if (lam == 0.f) {
     if (!reset && act) {
 #pragma unroll
-      for (int j = 0; j < DEC_MAX_K; ++j) {
+      for (int j = 0; j < KM; ++j) {
         if (j < k) {
           const int r = s_prev[j];
           if (r >= 0 && r < M) {
@@ -163,7 +165,7 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
           for (int r = 0; r < M; ++r) cnt[r] *= ns;
       }
 #pragma unroll
-      for (int j = 0; j < DEC_MAX_K; ++j) {
+      for (int j = 0; j < KM; ++j) {
         if (j < k) {
           wv[j] *= ns;
           wc[j] *= ns;
@@ -177,7 +179,7 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   if (act) {
     const float vc = a.V[(int64_t)s * a.ldv + (int64_t)hh * dh + c];
 #pragma unroll
-    for (int j = 0; j < DEC_MAX_K; ++j) {
+    for (int j = 0; j < KM; ++j) {
       if (j < k) {
         const int r = s_iw[j];
         const float f = __fdiv_rn(s_fw[j], ns);
@@ -197,13 +199,27 @@ bool rt_decode_fused_ok(int d_a, int n_sub, int k) {
   return d_a == 32 && k <= DEC_MAX_K && c1 <= 32 && kk <= 32 && pk_warp_slots(n_sub, c1, kk) > 0;
 }
 
-template <typename T, int S>
+template <typename T, int S, int KM>
 static cudaError_t launch_rt_decode_fused(const DecodeArgs& a, int threads, cudaStream_t st) {
   const size_t smem = ((size_t)2 * a.n_sub * 16 + 2 * 128 + 32 * S) * 4;
-  auto kern = rt_decode_kernel<T, 16, S>;
+  auto kern = rt_decode_kernel<T, 16, S, KM>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_k(kern, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), smem, st, a);
+}
+template <typename T, int KM>
+static cudaError_t launch_rt_decode_km(const DecodeArgs& a, cudaStream_t st) {
+  if (a.keys1) {  // one thread per value column, and at least the four address warps
+    if (!rt_decode_fused_ok(a.d_a, a.n_sub, a.k)) return cudaErrorInvalidValue;
+    const int threads = a.dh > 128 ? ((a.dh + 31) / 32) * 32 : 128;
+    switch (pk_warp_slots(a.n_sub, a.k < a.n_sub ? a.k : a.n_sub, a.k)) {
+      case 1: return launch_rt_decode_fused<T, 1, KM>(a, threads, st);
+      case 2: return launch_rt_decode_fused<T, 2, KM>(a, threads, st);
+      default: return launch_rt_decode_fused<T, 4, KM>(a, threads, st);
+    }
+  }
+  const int threads = ((a.dh + 31) / 32) * 32;  // one thread per value column
+  return launch_k(rt_decode_kernel<T, 0, 1, KM>, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), 0, st, a);
 }
 
 template <typename T>
@@ -211,17 +227,8 @@ cudaError_t launch_rt_decode(const DecodeArgs& a, cudaStream_t st) {
   if (a.S == 0) return cudaSuccess;
   if (a.k > DEC_MAX_K || a.dh > 1024) return cudaErrorInvalidValue;
   LaunchScope scope_("rt_decode", st);
-  if (a.keys1) {  // one thread per value column, and at least the four address warps
-    if (!rt_decode_fused_ok(a.d_a, a.n_sub, a.k)) return cudaErrorInvalidValue;
-    const int threads = a.dh > 128 ? ((a.dh + 31) / 32) * 32 : 128;
-    switch (pk_warp_slots(a.n_sub, a.k < a.n_sub ? a.k : a.n_sub, a.k)) {
-      case 1: return launch_rt_decode_fused<T, 1>(a, threads, st);
-      case 2: return launch_rt_decode_fused<T, 2>(a, threads, st);
-      default: return launch_rt_decode_fused<T, 4>(a, threads, st);
-    }
-  }
-  const int threads = ((a.dh + 31) / 32) * 32;  // one thread per value column
-  return launch_k(rt_decode_kernel<T, 0, 1>, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), 0, st, a);
+  if (a.k <= 16) return launch_rt_decode_km<T, 16>(a, st);
+  return launch_rt_decode_km<T, DEC_MAX_K>(a, st);
 }
 template cudaError_t launch_rt_decode<float>(const DecodeArgs&, cudaStream_t);
 template cudaError_t launch_rt_decode<bf16_t>(const DecodeArgs&, cudaStream_t);

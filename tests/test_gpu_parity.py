@@ -223,13 +223,33 @@ def lm_from_fixture(g):
 
 @pytest.mark.parametrize("name", ["lm_partial", "lm_full", "lm_partial_bos"])
 def test_bf16_lm_golden(cuda_ok, name):
-    """Tiny PARTIAL / FULL models in the bf16 stream: logits within 2e-3 of the reference run."""
+    """Tiny PARTIAL / FULL models in the bf16 stream against the reference's own run.  Both run free in bfloat16, so
+    a one-ulp difference in a layer's output (float32 sums in another order) can flip a later near-tie selection;
+    each row's logits must therefore agree within 2e-3 up to the row's first position where one of our layers
+    selects other slots than the reference did, that first difference must be a near-tie of the reference's own
+    input (margin below 1e-3), and most of every row is compared."""
     g = load(name)
     model = lm_from_fixture(g)
     idx = t(g["idx"]).long()
+    trace = []
     with torch.no_grad():
-        logits = model(idx).float().cpu().numpy()
-    assert rel_bf16(logits, g["logits"]) < TOL
+        logits = model._head(model.residual(idx, trace=trace), "logits").float().cpu().numpy()
+    P = lm_params(g)
+    B, T = g["idx"].shape
+    first = np.full(B, T)
+    for li in range(2):
+        prep = O.rt_prepare(P["layers"][li]["mem"], g[f"L{li}.x_in"], bf16_stream=True)
+        for key, mk in (("siw", "margin_w"), ("sir", "margin_r")):
+            bad = (np.sort(trace[li][key].cpu().numpy(), -1) != np.sort(g[f"L{li}.{key}"], -1)).any(-1)  # (B,h,T)
+            for b in range(B):
+                pos = np.where(bad[b].any(0))[0]
+                if len(pos) and pos[0] <= first[b]:
+                    p0 = pos[0]
+                    assert prep[mk][b, bad[b, :, p0], p0].max() < 1e-3, (name, li, key, b, p0)
+                    first[b] = p0
+    assert (first >= T // 2).all(), first
+    err = max(rel_bf16(logits[b, :first[b]], g["logits"][b, :first[b]]) for b in range(B))
+    assert err < TOL
     # layer inputs of the reference fed to our layer 0 / 1: selections exact where the margin allows
     P = lm_params(g)
     for li in range(2):
