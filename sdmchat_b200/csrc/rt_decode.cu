@@ -19,12 +19,48 @@ namespace sdm {
 
 constexpr int DEC_MAX_K = 32;
 
-// HALF > 0: the step selects its slots itself (warp 0 the write address, warp 1 the read address, S slots per
-// lane; shared-memory normalised sub-keys); HALF == 0: the selections come in siw/ww/sir/wr.  KM bounds k at
+// The address rows are read four floats at a time when their layout allows it.
+template <int HALF>
+__device__ __forceinline__ bool dec_zvec(const DecodeArgs& a) {
+  return HALF % 4 == 0 &&
+         ((reinterpret_cast<uintptr_t>(a.proj) & 15) | (a.ldp & 3) | (a.d_a & 3) | (a.h * a.d_a & 3)) == 0;
+}
+
+// One warp's sorted top-c1 of one address half (HALF floats at zh) for n_sub <= 32: lane j normalises sub-key j
+// (keys: the head's n_sub x HALF rows) in registers and scores it with the same fmaf order as half_dot, then one
+// 32-key bitonic sort orders (score desc, index asc).  Element e < c1 goes to vo[e] (score) and io[e] (sub-key id).
+template <int HALF>
+__device__ __forceinline__ void warp_half_list_own(const float* zh, bool zvec, const float* keys, int n_sub, int c1,
+                                                   float* vo, int* io) {
+  const int lane = threadIdx.x & 31;
+  float zn[HALF], kv[HALF];
+  normalize_half<HALF>(zh, zn, zvec);
+  KT key[1] = {0ull};  // padding: below every real key
+  if (lane < n_sub) {
+    const float* kr = keys + lane * HALF;
+    normalize_half<HALF>(kr, kv, HALF % 4 == 0 && (reinterpret_cast<uintptr_t>(kr) & 15) == 0);
+    float sc = 0.f;
+#pragma unroll
+    for (int dd = 0; dd < HALF; ++dd) sc = fmaf(zn[dd], kv[dd], sc);
+    if (sc != sc) sc = -INFINITY;
+    key[0] = pk_key(sc, (uint32_t)lane);
+  }
+  warp_sort_desc<1>(key);
+  if (lane < c1) {
+    vo[lane] = pk_key_score(key[0]);
+    io[lane] = (int)pk_key_tie(key[0]);
+  }
+}
+
+// HALF > 0: the step selects its slots itself (warps 0-3 the halves of the write and read addresses with SH sub-keys
+// per lane, warps 0 and 2 the combines with S candidates per lane; shared-memory normalised sub-keys); HALF == 0:
+// the selections come in siw/ww/sir/wr.  KM bounds k at
 // compile time: the touched rows are held in registers (four KM-long arrays), and KM 16 (for k <= 16) keeps the
 // block at about half the registers of KM 32, so twice as many (stream, head) blocks are resident.
-template <typename T, int HALF, int S, int KM>
-__global__ void rt_decode_kernel(DecodeArgs a) {
+// LBT, LBM: launch bounds (threads, resident blocks per SM); 128 threads x 6 blocks caps the register use at 80 so that
+// six (stream, head) blocks share an SM instead of five.
+template <typename T, int HALF, int S, int SH, int KM, int LBT = 1024, int LBM = 1>
+__global__ void __launch_bounds__(LBT, LBM) rt_decode_kernel(DecodeArgs a) {
   pdl_enter();
   __shared__ int s_ir[DEC_MAX_K], s_iw[DEC_MAX_K], s_prev[DEC_MAX_K];
   __shared__ float s_fr[DEC_MAX_K], s_fw[DEC_MAX_K], s_red[32];
@@ -38,21 +74,37 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   float* cnt = a.cnt + (int64_t)sh * M;
   int32_t* lw = a.last_w + (int64_t)sh * k;
   const int t = threadIdx.x, warp = t >> 5;
+  // inputs read only at the end (the value column written, the out-norm weight), fetched first
+  const float vc = t < dh ? a.V[(int64_t)s * a.ldv + (int64_t)hh * dh + t] : 0.f;
+  const float onw = (t < dh && a.out_norm) ? a.onorm_w[hh * dh + t] : 1.f;
   if constexpr (HALF > 0) {
-    const int n_sub = a.n_sub;
+    const int n_sub = a.n_sub, c1 = min(a.k, n_sub);
     float* kn = dec_smem;
-    for (int j = t; j < 2 * n_sub; j += blockDim.x) {  // F.normalize(keys, dim=-1) for this head
-      const float* src = (j < n_sub ? a.keys1 + ((int64_t)hh * n_sub + j) * HALF
-                                    : a.keys2 + ((int64_t)hh * n_sub + (j - n_sub)) * HALF);
-      float kv[HALF];
-      normalize_half<HALF>(src, kv);
+    if constexpr (SH > 1) {
+      for (int j = t; j < 2 * n_sub; j += blockDim.x) {  // F.normalize(keys, dim=-1) for this head
+        const float* src = (j < n_sub ? a.keys1 + ((int64_t)hh * n_sub + j) * HALF
+                                      : a.keys2 + ((int64_t)hh * n_sub + (j - n_sub)) * HALF);
+        float kv[HALF];
+        normalize_half<HALF>(src, kv);
 #pragma unroll
-      for (int dd = 0; dd < HALF; ++dd) kn[j * HALF + dd] = kv[dd];
+        for (int dd = 0; dd < HALF; ++dd) kn[j * HALF + dd] = kv[dd];
+      }
     }
     if (warp == 0) {
-      const int c1 = min(a.k, n_sub);
       const int nc = warp_candidates(reinterpret_cast<int*>(kn + 2 * n_sub * HALF + 2 * 128), c1, k);
       if (t == 0) s_nc = nc;
+    }
+    if constexpr (SH == 1) {
+      // n_sub <= 32: warps 0-3 build the (write keys, read queries) x (first, second half) lists at once, lane j
+      // normalising sub-key j itself, with no barrier before them
+      if (warp < 4) {
+        const int ad = warp >> 1, hf = warp & 1;
+        float* wsm = dec_smem + 2 * n_sub * HALF + ad * 128;  // per address: v1, i1, v2, i2
+        const float* zh = a.proj + (int64_t)s * a.ldp + (ad ? a.h * a.d_a : 0) + hh * a.d_a + hf * HALF;
+        const float* keys = (hf ? a.keys2 : a.keys1) + (int64_t)hh * n_sub * HALF;
+        warp_half_list_own<HALF>(zh, dec_zvec<HALF>(a), keys, n_sub, c1, wsm + hf * 64,
+                                 reinterpret_cast<int*>(wsm + hf * 64 + 32));
+      }
     }
   } else if (t < k) {  // slot ids are clamped into the state (see rt_scan.cu)
     s_ir[t] = min(max(a.sir[(int64_t)sh * k + t], 0), M - 1);
@@ -67,19 +119,18 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   const bool reset = a.reset && a.reset[s];
   __syncthreads();
   if constexpr (HALF > 0) {
-    // warps 0-3: (write keys, read queries) x (first, second half) lists in parallel, then warps 0 and 2 combine
+    // then warps 0 and 2 combine the halves of the write and the read address
     const int n_sub = a.n_sub, c1 = min(a.k, n_sub);
-    const float* kn = dec_smem;
-    float* wsm = dec_smem + 2 * n_sub * HALF + (warp >> 1) * 128;  // per address: v1, i1, v2, i2
-    const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(a.proj) & 15) | (a.ldp & 3) | (a.d_a & 3) |
-                                        (a.h * a.d_a & 3)) == 0;
-    if (warp < 4) {
-      const int ad = warp >> 1, hf = warp & 1;
-      const float* zh = a.proj + (int64_t)s * a.ldp + (ad ? a.h * a.d_a : 0) + hh * a.d_a + hf * HALF;
-      warp_half_list<HALF, S>(zh, zvec, kn + hf * n_sub * HALF, n_sub, c1, wsm + hf * 64,
-                              reinterpret_cast<int*>(wsm + hf * 64 + 32));
+    float* wsm = dec_smem + 2 * n_sub * HALF + (warp >> 1) * 128;
+    if constexpr (SH > 1) {
+      if (warp < 4) {
+        const int ad = warp >> 1, hf = warp & 1;
+        const float* zh = a.proj + (int64_t)s * a.ldp + (ad ? a.h * a.d_a : 0) + hh * a.d_a + hf * HALF;
+        warp_half_list<HALF, SH>(zh, dec_zvec<HALF>(a), dec_smem + hf * n_sub * HALF, n_sub, c1, wsm + hf * 64,
+                                 reinterpret_cast<int*>(wsm + hf * 64 + 32));
+      }
+      __syncthreads();
     }
-    __syncthreads();
     if (warp == 0 || warp == 2) {
       const float* gate = (warp == 0 && a.gate_col >= 0) ? a.proj + (int64_t)s * a.ldp + a.gate_col + hh : nullptr;
       warp_combine<S>(wsm, n_sub, c1, k, reinterpret_cast<const int*>(dec_smem + 2 * n_sub * HALF + 2 * 128), s_nc,
@@ -125,7 +176,7 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
     for (int w = 0; w < (int)((blockDim.x + 31) >> 5); ++w) tot += s_red[w];
     const float rs = a.out_norm ? rsqrt_rn(__fdiv_rn(tot, (float)dh) + a.out_norm_eps) : 1.f;
     float o = v;
-    if (a.out_norm) o = (o * rs) * a.onorm_w[hh * dh + c];
+    if (a.out_norm) o = (o * rs) * onw;
     const int64_t d = (int64_t)a.h * dh, col = (int64_t)hh * dh + c;
     T* r = static_cast<T*>(a.r);
     if (a.split) {
@@ -177,7 +228,6 @@ __global__ void rt_decode_kernel(DecodeArgs a) {
   // write: state <- lam * state + sum_j ww_j (e_{siw_j} v^T, e_{siw_j}); the k written rows are distinct (a
   // top-k).  With fade 0 (or after a reset) every row not cleared above is zero, so the written value is the write.
   if (act) {
-    const float vc = a.V[(int64_t)s * a.ldv + (int64_t)hh * dh + c];
 #pragma unroll
     for (int j = 0; j < KM; ++j) {
       if (j < k) {
@@ -199,10 +249,12 @@ bool rt_decode_fused_ok(int d_a, int n_sub, int k) {
   return d_a == 32 && k <= DEC_MAX_K && c1 <= 32 && kk <= 32 && pk_warp_slots(n_sub, c1, kk) > 0;
 }
 
-template <typename T, int S, int KM>
+template <typename T, int S, int SH, int KM>
 static cudaError_t launch_rt_decode_fused(const DecodeArgs& a, int threads, cudaStream_t st) {
   const size_t smem = ((size_t)2 * a.n_sub * 16 + 2 * 128 + 32 * S) * 4;
-  auto kern = rt_decode_kernel<T, 16, S, KM>;
+  void (*kern)(DecodeArgs) = rt_decode_kernel<T, 16, S, SH, KM>;
+  if constexpr (KM == 16)
+    if (threads == 128) kern = rt_decode_kernel<T, 16, S, SH, KM, 128, 6>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_k(kern, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), smem, st, a);
@@ -212,14 +264,19 @@ static cudaError_t launch_rt_decode_km(const DecodeArgs& a, cudaStream_t st) {
   if (a.keys1) {  // one thread per value column, and at least the four address warps
     if (!rt_decode_fused_ok(a.d_a, a.n_sub, a.k)) return cudaErrorInvalidValue;
     const int threads = a.dh > 128 ? ((a.dh + 31) / 32) * 32 : 128;
+    // S: candidate pairs (and sub-keys) per lane of the combine; the half lists sort n_sub keys, one per lane when
+    // n_sub <= 32 (a 32-key sort instead of the combine's 64 or 128)
+    const bool one = a.n_sub <= 32;
     switch (pk_warp_slots(a.n_sub, a.k < a.n_sub ? a.k : a.n_sub, a.k)) {
-      case 1: return launch_rt_decode_fused<T, 1, KM>(a, threads, st);
-      case 2: return launch_rt_decode_fused<T, 2, KM>(a, threads, st);
-      default: return launch_rt_decode_fused<T, 4, KM>(a, threads, st);
+      case 1: return launch_rt_decode_fused<T, 1, 1, KM>(a, threads, st);
+      case 2: return one ? launch_rt_decode_fused<T, 2, 1, KM>(a, threads, st)
+                         : launch_rt_decode_fused<T, 2, 2, KM>(a, threads, st);
+      default: return one ? launch_rt_decode_fused<T, 4, 1, KM>(a, threads, st)
+                          : launch_rt_decode_fused<T, 4, 4, KM>(a, threads, st);
     }
   }
   const int threads = ((a.dh + 31) / 32) * 32;  // one thread per value column
-  return launch_k(rt_decode_kernel<T, 0, 1, KM>, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), 0, st, a);
+  return launch_k(rt_decode_kernel<T, 0, 1, 1, KM>, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), 0, st, a);
 }
 
 template <typename T>
