@@ -29,15 +29,16 @@
 //   token t's reads with token t-1's writes (t-1 may be the last token of the previous chunk) and the state scan
 //   only materialises the final state (the last token's writes).
 //
-// rt_scan_kernel, one CTA per (b, hh, slice of SCAN_CW value columns): the slice of mem (M x SCAN_CW float32) and
+// rt_scan_kernel, one CTA per (b, hh, slice of CW value columns): the slice of mem (M x CW float32) and
 // cnt (M) stay in shared memory for the whole window.  Chunk inputs (record, read selections, value slice, the
 // intra num/den) are copied with cp.async one chunk ahead into a second buffer; chunk headers are loaded two
-// chunks ahead so every copy has its exact size.  32 warps per CTA.  Per chunk: reads (two eight-lane groups per
-// token, each taking half of its k reads; a lane group covers one 32-column row per 16-byte access, four read ids
-// per 16-byte load) add the faded state part to num; then the jobs update the state (eight lanes per slot: the sum
-// of the slot's entries, then one read-modify-write).  The fade is lazy: the state is sigma * P, a chunk multiplies
-// sigma by lam^Lc and writes add coef / sigma; when sigma would drop below 2^-40 the chunk instead scales P in one
-// pass.  All sums run in a fixed order: results are bit-reproducible.
+// chunks ahead so every copy has its exact size.  32 warps per CTA.  A lane group of CW/4 lanes covers one CW-column
+// row per 16-byte access (CW = 32: eight-lane groups; CW = 16, for batches too small to fill the SMs with 32-column
+// slices: four-lane groups).  Per chunk: reads (each token's k reads in two halves, one lane group each, four read
+// ids per 16-byte load) add the faded state part to num; then the jobs update the state (one lane group per slot:
+// the sum of the slot's entries, then one read-modify-write).  The fade is lazy: the state is sigma * P, a chunk
+// multiplies sigma by lam^Lc and writes add coef / sigma; when sigma would drop below 2^-40 the chunk instead scales
+// P in one pass.  All sums run in a fixed order, the same for either slice width: results are bit-reproducible.
 #include "kernels.cuh"
 #include "tma.cuh"
 
@@ -49,7 +50,8 @@ constexpr int SCAN_MAX_K = 32;
 constexpr int LIST_THREADS = 256;
 constexpr int LIST_WARPS = LIST_THREADS / 32;
 constexpr int LIST_MAX_DH = 256;
-constexpr int SCAN_CW = 32;  // value columns per scan CTA
+constexpr int SCAN_CW = 32;        // value columns per scan CTA
+constexpr int SCAN_CW_SMALL = 16;  // ... when B x h x 32-column slices would fill at most half the SMs
 constexpr int SCAN_WARPS = 32;
 constexpr int SCAN_THREADS = SCAN_WARPS * 32;
 constexpr float kTinyFade = 7.8886e-31f;  // 2^-100: fades below are treated as 0
@@ -129,8 +131,8 @@ __device__ __forceinline__ void copy_words_async(void* dst, const void* src, int
   }
   for (int i = done + tid; i < n; i += nt) cp_async4(d + i, s + i);
 }
-// rows of SCAN_CW words (w of them valid) with row stride `stride` words into rows of SCAN_CW words.
-__device__ __forceinline__ void copy_rows32_async(void* dst, const void* src, int rows, int w, int64_t stride,
+// rows of cw words (w of them valid) with row stride `stride` words into rows of cw words.
+__device__ __forceinline__ void copy_rows32_async(void* dst, const void* src, int rows, int w, int cw, int64_t stride,
                                                   int tid, int nt);
 
 __device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
@@ -606,7 +608,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
 struct ScanBuf {
   size_t hdr, rec, sir, wr, V, numi, deni, bytes;
 };
-__host__ __device__ inline ScanBuf scan_buf_layout(int k) {
+__host__ __device__ inline ScanBuf scan_buf_layout(int k, int cw) {
   const int L = chunk_len(k), E = L * k;
   ScanBuf s;
   size_t o = 0;
@@ -619,24 +621,24 @@ __host__ __device__ inline ScanBuf scan_buf_layout(int k) {
   s.rec = take(rec_layout(k).bytes);
   s.sir = take((size_t)E * 4);
   s.wr = take((size_t)E * 4);
-  s.V = take((size_t)L * SCAN_CW * 4);
-  s.numi = take((size_t)L * SCAN_CW * 4);
+  s.V = take((size_t)L * cw * 4);
+  s.numi = take((size_t)L * cw * 4);
   s.deni = take((size_t)L * 4 * 4);  // TMA mode: a 4-head-wide box per token (the head's column at hh % 4)
   s.bytes = o;
   return s;
 }
 // P | Pc | two chunk buffers (128-byte aligned) | lampow, plus 128 bytes to align the dynamic region's base.
-__host__ __device__ inline size_t scan_bufs_offset(int M) {
-  return ((align16((size_t)M * SCAN_CW * 4) + align16((size_t)M * 4)) + 127) & ~(size_t)127;
+__host__ __device__ inline size_t scan_bufs_offset(int M, int cw) {
+  return ((align16((size_t)M * cw * 4) + align16((size_t)M * 4)) + 127) & ~(size_t)127;
 }
-__host__ __device__ inline size_t scan_smem_bytes(int M, int k) {
-  return 128 + scan_bufs_offset(M) + 2 * scan_buf_layout(k).bytes + align16((size_t)(CH_MAX_L + 1) * 4);
+__host__ __device__ inline size_t scan_smem_bytes(int M, int k, int cw) {
+  return 128 + scan_bufs_offset(M, cw) + 2 * scan_buf_layout(k, cw).bytes + align16((size_t)(CH_MAX_L + 1) * 4);
 }
 
 // Issue the cp.async copies of chunk c's inputs (header hd) into buffer `buf` (all threads).
 __device__ __forceinline__ void scan_issue(const ScanArgs& a, unsigned char* buf, const ScanBuf& sb,
                                            const RecLayout& rl, int nch, int c, int4 hd, int b, int hh, int cs,
-                                           int ncols, bool want_reads) {
+                                           int ncols, int cw, bool want_reads) {
   const int tid = threadIdx.x, k = a.k, h = a.h, dh = a.dh, T = a.T;
   const int L = chunk_len(k), c0 = c * L, Lc = min(L, T - c0), E = Lc * k;
   const int64_t bh = (int64_t)b * h + hh;
@@ -644,14 +646,14 @@ __device__ __forceinline__ void scan_issue(const ScanArgs& a, unsigned char* buf
   const unsigned char* rec = a.rec + (bh * nch + c) * rl.bytes;
   copy_words_async(buf + sb.rec, rec, 2 * hd.x, tid, SCAN_THREADS);
   copy_words_async(buf + sb.rec + rl.ents, rec + rl.ents, 2 * hd.y, tid, SCAN_THREADS);
-  copy_rows32_async(buf + sb.V, a.V + tok0 * a.ldv + (int64_t)hh * dh + cs * SCAN_CW, Lc, ncols, a.ldv, tid,
+  copy_rows32_async(buf + sb.V, a.V + tok0 * a.ldv + (int64_t)hh * dh + cs * cw, Lc, ncols, cw, a.ldv, tid,
                     SCAN_THREADS);
   if (want_reads && hd.z > 0) {
     const int64_t sel0 = (bh * T + c0) * k;
     const int nr = hd.z;  // tokens before the first reset read the state
     copy_words_async(buf + sb.sir, a.sir + sel0, nr * k, tid, SCAN_THREADS);
     copy_words_async(buf + sb.wr, a.wr + sel0, nr * k, tid, SCAN_THREADS);
-    copy_rows32_async(buf + sb.numi, a.num + (tok0 * h + hh) * dh + cs * SCAN_CW, nr, ncols, (int64_t)h * dh, tid,
+    copy_rows32_async(buf + sb.numi, a.num + (tok0 * h + hh) * dh + cs * cw, nr, ncols, cw, (int64_t)h * dh, tid,
                       SCAN_THREADS);
     if (cs == 0) {
       float* dd = reinterpret_cast<float*>(buf + sb.deni);
@@ -662,17 +664,17 @@ __device__ __forceinline__ void scan_issue(const ScanArgs& a, unsigned char* buf
   cp_async_commit();
 }
 
-__device__ __forceinline__ void copy_rows32_async(void* dst, const void* src, int rows, int w, int64_t stride,
+__device__ __forceinline__ void copy_rows32_async(void* dst, const void* src, int rows, int w, int cw, int64_t stride,
                                                   int tid, int nt) {
   const uint32_t* s = static_cast<const uint32_t*>(src);
   uint32_t* d = static_cast<uint32_t*>(dst);
-  if (w == SCAN_CW && (reinterpret_cast<uintptr_t>(s) & 15) == 0 && (stride & 3) == 0) {
-    for (int i = tid; i < rows * (SCAN_CW / 4); i += nt) {
-      const int r = i / (SCAN_CW / 4), q = i % (SCAN_CW / 4);
-      cp_async16(d + r * SCAN_CW + 4 * q, s + r * stride + 4 * q);
+  if (w == cw && (reinterpret_cast<uintptr_t>(s) & 15) == 0 && (stride & 3) == 0) {
+    for (int i = tid; i < rows * (cw / 4); i += nt) {
+      const int r = i / (cw / 4), q = i % (cw / 4);
+      cp_async16(d + r * cw + 4 * q, s + r * stride + 4 * q);
     }
   } else {
-    copy_rows_async(dst, src, rows, w, SCAN_CW, stride, tid, nt);
+    copy_rows_async(dst, src, rows, w, cw, stride, tid, nt);
   }
 }
 
@@ -681,7 +683,7 @@ __device__ __forceinline__ void copy_rows32_async(void* dst, const void* src, in
 // the 4-head den box are 2-D tensor copies of L token rows.
 __device__ __forceinline__ void scan_issue_tma(const ScanArgs& a, unsigned char* buf, uint64_t* bar,
                                                const ScanBuf& sb, const RecLayout& rl, int nch, int c, int4 hd,
-                                               int b, int hh, int cs, bool want_reads, const CUtensorMap* mV,
+                                               int b, int hh, int cs, int cw, bool want_reads, const CUtensorMap* mV,
                                                const CUtensorMap* mN, const CUtensorMap* mD) {
   const int k = a.k, h = a.h, dh = a.dh, T = a.T;
   const int L = chunk_len(k), c0 = c * L;
@@ -689,7 +691,7 @@ __device__ __forceinline__ void scan_issue_tma(const ScanArgs& a, unsigned char*
   const unsigned char* rec = a.rec + (bh * nch + c) * rl.bytes;
   const uint32_t jb = (uint32_t)align16((size_t)hd.x * 8), eb = (uint32_t)align16((size_t)hd.y * 8);
   const int nr = want_reads ? hd.z : 0;
-  const uint32_t selb = (uint32_t)nr * k * 4, slab = (uint32_t)L * SCAN_CW * 4;
+  const uint32_t selb = (uint32_t)nr * k * 4, slab = (uint32_t)L * cw * 4;
   uint32_t total = 16 + jb + eb + slab;
   if (nr > 0) total += 2 * selb + slab + (cs == 0 ? (uint32_t)L * 16 : 0u);
   tma::mbar_arrive_expect_tx(bar, total);
@@ -697,7 +699,7 @@ __device__ __forceinline__ void scan_issue_tma(const ScanArgs& a, unsigned char*
                16, bar);
   if (jb) tma::load_1d(buf + sb.rec, rec, jb, bar);
   if (eb) tma::load_1d(buf + sb.rec + rl.ents, rec + rl.ents, eb, bar);
-  const int x = hh * dh + cs * SCAN_CW, y = b * T + c0;
+  const int x = hh * dh + cs * cw, y = b * T + c0;
   tma::load_2d(mV, bar, buf + sb.V, x, y);
   if (nr > 0) {
     const int64_t sel0 = (bh * T + c0) * k;
@@ -708,7 +710,7 @@ __device__ __forceinline__ void scan_issue_tma(const ScanArgs& a, unsigned char*
   }
 }
 
-template <int K>
+template <int K, int CW>
 __global__ void __launch_bounds__(SCAN_THREADS, 1)
     rt_scan_kernel(ScanArgs a, int nch, int n_slices, const __grid_constant__ CUtensorMap mapV,
                    const __grid_constant__ CUtensorMap mapN, const __grid_constant__ CUtensorMap mapD, int use_tma) {
@@ -718,24 +720,28 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
   const int k = K > 0 ? K : a.k;
   constexpr int KR = K > 0 ? K : SCAN_MAX_K;
-  constexpr bool kVecReads = K > 0 && K % 8 == 0;
+  constexpr int LPG = CW / 4, NG = 32 / LPG;  // lanes per group (one float4 each), groups per warp
+  // vector reads: each token's reads in two halves, one lane group each (the same sums in the same order for
+  // either slice width, so both give identical results), NG / 2 tokens per warp
+  constexpr int NP = 2, TPW = NG / NP;
+  constexpr bool kVecReads = K > 0 && K % (4 * NP) == 0;
   const int M = a.M, dh = a.dh, h = a.h, T = a.T;
   const int L = chunk_len(k);
   const RecLayout rl = rec_layout(k);
-  const ScanBuf sb = scan_buf_layout(k);
+  const ScanBuf sb = scan_buf_layout(k, CW);
   float4* P4 = reinterpret_cast<float4*>(smem);
   float* P = reinterpret_cast<float*>(smem);
-  float* Pc = reinterpret_cast<float*>(smem + align16((size_t)M * SCAN_CW * 4));
-  unsigned char* bufs = smem + scan_bufs_offset(M);
+  float* Pc = reinterpret_cast<float*>(smem + align16((size_t)M * CW * 4));
+  unsigned char* bufs = smem + scan_bufs_offset(M, CW);
   float* lampow = reinterpret_cast<float*>(bufs + 2 * sb.bytes);
 
   const int cs = blockIdx.x % n_slices;
   const int bh = blockIdx.x / n_slices;
   const int hh = bh % h, b = bh / h;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int grp = lane >> 3, c4 = lane & 7;
+  const int grp = lane / LPG, c4 = lane % LPG;
   const unsigned FULL = 0xffffffffu;
-  const int ncols = min(SCAN_CW, dh - cs * SCAN_CW);
+  const int ncols = min(CW, dh - cs * CW);
   const float lam = a.decay[hh];
   const int mode = fade_mode(lam);
   // fade 0: the intra pass already produced every read; only the final state (the last token's writes) is left
@@ -746,20 +752,20 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
 
   if (a.mem_in && mode != 0) {
     // the carried state (fade 0 keeps none of it past the first token, whose read the list kernel makes)
-    const float* mi = a.mem_in + ((int64_t)b * h + hh) * (int64_t)M * dh + cs * SCAN_CW;
-    for (int i = tid; i < M * SCAN_CW; i += SCAN_THREADS) {
-      const int r = i / SCAN_CW, cc = i % SCAN_CW;
+    const float* mi = a.mem_in + ((int64_t)b * h + hh) * (int64_t)M * dh + cs * CW;
+    for (int i = tid; i < M * CW; i += SCAN_THREADS) {
+      const int r = i / CW, cc = i % CW;
       P[i] = cc < ncols ? mi[(int64_t)r * dh + cc] : 0.f;
     }
     const float* ci = a.cnt_in + ((int64_t)b * h + hh) * (int64_t)M;
     for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] = ci[i];
   } else {
-    for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_THREADS) P4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = tid; i < M * (CW / 4); i += SCAN_THREADS) P4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] = 0.f;
   }
-  if (ncols < SCAN_CW) {  // columns past dh stay zero in both buffers (never copied, never stored)
-    for (int i = tid; i < 2 * L * SCAN_CW; i += SCAN_THREADS) {
-      const int bb = i / (L * SCAN_CW), j = i - bb * L * SCAN_CW;
+  if (ncols < CW) {  // columns past dh stay zero in both buffers (never copied, never stored)
+    for (int i = tid; i < 2 * L * CW; i += SCAN_THREADS) {
+      const int bb = i / (L * CW), j = i - bb * L * CW;
       reinterpret_cast<float*>(bufs + bb * sb.bytes + sb.V)[j] = 0.f;
       reinterpret_cast<float*>(bufs + bb * sb.bytes + sb.numi)[j] = 0.f;
     }
@@ -778,7 +784,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     }
     __syncthreads();
     if (tid == 0) {
-      scan_issue_tma(a, bufs, &full_bar[0], sb, rl, nch, c_begin, hdrs[c_begin], b, hh, cs, reads, &mapV, &mapN,
+      scan_issue_tma(a, bufs, &full_bar[0], sb, rl, nch, c_begin, hdrs[c_begin], b, hh, cs, CW, reads, &mapV, &mapN,
                      &mapD);
       if (c_begin + 1 < nch) hn = hdrs[c_begin + 1];
     }
@@ -786,7 +792,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     hd = hdrs[c_begin];
     hd1 = c_begin + 1 < nch ? hdrs[c_begin + 1] : make_int4(0, 0, 0, 0);
     __syncthreads();
-    scan_issue(a, bufs, sb, rl, nch, c_begin, hd, b, hh, cs, ncols, reads);
+    scan_issue(a, bufs, sb, rl, nch, c_begin, hd, b, hh, cs, ncols, CW, reads);
   }
 
   float sigma = 1.f;  // state = sigma * P
@@ -805,7 +811,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     } else {
       cp_async_wait_all();
       __syncthreads();
-      if (c + 1 < nch) scan_issue(a, bufs + (buf ^ 1) * sb.bytes, sb, rl, nch, c + 1, hd1, b, hh, cs, ncols, reads);
+      if (c + 1 < nch) scan_issue(a, bufs + (buf ^ 1) * sb.bytes, sb, rl, nch, c + 1, hd1, b, hh, cs, ncols, CW, reads);
       hd2 = c + 2 < nch ? hdrs[c + 2] : make_int4(0, 0, 0, 0);  // used two iterations on
     }
     const int njobs = hd.x, rd_end = hd.z, clear = hd.w;
@@ -820,46 +826,46 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
       const int dstr = use_tma ? 4 : 1, doff = use_tma ? (hh & 3) : 0;  // den of token t at deni[t * dstr + doff]
       const float sg = mode == 2 ? sigma : 1.f;
       if constexpr (kVecReads) {
-        // two eight-lane groups per token (reads [0, K/2) and [K/2, K)), two tokens per warp; read ids and weights
-        // four at a time; the halves are combined with one shuffle (the loop is warp-uniform, so every lane takes it)
-        const int half = grp & 1;
-        for (int tb = 2 * warp; tb < rd_end; tb += 2 * SCAN_WARPS) {
-          const int t = tb + (grp >> 1);
+        // two lane groups per token (reads [0, K/2) and [K/2, K)), TPW tokens per warp; read ids and weights four
+        // at a time; the halves are combined with one shuffle (the loop is warp-uniform, so every lane takes it)
+        const int half = grp % NP;
+        for (int tb = TPW * warp; tb < rd_end; tb += TPW * SCAN_WARPS) {
+          const int t = tb + grp / NP;
           const bool tv = t < rd_end;
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
           float dc = 0.f;
           if (tv) {
-            const int4* s4 = reinterpret_cast<const int4*>(sir_b + t * K + half * (K / 2));
-            const float4* w4 = reinterpret_cast<const float4*>(wr_b + t * K + half * (K / 2));
+            const int4* s4 = reinterpret_cast<const int4*>(sir_b + t * K + half * (K / NP));
+            const float4* w4 = reinterpret_cast<const float4*>(wr_b + t * K + half * (K / NP));
 #pragma unroll
-            for (int q = 0; q < K / 8; ++q) {
+            for (int q = 0; q < K / (4 * NP); ++q) {
               const int4 rr = s4[q];
               const float4 wv = w4[q];
               const int r0 = min(max(rr.x, 0), M - 1), r1 = min(max(rr.y, 0), M - 1);
               const int r2 = min(max(rr.z, 0), M - 1), r3 = min(max(rr.w, 0), M - 1);
-              fma4(acc, wv.x, P4[r0 * (SCAN_CW / 4) + c4]);
-              fma4(acc, wv.y, P4[r1 * (SCAN_CW / 4) + c4]);
-              fma4(acc, wv.z, P4[r2 * (SCAN_CW / 4) + c4]);
-              fma4(acc, wv.w, P4[r3 * (SCAN_CW / 4) + c4]);
+              fma4(acc, wv.x, P4[r0 * (CW / 4) + c4]);
+              fma4(acc, wv.y, P4[r1 * (CW / 4) + c4]);
+              fma4(acc, wv.z, P4[r2 * (CW / 4) + c4]);
+              fma4(acc, wv.w, P4[r3 * (CW / 4) + c4]);
               dc = fmaf(wv.x, Pc[r0], dc);
               dc = fmaf(wv.y, Pc[r1], dc);
               dc = fmaf(wv.z, Pc[r2], dc);
               dc = fmaf(wv.w, Pc[r3], dc);
             }
           }
-          acc.x += __shfl_xor_sync(FULL, acc.x, 8);
-          acc.y += __shfl_xor_sync(FULL, acc.y, 8);
-          acc.z += __shfl_xor_sync(FULL, acc.z, 8);
-          acc.w += __shfl_xor_sync(FULL, acc.w, 8);
-          dc += __shfl_xor_sync(FULL, dc, 8);
+          acc.x += __shfl_xor_sync(FULL, acc.x, LPG);
+          acc.y += __shfl_xor_sync(FULL, acc.y, LPG);
+          acc.z += __shfl_xor_sync(FULL, acc.z, LPG);
+          acc.w += __shfl_xor_sync(FULL, acc.w, LPG);
+          dc += __shfl_xor_sync(FULL, dc, LPG);
           if (!tv) continue;
           const float fade = sg * lampow[t];
           const int64_t tok = (int64_t)b * T + c0 + t;
           if (half == 0) {
-            const float4 ni = numi4[t * (SCAN_CW / 4) + c4];
+            const float4 ni = numi4[t * (CW / 4) + c4];
             const float o0 = fmaf(fade, acc.x, ni.x), o1 = fmaf(fade, acc.y, ni.y);
             const float o2 = fmaf(fade, acc.z, ni.z), o3 = fmaf(fade, acc.w, ni.w);
-            float* dst = a.num + (tok * h + hh) * dh + cs * SCAN_CW + 4 * c4;
+            float* dst = a.num + (tok * h + hh) * dh + cs * CW + 4 * c4;
             if (4 * c4 + 3 < ncols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
               *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
             } else {
@@ -873,7 +879,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
           }
         }
       } else {
-        // any k: warp per token, the four lane groups take reads g, g + 4, ...
+        // any k: warp per token, the NG lane groups take reads g, g + NG, ...
         for (int t = warp; t < rd_end; t += SCAN_WARPS) {
           int ri = 0;
           float wi = 0.f, pdi = 0.f;
@@ -884,14 +890,14 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
           }
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int q = 0; q < (KR + 3) / 4; ++q) {
-            const int ii = 4 * q + grp;
+          for (int q = 0; q < (KR + NG - 1) / NG; ++q) {
+            const int ii = NG * q + grp;
             const int r = __shfl_sync(FULL, ri, ii & 31);
             const float w = __shfl_sync(FULL, wi, ii & 31);
-            if (ii < k) fma4(acc, w, P4[r * (SCAN_CW / 4) + c4]);
+            if (ii < k) fma4(acc, w, P4[r * (CW / 4) + c4]);
           }
 #pragma unroll
-          for (int o = 8; o < 32; o <<= 1) {
+          for (int o = LPG; o < 32; o <<= 1) {
             acc.x += __shfl_xor_sync(FULL, acc.x, o);
             acc.y += __shfl_xor_sync(FULL, acc.y, o);
             acc.z += __shfl_xor_sync(FULL, acc.z, o);
@@ -901,10 +907,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
           const float fade = sg * lampow[t];
           const int64_t tok = (int64_t)b * T + c0 + t;
           if (grp == 0) {
-            const float4 ni = numi4[t * (SCAN_CW / 4) + c4];
+            const float4 ni = numi4[t * (CW / 4) + c4];
             const float o0 = fmaf(fade, acc.x, ni.x), o1 = fmaf(fade, acc.y, ni.y);
             const float o2 = fmaf(fade, acc.z, ni.z), o3 = fmaf(fade, acc.w, ni.w);
-            float* dst = a.num + (tok * h + hh) * dh + cs * SCAN_CW + 4 * c4;
+            float* dst = a.num + (tok * h + hh) * dh + cs * CW + 4 * c4;
             if (4 * c4 + 0 < ncols) dst[0] = o0;
             if (4 * c4 + 1 < ncols) dst[1] = o1;
             if (4 * c4 + 2 < ncols) dst[2] = o2;
@@ -937,14 +943,14 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
       }
     }
     if (pass) {
-      for (int i = tid; i < M * (SCAN_CW / 4); i += SCAN_THREADS) {
+      for (int i = tid; i < M * (CW / 4); i += SCAN_THREADS) {
         const float4 v = P4[i];
         P4[i] = make_float4(v.x * f, v.y * f, v.z * f, v.w * f);
       }
       for (int i = tid; i < M; i += SCAN_THREADS) Pc[i] *= f;
       __syncthreads();
     }
-    // writes: eight lanes per written slot, four slots per warp.  In TMA mode warp 0 instead issues the next
+    // writes: one lane group per written slot, NG slots per warp.  In TMA mode warp 0 instead issues the next
     // chunk's copies (each TMA instruction holds its thread for hundreds of cycles); their buffer has been free
     // since this chunk's first barrier.
     const int2* jobs = reinterpret_cast<const int2*>(cur + sb.rec);
@@ -953,13 +959,13 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     if (use_tma && warp == 0) {
       if (lane == 0 && c + 1 < nch) {
         tma::fence_proxy_async();
-        scan_issue_tma(a, bufs + (buf ^ 1) * sb.bytes, &full_bar[buf ^ 1], sb, rl, nch, c + 1, hn, b, hh, cs, reads,
-                       &mapV, &mapN, &mapD);
+        scan_issue_tma(a, bufs + (buf ^ 1) * sb.bytes, &full_bar[buf ^ 1], sb, rl, nch, c + 1, hn, b, hh, cs, CW,
+                       reads, &mapV, &mapN, &mapD);
         if (c + 2 < nch) hn = hdrs[c + 2];
       }
       __syncwarp();
     }
-    for (int jb = 4 * wwarp; wwarp >= 0 && jb < njobs; jb += 4 * nww) {
+    for (int jb = NG * wwarp; wwarp >= 0 && jb < njobs; jb += NG * nww) {
       const int j = jb + grp;
       if (j >= njobs) continue;
       const int2 jj = jobs[j];
@@ -970,12 +976,12 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
       for (int e = st; e < en; ++e) {
         const int2 q2 = ents[e];
         const float cf = __int_as_float(q2.y);
-        fma4(d, cf, V4[q2.x * (SCAN_CW / 4) + c4]);
+        fma4(d, cf, V4[q2.x * (CW / 4) + c4]);
         dc += cf;
       }
-      float4 p = P4[r * (SCAN_CW / 4) + c4];
+      float4 p = P4[r * (CW / 4) + c4];
       fma4(p, inv, d);
-      P4[r * (SCAN_CW / 4) + c4] = p;
+      P4[r * (CW / 4) + c4] = p;
       if (c4 == 0) Pc[r] = fmaf(inv, dc, Pc[r]);
     }
     hd = hd1;
@@ -986,8 +992,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
   const float fs = sigma;
   if (a.mem_out) {
     float* mo = a.mem_out + ((int64_t)b * h + hh) * (int64_t)M * dh;
-    for (int i = tid; i < M * SCAN_CW; i += SCAN_THREADS) {
-      const int r = i / SCAN_CW, cc = i % SCAN_CW, gc = cs * SCAN_CW + cc;
+    for (int i = tid; i < M * CW; i += SCAN_THREADS) {
+      const int r = i / CW, cc = i % CW, gc = cs * CW + cc;
       if (gc < dh) mo[(int64_t)r * dh + gc] = P[i] * fs;
     }
   }
@@ -999,7 +1005,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
 
 bool rt_scan_supported(int M, int dh, int k) {
   if (M < 1 || M > 65535 || dh < 1 || dh > LIST_MAX_DH || k < 1 || k > SCAN_MAX_K) return false;
-  return scan_smem_bytes(M, k) <= 227 * 1024 && list_layout(M, k, dh).total <= 227 * 1024;
+  return scan_smem_bytes(M, k, SCAN_CW) <= 227 * 1024 && list_layout(M, k, dh).total <= 227 * 1024;
 }
 
 size_t rt_scan_workspace_bytes(int B, int T, int h, int k) {
@@ -1013,34 +1019,54 @@ struct ScanMaps {
   int use_tma;
 };
 
-// TMA staging of the scan's chunk inputs: value and num slices of 32 columns (dh a multiple of 32), 1-D selection
+// TMA staging of the scan's chunk inputs: value and num slices of cw columns (dh a multiple of cw), 1-D selection
 // copies (k a multiple of 4), the 4-head den box (h a multiple of 4); else cp.async.
-static ScanMaps scan_maps(const ScanArgs& a) {
+static ScanMaps scan_maps(const ScanArgs& a, int cw) {
   ScanMaps m{};
   const int L = chunk_len(a.k);
   const uint64_t rows = (uint64_t)a.B * a.T;
-  const bool shape_ok = a.dh % SCAN_CW == 0 && a.k % 4 == 0 && a.h % 4 == 0 && (a.ldv % 4) == 0 &&
+  const bool shape_ok = a.dh % cw == 0 && a.k % 4 == 0 && a.h % 4 == 0 && (a.ldv % 4) == 0 &&
                         ((reinterpret_cast<uintptr_t>(a.sir) | reinterpret_cast<uintptr_t>(a.wr) |
                           reinterpret_cast<uintptr_t>(a.V) | reinterpret_cast<uintptr_t>(a.num) |
                           reinterpret_cast<uintptr_t>(a.den)) & 15) == 0;
   m.use_tma = shape_ok &&
               make_tensor_map_2d(&m.v, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.V, (uint64_t)a.h * a.dh, rows,
-                                 (uint64_t)a.ldv * 4, SCAN_CW, L, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                                 (uint64_t)a.ldv * 4, (uint32_t)cw, L, CU_TENSOR_MAP_SWIZZLE_NONE) &&
               make_tensor_map_2d(&m.num, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.num, (uint64_t)a.h * a.dh, rows,
-                                 (uint64_t)a.h * a.dh * 4, SCAN_CW, L, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                                 (uint64_t)a.h * a.dh * 4, (uint32_t)cw, L, CU_TENSOR_MAP_SWIZZLE_NONE) &&
               make_tensor_map_2d(&m.den, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.den, (uint64_t)a.h, rows,
                                  (uint64_t)a.h * 4, 4, L, CU_TENSOR_MAP_SWIZZLE_NONE);
   return m;
 }
 
+static int scan_num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cached[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+template <int K, int CW>
+static cudaError_t launch_state_scan(const ScanArgs& a, int nch, cudaStream_t st) {
+  const size_t ssm = scan_smem_bytes(a.M, a.k, CW);
+  cudaError_t e = cudaFuncSetAttribute(rt_scan_kernel<K, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm);
+  if (e != cudaSuccess) return e;
+  const int n_slices = (a.dh + CW - 1) / CW;
+  const ScanMaps m = scan_maps(a, CW);
+  LaunchScope scope_("rt_scan", st);
+  return launch_k(rt_scan_kernel<K, CW>, dim3((unsigned)((int64_t)a.B * a.h * n_slices)), dim3(SCAN_THREADS), ssm, st,
+                  a, nch, n_slices, m.v, m.num, m.den, m.use_tma);
+}
+
 template <int K, int DH>
-static cudaError_t launch_scan_k(const ScanArgs& a, int nch, int n_slices, cudaStream_t st) {
+static cudaError_t launch_scan_k(const ScanArgs& a, int nch, cudaStream_t st) {
   const size_t lsm = list_layout(a.M, a.k, a.dh).total;
   cudaError_t e =
       cudaFuncSetAttribute(rt_lists_kernel<K, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsm);
-  if (e != cudaSuccess) return e;
-  const size_t ssm = scan_smem_bytes(a.M, a.k);
-  e = cudaFuncSetAttribute(rt_scan_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm);
   if (e != cudaSuccess) return e;
   {
     LaunchScope scope_("rt_lists", st);
@@ -1048,22 +1074,25 @@ static cudaError_t launch_scan_k(const ScanArgs& a, int nch, int n_slices, cudaS
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  const ScanMaps m = scan_maps(a);
-  LaunchScope scope_("rt_scan", st);
-  return launch_k(rt_scan_kernel<K>, dim3((unsigned)((int64_t)a.B * a.h * n_slices)), dim3(SCAN_THREADS), ssm, st, a,
-                  nch, n_slices, m.v, m.num, m.den, m.use_tma);
+  // Each state CTA holds an SM for the whole window: when the 32-column slices of this launch would occupy at most
+  // half the SMs (a few rows per GPU), 16-column slices halve each CTA's shared-memory work and use twice the SMs.
+  if constexpr (K == 16) {
+    const int64_t ctas32 = (int64_t)a.B * a.h * ((a.dh + SCAN_CW - 1) / SCAN_CW);
+    if (2 * ctas32 <= scan_num_sms() && scan_smem_bytes(a.M, a.k, SCAN_CW_SMALL) <= 227 * 1024)
+      return launch_state_scan<K, SCAN_CW_SMALL>(a, nch, st);
+  }
+  return launch_state_scan<K, SCAN_CW>(a, nch, st);
 }
 
 cudaError_t launch_rt_scan(const ScanArgs& a, cudaStream_t st) {
   if (a.B == 0 || a.T == 0) return cudaSuccess;
   if (!a.rec || !rt_scan_supported(a.M, a.dh, a.k)) return cudaErrorInvalidValue;
   const int nch = (a.T + chunk_len(a.k) - 1) / chunk_len(a.k);
-  const int n_slices = (a.dh + SCAN_CW - 1) / SCAN_CW;
-  if (a.k == 16 && a.dh == 64) return launch_scan_k<16, 64>(a, nch, n_slices, st);
+  if (a.k == 16 && a.dh == 64) return launch_scan_k<16, 64>(a, nch, st);
   switch (a.k) {
-    case 16: return launch_scan_k<16, 0>(a, nch, n_slices, st);
-    case 4: return launch_scan_k<4, 0>(a, nch, n_slices, st);
-    default: return launch_scan_k<0, 0>(a, nch, n_slices, st);
+    case 16: return launch_scan_k<16, 0>(a, nch, st);
+    case 4: return launch_scan_k<4, 0>(a, nch, st);
+    default: return launch_scan_k<0, 0>(a, nch, st);
   }
 }
 

@@ -362,6 +362,78 @@ def test_scan_abi_against_token_recurrence(cuda_ok, dup):
         assert rel(cnt.cpu().numpy(), want_cnt) < 1e-5
 
 
+@pytest.mark.parametrize("B", [2, 10])
+def test_scan_skewed_hits_against_token_recurrence(cuda_ok, B):
+    """sdm_rt_scan at the bench's shape class (k 16, dh 64, 1,024 slots) with Zipf-like repetition: half the tokens
+    reuse one of three fixed selections, so a few tokens meet hundreds of earlier writes of their chunk while others
+    meet none.  Every fade mode, BOS resets and a ragged last chunk; against the oracle's token recurrence
+    (M:285-299).  B 2 runs the state scan on 16-column slices (few rows: 2 x 4 x 2 slices of 32 columns would fill
+    under half the SMs), B 10 on 32-column slices."""
+    from sdmchat_b200 import _lib
+    lib = _lib.lib()
+    rng = np.random.default_rng(11 + B)
+    h, T, n_sub, k, dh = 4, 200, 32, 16, 64
+    M = n_sub * n_sub
+    pool = [rng.choice(M, k, replace=False) for _ in range(3)]
+
+    def sel():
+        out = np.stack([rng.choice(M, k, replace=False) for _ in range(B * h * T)])
+        pick = rng.random(B * h * T)
+        for j in range(3):
+            m = (pick >= 0.5 + j / 6) & (pick < 0.5 + (j + 1) / 6)
+            out[m] = rng.permutation(pool[j])
+        return out.reshape(B, h, T, k).astype(np.int32)
+    siw, sir = sel(), sel()
+    ww = rng.random((B, h, T, k)).astype(np.float32)
+    wr = rng.random((B, h, T, k)).astype(np.float32)
+    V = rng.standard_normal((B, h, T, dh)).astype(np.float32)
+    lam = np.array([0.0, 0.8, 0.99, 1.0], np.float32)
+    reset = rng.random((B, T)) < 0.02
+    reset[1, 64] = True
+    want_num, want_den, want_mem, want_cnt = O.rt_scan_sequential(dict(siw=siw, ww=ww, sir=sir, wr=wr, V=V), lam, M,
+                                                                  reset)
+    Vt = t(V.transpose(0, 2, 1, 3).reshape(B * T, h * dh))
+    num = torch.empty(B, T, h, dh, device=DEV)
+    den = torch.empty(B, T, h, device=DEV)
+    mem = torch.empty(B, h, M, dh, device=DEV)
+    cnt = torch.empty(B, h, M, device=DEV)
+    ws = torch.empty(lib.sdm_rt_scan_workspace_size(B, T, h, k), dtype=torch.uint8, device=DEV)
+    args = [t(siw), t(ww), t(sir), t(wr), Vt]
+    lam_d, reset_d = t(lam), t(reset.astype(np.uint8))
+    outs = []
+    for _ in range(2):  # deterministic: two runs agree bit for bit
+        st = lib.sdm_rt_scan(*map(_lib.ptr, args), h * dh, _lib.ptr(lam_d), _lib.ptr(reset_d), B, T, h, n_sub, dh, k,
+                             None, None, _lib.ptr(num), _lib.ptr(den), _lib.ptr(mem), _lib.ptr(cnt), _lib.ptr(ws),
+                             ws.numel(), _lib.stream_ptr(torch.device(DEV)))
+        _lib.check(st, "sdm_rt_scan")
+        torch.cuda.synchronize()
+        outs.append((num.clone(), den.clone()))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    # causal bit for bit: a later token of the same chunk turned into one more copy of a pooled selection (more
+    # hits, a different split of the chunk's work) leaves every earlier token's num and den unchanged
+    p = 150
+    siw2, sir2 = siw.copy(), sir.copy()
+    siw2[:, :, p], sir2[:, :, p] = pool[0], pool[0]
+    args2 = [t(siw2), t(ww), t(sir2), t(wr), Vt]
+    num2, den2 = torch.empty_like(num), torch.empty_like(den)
+    _lib.check(lib.sdm_rt_scan(*map(_lib.ptr, args2), h * dh, _lib.ptr(lam_d), _lib.ptr(reset_d), B, T, h, n_sub, dh,
+                               k, None, None, _lib.ptr(num2), _lib.ptr(den2), _lib.ptr(mem), _lib.ptr(cnt),
+                               _lib.ptr(ws), ws.numel(), _lib.stream_ptr(torch.device(DEV))), "sdm_rt_scan")
+    torch.cuda.synchronize()
+    assert torch.equal(num2[:, :p], outs[0][0][:, :p]) and torch.equal(den2[:, :p], outs[0][1][:, :p])
+    assert not torch.equal(num2[:, p:], outs[0][0][:, p:])
+    # the reference outputs (mem, cnt of the first run are overwritten above: recompute them)
+    st = lib.sdm_rt_scan(*map(_lib.ptr, args), h * dh, _lib.ptr(lam_d), _lib.ptr(reset_d), B, T, h, n_sub, dh, k,
+                         None, None, _lib.ptr(num), _lib.ptr(den), _lib.ptr(mem), _lib.ptr(cnt), _lib.ptr(ws),
+                         ws.numel(), _lib.stream_ptr(torch.device(DEV)))
+    _lib.check(st, "sdm_rt_scan")
+    torch.cuda.synchronize()
+    assert rel(num.cpu().numpy().transpose(0, 2, 1, 3), want_num) < 1e-5
+    assert rel(den.cpu().numpy().transpose(0, 2, 1), want_den.reshape(B, h, T)) < 1e-5
+    assert rel(mem.cpu().numpy(), want_mem) < 1e-5
+    assert rel(cnt.cpu().numpy(), want_cnt) < 1e-5
+
+
 def test_trained_sdm_decode_sized_equals_batched(cuda_ok):
     """Decode-sized TrainedSdm calls select and read in one launch (ts_addr_gather_kernel); large calls use the
     addressing kernel and the batched gather.  The selections are identical and the reads agree to float32
