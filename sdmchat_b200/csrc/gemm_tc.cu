@@ -564,8 +564,11 @@ static cudaError_t launch_tc_bn(const bf16_t* x, int64_t ldx, const bf16_t* w, i
   auto kern = tc::gemm_tc_kernel<Epi, BN>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
+  // as few CTAs as finish the tiles in the same number of rounds: the SMs left over stay free for kernels of other
+  // streams (rows split over streams run side by side)
   const int64_t tiles = ceil_div(n, BN) * ceil_div(rows, tc::BM);
-  const int grid = (int)(tiles < tc::num_sms() ? tiles : tc::num_sms());
+  const int64_t rounds = ceil_div(tiles, (int64_t)tc::num_sms());
+  const int grid = (int)ceil_div(tiles, rounds);
   LaunchScope scope_("gemm_tc", st);
   return launch_k(kern, dim3(grid), dim3(tc::THREADS), C::SMEM_BYTES, st, ma, mb, rows, K, n, epi, kwrap);
 }
@@ -599,7 +602,7 @@ static cudaError_t launch_tc_pair(const bf16_t* x, int64_t ldx, const bf16_t* w,
     pairs_cap = max_pairs[dev] < pairs_cap ? max_pairs[dev] : pairs_cap;
   }
   const int64_t tiles = ceil_div(n, tc::PAIR_N) * ceil_div(rows, 2 * tc::BM);
-  const int pairs = (int)(tiles < pairs_cap ? tiles : pairs_cap);
+  const int pairs = (int)ceil_div(tiles, ceil_div(tiles, (int64_t)pairs_cap));  // same rounds, fewest pairs
   LaunchScope scope_("gemm_tc", st);
   return launch_k(kern, dim3(2 * pairs), dim3(tc::THREADS), C::SMEM_BYTES, st, ma, mb, rows, K, n, epi, kwrap);
 }

@@ -194,7 +194,9 @@ struct EpiResid {
 // Row-owned epilogues of the tied head (the tensor-core GEMM only): each epilogue thread owns one row of a
 // 128-column tile and reduces it in registers.  Logits are rounded to bfloat16 first, as the bf16 head stores them.
 // EpiCE: online logsumexp per (row, column tile) -> part[row * tiles_n + tile] = (max, sum exp(x - max)); the
-// target's logit -> tgt_logit[row].  ce_combine folds the partials into the summed cross-entropy.
+// target's logit -> tgt_logit[row].  ce_combine folds the partials into the summed cross-entropy.  The exponentials
+// of the max-shifted logits (all <= 0) use the hardware exponential __expf (relative error about 1e-6 there), summed
+// in four interleaved partial sums; the loss is a float64 sum of per-row terms, so this stays near 1e-7 relative.
 struct EpiCE {
   static constexpr bool kRowMode = true;
   const int32_t* targets;
@@ -213,19 +215,30 @@ struct EpiCE {
     rs.tgt = row < rows ? targets[row] : -1;
   }
   __device__ __forceinline__ void row_chunk(RowState& rs, int col0, int n, const uint32_t (&r)[32]) const {
+    if (col0 >= n) return;  // past the last column
     float v[32];
-    float cmax = -INFINITY;
+    if (col0 + 32 <= n) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      v[j] = col0 + j < n ? bf16_round(__uint_as_float(r[j])) : -INFINITY;
-      cmax = fmaxf(cmax, v[j]);
+      for (int j = 0; j < 32; j += 2) {  // the logits rounded to bfloat16, two per conversion
+        const __nv_bfloat162 p = __floats2bfloat162_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+        v[j] = __low2float(p);
+        v[j + 1] = __high2float(p);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = col0 + j < n ? bf16_round(__uint_as_float(r[j])) : -INFINITY;
     }
-    const float mn = fmaxf(rs.m, cmax);
-    float s = rs.m == -INFINITY ? 0.f : rs.s * expf(rs.m - mn);
+    float m4[4] = {v[0], v[1], v[2], v[3]};  // four independent chains, then a tree
 #pragma unroll
-    for (int j = 0; j < 32; ++j) s += v[j] == -INFINITY ? 0.f : expf(v[j] - mn);
+    for (int j = 4; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], v[j]);
+    const float cmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+    const float mn = fmaxf(rs.m, cmax);  // finite: column col0 is a real logit
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s4[j & 3] += __expf(v[j] - mn);  // exp(-inf) = 0 for columns past n
+    const float s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+    rs.s = (rs.m == -INFINITY ? 0.f : rs.s * __expf(rs.m - mn)) + s;
     rs.m = mn;
-    rs.s = s;
     const int t = rs.tgt - col0;
     if (t >= 0 && t < 32) {
 #pragma unroll
