@@ -284,7 +284,9 @@ struct EpiArgmax {
 // columns [32j, 32j + 16) are gate rows [16j, 16j + 16) and [32j + 16, 32j + 32) the up rows of the same f-indices,
 // so one thread's 32-column chunk holds both factors of 16 outputs.  Each is rounded as the bfloat16 reference
 // rounds: g and u (the Linear outputs), silu(g), then the product; only p = silu(g) * u reaches memory (bfloat16,
-// (rows, f) with row stride ldp, 32-byte row segments).
+// (rows, f) with row stride ldp, 32-byte row segments).  silu(g) = g / (1 + e^-g) with the hardware exponential and
+// division (a few 1e-7 relative before its bfloat16 rounding, which it changes only within that distance of a
+// rounding boundary).
 struct EpiSwiGLU {
   static constexpr bool kRowMode = true;
   bf16_t* p;
@@ -307,7 +309,7 @@ struct EpiSwiGLU {
       for (int j = 0; j < 2; ++j) {
         const float g = bf16_round(__uint_as_float(r[2 * i + j]));
         const float u = bf16_round(__uint_as_float(r[16 + 2 * i + j]));
-        v[j] = bf16_round(g / (1.f + expf(-g))) * u;
+        v[j] = bf16_round(__fdividef(g, 1.f + __expf(-g))) * u;
       }
       const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[0], v[1]);
       o[i] = *reinterpret_cast<const uint32_t*>(&b2);
