@@ -57,8 +57,8 @@ __device__ __forceinline__ void warp_half_list_own(const float* zh, bool zvec, c
 // the selections come in siw/ww/sir/wr.  KM bounds k at
 // compile time: the touched rows are held in registers (four KM-long arrays), and KM 16 (for k <= 16) keeps the
 // block at about half the registers of KM 32, so twice as many (stream, head) blocks are resident.
-// LBT, LBM: launch bounds (threads, resident blocks per SM); 128 threads x 6 blocks caps the register use at 80 so that
-// six (stream, head) blocks share an SM instead of five.
+// LBT, LBM: launch bounds (threads, resident blocks per SM); 128 threads x 8 blocks caps the register use at 64 (a few
+// spilled words) so that eight (stream, head) blocks share an SM instead of five.
 template <typename T, int HALF, int S, int SH, int KM, int LBT = 1024, int LBM = 1>
 __global__ void __launch_bounds__(LBT, LBM) rt_decode_kernel(DecodeArgs a) {
   pdl_enter();
@@ -254,7 +254,7 @@ static cudaError_t launch_rt_decode_fused(const DecodeArgs& a, int threads, cuda
   const size_t smem = ((size_t)2 * a.n_sub * 16 + 2 * 128 + 32 * S) * 4;
   void (*kern)(DecodeArgs) = rt_decode_kernel<T, 16, S, SH, KM>;
   if constexpr (KM == 16)
-    if (threads == 128) kern = rt_decode_kernel<T, 16, S, SH, KM, 128, 6>;
+    if (threads == 128) kern = rt_decode_kernel<T, 16, S, SH, KM, 128, 8>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_k(kern, dim3((unsigned)((int64_t)a.S * a.h)), dim3(threads), smem, st, a);

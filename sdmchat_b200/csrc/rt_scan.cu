@@ -329,13 +329,21 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
     for (int r = tid; r < M; r += LIST_THREADS) tmask[r] = 0ull;
     if (tid == 0) misc[11] = 0;
     __syncthreads();
-#pragma unroll
-    for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
-      const int e = tid + q * LIST_THREADS;
-      if (e < E) {
-        const int t = e / k;
-        const unsigned long long old = atomicOr(&tmask[siw_s[e]], 1ull << t);
-        if ((old >> t) & 1ull) misc[11] = 1;
+    // a warp takes one write index i of 32 consecutive tokens, so a slot that several of them write (repeated
+    // tokens) is set by one atomic per warp: the lanes writing the same slot are matched and their token bits are
+    // the matched lane mask shifted to the warp's first token
+    for (int p = warp; p < k * 2; p += LIST_WARPS) {
+      const int i = p % k, t = (p / k) * 32 + lane;
+      const bool ok = t < Lc;
+      const unsigned act = __ballot_sync(FULL, ok);
+      if (ok) {
+        const int r = siw_s[t * k + i];
+        const unsigned peers = __match_any_sync(act, r);
+        if (lane == __ffs(peers) - 1) {
+          const unsigned long long bits = (unsigned long long)peers << ((p / k) * 32);
+          const unsigned long long old = atomicOr(&tmask[r], bits);
+          if (old & bits) misc[11] = 1;
+        }
       }
     }
     __syncthreads();
