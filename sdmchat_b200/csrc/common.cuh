@@ -21,6 +21,15 @@ template <typename T> __device__ __forceinline__ float round_to(float x);
 template <> __device__ __forceinline__ float round_to<float>(float x) { return x; }
 template <> __device__ __forceinline__ float round_to<bf16_t>(float x) { return bf16_round(x); }
 
+// x / d for several x over one d, from inv = __frcp_rn(d) (the correctly rounded reciprocal): the product x * inv
+// corrected once by its exact residual, q + (x - q d) * inv with fused multiply-adds (Markstein's division step,
+// which gives the correctly rounded quotient; tests/test_division_cpu.py checks it against IEEE division).  Three
+// instructions per quotient instead of a full division each.
+__device__ __forceinline__ float div_rn_by(float x, float d, float inv) {
+  const float q = x * inv;
+  return fmaf(fmaf(-q, d, x), inv, q);
+}
+
 // Correctly rounded 1/sqrt(v): sqrt then divide, both IEEE round-to-nearest, as the CPU reference computes
 // torch.rsqrt (a square root and a division).
 __device__ __forceinline__ float rsqrt_rn(float v) { return __fdiv_rn(1.0f, __fsqrt_rn(v)); }

@@ -275,6 +275,80 @@ __global__ void __launch_bounds__(SMT_WARPS * 32) gemm_small_tc_kernel(const bf1
   if (row < rows && col < n) epi.apply(row0 + row, col, v);
 }
 
+// The same product with a 32 x 32 output tile per CTA (n >= 32): each CTA reads its 32 rows of x once for 32 columns
+// instead of 8, a quarter of the x traffic from L2, which bounds the 8-column tiles at a few hundred rows.  The
+// eight warps split K in 32-wide blocks (warp w takes blocks w, w + 8, ...); inside a block thread t of a quad
+// holds 8 consecutive k of its A rows and of its four B columns (one 16-byte load each) and feeds them to two k-steps
+// (values 4s .. 4s+3 of step s, the same permutation for A and B); 2 x 4 accumulator tiles per warp, the 8 partial
+// 32 x 32 tiles summed in shared memory in warp order (deterministic).
+template <typename Epi>
+__global__ void __launch_bounds__(SMT_WARPS * 32) gemm_small_tc32_kernel(const bf16_t* __restrict__ x, int64_t ldx,
+                                                                        const bf16_t* __restrict__ w, int64_t ldw,
+                                                                        int rows, int K, int n, Epi epi, int kwrap) {
+  pdl_enter();
+  __shared__ float part[SMT_WARPS][32][33];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row0 = blockIdx.y * 32;
+  x += (int64_t)row0 * ldx;
+  rows -= row0;
+  const int g = lane >> 2, t = lane & 3;
+  const int n0 = blockIdx.x * 32;
+  const bf16_t* wrow[4];
+  bool bval[4];
+#pragma unroll
+  for (int ct = 0; ct < 4; ++ct) {
+    const int nb = n0 + ct * 8 + g;  // this thread's B column of column tile ct
+    bval[ct] = nb < n;
+    wrow[ct] = w + (int64_t)(nb < n ? nb : n - 1) * ldw;
+  }
+  float c[2][4][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int ct = 0; ct < 4; ++ct)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c[mt][ct][e] = 0.f;
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  for (int kb = warp; kb < K / 32; kb += SMT_WARPS) {
+    const int k = kb * 32 + 8 * t, kw = k % kwrap;
+    uint4 b[4], a[2][2];  // a: [row tile][row g | g + 8]
+#pragma unroll
+    for (int ct = 0; ct < 4; ++ct) b[ct] = bval[ct] ? *reinterpret_cast<const uint4*>(wrow[ct] + kw) : z4;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int rh = 0; rh < 2; ++rh) {
+        const int row = mt * 16 + rh * 8 + g;
+        a[mt][rh] = row < rows ? *reinterpret_cast<const uint4*>(x + (int64_t)row * ldx + k) : z4;
+      }
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int ct = 0; ct < 4; ++ct)
+          mma_bf16_16816(c[mt][ct], u4w(a[mt][0], 2 * s2), u4w(a[mt][1], 2 * s2), u4w(a[mt][0], 2 * s2 + 1),
+                         u4w(a[mt][1], 2 * s2 + 1), u4w(b[ct], 2 * s2), u4w(b[ct], 2 * s2 + 1));
+  }
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int ct = 0; ct < 4; ++ct) {
+      part[warp][mt * 16 + g][ct * 8 + 2 * t] = c[mt][ct][0];
+      part[warp][mt * 16 + g][ct * 8 + 2 * t + 1] = c[mt][ct][1];
+      part[warp][mt * 16 + g + 8][ct * 8 + 2 * t] = c[mt][ct][2];
+      part[warp][mt * 16 + g + 8][ct * 8 + 2 * t + 1] = c[mt][ct][3];
+    }
+  __syncthreads();
+  for (int o = tid; o < 32 * 32; o += SMT_WARPS * 32) {
+    const int row = o >> 5, cc = o & 31, col = n0 + cc;
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < SMT_WARPS; ++q) v += part[q][row][cc];
+    if (row < rows && col < n) epi.apply(row0 + row, col, v);
+  }
+}
+
 static bool small_tc_ok(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K, int kwrap) {
   const uintptr_t ax = reinterpret_cast<uintptr_t>(x), aw = reinterpret_cast<uintptr_t>(w);
   return rows >= 1 && rows <= SMT_MAX_ROWS && K % 64 == 0 && kwrap % 64 == 0 && ldx % 8 == 0 && ldw % 8 == 0 &&
@@ -290,6 +364,10 @@ cudaError_t launch_gemm(const TA* x, int64_t ldx, const TA* w, int64_t ldw, int6
   if constexpr (sizeof(TA) == 2) {
     if (small_tc_ok(x, ldx, w, ldw, rows, K, kwrap)) {
       LaunchScope scope_("gemm_small_tc", st);
+      // 32-column tiles when they still give every SM a CTA (a few hundred rows), else 8-column tiles
+      if (n >= 32 && K % 32 == 0 && kwrap % 32 == 0 && ceil_div(n, 32) * ceil_div(rows, 32) >= 148)
+        return launch_k(gemm_small_tc32_kernel<Epi>, dim3((unsigned)ceil_div(n, 32), (unsigned)ceil_div(rows, 32)),
+                        dim3(SMT_WARPS * 32), 0, st, x, ldx, w, ldw, (int)rows, K, n, epi, kwrap);
       return launch_k(gemm_small_tc_kernel<Epi>, dim3((unsigned)ceil_div(n, 8), (unsigned)ceil_div(rows, 32)),
                       dim3(SMT_WARPS * 32), 0, st, x, ldx, w, ldw, (int)rows, K, n, epi, kwrap);
     }

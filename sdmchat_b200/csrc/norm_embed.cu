@@ -185,6 +185,9 @@ __global__ void __launch_bounds__(256) rt_finish_vec_kernel(const float* __restr
     for (int q = 0; q < STEPS; ++q) vals[i][q] = nr[g * STEPS + q];  // lane g: columns g*dh/8 .. +dh/8-1
     dv[i] = read_sum ? 0.f : den[it] + read_eps;
   }
+  float inv[FIN_ROWS];
+#pragma unroll
+  for (int i = 0; i < FIN_ROWS; ++i) inv[i] = read_sum ? 1.f : __frcp_rn(dv[i]);
 #pragma unroll
   for (int i = 0; i < FIN_ROWS; ++i) {
     float ss = 0.f;
@@ -192,10 +195,10 @@ __global__ void __launch_bounds__(256) rt_finish_vec_kernel(const float* __restr
     for (int q = 0; q < STEPS; ++q) {
       float4 v = vals[i][q];
       if (!read_sum) {
-        v.x = __fdiv_rn(v.x, dv[i]);
-        v.y = __fdiv_rn(v.y, dv[i]);
-        v.z = __fdiv_rn(v.z, dv[i]);
-        v.w = __fdiv_rn(v.w, dv[i]);
+        v.x = div_rn_by(v.x, dv[i], inv[i]);
+        v.y = div_rn_by(v.y, dv[i], inv[i]);
+        v.z = div_rn_by(v.z, dv[i], inv[i]);
+        v.w = div_rn_by(v.w, dv[i], inv[i]);
       }
       ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
       vals[i][q] = v;
@@ -441,9 +444,11 @@ cudaError_t launch_rt_finish(const float* num, const float* den, int64_t N, int 
                   read_sum, read_eps, out_norm, out_norm_eps, onorm_w, r, split);
 }
 // TrainedSdm address + read for decode-sized launches (track4_onesdm_models.py:438-456), one block of four warps
-// per (token, head): warp 0 selects the slots (the warp-per-address selection of the addressing kernels, so the
-// picks are identical) into shared memory and global memory (si, w), then the four warps gather the picked
-// value rows as ts_gather_split_kernel does.  Saves the separate addressing launch of every decode step.
+// per (token, head): warps 0 and 1 build the two halves' sorted lists (each lane normalising and scoring its own
+// sub-keys) while warp 2 lists the candidate pairs, warp 0 combines them (the warp-per-address selection of the
+// addressing kernels, so the picks are identical) into shared memory and global memory (si, w), then the four
+// warps gather the picked value rows as ts_gather_split_kernel does.  Saves the separate addressing launch of every
+// decode step.
 template <int HALF, int S>
 __global__ void __launch_bounds__(128) ts_addr_gather_kernel(const float* __restrict__ q, int64_t ldq,
                                                              const float* __restrict__ keys1,
@@ -453,7 +458,7 @@ __global__ void __launch_bounds__(128) ts_addr_gather_kernel(const float* __rest
                                                              int h, int dh, int32_t* __restrict__ si,
                                                              float* __restrict__ w, bf16_t* __restrict__ r, int split) {
   pdl_enter();
-  extern __shared__ float tsd_smem[];  // sub-keys (2 x n_sub x HALF), warp scratch (128), candidates (32 S)
+  extern __shared__ float tsd_smem[];  // warp scratch (128), candidates (32 S)
   __shared__ float part[4][256];
   __shared__ int s_si[32];
   __shared__ float s_w[32];
@@ -462,27 +467,17 @@ __global__ void __launch_bounds__(128) ts_addr_gather_kernel(const float* __rest
   const int64_t item = blockIdx.x;
   const int hh = (int)(item % h);
   const int64_t n = item / h;
-  float* kn = tsd_smem;
-  int* cand = reinterpret_cast<int*>(kn + 2 * n_sub * HALF + 128);
-  for (int j = threadIdx.x; j < 2 * n_sub; j += blockDim.x) {  // F.normalize(keys, dim=-1) for this head
-    const float* src = (j < n_sub ? keys1 + ((int64_t)hh * n_sub + j) * HALF
-                                  : keys2 + ((int64_t)hh * n_sub + (j - n_sub)) * HALF);
-    float kv[HALF];
-    normalize_half<HALF>(src, kv);
-#pragma unroll
-    for (int dd = 0; dd < HALF; ++dd) kn[j * HALF + dd] = kv[dd];
-  }
+  float* wsm = tsd_smem;  // v1, i1, v2, i2
+  int* cand = reinterpret_cast<int*>(tsd_smem + 128);
   const int c1 = kk < n_sub ? kk : n_sub;
-  if (warp == 0) {
+  if (warp < 2) {  // the two halves' lists in parallel, each lane normalising its own sub-keys
+    const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(q) & 15) | (ldq & 3) | (d_a & 3)) == 0;
+    const float* keys = (warp ? keys2 : keys1) + (int64_t)hh * n_sub * HALF;
+    warp_half_list_own<HALF, S>(q + n * ldq + (int64_t)hh * d_a + warp * HALF, zvec, keys, n_sub, c1, wsm + warp * 64,
+                                reinterpret_cast<int*>(wsm + warp * 64 + 32));
+  } else if (warp == 2) {
     const int nc = warp_candidates(cand, c1, kk);
     if (lane == 0) s_nc = nc;
-  }
-  __syncthreads();
-  float* wsm = kn + 2 * n_sub * HALF;  // v1, i1, v2, i2
-  if (warp < 2) {  // the two halves' lists in parallel
-    const bool zvec = HALF % 4 == 0 && ((reinterpret_cast<uintptr_t>(q) & 15) | (ldq & 3) | (d_a & 3)) == 0;
-    warp_half_list<HALF, S>(q + n * ldq + (int64_t)hh * d_a + warp * HALF, zvec, kn + warp * n_sub * HALF, n_sub,
-                            c1, wsm + warp * 64, reinterpret_cast<int*>(wsm + warp * 64 + 32));
   }
   __syncthreads();
   if (warp == 0) {
@@ -543,7 +538,7 @@ static cudaError_t launch_ts_addr_gather_s(const float* q, int64_t ldq, const fl
                                            const float* log_scale, int n_sub, int kk, const bf16_t* values,
                                            int64_t N, int h, int dh, int32_t* si, float* w, bf16_t* r, int split,
                                            cudaStream_t st) {
-  const size_t smem = ((size_t)2 * n_sub * 16 + 128 + 32 * S) * 4;
+  const size_t smem = ((size_t)128 + 32 * S) * 4;
   auto kern = ts_addr_gather_kernel<16, S>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

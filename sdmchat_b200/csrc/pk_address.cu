@@ -776,11 +776,11 @@ __global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_fast_kernel(
           sum += sc[j];
         }
       }
-      const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
+      const float g = gb ? gb[n * a.ldgate + hh] : 1.f, isum = __frcp_rn(sum);
 #pragma unroll
       for (int j = 0; j < C; ++j) {
         if (j < kk) {
-          const float wj = __fdiv_rn(sc[j], sum);
+          const float wj = div_rn_by(sc[j], sum, isum);
           sc[j] = gb ? wj * g : wj;
         }
       }
@@ -830,9 +830,9 @@ __global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_fast_kernel(
       float mx = -INFINITY, sum = 0.f;
       for (int j = 0; j < kk; ++j) mx = fmaxf(mx, pick_score(j) * scale);
       for (int j = 0; j < kk; ++j) sum += expf(pick_score(j) * scale - mx);
-      const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
+      const float g = gb ? gb[n * a.ldgate + hh] : 1.f, isum = __frcp_rn(sum);
       auto wt = [&](int j) {
-        const float wj = __fdiv_rn(expf(pick_score(j) * scale - mx), sum);
+        const float wj = div_rn_by(expf(pick_score(j) * scale - mx), sum, isum);
         return gb ? wj * g : wj;
       };
       if (vec) {
@@ -1061,9 +1061,9 @@ __global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_tc_kernel(Pk
     for (int e = 0; e < 8; ++e) ss = fmaf(kv[e], kv[e], ss);
     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
     // F.normalize: v / max(||v||, 1e-12), the norm as the sum of squares' correctly rounded square root
-    const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
+    const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f), inv = __frcp_rn(nrm);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) kv[e] = __fdiv_rn(kv[e], nrm);
+    for (int e = 0; e < 8; ++e) kv[e] = div_rn_by(kv[e], nrm, inv);
     pktc::put_chunk(opB, pktc::B_PART, rowb, hf * 2 + part, kv);
     const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     pktc::put_chunk(opB, pktc::B_PART, rowb, (1 - hf) * 2 + part, zero);
@@ -1076,9 +1076,9 @@ __global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_tc_kernel(Pk
       float ss = 0.f;
 #pragma unroll
       for (int dd = 0; dd < HALF; ++dd) ss = fmaf(zraw[hf * HALF + dd], zraw[hf * HALF + dd], ss);
-      const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
+      const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f), inv = __frcp_rn(nrm);
 #pragma unroll
-      for (int dd = 0; dd < HALF; ++dd) zraw[hf * HALF + dd] = live ? __fdiv_rn(zraw[hf * HALF + dd], nrm) : 0.f;
+      for (int dd = 0; dd < HALF; ++dd) zraw[hf * HALF + dd] = live ? div_rn_by(zraw[hf * HALF + dd], nrm, inv) : 0.f;
     }
     pktc::put_row(opA, pktc::A_PART, tid, zraw);
   }
@@ -1159,11 +1159,11 @@ __global__ void __launch_bounds__(PKF_THREADS, PkfOcc<C>::value) pk_tc_kernel(Pk
         sum += sc[j];
       }
     }
-    const float g = gb ? gb[n * a.ldgate + hh] : 1.f;
+    const float g = gb ? gb[n * a.ldgate + hh] : 1.f, isum = __frcp_rn(sum);
 #pragma unroll
     for (int j = 0; j < C; ++j) {
       if (j < kk) {
-        const float wj = __fdiv_rn(sc[j], sum);
+        const float wj = div_rn_by(sc[j], sum, isum);
         sc[j] = gb ? wj * g : wj;
       }
     }

@@ -45,8 +45,9 @@ __device__ __forceinline__ float half_dot(const float (&zn)[HALF], const float* 
 }
 
 // F.normalize of one half: src[0..HALF) / max(||src||, 1e-12).  vec: src is 16-byte aligned (HALF a multiple
-// of 4) and is read four floats at a time.
-template <int HALF>
+// of 4) and is read four floats at a time.  RCP: the quotients from one reciprocal (div_rn_by), else one IEEE
+// division each (fewer live registers, for register-capped kernels); both are correctly rounded.
+template <int HALF, bool RCP = true>
 __device__ __forceinline__ void normalize_half(const float* src, float (&zn)[HALF], bool vec = false) {
   if constexpr (HALF % 4 == 0) {
     if (vec) {
@@ -70,8 +71,14 @@ __device__ __forceinline__ void normalize_half(const float* src, float (&zn)[HAL
 #pragma unroll
   for (int dd = 0; dd < HALF; ++dd) ss = fmaf(zn[dd], zn[dd], ss);
   const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
+  if constexpr (RCP) {
+    const float inv = __frcp_rn(nrm);
 #pragma unroll
-  for (int dd = 0; dd < HALF; ++dd) zn[dd] = __fdiv_rn(zn[dd], nrm);
+    for (int dd = 0; dd < HALF; ++dd) zn[dd] = div_rn_by(zn[dd], nrm, inv);
+  } else {
+#pragma unroll
+    for (int dd = 0; dd < HALF; ++dd) zn[dd] = __fdiv_rn(zn[dd], nrm);
+  }
 }
 
 // First output element of address (token n, head hh): the (B, h, T_bh, kk) layout when T_bh > 0 (token
@@ -182,6 +189,43 @@ template <int S>
 __device__ __forceinline__ void warp_combine(const float* wsm, int n_sub, int c1, int kk, const int* cand, int nc,
                                              float scale, const float* gate, int32_t* si_out, float* w_out,
                                              float* sv_out);
+
+// warp_half_list with each lane normalising its own sub-keys (keys: the head's n_sub x HALF rows, global memory) in
+// registers instead of reading a block-normalised copy, so no barrier precedes it: lane l scores sub-keys l*S ..
+// l*S+S-1 (n_sub <= 32 S) with the same fmaf order as half_dot.  Element e < c1 of the sorted list goes to vo[e]
+// (score) and io[e] (sub-key id).
+template <int HALF, int S, bool RCP = true>
+__device__ __forceinline__ void warp_half_list_own(const float* zh, bool zvec, const float* keys, int n_sub, int c1,
+                                                   float* vo, int* io) {
+  const int lane = threadIdx.x & 31;
+  float zn[HALF];
+  normalize_half<HALF, RCP>(zh, zn, zvec);
+  KT key[S];
+#pragma unroll
+  for (int q = 0; q < S; ++q) {
+    const int j = lane * S + q;
+    key[q] = 0ull;  // padding: below every real key
+    if (j < n_sub) {
+      const float* kr = keys + j * HALF;
+      float kv[HALF];
+      normalize_half<HALF, RCP>(kr, kv, HALF % 4 == 0 && (reinterpret_cast<uintptr_t>(kr) & 15) == 0);
+      float sc = 0.f;
+#pragma unroll
+      for (int dd = 0; dd < HALF; ++dd) sc = fmaf(zn[dd], kv[dd], sc);
+      if (sc != sc) sc = -INFINITY;
+      key[q] = pk_key(sc, (uint32_t)j);
+    }
+  }
+  warp_sort_desc<S>(key);
+#pragma unroll
+  for (int q = 0; q < S; ++q) {
+    const int e = lane * S + q;
+    if (e < c1) {
+      vo[e] = pk_key_score(key[q]);
+      io[e] = (int)pk_key_tie(key[q]);
+    }
+  }
+}
 
 // One warp selects one address (z at zr, its two halves of HALF floats) against the head's normalised sub-keys
 // kn1/kn2 (n_sub x HALF each): (1) each half's n_sub scores, sorted by 64-bit (score, index) keys, give its top-c1

@@ -26,31 +26,6 @@ __device__ __forceinline__ bool dec_zvec(const DecodeArgs& a) {
          ((reinterpret_cast<uintptr_t>(a.proj) & 15) | (a.ldp & 3) | (a.d_a & 3) | (a.h * a.d_a & 3)) == 0;
 }
 
-// One warp's sorted top-c1 of one address half (HALF floats at zh) for n_sub <= 32: lane j normalises sub-key j
-// (keys: the head's n_sub x HALF rows) in registers and scores it with the same fmaf order as half_dot, then one
-// 32-key bitonic sort orders (score desc, index asc).  Element e < c1 goes to vo[e] (score) and io[e] (sub-key id).
-template <int HALF>
-__device__ __forceinline__ void warp_half_list_own(const float* zh, bool zvec, const float* keys, int n_sub, int c1,
-                                                   float* vo, int* io) {
-  const int lane = threadIdx.x & 31;
-  float zn[HALF], kv[HALF];
-  normalize_half<HALF>(zh, zn, zvec);
-  KT key[1] = {0ull};  // padding: below every real key
-  if (lane < n_sub) {
-    const float* kr = keys + lane * HALF;
-    normalize_half<HALF>(kr, kv, HALF % 4 == 0 && (reinterpret_cast<uintptr_t>(kr) & 15) == 0);
-    float sc = 0.f;
-#pragma unroll
-    for (int dd = 0; dd < HALF; ++dd) sc = fmaf(zn[dd], kv[dd], sc);
-    if (sc != sc) sc = -INFINITY;
-    key[0] = pk_key(sc, (uint32_t)lane);
-  }
-  warp_sort_desc<1>(key);
-  if (lane < c1) {
-    vo[lane] = pk_key_score(key[0]);
-    io[lane] = (int)pk_key_tie(key[0]);
-  }
-}
 
 // HALF > 0: the step selects its slots itself (warps 0-3 the halves of the write and read addresses with SH sub-keys
 // per lane, warps 0 and 2 the combines with S candidates per lane; shared-memory normalised sub-keys); HALF == 0:
@@ -102,7 +77,7 @@ __global__ void __launch_bounds__(LBT, LBM) rt_decode_kernel(DecodeArgs a) {
         float* wsm = dec_smem + 2 * n_sub * HALF + ad * 128;  // per address: v1, i1, v2, i2
         const float* zh = a.proj + (int64_t)s * a.ldp + (ad ? a.h * a.d_a : 0) + hh * a.d_a + hf * HALF;
         const float* keys = (hf ? a.keys2 : a.keys1) + (int64_t)hh * n_sub * HALF;
-        warp_half_list_own<HALF>(zh, dec_zvec<HALF>(a), keys, n_sub, c1, wsm + hf * 64,
+        warp_half_list_own<HALF, 1, false>(zh, dec_zvec<HALF>(a), keys, n_sub, c1, wsm + hf * 64,
                                  reinterpret_cast<int*>(wsm + hf * 64 + 32));
       }
     }

@@ -22,6 +22,12 @@ static inline uint32_t __float_as_uint(float f) { uint32_t u; memcpy(&u, &f, 4);
 static inline float __uint_as_float(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
 static inline float __fdiv_rn(float a, float b) { return a / b; }
 static inline float __fsqrt_rn(float a) { return std::sqrt(a); }
+static inline float __frcp_rn(float a) { return 1.0f / a; }
+// the kernels' shared-divisor quotient (common.cuh), with the host's fused multiply-add
+static inline float div_rn_by(float x, float d, float inv) {
+  const float q = x * inv;
+  return std::fma(std::fma(-q, d, x), inv, q);
+}
 template <class T> static inline T __ldg(const T* p) { return *p; }
 struct float4 { float x, y, z, w; };
 struct int4 { int x, y, z, w; };
