@@ -264,11 +264,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 // to the odd CTA's, and each finished accumulator to both CTAs' `acc_full`; every epilogue warp of both
 // CTAs arrives on the even CTA's `acc_empty`.  All waits are the bounded mbarrier waits; the two cluster barriers
 // (after set-up, before TMEM release) are reached on every path.
+// SPLIT (K = 2 x kwrap, x = [hi | lo] against one w): a stage holds the hi and the lo A tiles of one K block and
+// the one B tile both multiply, so each weight tile crosses L2 -> SMEM once instead of twice (the kernel is bound by
+// that operand traffic: its MMA thread waits on `full` for about 40 % of its time, on the accumulators for about 3 %).
 constexpr int PAIR_N = 256;
-template <int DEEP>
+template <int DEEP, bool SPLIT = false>
 struct Cfg2 {
-  static constexpr int STAGES = 5 + DEEP;
-  static constexpr uint32_t B_BYTES = (PAIR_N / 2) * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = SPLIT ? 4 : 5 + DEEP;
+  static constexpr uint32_t B_BYTES = (PAIR_N / 2) * BK * 2, STAGE_BYTES = (SPLIT ? 2 : 1) * A_BYTES + B_BYTES;
   static constexpr size_t RING_BYTES = (size_t)STAGES * STAGE_BYTES;
   static constexpr size_t SMEM_BYTES = RING_BYTES + (size_t)EPI_WARPS * 32 * STG_LD * 4 + 1024;
   static constexpr uint32_t TMEM_COLS = 2 * PAIR_N;
@@ -325,12 +328,13 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-template <typename Epi>
+template <typename Epi, bool SPLIT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int64_t rows,
                     int K, int n, Epi epi, int kwrap) {
   pdl_enter();
-  using C = Cfg2<RingStages<Epi>::deep>;
+  using C = Cfg2<RingStages<Epi>::deep, SPLIT>;
+  constexpr uint32_t B_OFF = (SPLIT ? 2 : 1) * A_BYTES;  // the B tile's offset in a stage
   extern __shared__ __align__(1024) unsigned char dsmem[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -344,7 +348,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int kt_count = (K + BK - 1) / BK;
+  const int kt_count = ((SPLIT ? kwrap : K) + BK - 1) / BK;
   const int tiles_n = (n + PAIR_N - 1) / PAIR_N;
   const int64_t tiles = (int64_t)tiles_n * ((rows + 2 * BM - 1) / (2 * BM));
 
@@ -396,7 +400,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * C::STAGE_BYTES);
           const uint32_t fb = peer_addr(&full_bar[s], 0);
           load_2d_pair(&tmA, fb, a_dst, kt * BK, m0);
-          load_2d_pair(&tmB, fb, a_dst + A_BYTES, (kt * BK) % kwrap, nb);
+          if constexpr (SPLIT) load_2d_pair(&tmA, fb, a_dst + A_BYTES, kt * BK + kwrap, m0);
+          load_2d_pair(&tmB, fb, a_dst + B_OFF, (kt * BK) % kwrap, nb);
         }
       }
     }
@@ -421,10 +426,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t a_base = smem_u32(ring + s * C::STAGE_BYTES);
-          const uint32_t b_base = a_base + A_BYTES;
+          const uint32_t b_base = a_base + B_OFF;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             umma_bf16_pair(dt, sw128_desc(a_base + kk * 32), sw128_desc(b_base + kk * 32), idesc, (kt | kk) != 0);
+          if constexpr (SPLIT) {  // the lo half of the same K block against the same weights
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              umma_bf16_pair(dt, sw128_desc(a_base + A_BYTES + kk * 32), sw128_desc(b_base + kk * 32), idesc, 1u);
+          }
           umma_commit_own(&empty_bar[s]);
         }
         if (ok) umma_commit_pair(&acc_full[buf]);
@@ -574,15 +584,15 @@ static cudaError_t launch_tc_bn(const bf16_t* x, int64_t ldx, const bf16_t* w, i
 }
 
 // CTA-pair launch: clusters of two, as many pairs as fit at once (the persistent loop covers the rest).
-template <typename Epi>
-static cudaError_t launch_tc_pair(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K,
-                                  int n, Epi epi, cudaStream_t st, int kwrap) {
-  using C = tc::Cfg2<tc::RingStages<Epi>::deep>;
+template <typename Epi, bool SPLIT>
+static cudaError_t launch_tc_pair_k(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K,
+                                    int n, Epi epi, cudaStream_t st, int kwrap) {
+  using C = tc::Cfg2<tc::RingStages<Epi>::deep, SPLIT>;
   CUtensorMap ma, mb;
   if (!tc::make_map(&ma, x, (uint64_t)K, (uint64_t)rows, (uint64_t)ldx, tc::BM) ||
       !tc::make_map(&mb, w, (uint64_t)kwrap, (uint64_t)n, (uint64_t)ldw, tc::PAIR_N / 2))
     return cudaErrorInvalidValue;
-  auto kern = tc::gemm_tc2_kernel<Epi>;
+  auto kern = tc::gemm_tc2_kernel<Epi, SPLIT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   static int max_pairs[64] = {0};
@@ -605,6 +615,14 @@ static cudaError_t launch_tc_pair(const bf16_t* x, int64_t ldx, const bf16_t* w,
   const int pairs = (int)ceil_div(tiles, ceil_div(tiles, (int64_t)pairs_cap));  // same rounds, fewest pairs
   LaunchScope scope_("gemm_tc", st);
   return launch_k(kern, dim3(2 * pairs), dim3(tc::THREADS), C::SMEM_BYTES, st, ma, mb, rows, K, n, epi, kwrap);
+}
+// A [hi | lo] input against one weight (K = 2 x kwrap) takes the split stages.
+template <typename Epi>
+static cudaError_t launch_tc_pair(const bf16_t* x, int64_t ldx, const bf16_t* w, int64_t ldw, int64_t rows, int K,
+                                  int n, Epi epi, cudaStream_t st, int kwrap) {
+  if (K == 2 * kwrap && kwrap % tc::BK == 0)
+    return launch_tc_pair_k<Epi, true>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
+  return launch_tc_pair_k<Epi, false>(x, ldx, w, ldw, rows, K, n, epi, st, kwrap);
 }
 
 // Column tile: 256 wide moves a third fewer operand bytes per flop; 128 wide when it finishes in fewer rounds of
