@@ -30,6 +30,17 @@ __device__ __forceinline__ float div_rn_by(float x, float d, float inv) {
   return fmaf(fmaf(-q, d, x), inv, q);
 }
 
+// acc = a * b + acc on two float lanes at once (sm_100's paired FMA): each lane rounds exactly as fmaf does, so the
+// results equal two scalar fmaf, at half the instructions.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 acc) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
+        "l"(*reinterpret_cast<const uint64_t*>(&acc)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+
 // Correctly rounded 1/sqrt(v): sqrt then divide, both IEEE round-to-nearest, as the CPU reference computes
 // torch.rsqrt (a square root and a division).
 __device__ __forceinline__ float rsqrt_rn(float v) { return __fdiv_rn(1.0f, __fsqrt_rn(v)); }

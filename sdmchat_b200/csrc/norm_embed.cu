@@ -294,30 +294,26 @@ __global__ void ts_gather_vec_kernel(const int32_t* __restrict__ si, const float
   const float my_w = lane < k ? w[item * k + lane] : 0.f;
   const bool active = 8 * lane < dh;
   const bf16_t* base = values + (int64_t)hh * M * dh + 8 * lane;
-  float acc[8];
+  float2 acc[4];  // columns (2q, 2q + 1) of the lane's eight
 #pragma unroll
-  for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+  for (int q = 0; q < 4; ++q) acc[q] = make_float2(0.f, 0.f);
 #pragma unroll 4
   for (int j = 0; j < k; ++j) {
     const int slot = __shfl_sync(0xffffffffu, my_s, j);
     const float wj = __shfl_sync(0xffffffffu, my_w, j);
     if (active) {
       const uint4 u = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)slot * dh));  // read-only: L1 reuse
-      const float4 a = unpack_bf16x4(make_uint2(u.x, u.y)), b = unpack_bf16x4(make_uint2(u.z, u.w));
-      acc[0] = fmaf(wj, a.x, acc[0]);
-      acc[1] = fmaf(wj, a.y, acc[1]);
-      acc[2] = fmaf(wj, a.z, acc[2]);
-      acc[3] = fmaf(wj, a.w, acc[3]);
-      acc[4] = fmaf(wj, b.x, acc[4]);
-      acc[5] = fmaf(wj, b.y, acc[5]);
-      acc[6] = fmaf(wj, b.z, acc[6]);
-      acc[7] = fmaf(wj, b.w, acc[7]);
+      const float2 w2 = make_float2(wj, wj);
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)  // a bfloat16 pair widened exactly: the low half to the first float
+        acc[q] = fma2(w2, make_float2(__uint_as_float(uw[q] << 16), __uint_as_float(uw[q] & 0xFFFF0000u)), acc[q]);
     }
   }
   if (active) {
     const int64_t n = item / h, c = (int64_t)hh * dh + 8 * lane;
-    store_split4<bf16_t>(r, n, (int64_t)h * dh, c, make_float4(acc[0], acc[1], acc[2], acc[3]), split);
-    store_split4<bf16_t>(r, n, (int64_t)h * dh, c + 4, make_float4(acc[4], acc[5], acc[6], acc[7]), split);
+    store_split4<bf16_t>(r, n, (int64_t)h * dh, c, make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y), split);
+    store_split4<bf16_t>(r, n, (int64_t)h * dh, c + 4, make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y), split);
   }
 }
 

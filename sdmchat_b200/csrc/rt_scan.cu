@@ -135,11 +135,11 @@ __device__ __forceinline__ void copy_words_async(void* dst, const void* src, int
 __device__ __forceinline__ void copy_rows32_async(void* dst, const void* src, int rows, int w, int cw, int64_t stride,
                                                   int tid, int nt);
 
-__device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {
-  acc.x = fmaf(w, v.x, acc.x);
-  acc.y = fmaf(w, v.y, acc.y);
-  acc.z = fmaf(w, v.z, acc.z);
-  acc.w = fmaf(w, v.w, acc.w);
+__device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {  // acc += w * v, as four fmaf
+  const float2 ww = make_float2(w, w);
+  const float2 lo = fma2(ww, make_float2(v.x, v.y), make_float2(acc.x, acc.y));
+  const float2 hi = fma2(ww, make_float2(v.z, v.w), make_float2(acc.z, acc.w));
+  acc = make_float4(lo.x, lo.y, hi.x, hi.y);
 }
 
 // Exclusive prefix sum of in(0) .. in(n-1) into out[0, n) by all LIST_THREADS threads (out must not be what in()
