@@ -297,17 +297,35 @@ __global__ void ts_gather_vec_kernel(const int32_t* __restrict__ si, const float
   float2 acc[4];  // columns (2q, 2q + 1) of the lane's eight
 #pragma unroll
   for (int q = 0; q < 4; ++q) acc[q] = make_float2(0.f, 0.f);
-#pragma unroll 4
-  for (int j = 0; j < k; ++j) {
-    const int slot = __shfl_sync(0xffffffffu, my_s, j);
-    const float wj = __shfl_sync(0xffffffffu, my_w, j);
-    if (active) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)slot * dh));  // read-only: L1 reuse
-      const float2 w2 = make_float2(wj, wj);
-      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+  auto row = [&](int slot, float wj) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)slot * dh));  // read-only: L1 reuse
+    const float2 w2 = make_float2(wj, wj);
+    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q)  // a bfloat16 pair widened exactly: the low half to the first float
-        acc[q] = fma2(w2, make_float2(__uint_as_float(uw[q] << 16), __uint_as_float(uw[q] & 0xFFFF0000u)), acc[q]);
+    for (int q = 0; q < 4; ++q)  // a bfloat16 pair widened exactly: the low half to the first float
+      acc[q] = fma2(w2, make_float2(__uint_as_float(uw[q] << 16), __uint_as_float(uw[q] & 0xFFFF0000u)), acc[q]);
+  };
+  if ((k & 3) == 0 && ((reinterpret_cast<uintptr_t>(si + item * k) | reinterpret_cast<uintptr_t>(w + item * k)) & 15) == 0) {
+    // four (slot, weight) pairs per pair of 16-byte loads, the same address on every lane (one L1 broadcast)
+    const int4* s4 = reinterpret_cast<const int4*>(si + item * k);
+    const float4* w4 = reinterpret_cast<const float4*>(w + item * k);
+#pragma unroll 2
+    for (int j = 0; j < k / 4; ++j) {
+      const int4 ss = __ldg(s4 + j);
+      const float4 ww = __ldg(w4 + j);
+      if (active) {
+        row(ss.x, ww.x);
+        row(ss.y, ww.y);
+        row(ss.z, ww.z);
+        row(ss.w, ww.w);
+      }
+    }
+  } else {
+#pragma unroll 4
+    for (int j = 0; j < k; ++j) {
+      const int slot = __shfl_sync(0xffffffffu, my_s, j);
+      const float wj = __shfl_sync(0xffffffffu, my_w, j);
+      if (active) row(slot, wj);
     }
   }
   if (active) {
