@@ -92,24 +92,37 @@ __device__ __forceinline__ uint32_t fast_key(float s, uint32_t j) {
   const uint32_t m = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
   return (m & ~FK_MASK) | (FK_MASK - j);
 }
+// Batcher's odd-even merge sort network on C keys (C a power of two): comparator I as (a, b), a < b, the larger key
+// to a.  63 comparators for 16 keys and 191 for 32, against 80 and 240 in a bitonic network; evaluated at compile
+// time, so every comparator is a pair of fixed registers.
+constexpr int oe_pair(int C, int idx) {  // comparator idx packed as a * 256 + b; -1 past the last; the count at -1
+  int n = 0;
+  for (int p = 1; p < C; p <<= 1)
+    for (int kk = p; kk >= 1; kk >>= 1)
+      for (int j = kk % p; j + kk < C; j += 2 * kk)
+        for (int i = 0; i < kk; ++i) {
+          const int a = i + j, b = i + j + kk;
+          if (b < C && a / (2 * p) == b / (2 * p)) {
+            if (n == idx) return a * 256 + b;
+            ++n;
+          }
+        }
+  return idx < 0 ? n : -1;
+}
+template <int C, int I>
+__device__ __forceinline__ void oe_apply(uint32_t (&k)[C]) {
+  if constexpr (I < oe_pair(C, -1)) {
+    constexpr int pr = oe_pair(C, I), a = pr >> 8, b = pr & 255;
+    const uint32_t hi = max(k[a], k[b]), lo = min(k[a], k[b]);
+    k[a] = hi;
+    k[b] = lo;
+    oe_apply<C, I + 1>(k);
+  }
+}
+// k[0..C) sorted descending; the keys are distinct, so any sorting network gives the same order.
 template <int C>
 __device__ __forceinline__ void bitonic_sort_desc32(uint32_t (&k)[C]) {
-#pragma unroll
-  for (int size = 2; size <= C; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-      for (int i = 0; i < C; ++i) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const uint32_t hi = max(k[i], k[j]), lo = min(k[i], k[j]);
-          const bool desc = (i & size) == 0;
-          k[i] = desc ? hi : lo;
-          k[j] = desc ? lo : hi;
-        }
-      }
-    }
-  }
+  oe_apply<C, 0>(k);
 }
 // Sort only k[0..NS) descending (NS a power of two dividing C); entries past NS are left as they are.
 template <int C, int NS>
