@@ -31,14 +31,18 @@ __device__ __forceinline__ float div_rn_by(float x, float d, float inv) {
 }
 
 // acc = a * b + acc on two float lanes at once (sm_100's paired FMA): each lane rounds exactly as fmaf does, so the
-// results equal two scalar fmaf, at half the instructions.
+// results equal two scalar fmaf, at half the instructions.  The lanes are packed into 64-bit registers inside the
+// asm (mov.b64 of a register pair), not by reinterpreting a float2 object's memory, which the compiler's alias
+// analysis may order before the stores that fill it.
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 acc) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
-        "l"(*reinterpret_cast<const uint64_t*>(&acc)));
-  return *reinterpret_cast<const float2*>(&d);
+  float2 r;
+  asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+      "fma.rn.f32x2 pd, pa, pb, pc;\n\t"
+      "mov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(acc.x), "f"(acc.y));
+  return r;
 }
 
 // Correctly rounded 1/sqrt(v): sqrt then divide, both IEEE round-to-nearest, as the CPU reference computes
