@@ -1301,14 +1301,18 @@ static cudaError_t launch_pk_warp(const PkArgs& a, int c1, int kk, cudaStream_t 
   }
 }
 
-// Launches with at most this many addresses use the warp-per-address kernel.
+// Launches with at most this many addresses use the warp-per-address kernel (measured crossovers: with top-16
+// lists the warp kernel keeps up with the block kernels to about 8,192 addresses; with top-32 lists over 72
+// sub-keys it takes 47 us at 4,096 addresses against 43 us for pk_fast_kernel, and 82 us against 43 us at 8,192).
 constexpr int64_t PK_WARP_MAX_ADDRESSES = 8192;
+constexpr int64_t PK_WARP_MAX_ADDRESSES_C32 = 3072;
 
 cudaError_t launch_pk_address(const PkArgs& a, cudaStream_t st) {
   if (a.N == 0) return cudaSuccess;
   const int c1 = a.k < a.n_sub ? a.k : a.n_sub;
   const int kk = a.k < c1 * c1 ? a.k : c1 * c1;
-  if (a.N * a.h * (a.pairs > 1 ? 2 : 1) <= PK_WARP_MAX_ADDRESSES && a.n_sub <= 128 && c1 <= 32 && kk <= 32) {
+  const int64_t warp_max = c1 > 16 ? PK_WARP_MAX_ADDRESSES_C32 : PK_WARP_MAX_ADDRESSES;
+  if (a.N * a.h * (a.pairs > 1 ? 2 : 1) <= warp_max && a.n_sub <= 128 && c1 <= 32 && kk <= 32) {
     switch (a.d_a / 2) {
       case 2: return launch_pk_warp<2>(a, c1, kk, st);
       case 4: return launch_pk_warp<4>(a, c1, kk, st);
