@@ -143,14 +143,23 @@ __device__ __forceinline__ void fma4(float4& acc, float w, const float4& v) {  /
 }
 
 // Exclusive prefix sum of in(0) .. in(n-1) into out[0, n) by all LIST_THREADS threads (out must not be what in()
-// reads); returns the total.  Ends with a barrier.
-template <typename In>
-__device__ __forceinline__ int block_exclusive_scan(In in, int* out, int n, int* wtot) {
+// reads); returns the total.  Ends with a barrier.  Thread t takes elements [t * per, (t + 1) * per); when that is
+// four (n = 4 x LIST_THREADS, the usual 1,024 slots) it reads them as in4(t) = in(4t .. 4t + 3) and writes them
+// with one 16-byte store, so a warp's accesses cover consecutive 16-byte words (no bank conflicts).
+template <typename In, typename In4>
+__device__ __forceinline__ int block_exclusive_scan(In in, In4 in4, int* out, int n, int* wtot) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int per = (n + LIST_THREADS - 1) / LIST_THREADS;
+  const bool v4 = n == 4 * LIST_THREADS && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
   const int s0 = tid * per, s1 = min(n, s0 + per);
+  int4 q = make_int4(0, 0, 0, 0);
   int sum = 0;
-  for (int i = s0; i < s1; ++i) sum += in(i);
+  if (v4) {
+    q = in4(tid);
+    sum = q.x + q.y + q.z + q.w;
+  } else {
+    for (int i = s0; i < s1; ++i) sum += in(i);
+  }
   int x = sum;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -170,13 +179,33 @@ __device__ __forceinline__ int block_exclusive_scan(In in, int* out, int n, int*
   }
   __syncthreads();
   int base = (warp ? wtot[warp - 1] : 0) + x - sum;
-  for (int i = s0; i < s1; ++i) {
-    out[i] = base;
-    base += in(i);
+  if (v4) {
+    reinterpret_cast<int4*>(out)[tid] = make_int4(base, base + q.x, base + q.x + q.y, base + q.x + q.y + q.z);
+  } else {
+    for (int i = s0; i < s1; ++i) {
+      out[i] = base;
+      base += in(i);
+    }
   }
   const int total = wtot[LIST_WARPS - 1];
   __syncthreads();
   return total;
+}
+
+// The chunk's write ids and weights in shared memory with k = 16: (token t, write index i) is held at word
+// t * 16 + (i ^ ((t >> 1) & 15)), a permutation within each token's row, so the 32 tokens of one write index (read
+// together when the slot masks are built) fall in 32 distinct banks instead of two.  The map is its own inverse.
+template <int K>
+__device__ __forceinline__ int wslot(int e) {
+  if constexpr (K == 16) return (e & ~15) | ((e & 15) ^ ((e >> 5) & 15));
+  else return e;
+}
+// four consecutive elements u = 0..3 moved to positions u ^ m
+template <typename V4>
+__device__ __forceinline__ V4 perm4(V4 v, int m) {
+  if (m & 1) v = V4{v.y, v.x, v.w, v.z};
+  if (m & 2) v = V4{v.z, v.w, v.x, v.y};
+  return v;
 }
 
 // ------------------------------------------------------------------------------------------------- list kernel
@@ -264,17 +293,20 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
     for (int e4 = tid; e4 < E / 4; e4 += LIST_THREADS) {
       const int4 sw = reinterpret_cast<const int4*>(a.siw + sel0)[e4];
       const int4 sr = reinterpret_cast<const int4*>(a.sir + sel0)[e4];
-      reinterpret_cast<int4*>(siw_s)[e4] = make_int4(min(max(sw.x, 0), M - 1), min(max(sw.y, 0), M - 1),
-                                                     min(max(sw.z, 0), M - 1), min(max(sw.w, 0), M - 1));
+      // k = 16: the four ids land permuted in one aligned group of the token's row (wslot)
+      const int sq = K == 16 ? (e4 >> 3) & 15 : 0, d4 = (e4 & ~3) | ((e4 & 3) ^ (sq >> 2));
+      reinterpret_cast<int4*>(siw_s)[d4] = perm4(make_int4(min(max(sw.x, 0), M - 1), min(max(sw.y, 0), M - 1),
+                                                           min(max(sw.z, 0), M - 1), min(max(sw.w, 0), M - 1)),
+                                                 sq & 3);
       reinterpret_cast<int4*>(sir_s)[e4] = make_int4(min(max(sr.x, 0), M - 1), min(max(sr.y, 0), M - 1),
                                                      min(max(sr.z, 0), M - 1), min(max(sr.w, 0), M - 1));
-      reinterpret_cast<float4*>(ww_s)[e4] = reinterpret_cast<const float4*>(a.ww + sel0)[e4];
+      reinterpret_cast<float4*>(ww_s)[d4] = perm4(reinterpret_cast<const float4*>(a.ww + sel0)[e4], sq & 3);
       reinterpret_cast<float4*>(wr_s)[e4] = reinterpret_cast<const float4*>(a.wr + sel0)[e4];
     }
   } else {
     for (int e = tid; e < E; e += LIST_THREADS) {
-      siw_s[e] = min(max(a.siw[sel0 + e], 0), M - 1);
-      ww_s[e] = a.ww[sel0 + e];
+      siw_s[wslot<K>(e)] = min(max(a.siw[sel0 + e], 0), M - 1);
+      ww_s[wslot<K>(e)] = a.ww[sel0 + e];
       sir_s[e] = min(max(a.sir[sel0 + e], 0), M - 1);
       wr_s[e] = a.wr[sel0 + e];
     }
@@ -337,7 +369,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
       const bool ok = t < Lc;
       const unsigned act = __ballot_sync(FULL, ok);
       if (ok) {
-        const int r = siw_s[t * k + i];
+        const int r = siw_s[wslot<K>(t * k + i)];
         const unsigned peers = __match_any_sync(act, r);
         if (lane == __ffs(peers) - 1) {
           const unsigned long long bits = (unsigned long long)peers << ((p / k) * 32);
@@ -348,7 +380,13 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
     }
     __syncthreads();
     if (misc[11] == 0) {
-      block_exclusive_scan([=](int r) { return __popcll(tmask[r]); }, run, M, misc);
+      block_exclusive_scan([=](int r) { return __popcll(tmask[r]); },
+                           [=](int g) {
+                             const ulonglong2 m0 = reinterpret_cast<const ulonglong2*>(tmask)[2 * g];
+                             const ulonglong2 m1 = reinterpret_cast<const ulonglong2*>(tmask)[2 * g + 1];
+                             return make_int4(__popcll(m0.x), __popcll(m0.y), __popcll(m1.x), __popcll(m1.y));
+                           },
+                           run, M, misc);
 #pragma unroll
       for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
         const int e = tid + q * LIST_THREADS;
@@ -371,11 +409,12 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
         if (e < E) pos[q] = atomicAdd(&cntt[siw_s[e]], 1);
       }
       __syncthreads();
-      block_exclusive_scan([=](int r) { return cntt[r]; }, run, M, misc);
+      block_exclusive_scan([=](int r) { return cntt[r]; },
+                           [=](int g) { return reinterpret_cast<const int4*>(cntt)[g]; }, run, M, misc);
 #pragma unroll
       for (int q = 0; q < CH_MAX_E / LIST_THREADS; ++q) {
         const int e = tid + q * LIST_THREADS;
-        if (e < E) ent[run[siw_s[e]] + pos[q]] = make_int2(e, __float_as_int(ww_s[e]));
+        if (e < E) ent[run[siw_s[e]] + pos[q]] = make_int2(wslot<K>(e), __float_as_int(ww_s[e]));  // (t, i) order
       }
       __syncthreads();
       for (int r = tid; r < M; r += LIST_THREADS) {
@@ -392,7 +431,7 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
         }
       }
       __syncthreads();
-      for (int x = tid; x < E; x += LIST_THREADS) ent[x].x = (siw_s[ent[x].x] << 16) | (ent[x].x / k);
+      for (int x = tid; x < E; x += LIST_THREADS) ent[x].x = (siw_s[wslot<K>(ent[x].x)] << 16) | (ent[x].x / k);
       __syncthreads();
     }
   }
@@ -424,8 +463,10 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
         const int* ssi = t > 0 ? siw_s + (t - 1) * k : prev_si;
         const float* sw = t > 0 ? ww_s + (t - 1) * k : prev_w;
         float m = 0.f;
-        for (int j = 0; j < k; ++j)
-          if (ri == ssi[j]) m += sw[j];
+        for (int j = 0; j < k; ++j) {
+          const int jj = t > 0 ? wslot<K>((t - 1) * k + j) - (t - 1) * k : j;  // write index order
+          if (ri == ssi[jj]) m += sw[jj];
+        }
         dsum = warp_sum(wi * m);
       }
       const int64_t tok = tok0 + t;
@@ -580,7 +621,8 @@ __global__ void __launch_bounds__(LIST_THREADS) rt_lists_kernel(ScanArgs a, int 
     cntt[r] = vc | (vc > 0 ? 1 << 11 : 0) | (vc >= kLongRun ? 1 << 22 : 0);
   }
   __syncthreads();
-  const int tot = block_exclusive_scan([=](int r) { return cntt[r]; }, pfx, M, misc);
+  const int tot = block_exclusive_scan([=](int r) { return cntt[r]; },
+                                       [=](int g) { return reinterpret_cast<const int4*>(cntt)[g]; }, pfx, M, misc);
   const int nent = tot & 0x7FF, njobs = (tot >> 11) & 0x7FF, nlong = tot >> 22;
   int2* jobs_s = reinterpret_cast<int2*>(rec_s);
   int2* ents_s = reinterpret_cast<int2*>(rec_s + rl.ents);
