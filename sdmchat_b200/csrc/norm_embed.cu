@@ -335,6 +335,59 @@ __global__ void ts_gather_vec_kernel(const int32_t* __restrict__ si, const float
   }
 }
 
+// Prefill gathers with every lane busy: an item's dh / 8 lanes (G, eight columns each) are packed back to back
+// across the block (blockDim.x / G items per block, a warp may hold lanes of two items), where
+// ts_gather_vec_kernel gives each item a whole warp and leaves 32 - G lanes idle (8 of 32 at dh = 192).  Each lane
+// sums its eight columns over the item's k rows in slot order with the same fused multiply-adds, so the results are
+// the same bit for bit.  Needs k % 4 == 0 and 16-byte aligned si, w and values.
+__global__ void __launch_bounds__(256) ts_gather_dense_kernel(const int32_t* __restrict__ si,
+                                                              const float* __restrict__ w,
+                                                              const bf16_t* __restrict__ values, int64_t N, int h,
+                                                              int M, int dh, int k, bf16_t* __restrict__ r, int split) {
+  pdl_enter();
+  const int G = dh >> 3;
+  const int il = (int)threadIdx.x / G, chunk = (int)threadIdx.x - il * G;
+  const int64_t item = (int64_t)blockIdx.x * ((int)blockDim.x / G) + il;
+  if (item >= N * h) return;
+  const int hh = (int)(item % h);
+  const bf16_t* base = values + (int64_t)hh * M * dh + 8 * chunk;
+  float2 acc[4];  // columns (2q, 2q + 1) of the lane's eight
+#pragma unroll
+  for (int q = 0; q < 4; ++q) acc[q] = make_float2(0.f, 0.f);
+  auto row = [&](int slot, float wj) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)slot * dh));  // read-only: L1 reuse
+    const float2 w2 = make_float2(wj, wj);
+    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)  // a bfloat16 pair widened exactly: the low half to the first float
+      acc[q] = fma2(w2, make_float2(__uint_as_float(uw[q] << 16), __uint_as_float(uw[q] & 0xFFFF0000u)), acc[q]);
+  };
+  const int4* s4 = reinterpret_cast<const int4*>(si + item * k);
+  const float4* w4 = reinterpret_cast<const float4*>(w + item * k);
+#pragma unroll 2
+  for (int j = 0; j < k / 4; ++j) {
+    const int4 ss = __ldg(s4 + j);
+    const float4 ww = __ldg(w4 + j);
+    row(ss.x, ww.x);
+    row(ss.y, ww.y);
+    row(ss.z, ww.z);
+    row(ss.w, ww.w);
+  }
+  const int64_t n = item / h, c = (int64_t)hh * dh + 8 * chunk;
+  store_split4<bf16_t>(r, n, (int64_t)h * dh, c, make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y), split);
+  store_split4<bf16_t>(r, n, (int64_t)h * dh, c + 4, make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y), split);
+}
+
+// Items per block of ts_gather_dense_kernel for G lanes per item: the fewest that fill whole warps, doubled while
+// the block stays within 256 threads; 0 when G lanes of one item do not fit.
+static int ts_dense_items(int G) {
+  int ipb = 1;
+  while ((G * ipb) % 32) ++ipb;
+  if (G * ipb > 256) return 0;
+  while (G * ipb * 2 <= 256) ipb *= 2;
+  return ipb;
+}
+
 // Decode-sized gathers: a block of 8 warps takes 2 (token, head) items, each item's k rows split over 4 warps (k/4
 // loads in flight per warp), the 4 partial rows summed in shared memory in warp order.
 __global__ void __launch_bounds__(256) ts_gather_split_kernel(const int32_t* __restrict__ si,
@@ -589,9 +642,16 @@ cudaError_t launch_ts_gather(const int32_t* si, const float* w, const T* values,
         return launch_k(ts_gather_split_kernel, dim3((unsigned)ceil_div(N * h, 2)), dim3(256), 0, st, si, w, values,
                         N, h, M, dh, k, r, split);
       }
+    }
+    const int ipb = dh % 8 == 0 ? ts_dense_items(dh / 8) : 0;
+    if (ipb > 0 && k % 4 == 0 && N * h >= 148 * 8 &&
+        ((reinterpret_cast<uintptr_t>(si) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(values)) &
+         15) == 0)
+      return launch_k(ts_gather_dense_kernel, dim3((unsigned)ceil_div(N * h, ipb)), dim3((unsigned)(ipb * (dh / 8))),
+                      0, st, si, w, values, N, h, M, dh, k, r, split);
+    if (dh % 8 == 0 && dh <= 256 && k <= 32 && (reinterpret_cast<uintptr_t>(values) & 15) == 0)
       return launch_k(ts_gather_vec_kernel, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, si, w, values, N,
                       h, M, dh, k, r, split);
-    }
   }
   return launch_k(ts_gather_kernel<T>, dim3((unsigned)ceil_div(N * h, 8)), dim3(256), 0, st, si, w, values, N, h, M,
                   dh, k, r, split);
