@@ -210,3 +210,26 @@ def test_scaled_trained_sdm_d1536_against_oracle(cuda_ok):
     ok, n, bad = same_selection(ts.last_si.cpu().numpy().reshape(si_o.shape), si_o, margin, 1e-6)
     assert ok, f"{bad} of {n}"
     assert rel(out, want) < 2e-3
+
+
+def test_scaled_trained_sdm_bf16_dense_gather_equals_small_calls(cuda_ok):
+    """The bf16 value gather of scaled FULL's TrainedSdm (dh 384): a large call (2,400 (token, head) items: the
+    dense-lane gather) against calls of 40 tokens (160 items: the per-warp gather), both summing each column over the
+    32 picked rows in slot order with fused multiply-adds.  Selections identical, outputs to the output GEMM's
+    rounding (the two call sizes take different GEMM kernels)."""
+    rng = np.random.default_rng(23)
+    torch.manual_seed(23)
+    n_sub = O.matched_sdm_n_sub(1536, 4096, 4, 32)
+    ts = S.TrainedSdm(1536, n_sub=n_sub, heads=4, d_a=32, k=32)
+    with torch.no_grad():
+        torch.nn.init.normal_(ts.values, std=0.02)
+        torch.nn.init.normal_(ts.wo.weight, std=0.02)
+    ts = ts.to(DEV).to(torch.bfloat16)
+    x = torch.from_numpy(rng.standard_normal((1, 600, 1536)).astype(np.float32)).to(DEV).bfloat16()
+    with torch.no_grad():
+        big = ts(x)
+        si_big = ts.last_si.clone().reshape(600, 4, 32)
+        for c0 in (0, 280, 560):
+            small = ts(x[:, c0:c0 + 40])
+            assert torch.equal(si_big[c0:c0 + 40], ts.last_si.reshape(40, 4, 32)), c0
+            assert rel_bf16(small.float().cpu().numpy(), big[:, c0:c0 + 40].float().cpu().numpy()) < 1e-4, c0
